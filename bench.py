@@ -1,0 +1,447 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized projection hot path (BASELINE metric:
+"Q4_K/Q8_0 GEMV HBM GB/s (% of peak); DFlash 16-token draft-block fwd/s").
+
+Default workload (the M = 1 Q4_K GEMV): one step is the
+DFlash decoder FFN of one token -- gate 4096->14336, up 4096->14336 (Q4_K),
+SiLU-gate, down 14336->4096 (Q4_K) -- through the C ABI (liblaguna_cuda.so).
+Weights are raw Q4_K super-blocks rotated through a pool larger than 3x the
+126 MB L2, so every step streams its 99 MB of weights from HBM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+  python bench.py --impl reference ...   # the reference's own shader code on host cores
+
+Multi-GPU (torchrun, one rank per GPU): each rank runs an independent token
+stream on its own weights (replicas, no collective on the data path);
+value = all ranks' bytes / max-over-ranks time ("scaling": "weak").
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MEASURED_PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+L2_BYTES = 126 * 1024 * 1024
+
+METRIC = "Q4_K/Q8_0 GEMV HBM GB/s (% of peak); DFlash 16-token draft-block fwd/s"
+
+
+def peaks():
+    try:
+        with open(MEASURED_PEAKS) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# Workloads: a list of projections (dtype, m, k, n) + the per-step op chain.
+
+WORKLOADS = {
+    # config 1: M=1 Q4_K GEMVs of the DFlash FFN (gate/up 4096->14336, down 14336->4096)
+    "ffn_q4k_m1": dict(dtype="q4k", m=1, shapes=[("gate", 4096, 14336), ("up", 4096, 14336),
+                                                  ("down", 14336, 4096)], ffn=True, config=1),
+    # config 0: Q8_0 4096x4096 GEMV
+    "gemv_q8_0": dict(dtype="q8_0", m=1, shapes=[("w", 4096, 4096)], ffn=False, config=0),
+    # config 2: M=16 draft block through the same FFN projections
+    "ffn_q4k_m16": dict(dtype="q4k", m=16, shapes=[("gate", 4096, 14336), ("up", 4096, 14336),
+                                                    ("down", 14336, 4096)], ffn=True, config=2),
+}
+
+
+def weight_bytes(dtype, k, n):
+    return n * (k // 256 * 144 if dtype == "q4k" else k // 32 * 34)
+
+
+def step_bytes(wl):
+    m = wl["m"]
+    tot = 0
+    for _, k, n in wl["shapes"]:
+        tot += weight_bytes(wl["dtype"], k, n) + 4 * m * (k + n)
+    return tot
+
+
+def launch_bytes(wl):
+    """Algorithmic bytes of one projection launch (W + x + y); all shapes of a
+    workload move the same bytes per launch."""
+    _, k, n = wl["shapes"][0]
+    return weight_bytes(wl["dtype"], k, n) + 4 * wl["m"] * (k + n)
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", str(self.idx),
+                 "-lms", "100", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    p = [s.strip() for s in line.split(",")]
+                    if len(p) >= 9:
+                        rows.append(p)
+            os.remove(self.path)
+        except Exception:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(s):
+            try:
+                return float(s.split()[0])
+            except Exception:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for nm, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def physical_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+# ---------------------------------------------------------------------------
+def cpu_reference_run(wl, budget_s: float, rng, use_ref: bool):
+    """Time the reference's CPU-runnable implementation of one projection of the
+    workload on a bounded row sample.  Returns (GB/s, kind, cores, sample)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    from laguna_raw_halo_strix_b200 import synth
+
+    dtype = orc.Q4_K if wl["dtype"] == "q4k" else orc.Q8_0
+    name, k, n = wl["shapes"][0]
+    m = wl["m"]
+    ref = None
+    if use_ref and os.path.exists(orc.REF_LIB):
+        ref = orc.RefShaders()
+    o = orc.Oracle()
+    cores = o.lib.lco_get_threads()
+    rows = 64
+    x = synth.activations(m, k, rng)
+    w = synth.weight_blocks(dtype, rows, k, rng)
+
+    def run_once(nrows):
+        ww = w[:nrows] if nrows <= w.shape[0] else np.concatenate([w] * (nrows // w.shape[0] + 1))[:nrows]
+        t0 = time.perf_counter()
+        if ref is not None:
+            wp = orc.pad4(ww)
+            for r in range(m):
+                c = np.zeros(nrows, np.float32)
+                push = np.array([k, nrows] + ([0] if dtype == orc.Q4_K else []), np.uint32).tobytes()
+                ref.run("proj_q4k" if dtype == orc.Q4_K else "proj_q8_0", [x[r], wp, c], push,
+                        orc.RefShaders.groups(nrows))
+        else:
+            o.proj(dtype, x, ww, k, nrows)
+        return time.perf_counter() - t0
+
+    t = run_once(rows)
+    per_row = max(t / rows, 1e-9)
+    nrows = int(min(n, max(rows, budget_s / per_row)))
+    w = synth.weight_blocks(dtype, min(nrows, 2048), k, rng)
+    t = run_once(nrows)
+    nbytes = weight_bytes(wl["dtype"], k, nrows) + 4 * m * (k + nrows)
+    kind = "reference" if ref is not None else "port"
+    sample = (f"{name} projection {k}->{nrows} of {n} rows, m={m}, "
+              f"{'reference GLSL shader compiled for the CPU (oracle/_ref)' if ref else 'C restatement (oracle)'}"
+              f", {t:.2f} s")
+    return nbytes / t / 1e9, kind, cores, sample
+
+
+# ---------------------------------------------------------------------------
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    wl = WORKLOADS[args.workload]
+    rng = np.random.default_rng(0)
+    vals = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        v, kind, cores, sample = cpu_reference_run(wl, 0.5, rng, use_ref=True)
+        if i >= args.warmup:
+            vals.append(v)
+            info = (kind, cores, sample)
+    value = statistics.median(vals)
+    kind, cores, sample = info
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
+        "config": {"workload": args.workload, "baseline_config": wl["config"]},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", default="ffn_q4k_m1", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from laguna_raw_halo_strix_b200 import lc, synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(dev)
+    ctx = lc.Context(local_rank)
+    ctx.set_stream(stream)
+
+    wl = WORKLOADS[args.workload]
+    dtype = lc.Q4_K if wl["dtype"] == "q4k" else lc.Q8_0
+    m = wl["m"]
+    rng = np.random.default_rng(1000 + rank)
+
+    # weight pool > 3x L2
+    set_bytes = sum(weight_bytes(wl["dtype"], k, n) for _, k, n in wl["shapes"])
+    pool = max(2, -(-3 * L2_BYTES // set_bytes))
+    base = {name: synth.weight_blocks(dtype, n, k, rng) for name, k, n in wl["shapes"]}
+    weights = []
+    for p in range(pool):
+        s = {}
+        for name, k, n in wl["shapes"]:
+            t = torch.from_numpy(base[name]).to(dev)
+            if p:
+                # distinct bytes per pool entry (flip nibbles/ints deterministically)
+                t = t ^ torch.tensor(p * 37 % 255, dtype=torch.uint8, device=dev)
+            s[name] = t
+        weights.append(s)
+    k0 = wl["shapes"][0][1]
+    x = torch.from_numpy(synth.activations(m, k0, rng)).to(dev)
+    bufs = {name: torch.empty(m, n, device=dev) for name, k, n in wl["shapes"]}
+    h = torch.empty(m, wl["shapes"][-1][1], device=dev) if wl["ffn"] else None
+    ev = []
+
+    def step(i, timed_events=None):
+        ws = weights[i % pool]
+        if wl["ffn"]:
+            (_, kg, ng), (_, ku, nu), (_, kd, nd) = wl["shapes"]
+            seq = [("gate", x, kg, ng), ("up", x, ku, nu)]
+            for name, xin, k, n in seq:
+                if timed_events is not None:
+                    timed_events.append(torch.cuda.Event(enable_timing=True))
+                    timed_events[-1].record(stream)
+                ctx.proj_m(dtype, xin, ws[name], bufs[name], m, k, n)
+                if timed_events is not None:
+                    timed_events.append(torch.cuda.Event(enable_timing=True))
+                    timed_events[-1].record(stream)
+            ctx.activation(bufs["gate"], bufs["up"], h, m * ng)
+            if timed_events is not None:
+                timed_events.append(torch.cuda.Event(enable_timing=True))
+                timed_events[-1].record(stream)
+            ctx.proj_m(dtype, h, ws["down"], bufs["down"], m, kd, nd)
+            if timed_events is not None:
+                timed_events.append(torch.cuda.Event(enable_timing=True))
+                timed_events[-1].record(stream)
+        else:
+            for name, k, n in wl["shapes"]:
+                if timed_events is not None:
+                    timed_events.append(torch.cuda.Event(enable_timing=True))
+                    timed_events[-1].record(stream)
+                ctx.proj_m(dtype, x, ws[name], bufs[name], m, k, n)
+                if timed_events is not None:
+                    timed_events.append(torch.cuda.Event(enable_timing=True))
+                    timed_events[-1].record(stream)
+
+    launches_per_step = (2 * len(wl["shapes"]) + (1 if wl["ffn"] else 0)) if m <= 16 else None
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        sampler = ClockSampler(physical_gpu_index(local_rank)) if rank == 0 else None
+        if sampler:
+            sampler.start()
+            time.sleep(0.3)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        start.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i, ev)
+        end.record(stream)
+        stream.synchronize()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        clocks = sampler.stop() if sampler else None
+        ms = start.elapsed_time(end)
+        # per-launch durations of the projections (the dominant kernel)
+        proj_ms = [ev[j].elapsed_time(ev[j + 1]) for j in range(0, len(ev), 2)]
+
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+
+        # ---- e2e: host buffers, H2D of the step's input + D2H of its result ----
+        x_host = torch.from_numpy(synth.activations(m, k0, rng)).pin_memory()
+        out_name = wl["shapes"][-1][0]
+        y_host = torch.empty(bufs[out_name].shape, dtype=torch.float32).pin_memory()
+        e2e_steps = max(10, args.steps // 2)
+        for i in range(3):
+            x.copy_(x_host, non_blocking=True)
+            step(i)
+            y_host.copy_(bufs[out_name], non_blocking=True)
+            stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            x.copy_(x_host, non_blocking=True)
+            step(i)
+            y_host.copy_(bufs[out_name], non_blocking=True)
+            stream.synchronize()
+        e2e_s = time.perf_counter() - t0
+        te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_s = float(te.item())
+
+    sb = step_bytes(wl)
+    value = world * sb * args.steps / (ms_max / 1e3) / 1e9
+    e2e_value = world * sb * e2e_steps / e2e_s / 1e9
+    hbm, tflops, peak_src = peaks()
+    per_launch_ms = statistics.mean(proj_ms)
+    achieved = launch_bytes(wl) / (per_launch_ms / 1e3) / 1e9
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            v, kind, cores, sample = cpu_reference_run(wl, 5.0, np.random.default_rng(7), use_ref=True)
+            cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample}
+        traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+                traffic = json.load(f).get(args.workload)
+        except Exception:
+            pass
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "q4k*f32" if wl["dtype"] == "q4k" else "q8_0*f32",
+            "data": "synthetic (seeded; BASELINE block/activation distributions)",
+            "config": {
+                "workload": args.workload,
+                "baseline_config": wl["config"],
+                "m": m,
+                "projections": [f"{nm} {k}->{n}" for nm, k, n in wl["shapes"]],
+                "bytes_per_step": sb,
+                "l2": f"weights rotated through {pool} sets of {set_bytes / 1e6:.1f} MB (> 3x the 126 MB L2)",
+                "parallelism": f"replicas x{world} (independent token streams, no collective)",
+            },
+            "roofline": {
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": hbm,
+                "peak_source": peak_src,
+                "unit": "GB/s",
+                "frac": achieved / hbm,
+                "traffic": traffic,
+                "kernel": "q4k_mma_kernel (+ x_pack_q4k)" if wl["dtype"] == "q4k" else "q8_mma_kernel (+ x_pack_q8)",
+                "per_launch_us": per_launch_ms * 1e3,
+                "bytes_per_launch": launch_bytes(wl),
+            },
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": int(x_host.numel() * 4),
+                    "d2h_bytes_per_step": int(y_host.numel() * 4), "steps": e2e_steps},
+            "clocks": clocks,
+            "gpu_launches": launches_per_step * args.steps if launches_per_step else None,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

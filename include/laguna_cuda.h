@@ -1,0 +1,221 @@
+/*
+ * laguna_cuda.h -- C ABI of the B200 (sm_100a) backend for laguna-raw's
+ * quantized projection path.
+ *
+ * This library replaces the reference's Vulkan runtime (src/vulkan.rs) and the
+ * shader launches behind its typed dispatch helpers (src/dflash.rs:979-1327,
+ * src/target.rs:1086-1162).  Weights stay in their raw GGUF block layout
+ * (Q8_0: 34-byte blocks of 32 elements; Q4_K: 144-byte super-blocks of 256)
+ * and are decoded inside the kernels.
+ *
+ * Conventions
+ *  - Every function returns an lc_status (0 = LC_OK); none aborts.  On failure
+ *    lc_last_error() returns a message (thread-local, valid until the next
+ *    call on the same thread).
+ *  - Compute entry points take DEVICE pointers (from lc_buf_device_ptr() or
+ *    any CUDA allocation on the context's device) and enqueue on the context's
+ *    stream.  They return once the work is enqueued, unless lc_set_sync(ctx, 1)
+ *    was called, in which case each call waits for its work like the
+ *    reference's fenced submit_compute (src/vulkan.rs:326-334).
+ *  - Sizes are uint32 like the reference's push constants
+ *    (e.g. kernels/proj_q8_0.comp:17-20); byte counts are size_t.
+ *  - Quantized weights are row-major: element (i, j) of an n x k projection is
+ *    element i*k + j of the GGUF tensor (kernels/proj_q8_0.comp:54,
+ *    kernels/proj_q4k.comp:134).  The quantized kernels require k to be a
+ *    multiple of the block size (32 for Q8_0, 256 for Q4_K) and the weight
+ *    pointer to be 16-byte aligned; other shapes return LC_ERR_UNSUPPORTED.
+ *  - f16 scales decode by the reference rule by default: subnormal halves map
+ *    to 2^-14 * (1 + m/1024) (kernels/proj_q8_0.comp:27-45).  lc_set_half_mode
+ *    selects IEEE decoding instead.
+ */
+#ifndef LAGUNA_CUDA_H
+#define LAGUNA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+typedef enum {
+    LC_OK = 0,
+    LC_ERR_INVALID = 1,      /* null pointer, size out of range, misaligned */
+    LC_ERR_UNSUPPORTED = 2,  /* dtype or shape this backend does not run    */
+    LC_ERR_CUDA = 3,         /* a CUDA runtime call failed                  */
+    LC_ERR_OOM = 4,          /* device allocation failed                    */
+    LC_ERR_TIMEOUT = 5,      /* a bounded device-side wait expired          */
+    LC_ERR_IO = 6            /* file could not be read / is not GGUF v3     */
+} lc_status;
+
+/* ---- tensor types: GGUF ids (src/gguf.rs:45-88) ------------------------- */
+enum {
+    LC_F32 = 0,
+    LC_F16 = 1,
+    LC_Q8_0 = 8,
+    LC_Q4_K = 12,
+    LC_BF16 = 30,
+    /* lc_dequant only: the reference CPU decoder's own "Q4_K" branch
+     * (src/dflash.rs:398-436), a bf16 d/k4/signs + 3-bit layout that differs
+     * from GGUF Q4_K; provided so test-dequant parity covers every branch. */
+    LC_Q4_K_DFLASH_CPU = 1012
+};
+
+/* ---- f16 decode modes ---------------------------------------------------- */
+enum {
+    LC_HALF_REF = 0,  /* reference rule (default) */
+    LC_HALF_IEEE = 1  /* IEEE-754 binary16        */
+};
+
+typedef struct lc_ctx lc_ctx;
+typedef struct lc_buf lc_buf;
+
+/* ---- runtime: replaces VulkanContext (src/vulkan.rs:5-100) -------------- */
+
+/* Message for the last failure on this thread ("" if none). */
+const char *lc_last_error(void);
+/* Library version string. */
+const char *lc_version(void);
+/* Number of CUDA devices visible. */
+int lc_device_count(int *count);
+/* VulkanContext::init (src/vulkan.rs:16-100): open `device`, create a stream. */
+int lc_init(int device, lc_ctx **out);
+/* Release the context and everything it owns (the reference leaks). */
+int lc_destroy(lc_ctx *ctx);
+/* Enqueue on an external cudaStream_t (NULL restores the context's own). */
+int lc_set_stream(lc_ctx *ctx, void *cuda_stream);
+/* The cudaStream_t work is enqueued on. */
+void *lc_get_stream(lc_ctx *ctx);
+/* Wait for all enqueued work: the fence wait of submit_compute
+ * (src/vulkan.rs:326-334). */
+int lc_synchronize(lc_ctx *ctx);
+/* 1: every compute call waits for completion (reference behaviour); 0: async. */
+int lc_set_sync(lc_ctx *ctx, int sync);
+/* LC_HALF_REF (default) or LC_HALF_IEEE for every f16 scale decode. */
+int lc_set_half_mode(lc_ctx *ctx, int mode);
+/* Device the context runs on. */
+int lc_ctx_device(lc_ctx *ctx, int *device);
+
+/* ---- buffers: replace GpuBuffer (src/vulkan.rs:342-452) ------------------ */
+
+/* GpuBuffer::new (src/vulkan.rs:350-398): `bytes` of device memory
+ * (256-byte aligned, zero-filled). */
+int lc_buf_alloc(lc_ctx *ctx, size_t bytes, lc_buf **out);
+/* Free a buffer (the reference's GpuBuffer has no Drop). */
+int lc_buf_free(lc_buf *buf);
+/* Device pointer of a buffer, for the compute entry points. */
+void *lc_buf_device_ptr(const lc_buf *buf);
+/* Size in bytes. */
+size_t lc_buf_size(const lc_buf *buf);
+/* GpuBuffer::upload (src/vulkan.rs:400-430): copy `bytes` host bytes to
+ * offset 0.  Synchronous with respect to the context's stream. */
+int lc_buf_upload(lc_buf *buf, const void *src, size_t bytes);
+/* Upload at a byte offset. */
+int lc_buf_upload_at(lc_buf *buf, size_t offset, const void *src, size_t bytes);
+/* Read `bytes` from a byte offset into host memory (waits for the stream). */
+int lc_buf_read(lc_buf *buf, size_t offset, void *dst, size_t bytes);
+/* GpuBuffer::read_f32 (src/vulkan.rs:432-452): read n floats from offset 0. */
+int lc_buf_read_f32(lc_buf *buf, float *dst, size_t n);
+
+/* ---- projections --------------------------------------------------------- */
+
+/* dispatch_proj / dispatch_proj_row (src/dflash.rs:1009-1052), kernels/proj.comp:
+ * c[i] = sum_j x[j] * w[row_major ? j*n + i : i*k + j]. */
+int lc_proj_f32(lc_ctx *ctx, const float *x, const float *w, float *c,
+                uint32_t k, uint32_t n, uint32_t row_major);
+/* Q8_0 projection, the WeightType::Q8_0 arm of dispatch_proj_quant_expert
+ * (src/target.rs:1118-1138) running kernels/proj_q8_0.comp:47-67. */
+int lc_proj_q8_0(lc_ctx *ctx, const float *x, const void *w, float *c,
+                 uint32_t k, uint32_t n);
+/* Q4_K projection, the WeightType::Q4_K arm (src/target.rs:1139-1160) running
+ * kernels/proj_q4k.comp:127-159; expert_offset is in elements (multiple of 256). */
+int lc_proj_q4k(lc_ctx *ctx, const float *x, const void *w, float *c,
+                uint32_t k, uint32_t n, uint32_t expert_offset);
+/* dispatch_proj_quant_expert (src/target.rs:1098-1162): dtype switch over
+ * LC_F32 / LC_Q8_0 / LC_Q4_K (expert_offset applies to Q4_K only, as in the
+ * reference; LC_F32 ignores it). */
+int lc_proj_quant(lc_ctx *ctx, int dtype, const float *x, const void *w,
+                  float *c, uint32_t k, uint32_t n, uint32_t expert_offset);
+/* M-row projection: the same projection applied to each row of x [m, k],
+ * writing c [m, n] -- the draft-block (m = 16) and lm_head (m = 1024) forms
+ * the reference would reach by m calls of the single-row dispatch. */
+int lc_proj_m(lc_ctx *ctx, int dtype, const float *x, const void *w, float *c,
+              uint32_t m, uint32_t k, uint32_t n, uint32_t expert_offset);
+
+/* ---- dequant ------------------------------------------------------------- */
+
+/* dequant_to_f32 (src/dflash.rs:331-465) on the device.  LC_Q8_0 / LC_F16 /
+ * LC_BF16 / LC_F32 / LC_Q4_K_DFLASH_CPU follow the CPU decoder branch for
+ * branch (reads bounded by src_bytes, missing elements 0); LC_Q4_K decodes
+ * GGUF Q4_K with the GPU shader formula of kernels/proj_q4k.comp:139-154.
+ * Other dtypes produce zeros like the reference's fallback arm. */
+int lc_dequant(lc_ctx *ctx, int dtype, const void *src, size_t src_bytes,
+               size_t n, float *out);
+
+/* ---- kernels interleaved with the projections ---------------------------- */
+
+/* dispatch_rmsnorm (src/dflash.rs:979-1007), kernels/rmsnorm.comp, over m rows
+ * of n: out = x * w * inversesqrt(mean(x^2) + eps).  out may alias x. */
+int lc_rmsnorm(lc_ctx *ctx, const float *w, const float *x, float *out,
+               uint32_t m, uint32_t n, float eps);
+/* dispatch_qk_norm_rope (src/dflash.rs:1093-1129), kernels/qk_norm_rope.comp,
+ * over m rows of n_heads*head_dim; row r is rotated at position pos0 + r.
+ * out may alias x. */
+int lc_qk_norm_rope(lc_ctx *ctx, const float *x, const float *w,
+                    const float *freq, float *out, uint32_t m,
+                    uint32_t n_heads, uint32_t head_dim, uint32_t rope_dim,
+                    float eps, uint32_t pos0);
+/* dispatch_activation (src/dflash.rs:1305-1327): h = silu(gate) * up. */
+int lc_activation(lc_ctx *ctx, const float *gate, const float *up, float *h,
+                  uint32_t n);
+/* dispatch_add (src/dflash.rs:1281-1303): c = a + b. */
+int lc_add(lc_ctx *ctx, const float *a, const float *b, float *c, uint32_t n);
+/* dispatch_gate_mul (src/dflash.rs:1236-1267): out[i] = v[i] * gate[i/head_dim]
+ * for i < n_hd (gate holds n_hd/head_dim values per row). */
+int lc_gate_mul(lc_ctx *ctx, const float *v, const float *gate, float *out,
+                uint32_t n_hd, uint32_t n_heads, uint32_t head_dim);
+/* The host softplus of src/dflash.rs:956-958 moved on-device:
+ * out = g > 20 ? g : ln(1 + e^g). */
+int lc_softplus(lc_ctx *ctx, const float *g, float *out, uint32_t n);
+/* dispatch_enc_aux_norm (src/dflash.rs:1201-1233), kernels/enc_aux_norm.comp. */
+int lc_enc_aux_norm(lc_ctx *ctx, const float *x, const float *w, float *y,
+                    uint32_t n_feat, uint32_t n_aux, uint32_t n_tokens,
+                    float eps);
+/* dispatch_mha_attn_seq (src/dflash.rs:1160-1198), kernels/mha_attn.comp, for
+ * m query rows q [m, n_q_heads*head_dim] over k, v [seq_len, n_kv_heads*head_dim];
+ * query r sits at position q_pos0 + r (key p is visible iff !causal || p <= pos). */
+int lc_mha_attn(lc_ctx *ctx, const float *q, const float *k, const float *v,
+                float *out, uint32_t m, uint32_t n_q_heads, uint32_t n_kv_heads,
+                uint32_t head_dim, uint32_t seq_len, float scale,
+                uint32_t q_pos0, uint32_t causal);
+/* RoPE frequency table (src/dflash.rs:901-907) on the host:
+ * freq[i] = 1 / base^(2i/rope_dim), i < rope_dim/2. */
+int lc_rope_freq(float *freq_host, uint32_t rope_dim, float base);
+
+/* ---- lm_head + argmax ----------------------------------------------------- */
+
+/* Order-preserving key of (logit, index), compared as SIGNED int64: the high
+ * 32 bits order the f32 value, the low 32 bits hold the index, so the maximum
+ * key is the largest logit with ties broken toward the LARGER index -- the
+ * rule of src/lib.rs:456-464 (Iterator::max_by keeps the last maximum).  A
+ * plain int64 MAX reduction (ncclInt64 / torch.int64) combines shards. */
+uint64_t lc_pack_key(float value, uint32_t index);
+float lc_key_value(uint64_t key);
+uint32_t lc_key_index(uint64_t key);
+/* Row-wise argmax of logits [m, n] into keys[m] (device); index = row_offset + j. */
+int lc_argmax_rows(lc_ctx *ctx, const float *logits, uint32_t m, uint32_t n,
+                   uint32_t row_offset, uint64_t *keys);
+/* project_normalized_hidden (src/target.rs:580-605) for m hidden rows fused
+ * with argmax (src/lib.rs:456-464): logits = x [m, k] . W[n_local rows]^T for
+ * a vocab shard whose first row is global row `row_offset`; keys[r] (device)
+ * receives the shard-local best (logit, global index).  `logits` (device,
+ * [m, n_local]) may be NULL; when given, the logits are written too. */
+int lc_lm_head_argmax(lc_ctx *ctx, int dtype, const float *x, const void *w,
+                      uint32_t m, uint32_t k, uint32_t n_local,
+                      uint32_t row_offset, uint64_t *keys, float *logits);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LAGUNA_CUDA_H */

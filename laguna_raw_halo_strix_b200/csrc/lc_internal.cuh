@@ -1,0 +1,125 @@
+// lc_internal.cuh -- shared declarations of the CUDA backend (not installed).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "laguna_cuda.h"
+
+// Context: one device, one stream, one grow-only scratch arena.
+struct lc_ctx {
+    int device = 0;
+    int num_sms = 148;
+    size_t smem_optin = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int sync = 0;
+    int half_mode = LC_HALF_REF;
+    // Grow-only scratch slots (see LC_SCRATCH_*).
+    void *scratch[4] = {nullptr, nullptr, nullptr, nullptr};
+    size_t scratch_bytes[4] = {0, 0, 0, 0};
+};
+
+struct lc_buf {
+    lc_ctx *ctx = nullptr;
+    void *ptr = nullptr;
+    size_t size = 0;
+};
+
+// Record an error message for lc_last_error() and return `code`.
+int lc_fail(int code, const char *fmt, ...);
+// After enqueuing kernels: check the launch, and wait if the context is sync.
+int lc_after_launch(lc_ctx *ctx, const char *what);
+// Scratch slots: packed activation fragments, logits of the argmax path,
+// the DFlash block-forward workspace, attention partials.
+enum { LC_SCRATCH_PACK = 0, LC_SCRATCH_LOGITS = 1, LC_SCRATCH_MODEL = 2, LC_SCRATCH_ATTN = 3 };
+// Grow-only scratch slot of at least `bytes` (256-byte aligned).  Returns
+// nullptr and sets the error on failure.  Waits for the stream before
+// reallocating.
+void *lc_scratch(lc_ctx *ctx, int slot, size_t bytes);
+// Make ctx->device current on this thread.
+int lc_use_device(lc_ctx *ctx);
+
+#define LC_REQUIRE(cond, code, ...)             \
+    do {                                        \
+        if (!(cond)) return lc_fail((code), __VA_ARGS__); \
+    } while (0)
+
+#define LC_CUDA(expr)                                                        \
+    do {                                                                     \
+        cudaError_t _e = (expr);                                             \
+        if (_e != cudaSuccess)                                               \
+            return lc_fail(_e == cudaErrorMemoryAllocation ? LC_ERR_OOM : LC_ERR_CUDA, \
+                           "%s: %s", #expr, cudaGetErrorString(_e));         \
+    } while (0)
+
+// ---- device helpers -------------------------------------------------------
+
+// f16 bits -> f32.  LC_HALF_REF keeps the implicit one on subnormals exactly
+// like kernels/proj_q8_0.comp:27-45 (sign | 113<<23 | mant<<13); otherwise IEEE.
+__device__ __forceinline__ float lc_half_to_f32(uint32_t h, int mode) {
+    h &= 0xFFFFu;
+    if (mode == LC_HALF_IEEE) return __half2float(__ushort_as_half((unsigned short)h));
+    uint32_t sign = (h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 0x1Fu;
+    uint32_t mant = (h & 0x3FFu) << 13;
+    uint32_t ebits = (e == 0u) ? (mant ? (113u << 23) : 0u) : (e == 31u ? 0x7F800000u : (e + 112u) << 23);
+    return __uint_as_float(sign | ebits | mant);
+}
+
+__device__ __forceinline__ uint32_t lc_h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 lc_u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// Split a float into f16 hi + f16 lo with hi + lo == v to ~22 bits.
+// part 0 -> hi, part 1 -> lo.
+__device__ __forceinline__ __half lc_split_part(float v, int part) {
+    __half hi = __float2half_rn(v);
+    if (part == 0) return hi;
+    return __float2half_rn(v - __half2float(hi));
+}
+
+__device__ __forceinline__ uint32_t lc_pack_h2(__half a, __half b) {
+    return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+}
+
+// Order-preserving (value, index) key; see lc_pack_key in laguna_cuda.h.
+__host__ __device__ __forceinline__ uint64_t lc_make_key(float v, uint32_t idx) {
+    uint32_t b;
+#ifdef __CUDA_ARCH__
+    b = __float_as_uint(v);
+#else
+    memcpy(&b, &v, 4);
+#endif
+    uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    uint64_t k = ((uint64_t)o << 32) | idx;
+    return k ^ 0x8000000000000000ull;
+}
+
+// mma.sync m16n8k16 f16 x f16 -> f32 (row.col).
+__device__ __forceinline__ void lc_mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// mma.sync m16n8k8 f16 x f16 -> f32 (row.col).
+__device__ __forceinline__ void lc_mma1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+}
+
+// Host-side launch helpers defined in the kernel files.
+namespace lc {
+int proj_q4k(lc_ctx *ctx, const float *x, const void *w, float *c, uint32_t m, uint32_t k, uint32_t n,
+             uint32_t expert_offset);
+int proj_q8_0(lc_ctx *ctx, const float *x, const void *w, float *c, uint32_t m, uint32_t k, uint32_t n);
+int proj_f32(lc_ctx *ctx, const float *x, const float *w, float *c, uint32_t m, uint32_t k, uint32_t n,
+             uint32_t row_major);
+}  // namespace lc

@@ -1,0 +1,262 @@
+"""ctypes binding of liblaguna_cuda.so (the C ABI declared in include/laguna_cuda.h).
+
+This module is a thin host-side mirror of the reference's dispatch helpers
+(src/dflash.rs:979-1327, src/target.rs:1086-1162): every method enqueues one
+library call on the context's stream.  Arguments are device pointers (ints) or
+torch CUDA tensors; torch is used only for device memory and streams.
+
+There is no CPU fallback: if the shared library cannot be loaded (or built
+with nvcc), importing the functions raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+import threading
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "liblaguna_cuda.so")
+CSRC = os.path.join(PKG, "csrc")
+
+LC_OK = 0
+LC_ERR_INVALID = 1
+LC_ERR_UNSUPPORTED = 2
+LC_ERR_CUDA = 3
+LC_ERR_OOM = 4
+LC_ERR_TIMEOUT = 5
+LC_ERR_IO = 6
+
+F32 = 0
+F16 = 1
+Q8_0 = 8
+Q4_K = 12
+BF16 = 30
+Q4_K_DFLASH_CPU = 1012
+
+HALF_REF = 0
+HALF_IEEE = 1
+
+_STATUS = {0: "LC_OK", 1: "LC_ERR_INVALID", 2: "LC_ERR_UNSUPPORTED", 3: "LC_ERR_CUDA", 4: "LC_ERR_OOM",
+           5: "LC_ERR_TIMEOUT", 6: "LC_ERR_IO"}
+
+
+class LagunaError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{_STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+_lock = threading.Lock()
+_lib = None
+
+_vp = C.c_void_p
+_u32 = C.c_uint32
+_f = C.c_float
+_sz = C.c_size_t
+_i = C.c_int
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "lc_last_error": (C.c_char_p, []),
+    "lc_version": (C.c_char_p, []),
+    "lc_device_count": (_i, [C.POINTER(_i)]),
+    "lc_init": (_i, [_i, C.POINTER(_vp)]),
+    "lc_destroy": (_i, [_vp]),
+    "lc_set_stream": (_i, [_vp, _vp]),
+    "lc_get_stream": (_vp, [_vp]),
+    "lc_synchronize": (_i, [_vp]),
+    "lc_set_sync": (_i, [_vp, _i]),
+    "lc_set_half_mode": (_i, [_vp, _i]),
+    "lc_ctx_device": (_i, [_vp, C.POINTER(_i)]),
+    "lc_buf_alloc": (_i, [_vp, _sz, C.POINTER(_vp)]),
+    "lc_buf_free": (_i, [_vp]),
+    "lc_buf_device_ptr": (_vp, [_vp]),
+    "lc_buf_size": (_sz, [_vp]),
+    "lc_buf_upload": (_i, [_vp, _vp, _sz]),
+    "lc_buf_upload_at": (_i, [_vp, _sz, _vp, _sz]),
+    "lc_buf_read": (_i, [_vp, _sz, _vp, _sz]),
+    "lc_buf_read_f32": (_i, [_vp, C.POINTER(_f), _sz]),
+    "lc_proj_f32": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32]),
+    "lc_proj_q8_0": (_i, [_vp, _vp, _vp, _vp, _u32, _u32]),
+    "lc_proj_q4k": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32]),
+    "lc_proj_quant": (_i, [_vp, _i, _vp, _vp, _vp, _u32, _u32, _u32]),
+    "lc_proj_m": (_i, [_vp, _i, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
+    "lc_dequant": (_i, [_vp, _i, _vp, _sz, _sz, _vp]),
+    "lc_rmsnorm": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _f]),
+    "lc_qk_norm_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _f, _u32]),
+    "lc_activation": (_i, [_vp, _vp, _vp, _vp, _u32]),
+    "lc_add": (_i, [_vp, _vp, _vp, _vp, _u32]),
+    "lc_gate_mul": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32]),
+    "lc_softplus": (_i, [_vp, _vp, _vp, _u32]),
+    "lc_enc_aux_norm": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _f]),
+    "lc_mha_attn": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _f, _u32, _u32]),
+    "lc_rope_freq": (_i, [C.POINTER(_f), _u32, _f]),
+    "lc_pack_key": (C.c_uint64, [_f, _u32]),
+    "lc_key_value": (_f, [C.c_uint64]),
+    "lc_key_index": (_u32, [C.c_uint64]),
+    "lc_argmax_rows": (_i, [_vp, _vp, _u32, _u32, _u32, _vp]),
+    "lc_lm_head_argmax": (_i, [_vp, _i, _vp, _vp, _u32, _u32, _u32, _u32, _vp, _vp]),
+}
+
+
+def _sources_newer(lib: str) -> bool:
+    if not os.path.exists(lib):
+        return True
+    t = os.path.getmtime(lib)
+    for d in (CSRC, os.path.join(os.path.dirname(PKG), "include")):
+        for f in os.listdir(d):
+            if f.endswith((".cu", ".cuh", ".h", ".cpp", ".hpp")) and os.path.getmtime(os.path.join(d, f)) > t:
+                return True
+    return False
+
+
+def build(force: bool = False) -> str:
+    """Compile the CUDA library in-tree (nvcc, sm_100a)."""
+    if force or _sources_newer(LIB_PATH):
+        subprocess.run(["make", "-s", "-j8", "-C", CSRC], check=True)
+    return LIB_PATH
+
+
+def lib():
+    """Load liblaguna_cuda.so (building it with nvcc if it is missing or stale)."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            path = build()
+            L = C.CDLL(path)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().lc_last_error().decode()
+
+
+def check(status: int, what: str = "") -> None:
+    if status != LC_OK:
+        raise LagunaError(status, f"{what}: {last_error()}" if what else last_error())
+
+
+def ptr(t) -> int:
+    """Device pointer of a torch tensor / int / None."""
+    if t is None:
+        return 0
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def pack_key(value: float, index: int) -> int:
+    return int(lib().lc_pack_key(value, index))
+
+
+def key_value(key: int) -> float:
+    return float(lib().lc_key_value(key & 0xFFFFFFFFFFFFFFFF))
+
+
+def key_index(key: int) -> int:
+    return int(lib().lc_key_index(key & 0xFFFFFFFFFFFFFFFF))
+
+
+class Context:
+    """An lc_ctx: one device, one stream (by default torch's current stream)."""
+
+    def __init__(self, device: int = 0, stream=None, sync: bool = False):
+        self.L = lib()
+        h = C.c_void_p()
+        check(self.L.lc_init(device, C.byref(h)), "lc_init")
+        self.h = h
+        self.device = device
+        if stream is not None:
+            self.set_stream(stream)
+        if sync:
+            check(self.L.lc_set_sync(self.h, 1))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.lc_destroy(self.h)
+            self.h = None
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream) -> None:
+        """stream: torch.cuda.Stream, raw cudaStream_t int, or None (own stream)."""
+        raw = getattr(stream, "cuda_stream", stream)
+        check(self.L.lc_set_stream(self.h, raw or None), "lc_set_stream")
+
+    def synchronize(self) -> None:
+        check(self.L.lc_synchronize(self.h), "lc_synchronize")
+
+    def set_half_mode(self, mode: int) -> None:
+        check(self.L.lc_set_half_mode(self.h, mode), "lc_set_half_mode")
+
+    # -- projections -----------------------------------------------------------
+    def proj_f32(self, x, w, c, k, n, row_major=0):
+        check(self.L.lc_proj_f32(self.h, ptr(x), ptr(w), ptr(c), k, n, row_major), "lc_proj_f32")
+
+    def proj_q8_0(self, x, w, c, k, n):
+        check(self.L.lc_proj_q8_0(self.h, ptr(x), ptr(w), ptr(c), k, n), "lc_proj_q8_0")
+
+    def proj_q4k(self, x, w, c, k, n, expert_offset=0):
+        check(self.L.lc_proj_q4k(self.h, ptr(x), ptr(w), ptr(c), k, n, expert_offset), "lc_proj_q4k")
+
+    def proj_quant(self, dtype, x, w, c, k, n, expert_offset=0):
+        check(self.L.lc_proj_quant(self.h, dtype, ptr(x), ptr(w), ptr(c), k, n, expert_offset), "lc_proj_quant")
+
+    def proj_m(self, dtype, x, w, c, m, k, n, expert_offset=0):
+        check(self.L.lc_proj_m(self.h, dtype, ptr(x), ptr(w), ptr(c), m, k, n, expert_offset), "lc_proj_m")
+
+    def dequant(self, dtype, src, src_bytes, n, out):
+        check(self.L.lc_dequant(self.h, dtype, ptr(src), src_bytes, n, ptr(out)), "lc_dequant")
+
+    # -- interleaved ops ---------------------------------------------------------
+    def rmsnorm(self, w, x, out, m, n, eps=1e-5):
+        check(self.L.lc_rmsnorm(self.h, ptr(w), ptr(x), ptr(out), m, n, eps), "lc_rmsnorm")
+
+    def qk_norm_rope(self, x, w, freq, out, m, n_heads, head_dim, rope_dim, eps, pos0):
+        check(self.L.lc_qk_norm_rope(self.h, ptr(x), ptr(w), ptr(freq), ptr(out), m, n_heads, head_dim, rope_dim,
+                                     eps, pos0), "lc_qk_norm_rope")
+
+    def activation(self, gate, up, h, n):
+        check(self.L.lc_activation(self.h, ptr(gate), ptr(up), ptr(h), n), "lc_activation")
+
+    def add(self, a, b, c, n):
+        check(self.L.lc_add(self.h, ptr(a), ptr(b), ptr(c), n), "lc_add")
+
+    def gate_mul(self, v, gate, out, n_hd, n_heads, head_dim):
+        check(self.L.lc_gate_mul(self.h, ptr(v), ptr(gate), ptr(out), n_hd, n_heads, head_dim), "lc_gate_mul")
+
+    def softplus(self, g, out, n):
+        check(self.L.lc_softplus(self.h, ptr(g), ptr(out), n), "lc_softplus")
+
+    def enc_aux_norm(self, x, w, y, n_feat, n_aux, n_tokens, eps=1e-5):
+        check(self.L.lc_enc_aux_norm(self.h, ptr(x), ptr(w), ptr(y), n_feat, n_aux, n_tokens, eps),
+              "lc_enc_aux_norm")
+
+    def mha_attn(self, q, k, v, out, m, n_q_heads, n_kv_heads, head_dim, seq_len, scale, q_pos0, causal=1):
+        check(self.L.lc_mha_attn(self.h, ptr(q), ptr(k), ptr(v), ptr(out), m, n_q_heads, n_kv_heads, head_dim,
+                                 seq_len, scale, q_pos0, causal), "lc_mha_attn")
+
+    def argmax_rows(self, logits, m, n, row_offset, keys):
+        check(self.L.lc_argmax_rows(self.h, ptr(logits), m, n, row_offset, ptr(keys)), "lc_argmax_rows")
+
+    def lm_head_argmax(self, dtype, x, w, m, k, n_local, row_offset, keys, logits=None):
+        check(self.L.lc_lm_head_argmax(self.h, dtype, ptr(x), ptr(w), m, k, n_local, row_offset, ptr(keys),
+                                       ptr(logits)), "lc_lm_head_argmax")
+
+
+def rope_freq(rope_dim: int, base: float = 500000.0):
+    import numpy as np
+
+    f = np.empty(max(rope_dim // 2, 1), np.float32)
+    check(lib().lc_rope_freq(f.ctypes.data_as(C.POINTER(C.c_float)), rope_dim, base), "lc_rope_freq")
+    return f[: rope_dim // 2]
