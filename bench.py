@@ -21,9 +21,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 import numpy as np
@@ -84,64 +82,80 @@ def launch_bytes(wl):
 
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock and throttle-reason sampling around the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Polls NVML (read-only queries) every ~2 ms in a background thread so that
+    even a short timed region is covered; samples taken between mark_begin()
+    and mark_end() are the ones reported.  Falls back to nvidia-smi."""
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.proc = None
-        self.path = None
+    # NVML clocks-event-reason bits
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
+
+    def __init__(self, dev):
+        import threading
+
+        self.samples = []  # (t, sm_mhz, reasons_bits)
+        self.t_begin = self.t_end = None
+        self.stop_flag = threading.Event()
+        self.thread = None
+        self.max_mhz = None
+        self.handle = None
+        try:
+            import pynvml as nv
+
+            nv.nvmlInit()
+            self.nv = nv
+            try:
+                import torch
+
+                uuid = str(torch.cuda.get_device_properties(dev).uuid)
+                self.handle = nv.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+            except Exception:
+                self.handle = nv.nvmlDeviceGetHandleByIndex(physical_gpu_index(dev.index or 0))
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM)
+        except Exception:
+            self.handle = None
+
+    def _poll(self):
+        nv = self.nv
+        while not self.stop_flag.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((time.perf_counter(), sm, rs))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def start(self):
-        try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", str(self.idx),
-                 "-lms", "100", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+        import threading
+
+        if self.handle is None:
+            return
+        self.thread = threading.Thread(target=self._poll, daemon=True)
+        self.thread.start()
+        time.sleep(0.05)
+
+    def mark_begin(self):
+        self.t_begin = time.perf_counter()
+
+    def mark_end(self):
+        self.t_end = time.perf_counter()
 
     def stop(self):
-        if self.proc is None:
+        if self.handle is None or self.thread is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        rows = []
-        try:
-            with open(self.path) as f:
-                for line in f:
-                    p = [s.strip() for s in line.split(",")]
-                    if len(p) >= 9:
-                        rows.append(p)
-            os.remove(self.path)
-        except Exception:
-            pass
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-
-        def num(s):
-            try:
-                return float(s.split()[0])
-            except Exception:
-                return None
-
-        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
-        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for nm, v in zip(names, r[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+        self.stop_flag.set()
+        self.thread.join(timeout=2)
+        inside = [s for s in self.samples if self.t_begin is not None and self.t_begin <= s[0] <= (self.t_end or 1e30)]
+        window = inside or self.samples
+        sm = [s[1] for s in window]
+        bits = 0
+        for s in window:
+            bits |= s[2]
+        reasons = sorted(name for b, name in self.REASONS.items() if bits & b)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(window), "samples_in_timed_region": len(inside), "source": "nvml"}
 
 
 def physical_gpu_index(local_rank: int) -> int:
@@ -285,75 +299,85 @@ def main():
     x = torch.from_numpy(synth.activations(m, k0, rng)).to(dev)
     bufs = {name: torch.empty(m, n, device=dev) for name, k, n in wl["shapes"]}
     h = torch.empty(m, wl["shapes"][-1][1], device=dev) if wl["ffn"] else None
-    ev = []
-
-    def step(i, timed_events=None):
+    def step(i):
         ws = weights[i % pool]
         if wl["ffn"]:
             (_, kg, ng), (_, ku, nu), (_, kd, nd) = wl["shapes"]
-            seq = [("gate", x, kg, ng), ("up", x, ku, nu)]
-            for name, xin, k, n in seq:
-                if timed_events is not None:
-                    timed_events.append(torch.cuda.Event(enable_timing=True))
-                    timed_events[-1].record(stream)
-                ctx.proj_m(dtype, xin, ws[name], bufs[name], m, k, n)
-                if timed_events is not None:
-                    timed_events.append(torch.cuda.Event(enable_timing=True))
-                    timed_events[-1].record(stream)
+            ctx.proj_m(dtype, x, ws["gate"], bufs["gate"], m, kg, ng)
+            ctx.proj_m(dtype, x, ws["up"], bufs["up"], m, ku, nu)
             ctx.activation(bufs["gate"], bufs["up"], h, m * ng)
-            if timed_events is not None:
-                timed_events.append(torch.cuda.Event(enable_timing=True))
-                timed_events[-1].record(stream)
             ctx.proj_m(dtype, h, ws["down"], bufs["down"], m, kd, nd)
-            if timed_events is not None:
-                timed_events.append(torch.cuda.Event(enable_timing=True))
-                timed_events[-1].record(stream)
         else:
             for name, k, n in wl["shapes"]:
-                if timed_events is not None:
-                    timed_events.append(torch.cuda.Event(enable_timing=True))
-                    timed_events[-1].record(stream)
                 ctx.proj_m(dtype, x, ws[name], bufs[name], m, k, n)
-                if timed_events is not None:
-                    timed_events.append(torch.cuda.Event(enable_timing=True))
-                    timed_events[-1].record(stream)
 
-    launches_per_step = (2 * len(wl["shapes"]) + (1 if wl["ffn"] else 0)) if m <= 16 else None
+    def dominant(i):
+        # the dominant kernel alone: the first projection shape, rotating weights
+        name, k, n = wl["shapes"][0]
+        ctx.proj_m(dtype, x, weights[i % pool][name], bufs[name], m, k, n)
+
+    # m <= 4: one persistent stream-K kernel per projection; m > 4: pack + tiled kernel
+    per_proj = 1 if m <= 4 else 2
+    launches_per_step = per_proj * len(wl["shapes"]) + (1 if wl["ffn"] else 0)
+    n_dom = max(args.steps, 3 * pool)
 
     with torch.cuda.stream(stream):
+        # eager warm-up: sizes scratch, sets kernel attributes
         for i in range(args.warmup):
             step(i)
         stream.synchronize()
+        # The decode loop runs as CUDA graphs: exactly K steps, and n_dom launches
+        # of the dominant projection (for its per-launch roofline figure).
+        g_steps = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_steps, stream=stream):
+            for i in range(args.steps):
+                step(args.warmup + i)
+        g_dom = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_dom, stream=stream):
+            for i in range(n_dom):
+                dominant(i)
+        g_steps.replay()
+        g_dom.replay()
+        stream.synchronize()
         if world > 1:
             dist.barrier()
-        sampler = ClockSampler(physical_gpu_index(local_rank)) if rank == 0 else None
+        sampler = ClockSampler(dev) if rank == 0 else None
         if sampler:
             sampler.start()
-            time.sleep(0.3)
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
+        if sampler:
+            sampler.mark_begin()
         start.record(stream)
-        for i in range(args.steps):
-            step(args.warmup + i, ev)
+        g_steps.replay()
         end.record(stream)
         stream.synchronize()
+        if sampler:
+            sampler.mark_end()
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
-        clocks = sampler.stop() if sampler else None
         ms = start.elapsed_time(end)
-        # per-launch durations of the projections (the dominant kernel)
-        proj_ms = [ev[j].elapsed_time(ev[j + 1]) for j in range(0, len(ev), 2)]
+        d0 = torch.cuda.Event(enable_timing=True)
+        d1 = torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        g_dom.replay()
+        d1.record(stream)
+        stream.synchronize()
+        clocks = sampler.stop() if sampler else None
+        per_launch_ms = d0.elapsed_time(d1) / n_dom
 
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_max = float(t.item())
+        del g_steps, g_dom
 
-        # ---- e2e: host buffers, H2D of the step's input + D2H of its result ----
+        # ---- e2e: host buffers, H2D of the step's input + D2H of its result,
+        # eager calls through the C ABI (ctypes), one host sync per step ----
         x_host = torch.from_numpy(synth.activations(m, k0, rng)).pin_memory()
         out_name = wl["shapes"][-1][0]
         y_host = torch.empty(bufs[out_name].shape, dtype=torch.float32).pin_memory()
@@ -381,7 +405,6 @@ def main():
     value = world * sb * args.steps / (ms_max / 1e3) / 1e9
     e2e_value = world * sb * e2e_steps / e2e_s / 1e9
     hbm, tflops, peak_src = peaks()
-    per_launch_ms = statistics.mean(proj_ms)
     achieved = launch_bytes(wl) / (per_launch_ms / 1e3) / 1e9
 
     if rank == 0:
@@ -425,7 +448,8 @@ def main():
                 "unit": "GB/s",
                 "frac": achieved / hbm,
                 "traffic": traffic,
-                "kernel": "q4k_mma_kernel (+ x_pack_q4k)" if wl["dtype"] == "q4k" else "q8_mma_kernel (+ x_pack_q8)",
+                "kernel": (("q4k_sk_kernel" if m <= 4 else "q4k_mma_kernel + x_pack_q4k") if wl["dtype"] == "q4k"
+                           else ("q8_sk_kernel" if m <= 4 else "q8_mma_kernel + x_pack_q8")),
                 "per_launch_us": per_launch_ms * 1e3,
                 "bytes_per_launch": launch_bytes(wl),
             },
@@ -433,7 +457,7 @@ def main():
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": int(x_host.numel() * 4),
                     "d2h_bytes_per_step": int(y_host.numel() * 4), "steps": e2e_steps},
             "clocks": clocks,
-            "gpu_launches": launches_per_step * args.steps if launches_per_step else None,
+            "gpu_launches": launches_per_step * args.steps,
         }
         print(json.dumps(line), flush=True)
     ctx.close()

@@ -215,6 +215,96 @@ int lc_lm_head_argmax(lc_ctx *ctx, int dtype, const float *x, const void *w,
                       uint32_t m, uint32_t k, uint32_t n_local,
                       uint32_t row_offset, uint64_t *keys, float *logits);
 
+/* ---- GGUF v3 reader: replaces GGUFReader (src/gguf.rs) ------------------- */
+
+typedef struct lc_gguf lc_gguf;
+
+/* TensorType::block_size / block_elements (src/gguf.rs:88-141) for the
+ * supported types (F32, F16, BF16, Q8_0, Q4_K); 0 for others. */
+uint64_t lc_type_block_bytes(int dtype);
+uint64_t lc_type_block_elements(int dtype);
+/* TensorInfo::n_bytes (src/gguf.rs:186-201): ceil(n/elements)*block_bytes. */
+uint64_t lc_tensor_bytes(int dtype, uint64_t n_elements);
+/* GGUFReader::open (src/gguf.rs:321-400): header, metadata, tensor infos,
+ * data offset aligned to general.alignment (default 32). */
+int lc_gguf_open(const char *path, lc_gguf **out);
+int lc_gguf_close(lc_gguf *g);
+uint64_t lc_gguf_tensor_count(const lc_gguf *g);
+/* Tensor i: name (valid while g is open), GGUF type id, dims, shape[4]
+ * (ne0 first), byte offset relative to the data section, byte size. */
+int lc_gguf_tensor_info(const lc_gguf *g, uint64_t i, const char **name, int *dtype, uint32_t *n_dims,
+                        uint64_t shape[4], uint64_t *offset, uint64_t *n_bytes);
+/* GGUFReader::tensor_by_name (src/gguf.rs:407): index or LC_ERR_INVALID. */
+int lc_gguf_find(const lc_gguf *g, const char *name, uint64_t *index);
+/* GGUFReader::read_tensor_data (src/gguf.rs:415-421): raw bytes into host memory. */
+int lc_gguf_read(lc_gguf *g, uint64_t index, void *dst, uint64_t bytes);
+/* Numeric / string metadata by key (any integer or float type). */
+int lc_gguf_meta_u64(const lc_gguf *g, const char *key, uint64_t *out);
+int lc_gguf_meta_f32(const lc_gguf *g, const char *key, float *out);
+int lc_gguf_meta_str(const lc_gguf *g, const char *key, const char **out);
+
+/* ---- DFlash draft model: replaces DFlashModel (src/dflash.rs:6-976) ------- */
+
+typedef struct {
+    uint32_t n_layers;    /* block_count */
+    uint32_t n_embd;      /* embedding_length */
+    uint32_t n_heads;     /* attention.head_count */
+    uint32_t n_kv_heads;  /* attention.head_count_kv */
+    uint32_t head_dim;    /* attention.key_length */
+    uint32_t rope_dim;    /* rope.dimension_count */
+    uint32_t n_ff;        /* feed_forward_length */
+    uint32_t n_aux;       /* len(target_layers): encoder inputs = n_aux * n_embd */
+    float rope_base;      /* rope.freq_base, default 500000 (src/dflash.rs:903) */
+    float norm_eps;       /* RMSNorm eps, 1e-5 (src/dflash.rs:987) */
+    float qk_eps;         /* QK-norm eps, 1e-6 (src/dflash.rs:1105) */
+} lc_dflash_hparams;
+
+typedef struct lc_dflash lc_dflash;
+
+/* Model::from_reader (src/model.rs:29-129) hyper-parameters with the
+ * laguna./dflash./bare key aliases of populate_metadata (src/gguf.rs:516-653). */
+int lc_gguf_dflash_hparams(const lc_gguf *g, lc_dflash_hparams *out);
+/* An empty model with device workspaces for up to max_ctx context rows and
+ * max_block block tokens. */
+int lc_dflash_create(lc_ctx *ctx, const lc_dflash_hparams *hp, uint32_t max_ctx, uint32_t max_block,
+                     lc_dflash **out);
+/* Model::upload_tensor_quantized (src/model.rs:174-184): upload one GGUF
+ * tensor by name ("blk.N.attn_q.weight", "fc.weight", ...).  Projection
+ * weights stay raw (F32 / Q8_0 / Q4_K); F16 / BF16 tensors are decoded to f32
+ * on the device with dequant_to_f32's rules. */
+int lc_dflash_set_tensor(lc_dflash *m, const char *name, int dtype, const void *host_data, size_t bytes);
+/* DFlashModel::load (src/dflash.rs:34-119) from a GGUF file, raw-block upload. */
+int lc_dflash_load_gguf(lc_ctx *ctx, const char *path, uint32_t max_ctx, uint32_t max_block, lc_dflash **out);
+int lc_dflash_destroy(lc_dflash *m);
+int lc_dflash_get_hparams(const lc_dflash *m, lc_dflash_hparams *out);
+/* DFlashModel::encode (src/dflash.rs:157-234) for n_ctx rows of target
+ * features [n_ctx, n_aux*n_embd] (device) -> enc_out [n_ctx, n_embd] (device). */
+int lc_dflash_encode(lc_dflash *m, const float *features, uint32_t n_ctx, float *enc_out);
+/* Per-layer context K/V of forward_injected_decode_hidden (src/dflash.rs:933-936)
+ * for every encoder row: row p is rotated at position p. */
+int lc_dflash_set_context(lc_dflash *m, const float *enc_out, uint32_t n_ctx);
+/* The layer loop of forward_injected_decode_hidden (src/dflash.rs:938-975)
+ * for a block of m token inputs x [m, n_embd] (device) at positions
+ * n_ctx .. n_ctx+m-1, attending causally over [context K/V; block K/V];
+ * hidden [m, n_embd] (device) gets the output_norm'ed states.  With n_ctx = 1
+ * and m = 1 this is the reference's computation. */
+int lc_dflash_decode_block(lc_dflash *m, const float *x, uint32_t m_tokens, float *hidden);
+/* forward_injected_decode_hidden (src/dflash.rs:877-976) with host buffers:
+ * features [n_aux*n_embd], token_input [n_embd] -> hidden [n_embd]. */
+int lc_dflash_forward_injected_decode_hidden(lc_dflash *m, const float *features_host, const float *token_host,
+                                             float *hidden_host);
+/* forward_from_input (src/dflash.rs:735-851), the legacy single-token decoder
+ * behind the `encode` CLI: input [n_embd] (device) -> hidden [n_embd]
+ * (device); when logits is not NULL, the fc.weight buffer reinterpreted as
+ * [n_vocab, n_embd] rows (src/dflash.rs:839-847) projects the hidden state and
+ * n_vocab receives the row count. */
+int lc_dflash_forward_from_input(lc_dflash *m, const float *input, float *hidden, float *logits,
+                                 uint32_t *n_vocab);
+/* forward_token (src/dflash.rs:469-733) behind the `forward` CLI: the input is
+ * token_embd read as [n_embd][vocab] (x[i] = emb[i*vocab + token_id],
+ * src/dflash.rs:482-485), then forward_from_input's layer loop. */
+int lc_dflash_forward_token(lc_dflash *m, uint32_t token_id, float *hidden, float *logits, uint32_t *n_vocab);
+
 #ifdef __cplusplus
 }
 #endif

@@ -202,7 +202,8 @@ extern "C" int lc_mha_attn(lc_ctx *ctx, const float *q, const float *k, const fl
     float *o_part = (float *)scr;
     float2 *ml_part = (float2 *)(scr + ((o_bytes + 255) & ~(size_t)255));
     const size_t smem = (size_t)(kQV * kHD + kHD * kTK + kTK * kHD + kQV * kTK) * 4;
-    LC_CUDA(cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    s = lc_set_smem_attr((const void *)attn_partial_kernel, smem);
+    if (s) return s;
     dim3 grid(n_kv_heads, splits, chunks);
     attn_partial_kernel<<<grid, kThreads, smem, ctx->stream>>>(q, seq_len ? k : q, seq_len ? v : q, o_part, ml_part,
                                                                (int)m, (int)n_q_heads, (int)n_kv_heads, (int)seq_len,

@@ -1,0 +1,306 @@
+// lc_gguf.cpp -- GGUF v3 reader, the C++ counterpart of the reference's
+// GGUFReader (src/gguf.rs:321-421) and of Model::from_reader's
+// hyper-parameter lookup (src/model.rs:29-129, src/gguf.rs:516-653).
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "laguna_cuda.h"
+
+int lc_fail(int code, const char *fmt, ...);
+
+namespace {
+
+struct Value {
+    enum Kind { NUM_U, NUM_I, NUM_F, BOOL, STR, ARR } kind = NUM_U;
+    uint64_t u = 0;
+    int64_t i = 0;
+    double f = 0;
+    std::string s;
+    std::vector<Value> arr;
+    bool as_u64(uint64_t *out) const {
+        // GGUFValue::as_u64 (src/gguf.rs:229-237): U32/U64/I32/I64 only
+        if (kind == NUM_U) return *out = u, true;
+        if (kind == NUM_I) return *out = (uint64_t)i, true;
+        return false;
+    }
+    bool as_f32(float *out) const {
+        // GGUFValue::as_f32 (src/gguf.rs:239-249)
+        if (kind == NUM_F) return *out = (float)f, true;
+        if (kind == NUM_U) return *out = (float)u, true;
+        if (kind == NUM_I) return *out = (float)i, true;
+        return false;
+    }
+};
+
+struct Tensor {
+    std::string name;
+    std::vector<uint64_t> shape;
+    int dtype = 0;
+    uint64_t offset = 0;
+};
+
+}  // namespace
+
+struct lc_gguf {
+    FILE *f = nullptr;
+    uint32_t version = 0;
+    std::vector<std::pair<std::string, Value>> meta;
+    std::map<std::string, size_t> meta_index;
+    std::vector<Tensor> tensors;
+    uint64_t data_offset = 0;
+};
+
+namespace {
+
+bool rd(FILE *f, void *p, size_t n) { return fread(p, 1, n, f) == n; }
+
+template <typename T>
+bool rdv(FILE *f, T *v) {
+    return rd(f, v, sizeof(T));
+}
+
+bool read_string(FILE *f, std::string *s) {
+    uint64_t n;
+    if (!rdv(f, &n) || n > (1ull << 32)) return false;
+    s->resize(n);
+    return n == 0 || rd(f, &(*s)[0], n);
+}
+
+// read_value (src/gguf.rs:441-514): GGUF value type ids 0..12.
+bool read_value(FILE *f, uint32_t type, Value *v, int depth = 0) {
+    if (depth > 4) return false;
+    switch (type) {
+    case 0: { uint8_t x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_U; v->u = x; return true; }
+    case 1: { int8_t x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_I; v->i = x; return true; }
+    case 2: { uint16_t x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_U; v->u = x; return true; }
+    case 3: { int16_t x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_I; v->i = x; return true; }
+    case 4: { uint32_t x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_U; v->u = x; return true; }
+    case 5: { int32_t x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_I; v->i = x; return true; }
+    case 6: { float x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_F; v->f = x; return true; }
+    case 7: { uint8_t x; if (!rdv(f, &x)) return false; v->kind = Value::BOOL; v->u = x != 0; return true; }
+    case 8: v->kind = Value::STR; return read_string(f, &v->s);
+    case 9: {
+        uint32_t at;
+        uint64_t n;
+        if (!rdv(f, &at) || !rdv(f, &n) || n > (1ull << 28)) return false;
+        v->kind = Value::ARR;
+        v->arr.resize(n);
+        for (uint64_t i = 0; i < n; i++)
+            if (!read_value(f, at, &v->arr[i], depth + 1)) return false;
+        return true;
+    }
+    case 10: { uint64_t x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_U; v->u = x; return true; }
+    case 11: { int64_t x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_I; v->i = x; return true; }
+    case 12: { double x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_F; v->f = x; return true; }
+    default: return false;
+    }
+}
+
+const Value *find_meta(const lc_gguf *g, const char *key) {
+    auto it = g->meta_index.find(key);
+    return it == g->meta_index.end() ? nullptr : &g->meta[it->second].second;
+}
+
+// One of the laguna./dflash./bare spellings of a key (populate_metadata,
+// src/gguf.rs:516-653).  The reference applies fields in file order, so when
+// several spellings are present the one stored last wins; same here.
+const Value *find_any(const lc_gguf *g, std::initializer_list<const char *> keys) {
+    const Value *v = nullptr;
+    size_t best = 0;
+    for (const char *k : keys) {
+        auto it = g->meta_index.find(k);
+        if (it != g->meta_index.end() && (!v || it->second >= best)) {
+            v = &g->meta[it->second].second;
+            best = it->second;
+        }
+    }
+    return v;
+}
+
+}  // namespace
+
+extern "C" uint64_t lc_type_block_bytes(int dtype) {
+    switch (dtype) {
+    case LC_F32: return 4;
+    case LC_F16: case LC_BF16: return 2;
+    case LC_Q8_0: return 34;
+    case LC_Q4_K: return 144;
+    default: return 0;
+    }
+}
+
+extern "C" uint64_t lc_type_block_elements(int dtype) {
+    switch (dtype) {
+    case LC_F32: case LC_F16: case LC_BF16: return 1;
+    case LC_Q8_0: return 32;
+    case LC_Q4_K: return 256;
+    default: return 0;
+    }
+}
+
+extern "C" uint64_t lc_tensor_bytes(int dtype, uint64_t n) {
+    const uint64_t be = lc_type_block_elements(dtype);
+    if (!be) return 0;
+    return (n + be - 1) / be * lc_type_block_bytes(dtype);
+}
+
+extern "C" int lc_gguf_open(const char *path, lc_gguf **out) {
+    if (!path || !out) return lc_fail(LC_ERR_INVALID, "lc_gguf_open: null argument");
+    *out = nullptr;
+    FILE *f = fopen(path, "rb");
+    if (!f) return lc_fail(LC_ERR_IO, "lc_gguf_open: cannot open %s", path);
+    lc_gguf *g = new lc_gguf();
+    g->f = f;
+    auto bad = [&](const char *what) {
+        lc_gguf_close(g);
+        return lc_fail(LC_ERR_IO, "lc_gguf_open(%s): %s", path, what);
+    };
+    char magic[4];
+    if (!rd(f, magic, 4) || memcmp(magic, "GGUF", 4) != 0) return bad("not a GGUF file");
+    if (!rdv(f, &g->version)) return bad("truncated header");
+    if (g->version != 3) return bad("only GGUF v3 is supported");
+    uint64_t n_tensors, n_fields;
+    if (!rdv(f, &n_tensors) || !rdv(f, &n_fields) || n_tensors > (1ull << 24) || n_fields > (1ull << 24))
+        return bad("bad counts");
+    for (uint64_t i = 0; i < n_fields; i++) {
+        std::string key;
+        uint32_t type;
+        Value v;
+        if (!read_string(f, &key) || !rdv(f, &type) || !read_value(f, type, &v)) return bad("bad metadata");
+        g->meta_index[key] = g->meta.size();
+        g->meta.emplace_back(std::move(key), std::move(v));
+    }
+    for (uint64_t i = 0; i < n_tensors; i++) {
+        Tensor t;
+        uint32_t nd, dt;
+        if (!read_string(f, &t.name) || !rdv(f, &nd) || nd > 4) return bad("bad tensor info");
+        t.shape.resize(nd);
+        for (uint32_t d = 0; d < nd; d++)
+            if (!rdv(f, &t.shape[d])) return bad("bad tensor shape");
+        if (!rdv(f, &dt) || !rdv(f, &t.offset)) return bad("bad tensor info");
+        t.dtype = (int)dt;
+        g->tensors.push_back(std::move(t));
+    }
+    long pos = ftell(f);
+    uint64_t align = 32;
+    if (const Value *a = find_meta(g, "general.alignment")) {
+        uint64_t v;
+        if (a->as_u64(&v) && v > 0) align = v;
+    }
+    g->data_offset = ((uint64_t)pos + align - 1) / align * align;
+    *out = g;
+    return LC_OK;
+}
+
+extern "C" int lc_gguf_close(lc_gguf *g) {
+    if (!g) return LC_OK;
+    if (g->f) fclose(g->f);
+    delete g;
+    return LC_OK;
+}
+
+extern "C" uint64_t lc_gguf_tensor_count(const lc_gguf *g) { return g ? g->tensors.size() : 0; }
+
+extern "C" int lc_gguf_tensor_info(const lc_gguf *g, uint64_t i, const char **name, int *dtype, uint32_t *n_dims,
+                                   uint64_t shape[4], uint64_t *offset, uint64_t *n_bytes) {
+    if (!g || i >= g->tensors.size()) return lc_fail(LC_ERR_INVALID, "lc_gguf_tensor_info: bad index");
+    const Tensor &t = g->tensors[i];
+    uint64_t n = 1;
+    for (uint64_t d : t.shape) n *= d;
+    if (name) *name = t.name.c_str();
+    if (dtype) *dtype = t.dtype;
+    if (n_dims) *n_dims = (uint32_t)t.shape.size();
+    if (shape)
+        for (int d = 0; d < 4; d++) shape[d] = d < (int)t.shape.size() ? t.shape[d] : 1;
+    if (offset) *offset = t.offset;
+    if (n_bytes) *n_bytes = lc_tensor_bytes(t.dtype, n);
+    return LC_OK;
+}
+
+extern "C" int lc_gguf_find(const lc_gguf *g, const char *name, uint64_t *index) {
+    if (!g || !name || !index) return lc_fail(LC_ERR_INVALID, "lc_gguf_find: null argument");
+    for (uint64_t i = 0; i < g->tensors.size(); i++)
+        if (g->tensors[i].name == name) return *index = i, LC_OK;
+    return lc_fail(LC_ERR_INVALID, "lc_gguf_find: no tensor named %s", name);
+}
+
+extern "C" int lc_gguf_read(lc_gguf *g, uint64_t index, void *dst, uint64_t bytes) {
+    if (!g || !dst || index >= g->tensors.size()) return lc_fail(LC_ERR_INVALID, "lc_gguf_read: bad argument");
+    uint64_t need;
+    lc_gguf_tensor_info(g, index, nullptr, nullptr, nullptr, nullptr, nullptr, &need);
+    if (bytes < need) return lc_fail(LC_ERR_INVALID, "lc_gguf_read: buffer of %llu < %llu bytes",
+                                     (unsigned long long)bytes, (unsigned long long)need);
+    if (fseeko(g->f, (off_t)(g->data_offset + g->tensors[index].offset), SEEK_SET) != 0 || !rd(g->f, dst, need))
+        return lc_fail(LC_ERR_IO, "lc_gguf_read: short read of %s", g->tensors[index].name.c_str());
+    return LC_OK;
+}
+
+extern "C" int lc_gguf_meta_u64(const lc_gguf *g, const char *key, uint64_t *out) {
+    const Value *v = g && key ? find_meta(g, key) : nullptr;
+    if (!v || !out || !v->as_u64(out)) return lc_fail(LC_ERR_INVALID, "lc_gguf_meta_u64: no integer %s", key);
+    return LC_OK;
+}
+
+extern "C" int lc_gguf_meta_f32(const lc_gguf *g, const char *key, float *out) {
+    const Value *v = g && key ? find_meta(g, key) : nullptr;
+    if (!v || !out || !v->as_f32(out)) return lc_fail(LC_ERR_INVALID, "lc_gguf_meta_f32: no number %s", key);
+    return LC_OK;
+}
+
+extern "C" int lc_gguf_meta_str(const lc_gguf *g, const char *key, const char **out) {
+    const Value *v = g && key ? find_meta(g, key) : nullptr;
+    if (!v || !out || v->kind != Value::STR) return lc_fail(LC_ERR_INVALID, "lc_gguf_meta_str: no string %s", key);
+    *out = v->s.c_str();
+    return LC_OK;
+}
+
+extern "C" int lc_gguf_dflash_hparams(const lc_gguf *g, lc_dflash_hparams *hp) {
+    if (!g || !hp) return lc_fail(LC_ERR_INVALID, "lc_gguf_dflash_hparams: null argument");
+    memset(hp, 0, sizeof(*hp));
+    auto u64 = [&](std::initializer_list<const char *> keys, int arr_index = -1) -> uint64_t {
+        const Value *v = find_any(g, keys);
+        uint64_t r = 0;
+        if (!v) return 0;
+        if (v->kind == Value::ARR) {
+            // head_count arrays: first element; head_count_kv arrays: second (src/gguf.rs:540-560)
+            size_t i = arr_index < 0 ? 0 : (size_t)arr_index;
+            if (i < v->arr.size()) v->arr[i].as_u64(&r);
+            return r;
+        }
+        v->as_u64(&r);
+        return r;
+    };
+    hp->n_layers = (uint32_t)u64({"block_count", "laguna.block_count", "dflash.block_count"});
+    hp->n_embd = (uint32_t)u64({"embedding_length", "laguna.embedding_length", "dflash.embedding_length"});
+    hp->n_ff = (uint32_t)u64({"feed_forward_length", "laguna.feed_forward_length", "dflash.feed_forward_length"});
+    hp->n_heads = (uint32_t)u64({"attention.head_count", "laguna.attention.head_count", "dflash.attention.head_count"}, 0);
+    {
+        const Value *v = find_any(g, {"attention.head_count_kv", "laguna.attention.head_count_kv",
+                                      "dflash.attention.head_count_kv"});
+        uint64_t r = 0;
+        if (v && v->kind == Value::ARR) {
+            if (v->arr.size() > 1) v->arr[1].as_u64(&r);
+        } else if (v) {
+            v->as_u64(&r);
+        }
+        hp->n_kv_heads = (uint32_t)r;
+    }
+    hp->head_dim = (uint32_t)u64({"laguna.attention.key_length", "dflash.attention.key_length"});
+    if (hp->head_dim == 0 && hp->n_heads) hp->head_dim = hp->n_embd / hp->n_heads;  // key_length absent
+    hp->rope_dim = (uint32_t)u64({"rope.dimension_count", "laguna.rope.dimension_count", "dflash.rope.dimension_count"});
+    hp->rope_base = 500000.0f;
+    if (const Value *v = find_any(g, {"rope.freq_base", "laguna.rope.freq_base", "dflash.rope.freq_base"})) {
+        float f;
+        if (v->as_f32(&f)) hp->rope_base = f;
+    }
+    if (const Value *v = find_any(g, {"target_layers", "laguna.target_layers", "dflash.target_layers"}))
+        if (v->kind == Value::ARR) hp->n_aux = (uint32_t)v->arr.size();
+    hp->norm_eps = 1e-5f;
+    hp->qk_eps = 1e-6f;
+    return LC_OK;
+}

@@ -18,8 +18,8 @@ struct lc_ctx {
     int sync = 0;
     int half_mode = LC_HALF_REF;
     // Grow-only scratch slots (see LC_SCRATCH_*).
-    void *scratch[4] = {nullptr, nullptr, nullptr, nullptr};
-    size_t scratch_bytes[4] = {0, 0, 0, 0};
+    void *scratch[8] = {};
+    size_t scratch_bytes[8] = {};
 };
 
 struct lc_buf {
@@ -34,13 +34,29 @@ int lc_fail(int code, const char *fmt, ...);
 int lc_after_launch(lc_ctx *ctx, const char *what);
 // Scratch slots: packed activation fragments, logits of the argmax path,
 // the DFlash block-forward workspace, attention partials.
-enum { LC_SCRATCH_PACK = 0, LC_SCRATCH_LOGITS = 1, LC_SCRATCH_MODEL = 2, LC_SCRATCH_ATTN = 3 };
+// LC_SCRATCH_FIXUP holds the split-tile sums of the stream-K projections and
+// must read zero between calls (the kernels leave it zeroed).
+enum {
+    LC_SCRATCH_PACK = 0,
+    LC_SCRATCH_LOGITS = 1,
+    LC_SCRATCH_MODEL = 2,
+    LC_SCRATCH_ATTN = 3,
+    LC_SCRATCH_FIXUP = 4,
+    LC_SCRATCH_COUNT = 8
+};
 // Grow-only scratch slot of at least `bytes` (256-byte aligned).  Returns
 // nullptr and sets the error on failure.  Waits for the stream before
 // reallocating.
 void *lc_scratch(lc_ctx *ctx, int slot, size_t bytes);
+// Same, and a newly allocated slot is zero-filled (on the context's stream).
+void *lc_scratch_zeroed(lc_ctx *ctx, int slot, size_t bytes);
 // Make ctx->device current on this thread.
 int lc_use_device(lc_ctx *ctx);
+// Raise a kernel's dynamic shared memory limit to at least `bytes` on the
+// current device; remembered per (device, kernel) so repeated calls (and calls
+// made while a stream is being captured into a CUDA graph) do not touch the
+// driver again.
+int lc_set_smem_attr(const void *kernel, size_t bytes);
 
 #define LC_REQUIRE(cond, code, ...)             \
     do {                                        \

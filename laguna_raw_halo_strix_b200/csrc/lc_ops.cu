@@ -274,13 +274,17 @@ extern "C" int lc_qk_norm_rope(lc_ctx *ctx, const float *x, const float *w, cons
     LC_REQUIRE(x && w && out && (freq || rope_dim == 0), LC_ERR_INVALID, "lc_qk_norm_rope: null pointer");
     LC_REQUIRE(head_dim > 0 && head_dim % 2 == 0, LC_ERR_INVALID, "lc_qk_norm_rope: head_dim %u must be even",
                head_dim);
-    LC_REQUIRE(rope_dim <= head_dim && rope_dim % 2 == 0, LC_ERR_INVALID,
-               "lc_qk_norm_rope: rope_dim %u must be even and <= head_dim %u", rope_dim, head_dim);
+    // qk_norm_rope.comp pairs dim with dim +/- head_dim/2 while rotating only
+    // dims < rope_dim; for 0 < rope_dim < head_dim that pair index leaves the
+    // head (head 0 reads before the buffer), and rope_dim > head_dim reads the
+    // frequency table past its end.  Only the well-defined forms are accepted.
+    LC_REQUIRE(rope_dim == 0 || rope_dim == head_dim, LC_ERR_UNSUPPORTED,
+               "lc_qk_norm_rope: rope_dim %u must be 0 or head_dim %u", rope_dim, head_dim);
     const size_t smem = ((size_t)n_heads * head_dim + n_heads) * 4;
     LC_REQUIRE(smem <= ctx->smem_optin, LC_ERR_UNSUPPORTED, "lc_qk_norm_rope: row of %u values too large",
                n_heads * head_dim);
     if (smem > 48 * 1024)
-        LC_CUDA(cudaFuncSetAttribute(qk_norm_rope_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (int s = lc_set_smem_attr((const void *)qk_norm_rope_kernel, smem)) return s;
     qk_norm_rope_kernel<<<m, 256, smem, ctx->stream>>>(x, w, freq, out, (int)n_heads, (int)head_dim, (int)rope_dim,
                                                         eps, pos0);
     return lc_after_launch(ctx, "lc_qk_norm_rope");

@@ -53,66 +53,109 @@ __device__ __forceinline__ __half2 h2_from_u6(uint32_t s) {
     return __hsub2(lc_u32_as_h2(v), __half2(__float2half_rn(1024.f), __float2half_rn(1024.f)));
 }
 
+// Power-of-two activation scale: x * 2^e has max|x * 2^e| in [2^13, 2^14), so
+// its f16 hi / lo split cannot overflow (f16 max 65504) however large the
+// activations grow; outputs are multiplied by 2^-e.  Both steps are exact.
+__device__ __forceinline__ void act_scale(float maxabs, float &s, float &inv) {
+    int e = 0;
+    if (maxabs > 0.f && maxabs < INFINITY) {
+        int x;
+        frexpf(maxabs, &x);  // maxabs = f * 2^x, f in [0.5, 1)
+        e = min(max(14 - x, -100), 100);
+    }
+    s = ldexpf(1.f, e);
+    inv = ldexpf(1.f, -e);
+}
+
 // ---------------------------------------------------------------------------
-// Activation packing.  Table entry (uint2 = B regs {b0b1, b2b3}) for
-// [block-step][n-tile][lane]; lanes = 8 when m == 1 (only columns 0/1 used).
+// Activation packing for the tiled kernels.  Table entry (uint2 = B regs
+// {b0b1, b2b3}) for [block-step][n-tile][lane]; column 2t'+p of n-tile nt is
+// token nt*4 + t' (p = f16 hi / lo).  One CTA per token slot (NT*4 of them)
+// finds the token's power-of-two scale (act_scale), records 2^-e in
+// inv_scale[token], and writes the 8 lanes of every k-step that carry it
+// (zeros for the padding slots past m).
+
+__device__ __forceinline__ float block_max_abs(const float *__restrict__ xr, int k) {
+    __shared__ float sh[32];
+    float v = 0.f;
+    for (int i = threadIdx.x; i < k; i += blockDim.x) v = fmaxf(v, fabsf(xr[i]));
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    v = (threadIdx.x < (blockDim.x >> 5)) ? sh[threadIdx.x] : 0.f;
+    if (threadIdx.x < 32)
+        for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (threadIdx.x == 0) sh[0] = v;
+    __syncthreads();
+    return sh[0];
+}
 
 // Q4_K: 17 k-steps per 256-element super-block: 16 main steps
 // js = h*8 + wi*2 + half, plus the min step (js = 16) carrying Sx.
-__global__ void x_pack_q4k(const float *__restrict__ x, uint2 *__restrict__ tab, int m, int k, int nt_count,
-                           int lanes, int total) {
-    int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= total) return;
-    int lane = idx % lanes;
-    int r = idx / lanes;
-    int nt = r % nt_count;
-    r /= nt_count;
-    int js = r % 17;
-    int sb = r / 17;
-    int g = lane >> 2, t = lane & 3;
-    int tok = nt * 4 + (g >> 1), part = g & 1;
-    uint2 v = make_uint2(0u, 0u);
-    if (tok < m) {
-        const float *xr = x + (size_t)tok * k + (size_t)sb * 256;
-        if (js < 16) {
-            int h = js >> 3, wi = (js >> 1) & 3, half = js & 1;
-            int jb = 16 * (t + 4 * h) + 4 * wi;
-            auto el = [&](int j) { return 64 * (j >> 5) + (j & 31) + 32 * half; };
-            v.x = lc_pack_h2(lc_split_part(xr[el(jb + 0)], part), lc_split_part(xr[el(jb + 2)], part));
-            v.y = lc_pack_h2(lc_split_part(xr[el(jb + 1)], part), lc_split_part(xr[el(jb + 3)], part));
-        } else {
-            float s0 = 0.f, s1 = 0.f;
-            for (int e = 0; e < 32; e++) {
-                s0 += xr[32 * (2 * t) + e];
-                s1 += xr[32 * (2 * t + 1) + e];
-            }
-            v.x = lc_pack_h2(lc_split_part(s0, part), lc_split_part(s1, part));
-        }
+__global__ void x_pack_q4k(const float *__restrict__ x, uint2 *__restrict__ tab, float *__restrict__ inv_scale, int m,
+                           int k, int nt_count) {
+    const int tk = blockIdx.x, nt = tk >> 2, tl = tk & 3;
+    const bool live = tk < m;
+    const float *xr = x + (size_t)(live ? tk : 0) * k;
+    float s = 0.f, inv = 0.f;
+    if (live) {
+        act_scale(block_max_abs(xr, k), s, inv);
+        if (threadIdx.x == 0) inv_scale[tk] = inv;
     }
-    tab[idx] = v;
+    const int nsb = k >> 8;
+    for (int e = threadIdx.x; e < nsb * 17 * 8; e += blockDim.x) {
+        const int t = e & 3, part = (e >> 2) & 1;
+        const int js = (e >> 3) % 17, sb = (e >> 3) / 17;
+        const int lane = 4 * (2 * tl + part) + t;
+        uint2 v = make_uint2(0u, 0u);
+        if (live) {
+            const float *xb = xr + (size_t)sb * 256;
+            if (js < 16) {
+                const int h = js >> 3, wi = (js >> 1) & 3, half = js & 1;
+                const int jb = 16 * (t + 4 * h) + 4 * wi;
+                auto el = [&](int j) { return 64 * (j >> 5) + (j & 31) + 32 * half; };
+                v.x = lc_pack_h2(lc_split_part(xb[el(jb + 0)] * s, part), lc_split_part(xb[el(jb + 2)] * s, part));
+                v.y = lc_pack_h2(lc_split_part(xb[el(jb + 1)] * s, part), lc_split_part(xb[el(jb + 3)] * s, part));
+            } else {
+                float s0 = 0.f, s1 = 0.f;
+                for (int i = 0; i < 32; i++) {
+                    s0 += xb[32 * (2 * t) + i];
+                    s1 += xb[32 * (2 * t + 1) + i];
+                }
+                // Sx / 32 keeps the scaled 32-element sums inside the f16 range;
+                // q4k_unit multiplies dmin by 32 to compensate (both exact)
+                v.x = lc_pack_h2(lc_split_part(s0 * s * 0.03125f, part), lc_split_part(s1 * s * 0.03125f, part));
+            }
+        }
+        tab[((size_t)(sb * 17 + js) * nt_count + nt) * 32 + lane] = v;
+    }
 }
 
 // Q8_0: 2 k-steps per 32-element block; thread t of step ks covers elements
 // 16*ks + 4t + {0..3}: b0b1 = (e0, e2), b2b3 = (e1, e3).
-__global__ void x_pack_q8(const float *__restrict__ x, uint2 *__restrict__ tab, int m, int k, int nt_count,
-                          int lanes, int total) {
-    int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= total) return;
-    int lane = idx % lanes;
-    int r = idx / lanes;
-    int nt = r % nt_count;
-    r /= nt_count;
-    int ks = r & 1;
-    int b = r >> 1;
-    int g = lane >> 2, t = lane & 3;
-    int tok = nt * 4 + (g >> 1), part = g & 1;
-    uint2 v = make_uint2(0u, 0u);
-    if (tok < m) {
-        const float *xr = x + (size_t)tok * k + (size_t)b * 32 + 16 * ks + 4 * t;
-        v.x = lc_pack_h2(lc_split_part(xr[0], part), lc_split_part(xr[2], part));
-        v.y = lc_pack_h2(lc_split_part(xr[1], part), lc_split_part(xr[3], part));
+__global__ void x_pack_q8(const float *__restrict__ x, uint2 *__restrict__ tab, float *__restrict__ inv_scale, int m,
+                          int k, int nt_count) {
+    const int tk = blockIdx.x, nt = tk >> 2, tl = tk & 3;
+    const bool live = tk < m;
+    const float *xr = x + (size_t)(live ? tk : 0) * k;
+    float s = 0.f, inv = 0.f;
+    if (live) {
+        act_scale(block_max_abs(xr, k), s, inv);
+        if (threadIdx.x == 0) inv_scale[tk] = inv;
     }
-    tab[idx] = v;
+    const int nb = k >> 5;
+    for (int e = threadIdx.x; e < nb * 2 * 8; e += blockDim.x) {
+        const int t = e & 3, part = (e >> 2) & 1;
+        const int ks = (e >> 3) & 1, b = e >> 4;
+        const int lane = 4 * (2 * tl + part) + t;
+        uint2 v = make_uint2(0u, 0u);
+        if (live) {
+            const float *xb = xr + (size_t)b * 32 + 16 * ks + 4 * t;
+            v.x = lc_pack_h2(lc_split_part(xb[0] * s, part), lc_split_part(xb[2] * s, part));
+            v.y = lc_pack_h2(lc_split_part(xb[1] * s, part), lc_split_part(xb[3] * s, part));
+        }
+        tab[((size_t)(b * 2 + ks) * nt_count + nt) * 32 + lane] = v;
+    }
 }
 
 // Copy `n16` 16-byte units of the packed table into shared memory.
@@ -123,7 +166,7 @@ __device__ __forceinline__ void copy_tab(uint4 *dst, const uint4 *src, int n16) 
 // Cross-warp reduction of the per-thread results and the store.
 template <int NT>
 __device__ __forceinline__ void reduce_store(float (&acc)[NT][4], float *red, float *c, int m, int n, int row0,
-                                             int atomic_out) {
+                                             int atomic_out, const float *__restrict__ inv_scale) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
@@ -142,6 +185,9 @@ __device__ __forceinline__ void reduce_store(float (&acc)[NT][4], float *red, fl
         }
         int tok = nt * 4 + t;
         if (tok < m) {
+            const float inv = inv_scale[tok];
+            y0 *= inv;
+            y1 *= inv;
             int r0 = row0 + g, r1 = row0 + g + 8;
             float *cr = c + (size_t)tok * n;
             if (atomic_out) {
@@ -156,13 +202,139 @@ __device__ __forceinline__ void reduce_store(float (&acc)[NT][4], float *red, fl
 }
 
 // ---------------------------------------------------------------------------
-// Q4_K.  Grid: x = 16-row tiles, y = K chunks of sb_per_chunk super-blocks.
+// Q4_K.
+//
+// The raw bytes of one 256-element super-block for rows g and g+8 of a
+// 16-row tile: headers (d, dmin, 12 scale bytes) and the thread's two 16-byte
+// chunks of nibbles (chunks t and t+4 of the 128).
+struct Q4Unit {
+    uint4 H0, H1, Q0a, Q0b, Q1a, Q1b;
+    __device__ __forceinline__ void load(const uint8_t *b0, const uint8_t *b1, int t) {
+        H0 = H1 = Q0a = Q0b = Q1a = Q1b = make_uint4(0, 0, 0, 0);
+        if (b0) {
+            H0 = ldg_stream(b0);
+            Q0a = ldg_stream(b0 + 16 + 16 * t);
+            Q0b = ldg_stream(b0 + 16 + 16 * (t + 4));
+        }
+        if (b1) {
+            H1 = ldg_stream(b1);
+            Q1a = ldg_stream(b1 + 16 + 16 * t);
+            Q1b = ldg_stream(b1 + 16 + 16 * (t + 4));
+        }
+    }
+};
+
+// One super-block of one 16-row tile on the tensor cores:
+// acc += d * S(sc*q*x) - dmin * S(m*Sx) for rows g, g+8 (c0,c1 / c2,c3).
+// tb points at the super-block's 17 k-steps of packed activations
+// (NT n-tiles x LANES lanes each).
+template <int NT, int LANES>
+__device__ __forceinline__ void q4k_unit(const Q4Unit &U, const uint2 *tb, int lane, int half_mode,
+                                         float (&acc)[NT][4]) {
+    constexpr int kStep = NT * LANES;
+    const int t = lane & 3;
+    const int p0 = t >> 1;
+    const __half2 kNeg1024 = __half2(__float2half_rn(-1024.f), __float2half_rn(-1024.f));
+    const __half2 kSixteenth = __half2(__float2half_rn(0.0625f), __float2half_rn(0.0625f));
+    const __half2 kNeg64 = __half2(__float2half_rn(-64.f), __float2half_rn(-64.f));
+    const __half2 k1024 = __half2(__float2half_rn(1024.f), __float2half_rn(1024.f));
+    const float dg = lc_half_to_f32(U.H0.x & 0xFFFFu, half_mode), dmg = lc_half_to_f32(U.H0.x >> 16, half_mode);
+    const float dg8 = lc_half_to_f32(U.H1.x & 0xFFFFu, half_mode), dmg8 = lc_half_to_f32(U.H1.x >> 16, half_mode);
+
+    // Scales of this thread's sub-blocks (get_scale_min_k4, proj_q4k.comp:113-125):
+    // lo0 = 2p0, hi0 = 2p0+1 (j < 4); lo1 = 2p0+4, hi1 = 2p0+5 (j >= 4).
+    __half2 mul[2][4], add[2][4];  // [row g / g+8][lo0, hi0, lo1, hi1]
+    uint32_t mpk[2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const uint4 H = r ? U.H1 : U.H0;
+        const uint32_t yy = H.y >> (16 * p0), ww = H.w >> (16 * p0);
+        const uint32_t s_lo0 = yy & 63u, s_hi0 = (yy >> 8) & 63u;
+        const uint32_t s_lo1 = (ww & 15u) | ((yy >> 2) & 0x30u);
+        const uint32_t s_hi1 = ((ww >> 8) & 15u) | ((yy >> 10) & 0x30u);
+        __half2 h;
+        h = h2_from_u6(s_lo0);
+        mul[r][0] = h;
+        add[r][0] = __hmul2(h, kNeg1024);
+        h = h2_from_u6(s_hi0);
+        mul[r][1] = __hmul2(h, kSixteenth);
+        add[r][1] = __hmul2(h, kNeg64);
+        h = h2_from_u6(s_lo1);
+        mul[r][2] = h;
+        add[r][2] = __hmul2(h, kNeg1024);
+        h = h2_from_u6(s_hi1);
+        mul[r][3] = __hmul2(h, kSixteenth);
+        add[r][3] = __hmul2(h, kNeg64);
+        // mins of sub-blocks 2t and 2t+1 for the min step
+        uint32_t m0, m1;
+        if (t < 2) {
+            const uint32_t zz = H.z >> (16 * t);
+            m0 = zz & 63u;
+            m1 = (zz >> 8) & 63u;
+        } else {
+            const uint32_t zz = H.z >> (16 * (t - 2)), wz = H.w >> (16 * (t - 2));
+            m0 = ((wz >> 4) & 15u) | ((zz >> 2) & 0x30u);
+            m1 = ((wz >> 12) & 15u) | ((zz >> 10) & 0x30u);
+        }
+        mpk[r] = lc_h2_as_u32(__hsub2(lc_u32_as_h2((m0 | 0x6400u) | ((m1 | 0x6400u) << 16)), k1024));
+    }
+
+    // two independent accumulation chains (h = 0 / h = 1) for MMA-level ILP
+    float cmh[2][NT][4], cmin[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) cmh[0][i][j] = cmh[1][i][j] = cmin[i][j] = 0.f;
+
+#pragma unroll
+    for (int wi = 0; wi < 4; wi++) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t xg = u4_get(h ? U.Q0b : U.Q0a, wi), xg8 = u4_get(h ? U.Q1b : U.Q1a, wi);
+            const uint32_t xgs = xg >> 8, xg8s = xg8 >> 8;
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const int si = 2 * h + half;  // lo0, hi0, lo1, hi1
+                const uint32_t mask = half ? 0x00F000F0u : 0x000F000Fu;
+                const uint32_t a0 =
+                    lc_h2_as_u32(__hfma2(lc_u32_as_h2((xg & mask) | 0x64006400u), mul[0][si], add[0][si]));
+                const uint32_t a1 =
+                    lc_h2_as_u32(__hfma2(lc_u32_as_h2((xg8 & mask) | 0x64006400u), mul[1][si], add[1][si]));
+                const uint32_t a2 =
+                    lc_h2_as_u32(__hfma2(lc_u32_as_h2((xgs & mask) | 0x64006400u), mul[0][si], add[0][si]));
+                const uint32_t a3 =
+                    lc_h2_as_u32(__hfma2(lc_u32_as_h2((xg8s & mask) | 0x64006400u), mul[1][si], add[1][si]));
+                const int js = h * 8 + wi * 2 + half;
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+                    uint2 b = make_uint2(0u, 0u);
+                    if (LANES == 32 || lane < LANES) b = tb[js * kStep + nt * LANES + lane];
+                    lc_mma16816(cmh[h][nt], a0, a1, a2, a3, b.x, b.y);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+        uint2 b = make_uint2(0u, 0u);
+        if (LANES == 32 || lane < LANES) b = tb[16 * kStep + nt * LANES + lane];
+        lc_mma1688(cmin[nt], mpk[0], mpk[1], b.x);
+        // the table carries Sx / 32 (see x_pack_q4k)
+        acc[nt][0] += dg * (cmh[0][nt][0] + cmh[1][nt][0]) - 32.f * dmg * cmin[nt][0];
+        acc[nt][1] += dg * (cmh[0][nt][1] + cmh[1][nt][1]) - 32.f * dmg * cmin[nt][1];
+        acc[nt][2] += dg8 * (cmh[0][nt][2] + cmh[1][nt][2]) - 32.f * dmg8 * cmin[nt][2];
+        acc[nt][3] += dg8 * (cmh[0][nt][3] + cmh[1][nt][3]) - 32.f * dmg8 * cmin[nt][3];
+    }
+}
+
+// Tiled form (any m up to 16 per launch, packed table in global memory).
+// Grid: x = 16-row tiles, y = K chunks of sb_per_chunk super-blocks.
 // Warp w of the CTA handles super-blocks w, w+kWarps, ... of the chunk.
 template <int NT, int LANES>
 __global__ void __launch_bounds__(kWarps * 32) q4k_mma_kernel(const uint2 *__restrict__ tab_g,
                                                               const uint8_t *__restrict__ w, float *__restrict__ c,
                                                               int m, int k, int n, int sb_per_chunk, int half_mode,
-                                                              int atomic_out) {
+                                                              int atomic_out, const float *__restrict__ inv_scale) {
     extern __shared__ __align__(16) unsigned char smem[];
     constexpr int kStep = NT * LANES;  // uint2 entries per k-step
     const int nsb = k >> 8;
@@ -188,114 +360,358 @@ __global__ void __launch_bounds__(kWarps * 32) q4k_mma_kernel(const uint2 *__res
 #pragma unroll
     for (int i = 0; i < NT; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
-    const int p0 = t >> 1;
-    const __half2 kNeg1024 = __half2(__float2half_rn(-1024.f), __float2half_rn(-1024.f));
-    const __half2 kSixteenth = __half2(__float2half_rn(0.0625f), __float2half_rn(0.0625f));
-    const __half2 kNeg64 = __half2(__float2half_rn(-64.f), __float2half_rn(-64.f));
-    const __half2 k1024 = __half2(__float2half_rn(1024.f), __float2half_rn(1024.f));
-
     for (int sbl = warp; sbl < nloc; sbl += kWarps) {
         const size_t off = (size_t)(sb0 + sbl) * 144;
-        uint4 H0 = make_uint4(0, 0, 0, 0), H1 = H0, Q0a = H0, Q0b = H0, Q1a = H0, Q1b = H0;
-        if (vg) {
-            H0 = ldg_stream(wg + off);
-            Q0a = ldg_stream(wg + off + 16 + 16 * t);
-            Q0b = ldg_stream(wg + off + 16 + 16 * (t + 4));
-        }
-        if (vg8) {
-            H1 = ldg_stream(wg8 + off);
-            Q1a = ldg_stream(wg8 + off + 16 + 16 * t);
-            Q1b = ldg_stream(wg8 + off + 16 + 16 * (t + 4));
-        }
-        const float dg = lc_half_to_f32(H0.x & 0xFFFFu, half_mode), dmg = lc_half_to_f32(H0.x >> 16, half_mode);
-        const float dg8 = lc_half_to_f32(H1.x & 0xFFFFu, half_mode), dmg8 = lc_half_to_f32(H1.x >> 16, half_mode);
+        Q4Unit U;
+        U.load(vg ? wg + off : nullptr, vg8 ? wg8 + off : nullptr, t);
+        q4k_unit<NT, LANES>(U, tab + (size_t)sbl * 17 * kStep, lane, half_mode, acc);
+    }
+    reduce_store<NT>(acc, red, c, m, n, row0, atomic_out, inv_scale);
+}
 
-        // Scales of this thread's sub-blocks (get_scale_min_k4, proj_q4k.comp:113-125):
-        // lo0 = 2p0, hi0 = 2p0+1 (j < 4); lo1 = 2p0+4, hi1 = 2p0+5 (j >= 4).
-        __half2 mul[2][4], add[2][4];  // [row g / g+8][lo0, hi0, lo1, hi1]
-        uint32_t mpk[2];
-#pragma unroll
-        for (int r = 0; r < 2; r++) {
-            const uint4 H = r ? H1 : H0;
-            const uint32_t yy = H.y >> (16 * p0), ww = H.w >> (16 * p0);
-            const uint32_t s_lo0 = yy & 63u, s_hi0 = (yy >> 8) & 63u;
-            const uint32_t s_lo1 = (ww & 15u) | ((yy >> 2) & 0x30u);
-            const uint32_t s_hi1 = ((ww >> 8) & 15u) | ((yy >> 10) & 0x30u);
-            __half2 h;
-            h = h2_from_u6(s_lo0);
-            mul[r][0] = h;
-            add[r][0] = __hmul2(h, kNeg1024);
-            h = h2_from_u6(s_hi0);
-            mul[r][1] = __hmul2(h, kSixteenth);
-            add[r][1] = __hmul2(h, kNeg64);
-            h = h2_from_u6(s_lo1);
-            mul[r][2] = h;
-            add[r][2] = __hmul2(h, kNeg1024);
-            h = h2_from_u6(s_hi1);
-            mul[r][3] = __hmul2(h, kSixteenth);
-            add[r][3] = __hmul2(h, kNeg64);
-            // mins of sub-blocks 2t and 2t+1 for the min step
-            uint32_t m0, m1;
-            if (t < 2) {
-                const uint32_t zz = H.z >> (16 * t);
-                m0 = zz & 63u;
-                m1 = (zz >> 8) & 63u;
-            } else {
-                const uint32_t zz = H.z >> (16 * (t - 2)), wz = H.w >> (16 * (t - 2));
-                m0 = ((wz >> 4) & 15u) | ((zz >> 2) & 0x30u);
-                m1 = ((wz >> 12) & 15u) | ((zz >> 10) & 0x30u);
-            }
-            mpk[r] = lc_h2_as_u32(__hsub2(lc_u32_as_h2((m0 | 0x6400u) | ((m1 | 0x6400u) << 16)), k1024));
+// ---------------------------------------------------------------------------
+// Persistent stream-K form for m <= 4 (one n-tile).  One CTA per SM builds
+// the packed activation table for the whole K in shared memory, then its
+// warps walk equal shares of the flattened (16-row tile, super-block) unit
+// space, prefetching the next unit's bytes while the tensor cores work on the
+// current one.  A tile whose super-blocks are split between warps is summed
+// in `fix_acc` with atomics; the warp that completes the tile's count writes
+// the row and leaves fix_acc / fix_cnt zero again for the next call.
+constexpr int kSkWarps = 16;
+
+struct Fixup {
+    float *acc;       // [tiles][16 rows][4 tokens]
+    unsigned *cnt;    // [tiles]
+};
+
+// Write (or accumulate) the finished part [sb_a, sb_b) of `tile`.
+template <int LANES>
+__device__ __forceinline__ void sk_flush(const float (&acc)[1][4], int tile, int sb_a, int sb_b, int S, int m,
+                                         int n, float *__restrict__ y, Fixup fx, int lane, const float *scl) {
+    const int g = lane >> 2, t = lane & 3;
+    const int tok = t;  // column pair (2t, 2t+1) = token t (hi, lo)
+    const bool vt = (LANES == 8) ? (t == 0) : (tok < m);
+    const int r0 = tile * 16 + g, r1 = r0 + 8;
+    const float inv = vt ? scl[2 * tok + 1] : 0.f;
+    const float y0 = (acc[0][0] + acc[0][1]) * inv, y1 = (acc[0][2] + acc[0][3]) * inv;
+    if (sb_a == 0 && sb_b == S) {
+        if (vt) {
+            if (r0 < n) y[(size_t)tok * n + r0] = y0;
+            if (r1 < n) y[(size_t)tok * n + r1] = y1;
         }
+        return;
+    }
+    float *fa = fx.acc + (size_t)tile * 64;
+    if (vt) {
+        atomicAdd(fa + g * 4 + tok, y0);
+        atomicAdd(fa + (g + 8) * 4 + tok, y1);
+    }
+    __threadfence();
+    __syncwarp();
+    unsigned last = 0;
+    if (lane == 0) {
+        const unsigned add = (unsigned)(sb_b - sb_a);
+        last = (atomicAdd(fx.cnt + tile, add) + add == (unsigned)S);
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    if (vt) {
+        const float v0 = atomicExch(fa + g * 4 + tok, 0.f);
+        const float v1 = atomicExch(fa + (g + 8) * 4 + tok, 0.f);
+        if (r0 < n) y[(size_t)tok * n + r0] = v0;
+        if (r1 < n) y[(size_t)tok * n + r1] = v1;
+    }
+    if (lane == 0) atomicExch(fx.cnt + tile, 0u);
+}
 
-        float cm[NT][4], cmin[NT][4];
-#pragma unroll
-        for (int i = 0; i < NT; i++)
-            cm[i][0] = cm[i][1] = cm[i][2] = cm[i][3] = cmin[i][0] = cmin[i][1] = cmin[i][2] = cmin[i][3] = 0.f;
+// Floats reserved for the sub-block sums: rounded up to a multiple of 4 so the
+// staged x that follows starts on a 16-byte boundary (float4 stores).
+__host__ __device__ __forceinline__ size_t sk_sx_floats(int m, int nsub) {
+    return ((size_t)m * nsub + 3) & ~(size_t)3;
+}
 
-        const uint2 *tb = tab + (size_t)sbl * 17 * kStep;
+// Prologue of the stream-K kernels: stage x [m, k] into shared memory, find
+// each token's activation scale (scl[2j] = 2^e, scl[2j+1] = 2^-e) and, when sx
+// is given, the per-32-element sums of the scaled f16 hi + lo split the tensor
+// cores will see (the offset terms they cancel must match the MMA products).
+__device__ __forceinline__ void sk_prologue_x(const float *__restrict__ x, int m, int k, float *xs, float *sx,
+                                              int sx_stride, float *scl) {
+    __shared__ unsigned smax[4];
+    if (threadIdx.x < 4) smax[threadIdx.x] = 0u;
+    __syncthreads();
+    const bool vec = (((uintptr_t)x) & 15) == 0;
+    const int n4 = (m * k) >> 2;
+    float mx[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        float4 v;
+        if (vec) {
+            v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+        } else {
+            v.x = __ldg(x + 4 * i);
+            v.y = __ldg(x + 4 * i + 1);
+            v.z = __ldg(x + 4 * i + 2);
+            v.w = __ldg(x + 4 * i + 3);
+        }
+        reinterpret_cast<float4 *>(xs)[i] = v;
+        const float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        const int tok = (4 * i) / k;
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const uint4 qg = h ? Q0b : Q0a;
-            const uint4 qg8 = h ? Q1b : Q1a;
+        for (int j = 0; j < 4; j++)
+            if (j == tok) mx[j] = fmaxf(mx[j], a);
+    }
 #pragma unroll
-            for (int wi = 0; wi < 4; wi++) {
-                const uint32_t xg = u4_get(qg, wi), xg8 = u4_get(qg8, wi);
-                const uint32_t xgs = xg >> 8, xg8s = xg8 >> 8;
+    for (int j = 0; j < 4; j++) {
+        float v = mx[j];
+        for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if ((threadIdx.x & 31) == 0 && j < m) atomicMax(smax + j, __float_as_uint(v));  // v >= 0: int order
+    }
+    __syncthreads();
+    if (threadIdx.x < m) act_scale(__uint_as_float(smax[threadIdx.x]), scl[2 * threadIdx.x], scl[2 * threadIdx.x + 1]);
+    __syncthreads();
+    if (!sx) return;
+    const int nsub = k >> 5;
+    const int lane = threadIdx.x & 31;
+    for (int i = threadIdx.x >> 5; i < m * nsub; i += blockDim.x >> 5) {
+        const int tok = i / nsub, s = i % nsub;
+        const float f = xs[(size_t)tok * k + 32 * s + lane] * scl[2 * tok];
+        const __half h = __float2half_rn(f);
+        float v = __half2float(h) + __half2float(__float2half_rn(f - __half2float(h)));
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) sx[tok * sx_stride + s] = v;
+    }
+}
+
+// f16 bits -> f32 for the per-block scales: IEEE convert, then the reference
+// rule for subnormals (2^-14 * (1 + m/1024) = IEEE value + sign * 2^-14).
+__device__ __forceinline__ float scale_f32(uint32_t h16, int half_mode) {
+    const float f = __half2float(__ushort_as_half((unsigned short)(h16 & 0xFFFFu)));
+    const bool sub = half_mode == LC_HALF_REF && (h16 & 0x7C00u) == 0u && (h16 & 0x3FFu) != 0u;
+    return f + (sub ? copysignf(6.103515625e-05f, f) : 0.f);  // branch-free select
+}
+
+// The raw bytes of one 256-element super-block for rows g and g+8 of a 16-row
+// tile: headers (d, dmin, 12 scale bytes) and nibble group t (bytes 32t..32t+31
+// of the 128, i.e. sub-blocks 2t -- low nibbles -- and 2t+1 -- high nibbles).
+struct Q4UnitG {
+    uint4 H0, H1, A0, B0, A1, B1;
+    __device__ __forceinline__ void load(const uint8_t *b0, const uint8_t *b1, int t) {
+        H0 = H1 = A0 = B0 = A1 = B1 = make_uint4(0, 0, 0, 0);
+        if (b0) {
+            H0 = ldg_stream(b0);
+            A0 = ldg_stream(b0 + 16 + 32 * t);
+            B0 = ldg_stream(b0 + 32 + 32 * t);
+        }
+        if (b1) {
+            H1 = ldg_stream(b1);
+            A1 = ldg_stream(b1 + 16 + 32 * t);
+            B1 = ldg_stream(b1 + 32 + 32 * t);
+        }
+    }
+};
+
+// One super-block of a 16-row tile for M tokens, with sub-block sums split by
+// the MMA itself.  A = 1024 + q (low nibbles) or 1024 + 16q (high nibbles),
+// one LOP3 per register and no scaling.  B (one n-tile per token) holds the
+// token's x hi / lo only at the k positions of one owner thread t' in columns
+// 2t' / 2t'+1, so thread t's accumulator columns are exactly the sums over its
+// own sub-block: C[half] = S((1024 + 16^half q) x) over sub-block 2t + half.
+// Scales, mins and the offset are applied once per (row, sub-block) in f32:
+//   y += d*sc/16^h * C - (1024/16^h * d*sc + dmin*m) * Sx.
+// tbl: this lane's entry (index g) of the super-block's table [16][M][8];
+// own: lane holds a B fragment (g / 2 == t).  sxs: Sx of sub-blocks 2t, 2t+1.
+template <int M>
+__device__ __forceinline__ void q4k_unit_masked(const Q4UnitG &U, const uint2 *tbl, bool own, const float *sxs,
+                                                int sx_stride, int half_mode, int t, float (&y)[M][2]) {
+    float c[2][M][4];
 #pragma unroll
-                for (int half = 0; half < 2; half++) {
-                    const int si = 2 * h + half;  // lo0, hi0, lo1, hi1
-                    const uint32_t mask = half ? 0x00F000F0u : 0x000F000Fu;
-                    const uint32_t a0 = lc_h2_as_u32(
-                        __hfma2(lc_u32_as_h2((xg & mask) | 0x64006400u), mul[0][si], add[0][si]));
-                    const uint32_t a1 = lc_h2_as_u32(
-                        __hfma2(lc_u32_as_h2((xg8 & mask) | 0x64006400u), mul[1][si], add[1][si]));
-                    const uint32_t a2 = lc_h2_as_u32(
-                        __hfma2(lc_u32_as_h2((xgs & mask) | 0x64006400u), mul[0][si], add[0][si]));
-                    const uint32_t a3 = lc_h2_as_u32(
-                        __hfma2(lc_u32_as_h2((xg8s & mask) | 0x64006400u), mul[1][si], add[1][si]));
-                    const int js = h * 8 + wi * 2 + half;
+    for (int h = 0; h < 2; h++)
 #pragma unroll
-                    for (int nt = 0; nt < NT; nt++) {
-                        uint2 b = make_uint2(0u, 0u);
-                        if (LANES == 32 || lane < LANES) b = tb[js * kStep + nt * LANES + lane];
-                        lc_mma16816(cm[nt], a0, a1, a2, a3, b.x, b.y);
-                    }
+        for (int j = 0; j < M; j++) c[h][j][0] = c[h][j][1] = c[h][j][2] = c[h][j][3] = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < 4; wi++) {
+#pragma unroll
+        for (int cc = 0; cc < 2; cc++) {
+            const uint32_t wg = u4_get(cc ? U.B0 : U.A0, wi), wg8 = u4_get(cc ? U.B1 : U.A1, wi);
+            const uint32_t wgs = wg >> 8, wg8s = wg8 >> 8;
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const uint32_t mask = half ? 0x00F000F0u : 0x000F000Fu;
+                const uint32_t a0 = (wg & mask) | 0x64006400u, a1 = (wg8 & mask) | 0x64006400u;
+                const uint32_t a2 = (wgs & mask) | 0x64006400u, a3 = (wg8s & mask) | 0x64006400u;
+                const int js = cc * 8 + wi * 2 + half;
+#pragma unroll
+                for (int j = 0; j < M; j++) {
+                    const uint2 b = tbl[(js * M + j) * 8];  // zero buffer for non-owner lanes
+                    lc_mma16816(c[half][j], a0, a1, a2, a3, b.x, b.y);
                 }
             }
         }
+    }
+    // epilogue: per row, scales / mins of sub-blocks 2t (lo) and 2t+1 (hi)
+    // (get_scale_min_k4, proj_q4k.comp:113-125; t >= 2 uses the j >= 4 packing)
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-            uint2 b = make_uint2(0u, 0u);
-            if (LANES == 32 || lane < LANES) b = tb[16 * kStep + nt * LANES + lane];
-            lc_mma1688(cmin[nt], mpk[0], mpk[1], b.x);
-            acc[nt][0] += dg * cm[nt][0] - dmg * cmin[nt][0];
-            acc[nt][1] += dg * cm[nt][1] - dmg * cmin[nt][1];
-            acc[nt][2] += dg8 * cm[nt][2] - dmg8 * cmin[nt][2];
-            acc[nt][3] += dg8 * cm[nt][3] - dmg8 * cmin[nt][3];
+    for (int r = 0; r < 2; r++) {
+        const uint4 H = r ? U.H1 : U.H0;
+        const float d = scale_f32(H.x, half_mode), dmin = scale_f32(H.x >> 16, half_mode);
+        const int sh = 16 * (t & 1);
+        const uint32_t yy = H.y >> sh, zz = H.z >> sh, ww = H.w >> sh;
+        // byte 0: sub-block 2t, byte 1: sub-block 2t+1 (both packings, then a select)
+        const uint32_t sc_a = yy & 0x3F3Fu, mn_a = zz & 0x3F3Fu;
+        const uint32_t sc_b = (ww & 0x0F0Fu) | ((yy >> 2) & 0x3030u);
+        const uint32_t mn_b = ((ww >> 4) & 0x0F0Fu) | ((zz >> 2) & 0x3030u);
+        const uint32_t sc2 = t < 2 ? sc_a : sc_b, mn2 = t < 2 ? mn_a : mn_b;
+        const float sc_lo = (float)(sc2 & 0xFFu), sc_hi = (float)((sc2 >> 8) & 0xFFu);
+        const float m_lo = (float)(mn2 & 0xFFu), m_hi = (float)((mn2 >> 8) & 0xFFu);
+        const float a_lo = d * sc_lo, a_hi = d * sc_hi * 0.0625f;
+        const float c_lo = fmaf(1024.f, a_lo, dmin * m_lo), c_hi = fmaf(1024.f, a_hi, dmin * m_hi);
+#pragma unroll
+        for (int j = 0; j < M; j++) {
+            const float2 sx = *reinterpret_cast<const float2 *>(sxs + j * sx_stride);
+            const float s_lo = c[0][j][2 * r] + c[0][j][2 * r + 1];
+            const float s_hi = c[1][j][2 * r] + c[1][j][2 * r + 1];
+            y[j][r] += (a_lo * s_lo + a_hi * s_hi) - (c_lo * sx.x + c_hi * sx.y);
         }
     }
-    reduce_store<NT>(acc, red, c, m, n, row0, atomic_out);
+}
+
+// Write (or accumulate) rows g, g+8 of `tile` for the finished part
+// [sb_a, sb_b); y holds this thread's partial over its own sub-blocks.
+template <int M>
+__device__ __forceinline__ void skm_flush(float (&y)[M][2], int tile, int sb_a, int sb_b, int S, int n,
+                                          float *__restrict__ out, Fixup fx, int lane, const float *scl) {
+    const int g = lane >> 2, t = lane & 3;
+    float v0 = 0.f, v1 = 0.f;  // token t's totals after the group reduction
+#pragma unroll
+    for (int j = 0; j < M; j++) {
+        float a = y[j][0], b = y[j][1];
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        a += __shfl_xor_sync(0xffffffffu, a, 2);
+        b += __shfl_xor_sync(0xffffffffu, b, 1);
+        b += __shfl_xor_sync(0xffffffffu, b, 2);
+        if (j == t) v0 = a * scl[2 * j + 1], v1 = b * scl[2 * j + 1];
+        y[j][0] = y[j][1] = 0.f;
+    }
+    const bool vt = t < M;
+    const int r0 = tile * 16 + g, r1 = r0 + 8;
+    if (sb_a == 0 && sb_b == S) {
+        if (vt) {
+            if (r0 < n) out[(size_t)t * n + r0] = v0;
+            if (r1 < n) out[(size_t)t * n + r1] = v1;
+        }
+        return;
+    }
+    float *fa = fx.acc + (size_t)tile * 64;
+    if (vt) {
+        atomicAdd(fa + g * 4 + t, v0);
+        atomicAdd(fa + (g + 8) * 4 + t, v1);
+    }
+    __threadfence();
+    __syncwarp();
+    unsigned last = 0;
+    if (lane == 0) {
+        const unsigned add = (unsigned)(sb_b - sb_a);
+        last = (atomicAdd(fx.cnt + tile, add) + add == (unsigned)S);
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    if (vt) {
+        const float a = atomicExch(fa + g * 4 + t, 0.f);
+        const float b = atomicExch(fa + (g + 8) * 4 + t, 0.f);
+        if (r0 < n) out[(size_t)t * n + r0] = a;
+        if (r1 < n) out[(size_t)t * n + r1] = b;
+    }
+    if (lane == 0) atomicExch(fx.cnt + tile, 0u);
+}
+
+// Persistent stream-K Q4_K projection for M <= 4 tokens.  One CTA per SM
+// stages x in shared memory and builds the masked B table for the whole K,
+// then its warps walk equal shares of the flattened (16-row tile,
+// super-block) unit space, prefetching the next unit's bytes while the tensor
+// cores work on the current one.  A tile whose super-blocks are split between
+// warps is summed in `fx.acc` with atomics; the warp that completes the tile's
+// count writes the rows and leaves fx.acc / fx.cnt zero for the next call.
+template <int M>
+__global__ void __launch_bounds__(kSkWarps * 32, 1) q4k_sk_kernel(const float *__restrict__ x,
+                                                                  const uint8_t *__restrict__ w,
+                                                                  float *__restrict__ y, int k, int n,
+                                                                  int half_mode, Fixup fx) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int S = k >> 8;  // super-blocks per row
+    const int nsub = S * 8;
+    uint2 *tab = reinterpret_cast<uint2 *>(smem);                            // [S][16][M][8]
+    float *sx = reinterpret_cast<float *>(smem + (size_t)S * 16 * M * 64);  // [M][nsub]
+    float *xs = sx + sk_sx_floats(M, nsub);                                  // [M][k]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const size_t rowbytes = (size_t)S * 144;
+    const int T = (n + 15) >> 4;
+    const long long TS = (long long)T * S;
+    const long long Wt = (long long)gridDim.x * kSkWarps;
+    const long long wid = (long long)blockIdx.x * kSkWarps + warp;
+    const long long u0 = TS * wid / Wt;
+    const int n_units = (int)(TS * (wid + 1) / Wt - u0);
+    int tile = (int)(u0 / S), sub = (int)(u0 % S);
+
+    // Start streaming the first two units' weights before the prologue.
+    int pt = tile, ps = sub, loaded = 0;
+    auto load_next = [&](Q4UnitG &U) {
+        if (loaded >= n_units) return;
+        const int rg = pt * 16 + g, rg8 = rg + 8;
+        U.load(rg < n ? w + (size_t)rg * rowbytes + (size_t)ps * 144 : nullptr,
+               rg8 < n ? w + (size_t)rg8 * rowbytes + (size_t)ps * 144 : nullptr, t);
+        if (++ps == S) ps = 0, ++pt;
+        ++loaded;
+    };
+    Q4UnitG A, B;
+    load_next(A);
+    load_next(B);
+
+    // Prologue: x -> shared, per-token scales, split sub-block sums, then the table.
+    __shared__ float scl[8];
+    __shared__ __align__(16) uint2 zbuf[16 * M * 8];
+    for (int i = threadIdx.x; i < 16 * M * 8; i += blockDim.x) zbuf[i] = make_uint2(0u, 0u);
+    sk_prologue_x(x, M, k, xs, sx, nsub, scl);
+    for (int idx = threadIdx.x; idx < S * 16 * M * 8; idx += blockDim.x) {
+        const int e = idx & 7;
+        const int j = (idx >> 3) % M;
+        const int js = (idx / (8 * M)) & 15;
+        const int sb = idx / (8 * M * 16);
+        const int to = e >> 1, part = e & 1;  // owner thread, hi / lo
+        const int cc = js >> 3, wi = (js >> 1) & 3, half = js & 1;
+        const float *xr = xs + (size_t)j * k + (size_t)sb * 256 + 64 * to + 16 * cc + 4 * wi + 32 * half;
+        const float s = scl[2 * j];
+        uint2 v;
+        v.x = lc_pack_h2(lc_split_part(xr[0] * s, part), lc_split_part(xr[2] * s, part));
+        v.y = lc_pack_h2(lc_split_part(xr[1] * s, part), lc_split_part(xr[3] * s, part));
+        tab[idx] = v;
+    }
+    __syncthreads();
+
+    // Lanes that carry no B fragment (g / 2 != t) read a zero block instead,
+    // so the k-step loop has no predicate.
+    const bool own = (g >> 1) == t;
+    float acc[M][2];
+#pragma unroll
+    for (int j = 0; j < M; j++) acc[j][0] = acc[j][1] = 0.f;
+    int seg0 = sub, done = 0;
+    auto step = [&](Q4UnitG &U) {
+        const uint2 *tbl = own ? tab + (size_t)sub * 16 * M * 8 + g : zbuf;
+        q4k_unit_masked<M>(U, tbl, own, sx + sub * 8 + 2 * t, nsub, half_mode, t, acc);
+        load_next(U);  // U's registers are free again: refill with the unit after next
+        ++done;
+        if (sub == S - 1 || done == n_units) {
+            skm_flush<M>(acc, tile, seg0, sub + 1, S, n, y, fx, lane, scl);
+            seg0 = 0;
+        }
+        if (++sub == S) sub = 0, ++tile;
+    };
+    while (done < n_units) {
+        step(A);
+        if (done == n_units) break;
+        step(B);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -310,43 +726,14 @@ __device__ __forceinline__ void q8_quads(uint32_t u, uint32_t &lo, uint32_t &hi)
     hi = lc_h2_as_u32(__hsub2(lc_u32_as_h2(__byte_perm(b, 0x64646464u, 0x4341)), k1152));
 }
 
-template <int NT, int LANES>
-__global__ void __launch_bounds__(kWarps * 32) q8_mma_kernel(const uint2 *__restrict__ tab_g,
-                                                             const uint8_t *__restrict__ w, float *__restrict__ c,
-                                                             int m, int k, int n, int pairs_per_chunk,
-                                                             int half_mode, int atomic_out) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    constexpr int kStep = NT * LANES;
-    const int npairs = k >> 6;
-    const int p0 = blockIdx.y * pairs_per_chunk;
-    const int nloc = min(pairs_per_chunk, npairs - p0);
-    uint2 *tab = reinterpret_cast<uint2 *>(smem);
-    float *red = reinterpret_cast<float *>(smem + (size_t)pairs_per_chunk * 4 * kStep * 8);
-
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 2, t = lane & 3;
-    const int row0 = blockIdx.x * 16;
-    const int rg = row0 + g, rg8 = row0 + g + 8;
-    const bool vg = rg < n, vg8 = rg8 < n;
-    const size_t rowbytes = (size_t)npairs * 68;
-    const uint8_t *wr[2] = {w + (size_t)(vg ? rg : 0) * rowbytes, w + (size_t)(vg8 ? rg8 : 0) * rowbytes};
-    const bool vr[2] = {vg, vg8};
-
-    copy_tab(reinterpret_cast<uint4 *>(tab), reinterpret_cast<const uint4 *>(tab_g + (size_t)p0 * 4 * kStep),
-             nloc * 4 * kStep / 2);
-    __syncthreads();
-
-    float acc[NT][4];
-#pragma unroll
-    for (int i = 0; i < NT; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-
-    for (int pl = warp; pl < nloc; pl += kWarps) {
-        const size_t off = (size_t)(p0 + pl) * 68;
-        uint32_t wd[2][8];
+// The words of one block pair that thread (g, t) needs for rows g and g+8.
+struct Q8Unit {
+    uint32_t wd[2][8];
+    __device__ __forceinline__ void load(const uint8_t *b0, const uint8_t *b1, int t) {
 #pragma unroll
         for (int r = 0; r < 2; r++) {
-            const uint8_t *b = wr[r] + off;
-            if (vr[r]) {
+            const uint8_t *b = r ? b1 : b0;
+            if (b) {
                 wd[r][0] = ldg_u32(b + 4 * t);
                 wd[r][1] = ldg_u32(b + 4 * (t + 1));
                 wd[r][2] = ldg_u32(b + 4 * (t + 4));
@@ -360,48 +747,170 @@ __global__ void __launch_bounds__(kWarps * 32) q8_mma_kernel(const uint2 *__rest
                 for (int i = 0; i < 8; i++) wd[r][i] = 0u;
             }
         }
-        const float dA0 = lc_half_to_f32(wd[0][6] & 0xFFFFu, half_mode);
-        const float dB0 = lc_half_to_f32(wd[0][7] >> 16, half_mode);
-        const float dA1 = lc_half_to_f32(wd[1][6] & 0xFFFFu, half_mode);
-        const float dB1 = lc_half_to_f32(wd[1][7] >> 16, half_mode);
-        const uint2 *tb = tab + (size_t)pl * 4 * kStep;
+    }
+};
+
+// One block pair (two 32-element blocks) of a 16-row tile: acc += d * S(q*x)
+// per block.  tb points at the pair's 4 k-steps of packed activations.
+template <int NT, int LANES>
+__device__ __forceinline__ void q8_unit(const Q8Unit &U, const uint2 *tb, int lane, int half_mode,
+                                        float (&acc)[NT][4]) {
+    constexpr int kStep = NT * LANES;
+    const float dA0 = lc_half_to_f32(U.wd[0][6] & 0xFFFFu, half_mode);
+    const float dB0 = lc_half_to_f32(U.wd[0][7] >> 16, half_mode);
+    const float dA1 = lc_half_to_f32(U.wd[1][6] & 0xFFFFu, half_mode);
+    const float dB1 = lc_half_to_f32(U.wd[1][7] >> 16, half_mode);
 #pragma unroll
-        for (int blk = 0; blk < 2; blk++) {
-            float cm[NT][4];
+    for (int blk = 0; blk < 2; blk++) {
+        float cm[NT][4];
 #pragma unroll
-            for (int i = 0; i < NT; i++) cm[i][0] = cm[i][1] = cm[i][2] = cm[i][3] = 0.f;
+        for (int i = 0; i < NT; i++) cm[i][0] = cm[i][1] = cm[i][2] = cm[i][3] = 0.f;
 #pragma unroll
-            for (int ks = 0; ks < 2; ks++) {
-                uint32_t q0, q1;
-                if (blk == 0) {
-                    q0 = __funnelshift_r(wd[0][2 * ks], wd[0][2 * ks + 1], 16);
-                    q1 = __funnelshift_r(wd[1][2 * ks], wd[1][2 * ks + 1], 16);
-                } else {
-                    q0 = wd[0][4 + ks];
-                    q1 = wd[1][4 + ks];
-                }
-                uint32_t a0, a2, a1, a3;
-                q8_quads(q0, a0, a2);
-                q8_quads(q1, a1, a3);
-                const int js = blk * 2 + ks;
-#pragma unroll
-                for (int nt = 0; nt < NT; nt++) {
-                    uint2 b = make_uint2(0u, 0u);
-                    if (LANES == 32 || lane < LANES) b = tb[js * kStep + nt * LANES + lane];
-                    lc_mma16816(cm[nt], a0, a1, a2, a3, b.x, b.y);
-                }
+        for (int ks = 0; ks < 2; ks++) {
+            uint32_t q0, q1;
+            if (blk == 0) {
+                q0 = __funnelshift_r(U.wd[0][2 * ks], U.wd[0][2 * ks + 1], 16);
+                q1 = __funnelshift_r(U.wd[1][2 * ks], U.wd[1][2 * ks + 1], 16);
+            } else {
+                q0 = U.wd[0][4 + ks];
+                q1 = U.wd[1][4 + ks];
             }
-            const float d0 = blk ? dB0 : dA0, d1 = blk ? dB1 : dA1;
+            uint32_t a0, a2, a1, a3;
+            q8_quads(q0, a0, a2);
+            q8_quads(q1, a1, a3);
+            const int js = blk * 2 + ks;
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                acc[nt][0] += d0 * cm[nt][0];
-                acc[nt][1] += d0 * cm[nt][1];
-                acc[nt][2] += d1 * cm[nt][2];
-                acc[nt][3] += d1 * cm[nt][3];
+                uint2 b = make_uint2(0u, 0u);
+                if (LANES == 32 || lane < LANES) b = tb[js * kStep + nt * LANES + lane];
+                lc_mma16816(cm[nt], a0, a1, a2, a3, b.x, b.y);
             }
         }
+        const float d0 = blk ? dB0 : dA0, d1 = blk ? dB1 : dA1;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            acc[nt][0] += d0 * cm[nt][0];
+            acc[nt][1] += d0 * cm[nt][1];
+            acc[nt][2] += d1 * cm[nt][2];
+            acc[nt][3] += d1 * cm[nt][3];
+        }
     }
-    reduce_store<NT>(acc, red, c, m, n, row0, atomic_out);
+}
+
+template <int NT, int LANES>
+__global__ void __launch_bounds__(kWarps * 32) q8_mma_kernel(const uint2 *__restrict__ tab_g,
+                                                             const uint8_t *__restrict__ w, float *__restrict__ c,
+                                                             int m, int k, int n, int pairs_per_chunk,
+                                                             int half_mode, int atomic_out,
+                                                             const float *__restrict__ inv_scale) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    constexpr int kStep = NT * LANES;
+    const int npairs = k >> 6;
+    const int p0 = blockIdx.y * pairs_per_chunk;
+    const int nloc = min(pairs_per_chunk, npairs - p0);
+    uint2 *tab = reinterpret_cast<uint2 *>(smem);
+    float *red = reinterpret_cast<float *>(smem + (size_t)pairs_per_chunk * 4 * kStep * 8);
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int row0 = blockIdx.x * 16;
+    const int rg = row0 + g, rg8 = row0 + g + 8;
+    const size_t rowbytes = (size_t)npairs * 68;
+
+    copy_tab(reinterpret_cast<uint4 *>(tab), reinterpret_cast<const uint4 *>(tab_g + (size_t)p0 * 4 * kStep),
+             nloc * 4 * kStep / 2);
+    __syncthreads();
+
+    float acc[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; i++) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
+    for (int pl = warp; pl < nloc; pl += kWarps) {
+        const size_t off = (size_t)(p0 + pl) * 68;
+        Q8Unit U;
+        U.load(rg < n ? w + (size_t)rg * rowbytes + off : nullptr, rg8 < n ? w + (size_t)rg8 * rowbytes + off : nullptr,
+               t);
+        q8_unit<NT, LANES>(U, tab + (size_t)pl * 4 * kStep, lane, half_mode, acc);
+    }
+    reduce_store<NT>(acc, red, c, m, n, row0, atomic_out, inv_scale);
+}
+
+// Persistent stream-K form for m <= 4 (see q4k_sk_kernel); units are
+// (16-row tile, block pair).
+template <int LANES>
+__global__ void __launch_bounds__(kSkWarps * 32, 1) q8_sk_kernel(const float *__restrict__ x,
+                                                                 const uint8_t *__restrict__ w,
+                                                                 float *__restrict__ y, int m, int k, int n,
+                                                                 int half_mode, Fixup fx) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int S = k >> 6;  // block pairs per row
+    uint2 *tab = reinterpret_cast<uint2 *>(smem);
+    float *sx = reinterpret_cast<float *>(smem + (size_t)S * 4 * LANES * 8);  // [m][k/32] (unused sums)
+    float *xs = sx + sk_sx_floats(m, k >> 5);                                 // [m][k], 16-B aligned
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const size_t rowbytes = (size_t)S * 68;
+    const int T = (n + 15) >> 4;
+    const long long TS = (long long)T * S;
+    const long long Wt = (long long)gridDim.x * kSkWarps;
+    const long long wid = (long long)blockIdx.x * kSkWarps + warp;
+    const long long u0 = TS * wid / Wt;
+    const int n_units = (int)(TS * (wid + 1) / Wt - u0);
+    int tile = (int)(u0 / S), sub = (int)(u0 % S);
+
+    int pt = tile, ps = sub, loaded = 0;
+    auto load_next = [&](Q8Unit &U) {
+        if (loaded >= n_units) return;
+        const int rg = pt * 16 + g, rg8 = rg + 8;
+        U.load(rg < n ? w + (size_t)rg * rowbytes + (size_t)ps * 68 : nullptr,
+               rg8 < n ? w + (size_t)rg8 * rowbytes + (size_t)ps * 68 : nullptr, t);
+        if (++ps == S) ps = 0, ++pt;
+        ++loaded;
+    };
+    Q8Unit A, B;
+    load_next(A);
+    load_next(B);
+
+    // B-fragment table: pair p, k-step js = blk*2 + ks covers elements
+    // 64p + 32blk + 16ks + 4tt + {0..3}: (e0, e2), (e1, e3).
+    __shared__ float scl[8];
+    sk_prologue_x(x, m, k, xs, nullptr, 0, scl);
+    (void)sx;
+    for (int idx = threadIdx.x; idx < S * 4 * LANES; idx += blockDim.x) {
+        const int ln = idx % LANES;
+        const int js = (idx / LANES) & 3;
+        const int p = idx / (LANES * 4);
+        const int gg = ln >> 2, tt = ln & 3;
+        const int tok = gg >> 1, part = gg & 1;
+        uint2 v = make_uint2(0u, 0u);
+        if (tok < m) {
+            const float *xr = xs + (size_t)tok * k + (size_t)p * 64 + 16 * js + 4 * tt;
+            const float s = scl[2 * tok];
+            v.x = lc_pack_h2(lc_split_part(xr[0] * s, part), lc_split_part(xr[2] * s, part));
+            v.y = lc_pack_h2(lc_split_part(xr[1] * s, part), lc_split_part(xr[3] * s, part));
+        }
+        tab[idx] = v;
+    }
+    __syncthreads();
+
+    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+    int seg0 = sub, done = 0;
+    auto step = [&](Q8Unit &U) {
+        q8_unit<1, LANES>(U, tab + (size_t)sub * 4 * LANES, lane, half_mode, acc);
+        load_next(U);
+        ++done;
+        if (sub == S - 1 || done == n_units) {
+            sk_flush<LANES>(acc, tile, seg0, sub + 1, S, m, n, y, fx, lane, scl);
+            acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.f;
+            seg0 = 0;
+        }
+        if (++sub == S) sub = 0, ++tile;
+    };
+    while (done < n_units) {
+        step(A);
+        if (done == n_units) break;
+        step(B);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -466,17 +975,14 @@ __global__ void f32_cols_kernel(const float *__restrict__ x, const float *__rest
 // ---------------------------------------------------------------------------
 template <typename K>
 int set_smem(K kernel, size_t bytes) {
-    if (bytes > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-        if (e != cudaSuccess) return lc_fail(LC_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    }
+    if (bytes > 48 * 1024) return lc_set_smem_attr((const void *)kernel, bytes);
     return LC_OK;
 }
 
 constexpr size_t kTabSmemBudget = 100 * 1024;
 
 template <int NT, int LANES>
-int launch_q4k(lc_ctx *ctx, const uint2 *tab, const uint8_t *w, float *c, int m, int k, int n) {
+int launch_q4k(lc_ctx *ctx, const uint2 *tab, const float *inv_scale, const uint8_t *w, float *c, int m, int k, int n) {
     const int nsb = k >> 8;
     const size_t per_sb = (size_t)17 * NT * LANES * 8;
     int spc = (int)std::min<size_t>((size_t)nsb, std::max<size_t>(1, kTabSmemBudget / per_sb));
@@ -488,12 +994,21 @@ int launch_q4k(lc_ctx *ctx, const uint2 *tab, const uint8_t *w, float *c, int m,
     if (kch > 1) LC_CUDA(cudaMemsetAsync(c, 0, (size_t)m * n * 4, ctx->stream));
     dim3 grid((n + 15) / 16, kch);
     q4k_mma_kernel<NT, LANES><<<grid, kWarps * 32, smem, ctx->stream>>>(tab, w, c, m, k, n, spc, ctx->half_mode,
-                                                                         kch > 1);
+                                                                         kch > 1, inv_scale);
+    return LC_OK;
+}
+
+template <int M>
+int launch_q4k_sk(lc_ctx *ctx, int grid, size_t smem, const float *x, const uint8_t *w, float *c, uint32_t k,
+                  uint32_t n, Fixup fx) {
+    int s = set_smem(q4k_sk_kernel<M>, smem);
+    if (s) return s;
+    q4k_sk_kernel<M><<<grid, kSkWarps * 32, smem, ctx->stream>>>(x, w, c, (int)k, (int)n, ctx->half_mode, fx);
     return LC_OK;
 }
 
 template <int NT, int LANES>
-int launch_q8(lc_ctx *ctx, const uint2 *tab, const uint8_t *w, float *c, int m, int k, int n) {
+int launch_q8(lc_ctx *ctx, const uint2 *tab, const float *inv_scale, const uint8_t *w, float *c, int m, int k, int n) {
     const int npairs = k >> 6;
     const size_t per_pair = (size_t)4 * NT * LANES * 8;
     int ppc = (int)std::min<size_t>((size_t)npairs, std::max<size_t>(1, kTabSmemBudget / per_pair));
@@ -505,7 +1020,7 @@ int launch_q8(lc_ctx *ctx, const uint2 *tab, const uint8_t *w, float *c, int m, 
     if (kch > 1) LC_CUDA(cudaMemsetAsync(c, 0, (size_t)m * n * 4, ctx->stream));
     dim3 grid((n + 15) / 16, kch);
     q8_mma_kernel<NT, LANES><<<grid, kWarps * 32, smem, ctx->stream>>>(tab, w, c, m, k, n, ppc, ctx->half_mode,
-                                                                        kch > 1);
+                                                                        kch > 1, inv_scale);
     return LC_OK;
 }
 
@@ -522,26 +1037,42 @@ int proj_q4k(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m, 
     LC_REQUIRE(((uintptr_t)wv & 15) == 0, LC_ERR_INVALID, "proj_q4k: weight pointer not 16-byte aligned");
     const uint8_t *w = (const uint8_t *)wv + (size_t)(expert_offset / 256) * 144;
     const int nsb = k / 256;
+    if (m <= 4) {
+        const size_t smem = (size_t)nsb * 16 * m * 64 + sk_sx_floats((int)m, nsb * 8) * 4 + (size_t)m * k * 4;
+        if (smem + 8192 <= ctx->smem_optin) {  // + static shared (zero block, scales)
+            const int T = (int)((n + 15) / 16);
+            Fixup fx;
+            fx.acc = (float *)lc_scratch_zeroed(ctx, LC_SCRATCH_FIXUP, (size_t)T * 64 * 4 + (size_t)T * 4 + 256);
+            if (!fx.acc) return LC_ERR_OOM;
+            fx.cnt = (unsigned *)(fx.acc + (size_t)T * 64);
+            const long long units = (long long)T * nsb;
+            const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, (units + 31) / 32));
+            switch (m) {
+            case 1: return launch_q4k_sk<1>(ctx, grid, smem, x, w, c, k, n, fx);
+            case 2: return launch_q4k_sk<2>(ctx, grid, smem, x, w, c, k, n, fx);
+            case 3: return launch_q4k_sk<3>(ctx, grid, smem, x, w, c, k, n, fx);
+            default: return launch_q4k_sk<4>(ctx, grid, smem, x, w, c, k, n, fx);
+            }
+        }
+    }
     for (uint32_t t0 = 0; t0 < m; t0 += 16) {
         const int mm = (int)std::min<uint32_t>(16, m - t0);
         const int nt = (mm + 3) / 4;
-        const int lanes = mm == 1 ? 8 : 32;
-        const int total = nsb * 17 * nt * lanes;
-        uint2 *tab = (uint2 *)lc_scratch(ctx, LC_SCRATCH_PACK, (size_t)total * 8);
+        const size_t tab_bytes = (size_t)nsb * 17 * nt * 32 * 8;
+        uint2 *tab = (uint2 *)lc_scratch(ctx, LC_SCRATCH_PACK, tab_bytes + 16 * 4);
         if (!tab) return LC_ERR_OOM;
-        x_pack_q4k<<<(total + 255) / 256, 256, 0, ctx->stream>>>(x + (size_t)t0 * k, tab, mm, k, nt, lanes, total);
+        float *inv = (float *)((char *)tab + tab_bytes);
+        x_pack_q4k<<<nt * 4, 256, 0, ctx->stream>>>(x + (size_t)t0 * k, tab, inv, mm, (int)k, nt);
         float *cc = c + (size_t)t0 * n;
         int s;
-        if (mm == 1)
-            s = launch_q4k<1, 8>(ctx, tab, w, cc, mm, k, n);
-        else if (nt == 1)
-            s = launch_q4k<1, 32>(ctx, tab, w, cc, mm, k, n);
+        if (nt == 1)
+            s = launch_q4k<1, 32>(ctx, tab, inv, w, cc, mm, k, n);
         else if (nt == 2)
-            s = launch_q4k<2, 32>(ctx, tab, w, cc, mm, k, n);
+            s = launch_q4k<2, 32>(ctx, tab, inv, w, cc, mm, k, n);
         else if (nt == 3)
-            s = launch_q4k<3, 32>(ctx, tab, w, cc, mm, k, n);
+            s = launch_q4k<3, 32>(ctx, tab, inv, w, cc, mm, k, n);
         else
-            s = launch_q4k<4, 32>(ctx, tab, w, cc, mm, k, n);
+            s = launch_q4k<4, 32>(ctx, tab, inv, w, cc, mm, k, n);
         if (s) return s;
     }
     return LC_OK;
@@ -556,26 +1087,51 @@ int proj_q8_0(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m,
         return LC_OK;
     }
     const int nblk = k / 32;
+    if (m <= 4) {
+        const int lanes = m == 1 ? 8 : 32;
+        const int S = (int)(k / 64);
+        const size_t smem = (size_t)S * 4 * lanes * 8 + sk_sx_floats((int)m, (int)(k / 32)) * 4 + (size_t)m * k * 4;
+        if (smem + 8192 <= ctx->smem_optin) {  // + static shared (zero block, scales)
+            const int T = (int)((n + 15) / 16);
+            Fixup fx;
+            fx.acc = (float *)lc_scratch_zeroed(ctx, LC_SCRATCH_FIXUP, (size_t)T * 64 * 4 + (size_t)T * 4 + 256);
+            if (!fx.acc) return LC_ERR_OOM;
+            fx.cnt = (unsigned *)(fx.acc + (size_t)T * 64);
+            const long long units = (long long)T * S;
+            const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, (units + 31) / 32));
+            int s;
+            if (m == 1) {
+                s = set_smem(q8_sk_kernel<8>, smem);
+                if (s) return s;
+                q8_sk_kernel<8><<<grid, kSkWarps * 32, smem, ctx->stream>>>(x, w, c, (int)m, (int)k, (int)n,
+                                                                           ctx->half_mode, fx);
+            } else {
+                s = set_smem(q8_sk_kernel<32>, smem);
+                if (s) return s;
+                q8_sk_kernel<32><<<grid, kSkWarps * 32, smem, ctx->stream>>>(x, w, c, (int)m, (int)k, (int)n,
+                                                                            ctx->half_mode, fx);
+            }
+            return LC_OK;
+        }
+    }
     for (uint32_t t0 = 0; t0 < m; t0 += 16) {
         const int mm = (int)std::min<uint32_t>(16, m - t0);
         const int nt = (mm + 3) / 4;
-        const int lanes = mm == 1 ? 8 : 32;
-        const int total = nblk * 2 * nt * lanes;
-        uint2 *tab = (uint2 *)lc_scratch(ctx, LC_SCRATCH_PACK, (size_t)total * 8);
+        const size_t tab_bytes = (size_t)nblk * 2 * nt * 32 * 8;
+        uint2 *tab = (uint2 *)lc_scratch(ctx, LC_SCRATCH_PACK, tab_bytes + 16 * 4);
         if (!tab) return LC_ERR_OOM;
-        x_pack_q8<<<(total + 255) / 256, 256, 0, ctx->stream>>>(x + (size_t)t0 * k, tab, mm, k, nt, lanes, total);
+        float *inv = (float *)((char *)tab + tab_bytes);
+        x_pack_q8<<<nt * 4, 256, 0, ctx->stream>>>(x + (size_t)t0 * k, tab, inv, mm, (int)k, nt);
         float *cc = c + (size_t)t0 * n;
         int s;
-        if (mm == 1)
-            s = launch_q8<1, 8>(ctx, tab, w, cc, mm, k, n);
-        else if (nt == 1)
-            s = launch_q8<1, 32>(ctx, tab, w, cc, mm, k, n);
+        if (nt == 1)
+            s = launch_q8<1, 32>(ctx, tab, inv, w, cc, mm, k, n);
         else if (nt == 2)
-            s = launch_q8<2, 32>(ctx, tab, w, cc, mm, k, n);
+            s = launch_q8<2, 32>(ctx, tab, inv, w, cc, mm, k, n);
         else if (nt == 3)
-            s = launch_q8<3, 32>(ctx, tab, w, cc, mm, k, n);
+            s = launch_q8<3, 32>(ctx, tab, inv, w, cc, mm, k, n);
         else
-            s = launch_q8<4, 32>(ctx, tab, w, cc, mm, k, n);
+            s = launch_q8<4, 32>(ctx, tab, inv, w, cc, mm, k, n);
         if (s) return s;
     }
     return LC_OK;

@@ -3,6 +3,9 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <map>
+#include <mutex>
+
 #include "lc_internal.cuh"
 
 static thread_local char g_err[1024] = "";
@@ -63,7 +66,7 @@ extern "C" int lc_destroy(lc_ctx *ctx) {
     lc_use_device(ctx);
     if (ctx->own_stream) cudaStreamSynchronize(ctx->own_stream);
     if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < LC_SCRATCH_COUNT; i++)
         if (ctx->scratch[i]) cudaFree(ctx->scratch[i]);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
@@ -105,6 +108,20 @@ extern "C" int lc_ctx_device(lc_ctx *ctx, int *device) {
     return LC_OK;
 }
 
+int lc_set_smem_attr(const void *kernel, size_t bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<int, const void *>, size_t> done;
+    int dev = 0;
+    LC_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    size_t &have = done[{dev, kernel}];
+    if (have >= bytes) return LC_OK;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return lc_fail(LC_ERR_CUDA, "cudaFuncSetAttribute(%zu): %s", bytes, cudaGetErrorString(e));
+    have = bytes;
+    return LC_OK;
+}
+
 int lc_after_launch(lc_ctx *ctx, const char *what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return lc_fail(LC_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
@@ -138,6 +155,19 @@ void *lc_scratch(lc_ctx *ctx, int slot, size_t bytes) {
     }
     ctx->scratch_bytes[slot] = want;
     return ctx->scratch[slot];
+}
+
+void *lc_scratch_zeroed(lc_ctx *ctx, int slot, size_t bytes) {
+    const bool grow = bytes > ctx->scratch_bytes[slot];
+    void *p = lc_scratch(ctx, slot, bytes);
+    if (p && grow) {
+        cudaError_t e = cudaMemsetAsync(p, 0, ctx->scratch_bytes[slot], ctx->stream);
+        if (e != cudaSuccess) {
+            lc_fail(LC_ERR_CUDA, "scratch memset: %s", cudaGetErrorString(e));
+            return nullptr;
+        }
+    }
+    return p;
 }
 
 // ---- buffers ---------------------------------------------------------------

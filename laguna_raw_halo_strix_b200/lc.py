@@ -97,7 +97,42 @@ SIGNATURES = {
     "lc_key_index": (_u32, [C.c_uint64]),
     "lc_argmax_rows": (_i, [_vp, _vp, _u32, _u32, _u32, _vp]),
     "lc_lm_head_argmax": (_i, [_vp, _i, _vp, _vp, _u32, _u32, _u32, _u32, _vp, _vp]),
+    # GGUF reader
+    "lc_type_block_bytes": (C.c_uint64, [_i]),
+    "lc_type_block_elements": (C.c_uint64, [_i]),
+    "lc_tensor_bytes": (C.c_uint64, [_i, C.c_uint64]),
+    "lc_gguf_open": (_i, [C.c_char_p, C.POINTER(_vp)]),
+    "lc_gguf_close": (_i, [_vp]),
+    "lc_gguf_tensor_count": (C.c_uint64, [_vp]),
+    "lc_gguf_tensor_info": (_i, [_vp, C.c_uint64, C.POINTER(C.c_char_p), C.POINTER(_i), C.POINTER(_u32),
+                                 C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
+    "lc_gguf_find": (_i, [_vp, C.c_char_p, C.POINTER(C.c_uint64)]),
+    "lc_gguf_read": (_i, [_vp, C.c_uint64, _vp, C.c_uint64]),
+    "lc_gguf_meta_u64": (_i, [_vp, C.c_char_p, C.POINTER(C.c_uint64)]),
+    "lc_gguf_meta_f32": (_i, [_vp, C.c_char_p, C.POINTER(_f)]),
+    "lc_gguf_meta_str": (_i, [_vp, C.c_char_p, C.POINTER(C.c_char_p)]),
+    "lc_gguf_dflash_hparams": (_i, [_vp, _vp]),
+    # DFlash model
+    "lc_dflash_create": (_i, [_vp, _vp, _u32, _u32, C.POINTER(_vp)]),
+    "lc_dflash_set_tensor": (_i, [_vp, C.c_char_p, _i, _vp, _sz]),
+    "lc_dflash_load_gguf": (_i, [_vp, C.c_char_p, _u32, _u32, C.POINTER(_vp)]),
+    "lc_dflash_destroy": (_i, [_vp]),
+    "lc_dflash_get_hparams": (_i, [_vp, _vp]),
+    "lc_dflash_encode": (_i, [_vp, _vp, _u32, _vp]),
+    "lc_dflash_set_context": (_i, [_vp, _vp, _u32]),
+    "lc_dflash_decode_block": (_i, [_vp, _vp, _u32, _vp]),
+    "lc_dflash_forward_injected_decode_hidden": (_i, [_vp, _vp, _vp, _vp]),
+    "lc_dflash_forward_from_input": (_i, [_vp, _vp, _vp, _vp, C.POINTER(_u32)]),
+    "lc_dflash_forward_token": (_i, [_vp, _u32, _vp, _vp, C.POINTER(_u32)]),
 }
+
+
+class HParams(C.Structure):
+    """lc_dflash_hparams (include/laguna_cuda.h)."""
+
+    _fields_ = [("n_layers", _u32), ("n_embd", _u32), ("n_heads", _u32), ("n_kv_heads", _u32),
+                ("head_dim", _u32), ("rope_dim", _u32), ("n_ff", _u32), ("n_aux", _u32),
+                ("rope_base", _f), ("norm_eps", _f), ("qk_eps", _f)]
 
 
 def _sources_newer(lib: str) -> bool:

@@ -139,6 +139,9 @@ class Oracle:
         return y
 
     def qk_norm_rope(self, x, w, freq, n_heads, head_dim, rope_dim, eps, pos):
+        # The shader's pair index leaves the head unless rope_dim is 0 or head_dim.
+        if rope_dim not in (0, head_dim):
+            raise ValueError("qk_norm_rope: rope_dim must be 0 or head_dim")
         x = np.ascontiguousarray(x, np.float32)
         m = x.size // (n_heads * head_dim)
         pos = np.ascontiguousarray(np.broadcast_to(np.asarray(pos, np.uint32), (m,)), np.uint32)

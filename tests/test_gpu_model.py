@@ -1,0 +1,141 @@
+"""GPU parity of the DFlash draft model (lc_dflash_*) against the CPU oracle of
+the reference's op sequence (oracle/dflash_oracle.py).
+
+Tolerance (north star): hidden states within rel-L2 <= 2e-3; projections
+inside are f32-accumulated on the tensor cores with exact operands, so the
+observed error is far smaller.
+"""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+import oracle as orc
+from conftest import ROOT, to_dev
+from dflash_oracle import DFlashOracle, make_model, tensor_shape
+from gguf_writer import write_gguf
+from laguna_raw_halo_strix_b200 import lc
+from laguna_raw_halo_strix_b200.model import DFlash, hparams
+
+pytestmark = pytest.mark.gpu
+
+HP = dict(n_layers=2, n_embd=512, n_heads=4, n_kv_heads=2, head_dim=128, rope_dim=128, n_ff=768, n_aux=2,
+          rope_base=500000.0, norm_eps=1e-5, qk_eps=1e-6)
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def build(ctx, tensors, max_ctx=64, max_block=16):
+    m = DFlash(ctx, hparams(**{k: HP[k] for k in HP}), max_ctx=max_ctx, max_block=max_block)
+    for name, (dt, a) in tensors.items():
+        m.set_tensor(name, dt, a)
+    return m
+
+
+@pytest.fixture(scope="module", params=[orc.Q4_K, orc.Q8_0])
+def model(request, ctx):
+    rng = np.random.default_rng(42)
+    t = make_model(HP, request.param, rng)
+    gm = build(ctx, t)
+    yield t, gm, DFlashOracle(HP, t)
+    gm.close()  # before the session context goes away
+
+
+@pytest.mark.parametrize("n_ctx,m", [(1, 1), (40, 16), (7, 3)])
+def test_block_decode(model, dev, n_ctx, m):
+    import torch
+
+    t, gm, om = model
+    rng = np.random.default_rng(n_ctx * 31 + m)
+    E, A = HP["n_embd"], HP["n_aux"]
+    feats = rng.standard_normal((n_ctx, A * E)).astype(np.float32)
+    toks = rng.standard_normal((m, E)).astype(np.float32)
+    enc_ref = om.encode(feats)
+    hid_ref = om.decode_block(toks, om.context_kv(enc_ref))
+    enc = torch.empty(n_ctx, E, device=dev)
+    hid = torch.empty(m, E, device=dev)
+    gm.encode(to_dev(feats, dev), n_ctx, enc)
+    gm.set_context(enc, n_ctx)
+    gm.decode_block(to_dev(toks, dev), m, hid)
+    torch.cuda.synchronize()
+    assert rel_l2(enc.cpu().numpy(), enc_ref) <= 2e-3
+    got = hid.cpu().numpy()
+    for r in range(m):
+        assert rel_l2(got[r], hid_ref[r]) <= 2e-3, r
+    # decoding again (same context, cache rows past n_ctx overwritten) is repeatable
+    gm.decode_block(to_dev(toks, dev), m, hid)
+    torch.cuda.synchronize()
+    assert rel_l2(hid.cpu().numpy(), got) <= 1e-6
+
+
+def test_forward_injected_decode_hidden(model):
+    t, gm, om = model
+    rng = np.random.default_rng(5)
+    feats = rng.standard_normal(HP["n_aux"] * HP["n_embd"]).astype(np.float32)
+    tok = rng.standard_normal(HP["n_embd"]).astype(np.float32)
+    got = gm.forward_injected_decode_hidden(feats, tok)
+    ref = om.forward_injected_decode_hidden(feats, tok)
+    assert rel_l2(got, ref) <= 2e-3
+
+
+def test_forward_from_input_and_fc_head(model, dev):
+    import torch
+
+    t, gm, om = model
+    rng = np.random.default_rng(6)
+    inp = rng.standard_normal(HP["n_embd"]).astype(np.float32)
+    hid = torch.empty(HP["n_embd"], device=dev)
+    logits = torch.empty(HP["n_aux"] * HP["n_embd"], device=dev)
+    nv = gm.forward_from_input(to_dev(inp, dev), hid, logits)
+    torch.cuda.synchronize()
+    ref_h = om.forward_from_input(inp)
+    assert rel_l2(hid.cpu().numpy(), ref_h) <= 2e-3
+    assert nv == HP["n_aux"] * HP["n_embd"]
+    ref_l = om.fc_logits(ref_h)
+    assert rel_l2(logits.cpu().numpy()[:nv], ref_l) <= 2e-3
+
+
+def test_gguf_load_forward_token_and_cli(ctx, dev, tmp_path):
+    import torch
+
+    rng = np.random.default_rng(7)
+    t = make_model(HP, orc.Q4_K, rng)
+    vocab = 300
+    emb = (0.1 * rng.standard_normal(vocab * HP["n_embd"])).astype(np.float32)
+    t["token_embd.weight"] = (orc.F32, emb)
+    meta = {"general.architecture": "dflash", "dflash.block_count": HP["n_layers"],
+            "dflash.embedding_length": HP["n_embd"], "dflash.feed_forward_length": HP["n_ff"],
+            "dflash.attention.head_count": HP["n_heads"], "dflash.attention.head_count_kv": HP["n_kv_heads"],
+            "dflash.attention.key_length": HP["head_dim"], "dflash.rope.dimension_count": HP["rope_dim"],
+            "dflash.rope.freq_base": HP["rope_base"], "dflash.target_layers": [3, 7]}
+    tensors = []
+    for name, (dt, a) in t.items():
+        shape = (HP["n_embd"], vocab) if name == "token_embd.weight" else tensor_shape(name, HP)
+        tensors.append((name, dt, shape, np.ascontiguousarray(a).view(np.uint8)))
+    path = str(tmp_path / "dflash.gguf")
+    write_gguf(path, meta, tensors)
+    gm = DFlash(ctx, gguf_path=path, max_ctx=8, max_block=4)
+    assert (gm.hp.n_layers, gm.hp.n_embd, gm.hp.n_aux) == (HP["n_layers"], HP["n_embd"], 2)
+    om = DFlashOracle(HP, t)
+    hid = torch.empty(HP["n_embd"], device=dev)
+    tok = 123
+    gm.forward_token(tok, hid)
+    torch.cuda.synchronize()
+    inp = emb.reshape(HP["n_embd"], vocab)[:, tok]  # x[i] = emb[i*vocab + tok] (src/dflash.rs:482-485)
+    assert rel_l2(hid.cpu().numpy(), om.forward_from_input(inp)) <= 2e-3
+    with pytest.raises(lc.LagunaError):
+        gm.forward_token(vocab, hid)
+    gm.close()
+
+    cli = os.path.join(ROOT, "laguna_raw_halo_strix_b200", "laguna-cuda")
+    for cmd, expect in ((["test-dequant"], "test-dequant: PASS"), (["test-matmul"], "test-matmul: PASS"),
+                        (["test-rmsnorm"], "test-rmsnorm: PASS"), (["info", path], "block_count: 2"),
+                        (["shapes", path], "blk.1.ffn_down.weight"), (["forward", path, "5"], "forward pass complete"),
+                        (["encode", path], "encode+decode complete"), (["draft", path, "6", "3"], "finite 1")):
+        r = subprocess.run([cli] + cmd, capture_output=True, text=True, timeout=120)
+        assert r.returncode == 0 and expect in r.stdout, (cmd, r.stdout, r.stderr)
