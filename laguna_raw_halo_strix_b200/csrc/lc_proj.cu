@@ -384,112 +384,6 @@ struct Fixup {
     unsigned *cnt;    // [tiles]
 };
 
-// Write (or accumulate) the finished part [sb_a, sb_b) of `tile`.
-template <int LANES>
-__device__ __forceinline__ void sk_flush(const float (&acc)[1][4], int tile, int sb_a, int sb_b, int S, int m,
-                                         int n, float *__restrict__ y, Fixup fx, int lane, const float *scl) {
-    const int g = lane >> 2, t = lane & 3;
-    const int tok = t;  // column pair (2t, 2t+1) = token t (hi, lo)
-    const bool vt = (LANES == 8) ? (t == 0) : (tok < m);
-    const int r0 = tile * 16 + g, r1 = r0 + 8;
-    const float inv = vt ? scl[2 * tok + 1] : 0.f;
-    const float y0 = (acc[0][0] + acc[0][1]) * inv, y1 = (acc[0][2] + acc[0][3]) * inv;
-    if (sb_a == 0 && sb_b == S) {
-        if (vt) {
-            if (r0 < n) y[(size_t)tok * n + r0] = y0;
-            if (r1 < n) y[(size_t)tok * n + r1] = y1;
-        }
-        return;
-    }
-    float *fa = fx.acc + (size_t)tile * 64;
-    if (vt) {
-        atomicAdd(fa + g * 4 + tok, y0);
-        atomicAdd(fa + (g + 8) * 4 + tok, y1);
-    }
-    __threadfence();
-    __syncwarp();
-    unsigned last = 0;
-    if (lane == 0) {
-        const unsigned add = (unsigned)(sb_b - sb_a);
-        last = (atomicAdd(fx.cnt + tile, add) + add == (unsigned)S);
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) return;
-    __threadfence();
-    if (vt) {
-        const float v0 = atomicExch(fa + g * 4 + tok, 0.f);
-        const float v1 = atomicExch(fa + (g + 8) * 4 + tok, 0.f);
-        if (r0 < n) y[(size_t)tok * n + r0] = v0;
-        if (r1 < n) y[(size_t)tok * n + r1] = v1;
-    }
-    if (lane == 0) atomicExch(fx.cnt + tile, 0u);
-}
-
-// Floats reserved for the sub-block sums: rounded up to a multiple of 4 so the
-// staged x that follows starts on a 16-byte boundary (float4 stores).
-__host__ __device__ __forceinline__ size_t sk_sx_floats(int m, int nsub) {
-    return ((size_t)m * nsub + 3) & ~(size_t)3;
-}
-
-// Prologue of the stream-K kernels: stage x [m, k] into shared memory, find
-// each token's activation scale (scl[2j] = 2^e, scl[2j+1] = 2^-e) and, when sx
-// is given, the per-32-element sums of the scaled f16 hi + lo split the tensor
-// cores will see (the offset terms they cancel must match the MMA products).
-__device__ __forceinline__ void sk_prologue_x(const float *__restrict__ x, int m, int k, float *xs, float *sx,
-                                              int sx_stride, float *scl) {
-    __shared__ unsigned smax[4];
-    if (threadIdx.x < 4) smax[threadIdx.x] = 0u;
-    __syncthreads();
-    const bool vec = (((uintptr_t)x) & 15) == 0;
-    const int n4 = (m * k) >> 2;
-    float mx[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-        float4 v;
-        if (vec) {
-            v = __ldg(reinterpret_cast<const float4 *>(x) + i);
-        } else {
-            v.x = __ldg(x + 4 * i);
-            v.y = __ldg(x + 4 * i + 1);
-            v.z = __ldg(x + 4 * i + 2);
-            v.w = __ldg(x + 4 * i + 3);
-        }
-        reinterpret_cast<float4 *>(xs)[i] = v;
-        const float a = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        const int tok = (4 * i) / k;
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-            if (j == tok) mx[j] = fmaxf(mx[j], a);
-    }
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        float v = mx[j];
-        for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if ((threadIdx.x & 31) == 0 && j < m) atomicMax(smax + j, __float_as_uint(v));  // v >= 0: int order
-    }
-    __syncthreads();
-    if (threadIdx.x < m) act_scale(__uint_as_float(smax[threadIdx.x]), scl[2 * threadIdx.x], scl[2 * threadIdx.x + 1]);
-    __syncthreads();
-    if (!sx) return;
-    const int nsub = k >> 5;
-    const int lane = threadIdx.x & 31;
-    for (int i = threadIdx.x >> 5; i < m * nsub; i += blockDim.x >> 5) {
-        const int tok = i / nsub, s = i % nsub;
-        const float f = xs[(size_t)tok * k + 32 * s + lane] * scl[2 * tok];
-        const __half h = __float2half_rn(f);
-        float v = __half2float(h) + __half2float(__float2half_rn(f - __half2float(h)));
-        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) sx[tok * sx_stride + s] = v;
-    }
-}
-
-// f16 bits -> f32 for the per-block scales: IEEE convert, then the reference
-// rule for subnormals (2^-14 * (1 + m/1024) = IEEE value + sign * 2^-14).
-__device__ __forceinline__ float scale_f32(uint32_t h16, int half_mode) {
-    const float f = __half2float(__ushort_as_half((unsigned short)(h16 & 0xFFFFu)));
-    const bool sub = half_mode == LC_HALF_REF && (h16 & 0x7C00u) == 0u && (h16 & 0x3FFu) != 0u;
-    return f + (sub ? copysignf(6.103515625e-05f, f) : 0.f);  // branch-free select
-}
-
 // The raw bytes of one 256-element super-block for rows g and g+8 of a 16-row
 // tile: headers (d, dmin, 12 scale bytes) and nibble group t (bytes 32t..32t+31
 // of the 128, i.e. sub-blocks 2t -- low nibbles -- and 2t+1 -- high nibbles).
@@ -510,67 +404,190 @@ struct Q4UnitG {
     }
 };
 
-// One super-block of a 16-row tile for M tokens, with sub-block sums split by
-// the MMA itself.  A = 1024 + q (low nibbles) or 1024 + 16q (high nibbles),
-// one LOP3 per register and no scaling.  B (one n-tile per token) holds the
-// token's x hi / lo only at the k positions of one owner thread t' in columns
-// 2t' / 2t'+1, so thread t's accumulator columns are exactly the sums over its
-// own sub-block: C[half] = S((1024 + 16^half q) x) over sub-block 2t + half.
-// Scales, mins and the offset are applied once per (row, sub-block) in f32:
-//   y += d*sc/16^h * C - (1024/16^h * d*sc + dmin*m) * Sx.
-// tbl: this lane's entry (index g) of the super-block's table [16][M][8];
-// own: lane holds a B fragment (g / 2 == t).  sxs: Sx of sub-blocks 2t, 2t+1.
+// ---------------------------------------------------------------------------
+// Integer tensor-core path (m <= 4 tokens).
+//
+// A is the raw weight integers: Q4_K nibbles become u8 with one mask (low
+// nibbles) or a shift and a mask (high nibbles); Q8_0 bytes are used as s8
+// unchanged.  B is the activation as a 16-bit integer split into two s8
+// digits, x ~= (256*hi + lo) * inv, with one power-free scale per 32-element
+// sub-block (inv = max|x| / 32639), so an outlier only coarsens its own
+// sub-block.  mma.m16n8k32 (u8 x s8 or s8 x s8 -> s32) sums exactly; k = 32 is
+// one sub-block, so the per-sub-block f16 scales are applied once per (row,
+// sub-block) in f32.  As in the f16 path, each thread owns B columns
+// (2t, 2t+1) = (hi, lo digit) of its own k positions, so the accumulator
+// columns a thread holds are the sums over its own sub-block.
+
+__device__ __forceinline__ void lc_imma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Shared-memory layout of the integer stream-K kernels for M tokens and k:
+//   [0, 4Mk)          staged x (f32); reused for the B table once digits exist
+//   [4Mk, 6Mk)        digits: int8 [M][2][k] (hi, lo)
+//   [6Mk, 6Mk + Mk/4) per sub-block (Sx, inv): float2 [M][k/32]
+__host__ __device__ __forceinline__ size_t ski_smem_bytes(int m, int k) {
+    return (size_t)m * k * 6 + (size_t)m * (k / 32) * 8;
+}
+
+// Prologue: stage x, then per 32-element sub-block (one warp each): Sx, scale,
+// digits.  Ends with a barrier.
+__device__ __forceinline__ void ski_prologue(const float *__restrict__ x, int m, int k, float *xs, int8_t *dig,
+                                             float2 *sbi) {
+    const bool vec = (((uintptr_t)x) & 15) == 0;
+    const int n4 = (m * k) >> 2;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        float4 v;
+        if (vec) {
+            v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+        } else {
+            v.x = __ldg(x + 4 * i);
+            v.y = __ldg(x + 4 * i + 1);
+            v.z = __ldg(x + 4 * i + 2);
+            v.w = __ldg(x + 4 * i + 3);
+        }
+        reinterpret_cast<float4 *>(xs)[i] = v;
+    }
+    __syncthreads();
+    // One thread per 32-element sub-block; element e is read at (e + s) mod 32
+    // so the 32 threads of a warp hit 32 different banks.
+    const int nsub = k >> 5;
+    for (int i = threadIdx.x; i < m * nsub; i += blockDim.x) {
+        const float *xr = xs + (size_t)i * 32;  // token rows are contiguous: sub-block i of [m*nsub]
+        float mx = 0.f, sum = 0.f;
+#pragma unroll 8
+        for (int e = 0; e < 32; e++) {
+            const float v = xr[(e + i) & 31];
+            mx = fmaxf(mx, fabsf(v));
+            sum += v;
+        }
+        const bool fin = mx < INFINITY;  // false for inf / nan
+        const float scale = (mx > 0.f && fin) ? 32639.f / mx : 0.f;
+        const float inv = mx > 0.f ? (fin ? mx * (1.f / 32639.f) : __int_as_float(0x7FC00000)) : 0.f;
+        const int tok = i / nsub, s = i - tok * nsub;
+        int8_t *dh = dig + ((size_t)tok * 2 + 0) * k + 32 * s;
+        int8_t *dl = dig + ((size_t)tok * 2 + 1) * k + 32 * s;
+#pragma unroll 8
+        for (int e = 0; e < 32; e++) {
+            const int ee = (e + i) & 31;
+            const int xi = __float2int_rn(xr[ee] * scale);
+            const int hi = (xi + 128) >> 8;
+            dh[ee] = (int8_t)hi;
+            dl[ee] = (int8_t)(xi - (hi << 8));
+        }
+        sbi[i] = make_float2(sum, inv);
+    }
+    __syncthreads();
+}
+
+// int32 -> f32 without the conversion unit, exact for |v| < 2^22:
+// the bits of 1.5 * 2^23 + v, minus 1.5 * 2^23.  Each digit's MMA sum stays
+// far below that (Q4_K: 32 * 15 * 128 < 2^16; Q8_0: 32 * 128 * 128 = 2^19),
+// so the hi and lo sums are converted separately and combined in f32.
+__device__ __forceinline__ float i2f_small(int v) {
+    return __int_as_float(v + 0x4B400000) - 12582912.f;
+}
+
+// (d, dmin) of a header word -> two floats.  The reference rule for subnormal
+// halves (2^-14 * (1 + m/1024)) is the half with its exponent field set to 1,
+// applied branch-free to both halves: per half, bit 10 is OR-ed in when the
+// exponent is 0 and the mantissa is not (ref = 0x04000400 mask, IEEE = 0).
+__device__ __forceinline__ float2 scales2_f32(uint32_t h2, uint32_t ref_mask) {
+    const uint32_t man = h2 & 0x03FF03FFu, ex = h2 & 0x7C007C00u;
+    const uint32_t m_nz = (man + 0x03FF03FFu) & 0x04000400u;     // bit 10: mantissa != 0
+    const uint32_t e_nz = ((ex + 0x7C007C00u) & 0x80008000u) >> 5;  // bit 10: exponent != 0
+    const uint32_t fixed = h2 | (m_nz & ~e_nz & ref_mask);
+    return __half22float2(lc_u32_as_h2(fixed));
+}
+
+// Two 6-bit values in bytes 0 / 1 -> floats, exactly (PRMT to 1024 + v halves).
+__device__ __forceinline__ float2 u6pair_f32(uint32_t v2) {
+    const __half2 h = __hsub2(lc_u32_as_h2(__byte_perm(v2, 0x64646464u, 0x4140)),
+                              __half2(__float2half_rn(1024.f), __float2half_rn(1024.f)));
+    return __half22float2(h);
+}
+
+__device__ __forceinline__ void lc_imma_u8s8_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ void lc_imma_s8s8_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ uint32_t dig4(const int8_t *dig, size_t idx) {
+    return *reinterpret_cast<const uint32_t *>(dig + idx);
+}
+
+// One Q4_K super-block of a 16-row tile, integer MMAs.  tbl: this lane's
+// entry of the super-block's table [8 MMAs][M][8] (zero block for non-owner
+// lanes); sb4: float4 (Sx, inv of sub-block 2t, Sx, inv of 2t+1) of token 0,
+// tokens sb4_stride float4 apart.
 template <int M>
-__device__ __forceinline__ void q4k_unit_masked(const Q4UnitG &U, const uint2 *tbl, bool own, const float *sxs,
-                                                int sx_stride, int half_mode, int t, float (&y)[M][2]) {
-    float c[2][M][4];
+__device__ __forceinline__ void q4k_unit_int(const Q4UnitG &U, const uint2 *tbl, const float4 *sb4, int sb4_stride,
+                                             uint32_t ref_mask, int t, float (&y)[M][2]) {
+    int c[2][M][4];
 #pragma unroll
-    for (int h = 0; h < 2; h++)
+    for (int half = 0; half < 2; half++) {
 #pragma unroll
-        for (int j = 0; j < M; j++) c[h][j][0] = c[h][j][1] = c[h][j][2] = c[h][j][3] = 0.f;
+        for (int i = 0; i < 4; i++) {
+            const uint4 &Pg = i < 2 ? U.A0 : U.B0;
+            const uint4 &Pg8 = i < 2 ? U.A1 : U.B1;
+            uint32_t w0g = (i & 1) ? Pg.z : Pg.x, w1g = (i & 1) ? Pg.w : Pg.y;
+            uint32_t w0g8 = (i & 1) ? Pg8.z : Pg8.x, w1g8 = (i & 1) ? Pg8.w : Pg8.y;
+            if (half) {
+                w0g >>= 4;
+                w1g >>= 4;
+                w0g8 >>= 4;
+                w1g8 >>= 4;
+            }
+            const uint32_t a0 = w0g & 0x0F0F0F0Fu, a2 = w1g & 0x0F0F0F0Fu;
+            const uint32_t a1 = w0g8 & 0x0F0F0F0Fu, a3 = w1g8 & 0x0F0F0F0Fu;
 #pragma unroll
-    for (int wi = 0; wi < 4; wi++) {
-#pragma unroll
-        for (int cc = 0; cc < 2; cc++) {
-            const uint32_t wg = u4_get(cc ? U.B0 : U.A0, wi), wg8 = u4_get(cc ? U.B1 : U.A1, wi);
-            const uint32_t wgs = wg >> 8, wg8s = wg8 >> 8;
-#pragma unroll
-            for (int half = 0; half < 2; half++) {
-                const uint32_t mask = half ? 0x00F000F0u : 0x000F000Fu;
-                const uint32_t a0 = (wg & mask) | 0x64006400u, a1 = (wg8 & mask) | 0x64006400u;
-                const uint32_t a2 = (wgs & mask) | 0x64006400u, a3 = (wg8s & mask) | 0x64006400u;
-                const int js = cc * 8 + wi * 2 + half;
-#pragma unroll
-                for (int j = 0; j < M; j++) {
-                    const uint2 b = tbl[(js * M + j) * 8];  // zero buffer for non-owner lanes
-                    lc_mma16816(c[half][j], a0, a1, a2, a3, b.x, b.y);
-                }
+            for (int j = 0; j < M; j++) {
+                const uint2 b = tbl[((half * 4 + i) * M + j) * 8];
+                if (i == 0)
+                    lc_imma_u8s8_z(c[half][j], a0, a1, a2, a3, b.x, b.y);
+                else
+                    lc_imma_u8s8(c[half][j], a0, a1, a2, a3, b.x, b.y);
             }
         }
     }
-    // epilogue: per row, scales / mins of sub-blocks 2t (lo) and 2t+1 (hi)
+    // per row: scales / mins of sub-blocks 2t (lo nibbles) and 2t+1 (hi nibbles)
     // (get_scale_min_k4, proj_q4k.comp:113-125; t >= 2 uses the j >= 4 packing)
+    const int sh = 16 * (t & 1);
 #pragma unroll
     for (int r = 0; r < 2; r++) {
         const uint4 H = r ? U.H1 : U.H0;
-        const float d = scale_f32(H.x, half_mode), dmin = scale_f32(H.x >> 16, half_mode);
-        const int sh = 16 * (t & 1);
+        const float2 dd = scales2_f32(H.x, ref_mask);  // (d, dmin)
         const uint32_t yy = H.y >> sh, zz = H.z >> sh, ww = H.w >> sh;
-        // byte 0: sub-block 2t, byte 1: sub-block 2t+1 (both packings, then a select)
-        const uint32_t sc_a = yy & 0x3F3Fu, mn_a = zz & 0x3F3Fu;
         const uint32_t sc_b = (ww & 0x0F0Fu) | ((yy >> 2) & 0x3030u);
         const uint32_t mn_b = ((ww >> 4) & 0x0F0Fu) | ((zz >> 2) & 0x3030u);
-        const uint32_t sc2 = t < 2 ? sc_a : sc_b, mn2 = t < 2 ? mn_a : mn_b;
-        const float sc_lo = (float)(sc2 & 0xFFu), sc_hi = (float)((sc2 >> 8) & 0xFFu);
-        const float m_lo = (float)(mn2 & 0xFFu), m_hi = (float)((mn2 >> 8) & 0xFFu);
-        const float a_lo = d * sc_lo, a_hi = d * sc_hi * 0.0625f;
-        const float c_lo = fmaf(1024.f, a_lo, dmin * m_lo), c_hi = fmaf(1024.f, a_hi, dmin * m_hi);
+        const float2 sc = u6pair_f32(t < 2 ? (yy & 0x3F3Fu) : sc_b);
+        const float2 mn = u6pair_f32(t < 2 ? (zz & 0x3F3Fu) : mn_b);
+        const float ds_lo = dd.x * sc.x, ds_hi = dd.x * sc.y;
+        const float dm_lo = dd.y * mn.x, dm_hi = dd.y * mn.y;
 #pragma unroll
         for (int j = 0; j < M; j++) {
-            const float2 sx = *reinterpret_cast<const float2 *>(sxs + j * sx_stride);
-            const float s_lo = c[0][j][2 * r] + c[0][j][2 * r + 1];
-            const float s_hi = c[1][j][2 * r] + c[1][j][2 * r + 1];
-            y[j][r] += (a_lo * s_lo + a_hi * s_hi) - (c_lo * sx.x + c_hi * sx.y);
+            const float4 f = sb4[j * sb4_stride];  // Sx_lo, inv_lo, Sx_hi, inv_hi
+            const float s_lo = fmaf(i2f_small(c[0][j][2 * r]), 256.f, i2f_small(c[0][j][2 * r + 1]));
+            const float s_hi = fmaf(i2f_small(c[1][j][2 * r]), 256.f, i2f_small(c[1][j][2 * r + 1]));
+            float v = fmaf(ds_lo * f.y, s_lo, y[j][r]);
+            v = fmaf(ds_hi * f.w, s_hi, v);
+            v = fmaf(-dm_lo, f.x, v);
+            y[j][r] = fmaf(-dm_hi, f.z, v);
         }
     }
 }
@@ -579,7 +596,7 @@ __device__ __forceinline__ void q4k_unit_masked(const Q4UnitG &U, const uint2 *t
 // [sb_a, sb_b); y holds this thread's partial over its own sub-blocks.
 template <int M>
 __device__ __forceinline__ void skm_flush(float (&y)[M][2], int tile, int sb_a, int sb_b, int S, int n,
-                                          float *__restrict__ out, Fixup fx, int lane, const float *scl) {
+                                          float *__restrict__ out, Fixup fx, int lane) {
     const int g = lane >> 2, t = lane & 3;
     float v0 = 0.f, v1 = 0.f;  // token t's totals after the group reduction
 #pragma unroll
@@ -589,7 +606,7 @@ __device__ __forceinline__ void skm_flush(float (&y)[M][2], int tile, int sb_a, 
         a += __shfl_xor_sync(0xffffffffu, a, 2);
         b += __shfl_xor_sync(0xffffffffu, b, 1);
         b += __shfl_xor_sync(0xffffffffu, b, 2);
-        if (j == t) v0 = a * scl[2 * j + 1], v1 = b * scl[2 * j + 1];
+        if (j == t) v0 = a, v1 = b;
         y[j][0] = y[j][1] = 0.f;
     }
     const bool vt = t < M;
@@ -626,7 +643,7 @@ __device__ __forceinline__ void skm_flush(float (&y)[M][2], int tile, int sb_a, 
 }
 
 // Persistent stream-K Q4_K projection for M <= 4 tokens.  One CTA per SM
-// stages x in shared memory and builds the masked B table for the whole K,
+// digitises x into shared memory and builds the B table for the whole K,
 // then its warps walk equal shares of the flattened (16-row tile,
 // super-block) unit space, prefetching the next unit's bytes while the tensor
 // cores work on the current one.  A tile whose super-blocks are split between
@@ -639,10 +656,11 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) q4k_sk_kernel(const float *_
                                                                   int half_mode, Fixup fx) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int S = k >> 8;  // super-blocks per row
-    const int nsub = S * 8;
-    uint2 *tab = reinterpret_cast<uint2 *>(smem);                            // [S][16][M][8]
-    float *sx = reinterpret_cast<float *>(smem + (size_t)S * 16 * M * 64);  // [M][nsub]
-    float *xs = sx + sk_sx_floats(M, nsub);                                  // [M][k]
+    float *xs = reinterpret_cast<float *>(smem);
+    uint2 *tab = reinterpret_cast<uint2 *>(smem);  // replaces xs: [S][8][M][8]
+    int8_t *dig = reinterpret_cast<int8_t *>(smem + (size_t)M * k * 4);
+    float2 *sbi = reinterpret_cast<float2 *>(smem + (size_t)M * k * 6);
+    __shared__ __align__(16) uint2 zbuf[8 * M * 8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const size_t rowbytes = (size_t)S * 144;
@@ -664,45 +682,42 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) q4k_sk_kernel(const float *_
         if (++ps == S) ps = 0, ++pt;
         ++loaded;
     };
-    Q4UnitG A, B;
+    Q4UnitG A, B, C;  // three units in flight per warp
     load_next(A);
     load_next(B);
+    load_next(C);
 
-    // Prologue: x -> shared, per-token scales, split sub-block sums, then the table.
-    __shared__ float scl[8];
-    __shared__ __align__(16) uint2 zbuf[16 * M * 8];
-    for (int i = threadIdx.x; i < 16 * M * 8; i += blockDim.x) zbuf[i] = make_uint2(0u, 0u);
-    sk_prologue_x(x, M, k, xs, sx, nsub, scl);
-    for (int idx = threadIdx.x; idx < S * 16 * M * 8; idx += blockDim.x) {
+    for (int i = threadIdx.x; i < 8 * M * 8; i += blockDim.x) zbuf[i] = make_uint2(0u, 0u);
+    ski_prologue(x, M, k, xs, dig, sbi);
+    // Table entry (sub, mma = half*4 + i, token j, e = 2*owner + digit): the
+    // owner's 8 k positions are elements 256sub + 64owner + 32half + 8i + 0..7.
+    for (int idx = threadIdx.x; idx < S * 8 * M * 8; idx += blockDim.x) {
         const int e = idx & 7;
         const int j = (idx >> 3) % M;
-        const int js = (idx / (8 * M)) & 15;
-        const int sb = idx / (8 * M * 16);
-        const int to = e >> 1, part = e & 1;  // owner thread, hi / lo
-        const int cc = js >> 3, wi = (js >> 1) & 3, half = js & 1;
-        const float *xr = xs + (size_t)j * k + (size_t)sb * 256 + 64 * to + 16 * cc + 4 * wi + 32 * half;
-        const float s = scl[2 * j];
-        uint2 v;
-        v.x = lc_pack_h2(lc_split_part(xr[0] * s, part), lc_split_part(xr[2] * s, part));
-        v.y = lc_pack_h2(lc_split_part(xr[1] * s, part), lc_split_part(xr[3] * s, part));
-        tab[idx] = v;
+        const int mm = (idx / (8 * M)) & 7;
+        const int sb = idx / (64 * M);
+        const int to = e >> 1, dg = e & 1, half = mm >> 2, i = mm & 3;
+        const size_t base = ((size_t)j * 2 + dg) * k + (size_t)sb * 256 + 64 * to + 32 * half + 8 * i;
+        tab[idx] = make_uint2(dig4(dig, base), dig4(dig, base + 4));
     }
     __syncthreads();
 
     // Lanes that carry no B fragment (g / 2 != t) read a zero block instead,
     // so the k-step loop has no predicate.
     const bool own = (g >> 1) == t;
+    const int sb4_stride = k >> 6;  // float4 per token
     float acc[M][2];
 #pragma unroll
     for (int j = 0; j < M; j++) acc[j][0] = acc[j][1] = 0.f;
+    const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
     int seg0 = sub, done = 0;
     auto step = [&](Q4UnitG &U) {
-        const uint2 *tbl = own ? tab + (size_t)sub * 16 * M * 8 + g : zbuf;
-        q4k_unit_masked<M>(U, tbl, own, sx + sub * 8 + 2 * t, nsub, half_mode, t, acc);
-        load_next(U);  // U's registers are free again: refill with the unit after next
+        const uint2 *tbl = own ? tab + (size_t)sub * 64 * M + g : zbuf;
+        q4k_unit_int<M>(U, tbl, reinterpret_cast<const float4 *>(sbi) + sub * 4 + t, sb4_stride, ref_mask, t, acc);
+        load_next(U);  // U's registers are free again: refill with the unit three ahead
         ++done;
         if (sub == S - 1 || done == n_units) {
-            skm_flush<M>(acc, tile, seg0, sub + 1, S, n, y, fx, lane, scl);
+            skm_flush<M>(acc, tile, seg0, sub + 1, S, n, y, fx, lane);
             seg0 = 0;
         }
         if (++sub == S) sub = 0, ++tile;
@@ -711,6 +726,8 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) q4k_sk_kernel(const float *_
         step(A);
         if (done == n_units) break;
         step(B);
+        if (done == n_units) break;
+        step(C);
     }
 }
 
@@ -835,18 +852,85 @@ __global__ void __launch_bounds__(kWarps * 32) q8_mma_kernel(const uint2 *__rest
     reduce_store<NT>(acc, red, c, m, n, row0, atomic_out, inv_scale);
 }
 
-// Persistent stream-K form for m <= 4 (see q4k_sk_kernel); units are
-// (16-row tile, block pair).
-template <int LANES>
+// The words of one Q8_0 block pair (68 B) that thread (g, t) needs for rows g
+// and g+8: q_A[8t..8t+7] (pair bytes 2+8t.., words 2t..2t+2), q_B[8t..8t+7]
+// (words 9+2t, 10+2t), d_A (word 0 low half), d_B (word 8 high half).
+struct Q8UnitI {
+    uint32_t w[2][7];
+    __device__ __forceinline__ void load(const uint8_t *b0, const uint8_t *b1, int t) {
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const uint8_t *b = r ? b1 : b0;
+            if (b) {
+                w[r][0] = ldg_u32(b + 8 * t);
+                w[r][1] = ldg_u32(b + 8 * t + 4);
+                w[r][2] = ldg_u32(b + 8 * t + 8);
+                w[r][3] = ldg_u32(b + 36 + 8 * t);
+                w[r][4] = ldg_u32(b + 40 + 8 * t);
+                w[r][5] = ldg_u32(b);
+                w[r][6] = ldg_u32(b + 32);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 7; i++) w[r][i] = 0u;
+            }
+        }
+    }
+};
+
+// One Q8_0 block pair of a 16-row tile, integer MMAs (one k = 32 MMA per
+// block and token).  sb4: float4 (Sx, inv of block 2p, Sx, inv of block 2p+1).
+template <int M>
+__device__ __forceinline__ void q8_unit_int(const Q8UnitI &U, const uint2 *tbl, const float4 *sb4, int sb4_stride,
+                                            uint32_t ref_mask, float (&y)[M][2]) {
+    int c[2][M][4];
+#pragma unroll
+    for (int blk = 0; blk < 2; blk++) {
+        uint32_t a0, a1, a2, a3;
+        if (blk == 0) {
+            a0 = __funnelshift_r(U.w[0][0], U.w[0][1], 16);
+            a2 = __funnelshift_r(U.w[0][1], U.w[0][2], 16);
+            a1 = __funnelshift_r(U.w[1][0], U.w[1][1], 16);
+            a3 = __funnelshift_r(U.w[1][1], U.w[1][2], 16);
+        } else {
+            a0 = U.w[0][3];
+            a2 = U.w[0][4];
+            a1 = U.w[1][3];
+            a3 = U.w[1][4];
+        }
+#pragma unroll
+        for (int j = 0; j < M; j++) {
+            const uint2 b = tbl[(blk * M + j) * 8];
+            lc_imma_s8s8_z(c[blk][j], a0, a1, a2, a3, b.x, b.y);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        // d_A: low half of word 0; d_B: high half of word 8
+        const float2 dd = scales2_f32(__byte_perm(U.w[r][5], U.w[r][6], 0x7610), ref_mask);
+#pragma unroll
+        for (int j = 0; j < M; j++) {
+            const float4 f = sb4[j * sb4_stride];
+            const float sA = fmaf(i2f_small(c[0][j][2 * r]), 256.f, i2f_small(c[0][j][2 * r + 1]));
+            const float sB = fmaf(i2f_small(c[1][j][2 * r]), 256.f, i2f_small(c[1][j][2 * r + 1]));
+            y[j][r] = fmaf(dd.y * f.w, sB, fmaf(dd.x * f.y, sA, y[j][r]));
+        }
+    }
+}
+
+// Persistent stream-K Q8_0 projection for M <= 4 tokens (see q4k_sk_kernel);
+// units are (16-row tile, block pair).
+template <int M>
 __global__ void __launch_bounds__(kSkWarps * 32, 1) q8_sk_kernel(const float *__restrict__ x,
                                                                  const uint8_t *__restrict__ w,
-                                                                 float *__restrict__ y, int m, int k, int n,
+                                                                 float *__restrict__ y, int k, int n,
                                                                  int half_mode, Fixup fx) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int S = k >> 6;  // block pairs per row
-    uint2 *tab = reinterpret_cast<uint2 *>(smem);
-    float *sx = reinterpret_cast<float *>(smem + (size_t)S * 4 * LANES * 8);  // [m][k/32] (unused sums)
-    float *xs = sx + sk_sx_floats(m, k >> 5);                                 // [m][k], 16-B aligned
+    float *xs = reinterpret_cast<float *>(smem);
+    uint2 *tab = reinterpret_cast<uint2 *>(smem);  // replaces xs: [S][2][M][8]
+    int8_t *dig = reinterpret_cast<int8_t *>(smem + (size_t)M * k * 4);
+    float2 *sbi = reinterpret_cast<float2 *>(smem + (size_t)M * k * 6);
+    __shared__ __align__(16) uint2 zbuf[2 * M * 8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const size_t rowbytes = (size_t)S * 68;
@@ -859,7 +943,7 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) q8_sk_kernel(const float *__
     int tile = (int)(u0 / S), sub = (int)(u0 % S);
 
     int pt = tile, ps = sub, loaded = 0;
-    auto load_next = [&](Q8Unit &U) {
+    auto load_next = [&](Q8UnitI &U) {
         if (loaded >= n_units) return;
         const int rg = pt * 16 + g, rg8 = rg + 8;
         U.load(rg < n ? w + (size_t)rg * rowbytes + (size_t)ps * 68 : nullptr,
@@ -867,41 +951,40 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) q8_sk_kernel(const float *__
         if (++ps == S) ps = 0, ++pt;
         ++loaded;
     };
-    Q8Unit A, B;
+    Q8UnitI A, B, C;  // three units in flight per warp
     load_next(A);
     load_next(B);
+    load_next(C);
 
-    // B-fragment table: pair p, k-step js = blk*2 + ks covers elements
-    // 64p + 32blk + 16ks + 4tt + {0..3}: (e0, e2), (e1, e3).
-    __shared__ float scl[8];
-    sk_prologue_x(x, m, k, xs, nullptr, 0, scl);
-    (void)sx;
-    for (int idx = threadIdx.x; idx < S * 4 * LANES; idx += blockDim.x) {
-        const int ln = idx % LANES;
-        const int js = (idx / LANES) & 3;
-        const int p = idx / (LANES * 4);
-        const int gg = ln >> 2, tt = ln & 3;
-        const int tok = gg >> 1, part = gg & 1;
-        uint2 v = make_uint2(0u, 0u);
-        if (tok < m) {
-            const float *xr = xs + (size_t)tok * k + (size_t)p * 64 + 16 * js + 4 * tt;
-            const float s = scl[2 * tok];
-            v.x = lc_pack_h2(lc_split_part(xr[0] * s, part), lc_split_part(xr[2] * s, part));
-            v.y = lc_pack_h2(lc_split_part(xr[1] * s, part), lc_split_part(xr[3] * s, part));
-        }
-        tab[idx] = v;
+    for (int i = threadIdx.x; i < 2 * M * 8; i += blockDim.x) zbuf[i] = make_uint2(0u, 0u);
+    ski_prologue(x, M, k, xs, dig, sbi);
+    // Table entry (pair p, block blk, token j, e = 2*owner + digit): the
+    // owner's 8 k positions are elements 64p + 32blk + 8owner + 0..7.
+    for (int idx = threadIdx.x; idx < S * 2 * M * 8; idx += blockDim.x) {
+        const int e = idx & 7;
+        const int j = (idx >> 3) % M;
+        const int blk = (idx / (8 * M)) & 1;
+        const int p = idx / (16 * M);
+        const int to = e >> 1, dg = e & 1;
+        const size_t base = ((size_t)j * 2 + dg) * k + (size_t)p * 64 + 32 * blk + 8 * to;
+        tab[idx] = make_uint2(dig4(dig, base), dig4(dig, base + 4));
     }
     __syncthreads();
 
-    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+    const bool own = (g >> 1) == t;
+    const int sb4_stride = k >> 6;
+    float acc[M][2];
+#pragma unroll
+    for (int j = 0; j < M; j++) acc[j][0] = acc[j][1] = 0.f;
+    const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
     int seg0 = sub, done = 0;
-    auto step = [&](Q8Unit &U) {
-        q8_unit<1, LANES>(U, tab + (size_t)sub * 4 * LANES, lane, half_mode, acc);
+    auto step = [&](Q8UnitI &U) {
+        const uint2 *tbl = own ? tab + (size_t)sub * 16 * M + g : zbuf;
+        q8_unit_int<M>(U, tbl, reinterpret_cast<const float4 *>(sbi) + sub, sb4_stride, ref_mask, acc);
         load_next(U);
         ++done;
         if (sub == S - 1 || done == n_units) {
-            sk_flush<LANES>(acc, tile, seg0, sub + 1, S, m, n, y, fx, lane, scl);
-            acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.f;
+            skm_flush<M>(acc, tile, seg0, sub + 1, S, n, y, fx, lane);
             seg0 = 0;
         }
         if (++sub == S) sub = 0, ++tile;
@@ -910,6 +993,8 @@ __global__ void __launch_bounds__(kSkWarps * 32, 1) q8_sk_kernel(const float *__
         step(A);
         if (done == n_units) break;
         step(B);
+        if (done == n_units) break;
+        step(C);
     }
 }
 
@@ -1007,6 +1092,15 @@ int launch_q4k_sk(lc_ctx *ctx, int grid, size_t smem, const float *x, const uint
     return LC_OK;
 }
 
+template <int M>
+int launch_q8_sk(lc_ctx *ctx, int grid, size_t smem, const float *x, const uint8_t *w, float *c, uint32_t k,
+                 uint32_t n, Fixup fx) {
+    int s = set_smem(q8_sk_kernel<M>, smem);
+    if (s) return s;
+    q8_sk_kernel<M><<<grid, kSkWarps * 32, smem, ctx->stream>>>(x, w, c, (int)k, (int)n, ctx->half_mode, fx);
+    return LC_OK;
+}
+
 template <int NT, int LANES>
 int launch_q8(lc_ctx *ctx, const uint2 *tab, const float *inv_scale, const uint8_t *w, float *c, int m, int k, int n) {
     const int npairs = k >> 6;
@@ -1038,7 +1132,7 @@ int proj_q4k(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m, 
     const uint8_t *w = (const uint8_t *)wv + (size_t)(expert_offset / 256) * 144;
     const int nsb = k / 256;
     if (m <= 4) {
-        const size_t smem = (size_t)nsb * 16 * m * 64 + sk_sx_floats((int)m, nsb * 8) * 4 + (size_t)m * k * 4;
+        const size_t smem = ski_smem_bytes((int)m, (int)k);
         if (smem + 8192 <= ctx->smem_optin) {  // + static shared (zero block, scales)
             const int T = (int)((n + 15) / 16);
             Fixup fx;
@@ -1088,10 +1182,9 @@ int proj_q8_0(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m,
     }
     const int nblk = k / 32;
     if (m <= 4) {
-        const int lanes = m == 1 ? 8 : 32;
         const int S = (int)(k / 64);
-        const size_t smem = (size_t)S * 4 * lanes * 8 + sk_sx_floats((int)m, (int)(k / 32)) * 4 + (size_t)m * k * 4;
-        if (smem + 8192 <= ctx->smem_optin) {  // + static shared (zero block, scales)
+        const size_t smem = ski_smem_bytes((int)m, (int)k);
+        if (smem + 8192 <= ctx->smem_optin) {  // + static shared (zero block)
             const int T = (int)((n + 15) / 16);
             Fixup fx;
             fx.acc = (float *)lc_scratch_zeroed(ctx, LC_SCRATCH_FIXUP, (size_t)T * 64 * 4 + (size_t)T * 4 + 256);
@@ -1099,19 +1192,12 @@ int proj_q8_0(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m,
             fx.cnt = (unsigned *)(fx.acc + (size_t)T * 64);
             const long long units = (long long)T * S;
             const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, (units + 31) / 32));
-            int s;
-            if (m == 1) {
-                s = set_smem(q8_sk_kernel<8>, smem);
-                if (s) return s;
-                q8_sk_kernel<8><<<grid, kSkWarps * 32, smem, ctx->stream>>>(x, w, c, (int)m, (int)k, (int)n,
-                                                                           ctx->half_mode, fx);
-            } else {
-                s = set_smem(q8_sk_kernel<32>, smem);
-                if (s) return s;
-                q8_sk_kernel<32><<<grid, kSkWarps * 32, smem, ctx->stream>>>(x, w, c, (int)m, (int)k, (int)n,
-                                                                            ctx->half_mode, fx);
+            switch (m) {
+            case 1: return launch_q8_sk<1>(ctx, grid, smem, x, w, c, k, n, fx);
+            case 2: return launch_q8_sk<2>(ctx, grid, smem, x, w, c, k, n, fx);
+            case 3: return launch_q8_sk<3>(ctx, grid, smem, x, w, c, k, n, fx);
+            default: return launch_q8_sk<4>(ctx, grid, smem, x, w, c, k, n, fx);
             }
-            return LC_OK;
         }
     }
     for (uint32_t t0 = 0; t0 < m; t0 += 16) {
