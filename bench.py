@@ -73,6 +73,11 @@ def step_bytes(wl):
     return tot
 
 
+def workload_config(name, wl):
+    return {"workload": name, "baseline_config": wl["config"], "m": wl["m"],
+            "projections": [f"{nm} {k}->{n}" for nm, k, n in wl["shapes"]], "bytes_per_step": step_bytes(wl)}
+
+
 def launch_bytes(wl):
     """Algorithmic bytes of one projection launch (W + x + y); all shapes of a
     workload move the same bytes per launch."""
@@ -168,50 +173,100 @@ def physical_gpu_index(local_rank: int) -> int:
 
 
 # ---------------------------------------------------------------------------
-def cpu_reference_run(wl, budget_s: float, rng, use_ref: bool):
-    """Time the reference's CPU-runnable implementation of one projection of the
-    workload on a bounded row sample.  Returns (GB/s, kind, cores, sample)."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as orc
-    from laguna_raw_halo_strix_b200 import synth
+class CpuReference:
+    """The reference's CPU-runnable implementation of one workload step: its
+    GLSL projection shaders (kernels/proj_q4k.comp, kernels/proj_q8_0.comp) and
+    kernels/activation.comp compiled for the host (oracle/_ref, OpenMP over
+    the invocations), else the C restatement of the same algorithm (oracle/).
 
-    dtype = orc.Q4_K if wl["dtype"] == "q4k" else orc.Q8_0
-    name, k, n = wl["shapes"][0]
-    m = wl["m"]
-    ref = None
-    if use_ref and os.path.exists(orc.REF_LIB):
-        ref = orc.RefShaders()
-    o = orc.Oracle()
-    cores = o.lib.lco_get_threads()
-    rows = 64
-    x = synth.activations(m, k, rng)
-    w = synth.weight_blocks(dtype, rows, k, rng)
+    A step is the workload's projections for all m tokens (and the SiLU gate
+    of the FFN), restricted to the first `frac` of each projection's rows when
+    a bounded sample is asked for."""
 
-    def run_once(nrows):
-        ww = w[:nrows] if nrows <= w.shape[0] else np.concatenate([w] * (nrows // w.shape[0] + 1))[:nrows]
-        t0 = time.perf_counter()
-        if ref is not None:
-            wp = orc.pad4(ww)
-            for r in range(m):
-                c = np.zeros(nrows, np.float32)
-                push = np.array([k, nrows] + ([0] if dtype == orc.Q4_K else []), np.uint32).tobytes()
-                ref.run("proj_q4k" if dtype == orc.Q4_K else "proj_q8_0", [x[r], wp, c], push,
-                        orc.RefShaders.groups(nrows))
+    def __init__(self, wl, rng):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as orc
+        from laguna_raw_halo_strix_b200 import synth
+
+        self.orc, self.wl = orc, wl
+        self.dtype = orc.Q4_K if wl["dtype"] == "q4k" else orc.Q8_0
+        self.ref = orc.RefShaders() if os.path.exists(orc.REF_LIB) else None
+        self.port = orc.Oracle()
+        self.cores = self.port.lib.lco_get_threads()
+        self.kind = "reference" if self.ref is not None else "port"
+        self.w = {nm: synth.weight_blocks(self.dtype, n, k, rng) for nm, k, n in wl["shapes"]}
+        self.wp = {nm: orc.pad4(w) for nm, w in self.w.items()} if self.ref is not None else None
+        self.x = synth.activations(wl["m"], wl["shapes"][0][1], rng)
+
+    def _proj(self, name, x, k, rows):
+        orc, m = self.orc, x.shape[0]
+        c = np.zeros((m, rows), np.float32)
+        if self.ref is None:
+            return self.port.proj(self.dtype, x, self.w[name][:rows], k, rows)
+        shader = "proj_q4k" if self.dtype == orc.Q4_K else "proj_q8_0"
+        for r in range(m):
+            push = np.array([k, rows] + ([0] if self.dtype == orc.Q4_K else []), np.uint32).tobytes()
+            self.ref.run(shader, [np.ascontiguousarray(x[r]), self.wp[name], c[r]], push,
+                         orc.RefShaders.groups(rows))
+        return c
+
+    def step(self, frac=1.0):
+        """One (sampled) step; returns the algorithmic bytes it moved."""
+        wl, m = self.wl, self.wl["m"]
+        nbytes = 0
+        rows = {nm: max(16, int(n * frac)) for nm, k, n in wl["shapes"]}
+        if wl["ffn"]:
+            (_, kg, _), (_, ku, _), (_, kd, nd) = wl["shapes"]
+            g = self._proj("gate", self.x, kg, rows["gate"])
+            u = self._proj("up", self.x, ku, rows["up"])
+            na = m * min(rows["gate"], rows["up"])
+            h = np.zeros((m, kd), np.float32)
+            gv, uv = g[:, :na // m].ravel().copy(), u[:, :na // m].ravel().copy()
+            hv = np.zeros(na, np.float32)
+            if self.ref is not None:
+                self.ref.run("activation", [gv, uv, hv], np.array([na], np.uint32).tobytes(),
+                             self.orc.RefShaders.groups(na))
+            else:
+                hv = self.port.activation(gv, uv)
+            h[:, :na // m] = hv.reshape(m, -1)
+            self._proj("down", h, kd, rows["down"])
+            for nm, k, n in wl["shapes"]:
+                nbytes += weight_bytes(wl["dtype"], k, rows[nm]) + 4 * m * (k + rows[nm])
         else:
-            o.proj(dtype, x, ww, k, nrows)
-        return time.perf_counter() - t0
+            for nm, k, n in wl["shapes"]:
+                self._proj(nm, self.x, k, rows[nm])
+                nbytes += weight_bytes(wl["dtype"], k, rows[nm]) + 4 * m * (k + rows[nm])
+        return nbytes
 
-    t = run_once(rows)
-    per_row = max(t / rows, 1e-9)
-    nrows = int(min(n, max(rows, budget_s / per_row)))
-    w = synth.weight_blocks(dtype, min(nrows, 2048), k, rng)
-    t = run_once(nrows)
-    nbytes = weight_bytes(wl["dtype"], k, nrows) + 4 * m * (k + nrows)
-    kind = "reference" if ref is not None else "port"
-    sample = (f"{name} projection {k}->{nrows} of {n} rows, m={m}, "
-              f"{'reference GLSL shader compiled for the CPU (oracle/_ref)' if ref else 'C restatement (oracle)'}"
-              f", {t:.2f} s")
-    return nbytes / t / 1e9, kind, cores, sample
+    def describe(self):
+        return ("reference GLSL shaders compiled for the CPU (oracle/_ref)" if self.ref is not None
+                else "C restatement of the reference algorithm (oracle/)")
+
+
+def cpu_baseline(wl, min_seconds, rng):
+    """Full workload steps on the host cores, repeated until min_seconds of
+    CPU work; returns (GB/s, kind, cores, sample)."""
+    cr = CpuReference(wl, rng)
+    cr.step(0.02)  # warm (page in, thread pool)
+    t0 = time.perf_counter()
+    cr.step(0.05)
+    est_full = (time.perf_counter() - t0) / 0.05
+    frac = min(1.0, min_seconds / max(est_full, 1e-9))
+    nbytes, passes = 0, 0
+    t0 = time.perf_counter()
+    while True:
+        nbytes += cr.step(frac)
+        passes += 1
+        if time.perf_counter() - t0 >= min_seconds:
+            break
+    t = time.perf_counter() - t0
+    what = "full steps" if frac >= 1.0 else f"steps sampled to {frac:.1%} of each projection's rows"
+    sample = (f"{passes} {what} of {args_workload_desc(wl)}, {cr.describe()}, {t:.1f} s on {cr.cores} threads")
+    return nbytes / t / 1e9, cr.kind, cr.cores, sample
+
+
+def args_workload_desc(wl):
+    return ", ".join(f"{nm} {k}->{n}" for nm, k, n in wl["shapes"]) + f" (m={wl['m']})"
 
 
 # ---------------------------------------------------------------------------
@@ -220,21 +275,30 @@ def run_reference_arm(args):
     if rank != 0:
         return 0
     wl = WORKLOADS[args.workload]
-    rng = np.random.default_rng(0)
+    cr = CpuReference(wl, np.random.default_rng(0))
+    # each step: the workload's step, sampled to the rows that keep the whole
+    # run near 2 minutes of CPU time
+    cr.step(0.02)
+    t0 = time.perf_counter()
+    cr.step(0.05)
+    est_full = (time.perf_counter() - t0) / 0.05
+    frac = min(1.0, 120.0 / (args.warmup + args.steps) / max(est_full, 1e-9))
     vals = []
-    info = None
     for i in range(args.warmup + args.steps):
-        v, kind, cores, sample = cpu_reference_run(wl, 0.5, rng, use_ref=True)
+        t0 = time.perf_counter()
+        nb = cr.step(frac)
+        dt = time.perf_counter() - t0
         if i >= args.warmup:
-            vals.append(v)
-            info = (kind, cores, sample)
+            vals.append(nb / dt / 1e9)
     value = statistics.median(vals)
-    kind, cores, sample = info
+    kind, cores = cr.kind, cr.cores
+    what = "the full step" if frac >= 1.0 else f"the step sampled to {frac:.1%} of each projection's rows"
+    sample = f"per step {what} of {args_workload_desc(wl)}, {cr.describe()}, median of {args.steps} steps"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
-        "config": {"workload": args.workload, "baseline_config": wl["config"]},
+        "config": dict(workload_config(args.workload, wl), parallelism="host cores (rank 0 only)"),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -410,7 +474,7 @@ def main():
     if rank == 0:
         cpu = None
         if not args.no_cpu_baseline and world == 1:
-            v, kind, cores, sample = cpu_reference_run(wl, 5.0, np.random.default_rng(7), use_ref=True)
+            v, kind, cores, sample = cpu_baseline(wl, 10.0, np.random.default_rng(7))
             cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample}
         traffic = None
         try:
@@ -431,15 +495,9 @@ def main():
             "vs_baseline": None,
             "dtype": "q4k*f32" if wl["dtype"] == "q4k" else "q8_0*f32",
             "data": "synthetic (seeded; BASELINE block/activation distributions)",
-            "config": {
-                "workload": args.workload,
-                "baseline_config": wl["config"],
-                "m": m,
-                "projections": [f"{nm} {k}->{n}" for nm, k, n in wl["shapes"]],
-                "bytes_per_step": sb,
-                "l2": f"weights rotated through {pool} sets of {set_bytes / 1e6:.1f} MB (> 3x the 126 MB L2)",
-                "parallelism": f"replicas x{world} (independent token streams, no collective)",
-            },
+            "config": dict(workload_config(args.workload, wl),
+                           l2=f"weights rotated through {pool} sets of {set_bytes / 1e6:.1f} MB (> 3x the 126 MB L2)",
+                           parallelism=f"replicas x{world} (independent token streams, no collective)"),
             "roofline": {
                 "bound": "hbm",
                 "achieved": achieved,
