@@ -22,6 +22,7 @@
 // shared memory.  The k-index <-> element permutation of A and B is the same,
 // so the sum is the reference's dot product in a different association order.
 #include <algorithm>
+#include <mutex>
 
 #include "lc_internal.cuh"
 
@@ -1289,4 +1290,91 @@ extern "C" int lc_proj_quant(lc_ctx *ctx, int dtype, const float *x, const void 
 extern "C" int lc_proj_m(lc_ctx *ctx, int dtype, const float *x, const void *w, float *c, uint32_t m, uint32_t k,
                          uint32_t n, uint32_t expert_offset) {
     return proj_common(ctx, dtype, x, w, c, m, k, n, dtype == LC_Q4_K ? expert_offset : 0, "lc_proj_m");
+}
+
+// ---------------------------------------------------------------------------
+// Q4_K projection that allocates no device memory.
+//
+// lc_proj_q4k / lc_proj_m take their stream-K split-tile scratch from the
+// context's scratch pool, which grows with cudaMalloc on first use of a larger
+// shape.  Some callers cannot allocate on the call path: a serving loop whose
+// memory planner has already handed all of HBM to weights and the K/V cache
+// (a cudaMalloc there fails or fragments that plan), or a latency-bound decode
+// loop that must not pay cudaMalloc's implicit device-wide synchronisation,
+// which stalls every other stream on the GPU.  This variant runs the same
+// stream-K kernel with its scratch in a fixed static device array instead.
+//
+// Limits: m in 1..4 tokens, n <= kStaticMaxTiles * 16 rows, and the staged
+// activations of m * k must fit in shared memory.  The array must be all zero
+// when a launch starts; it is zero when the module loads and every completed
+// launch leaves it zero again (the last contributor to a split tile clears its
+// entries).  Calls that overlap on the GPU (two streams, or two contexts on one
+// device) share the array and race; callers serialise them.
+
+constexpr int kStaticMaxTiles = 4096;  // n <= 65536 rows
+constexpr size_t kStaticScratchBytes = (size_t)kStaticMaxTiles * 64 * 4 + (size_t)kStaticMaxTiles * 4;
+
+static __device__ __align__(256) unsigned char g_static_fixup[kStaticScratchBytes];
+
+namespace {
+
+std::mutex g_static_mu;
+void *g_static_ptr[64];  // per device ordinal, set up once with that device current
+
+// Set-up on the first call per device: resolve the array's device address.
+// That first call should come before any stream capture on the device.
+int static_fixup_ptr(lc_ctx *ctx, void **out) {
+    LC_REQUIRE(ctx->device >= 0 && ctx->device < 64, LC_ERR_INVALID, "static scratch: device %d out of range",
+               ctx->device);
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_ptr[ctx->device]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_fixup);
+        LC_REQUIRE(e == cudaSuccess && p, LC_ERR_CUDA, "static scratch: cudaGetSymbolAddress failed: %s",
+                   cudaGetErrorString(e));
+        g_static_ptr[ctx->device] = p;
+    }
+    *out = g_static_ptr[ctx->device];
+    return LC_OK;
+}
+
+}  // namespace
+
+extern "C" int lc_proj_q4k_static(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m, uint32_t k,
+                                  uint32_t n, uint32_t expert_offset) {
+    LC_REQUIRE(ctx, LC_ERR_INVALID, "lc_proj_q4k_static: null ctx");
+    if (m == 0 || n == 0) return LC_OK;
+    LC_REQUIRE(x && wv && c, LC_ERR_INVALID, "lc_proj_q4k_static: null pointer");
+    LC_REQUIRE(m <= 4, LC_ERR_UNSUPPORTED, "lc_proj_q4k_static: m=%u tokens, at most 4", m);
+    LC_REQUIRE(k > 0 && k % 256 == 0, LC_ERR_UNSUPPORTED, "lc_proj_q4k_static: k=%u is not a positive multiple of 256",
+               k);
+    LC_REQUIRE(expert_offset % 256 == 0, LC_ERR_UNSUPPORTED,
+               "lc_proj_q4k_static: expert_offset=%u not a multiple of 256", expert_offset);
+    LC_REQUIRE(n <= (uint32_t)kStaticMaxTiles * 16, LC_ERR_UNSUPPORTED,
+               "lc_proj_q4k_static: n=%u rows exceeds the static scratch limit of %d rows", n, kStaticMaxTiles * 16);
+    LC_REQUIRE(((uintptr_t)wv & 15) == 0, LC_ERR_INVALID, "lc_proj_q4k_static: weight pointer not 16-byte aligned");
+    int s = lc_use_device(ctx);
+    if (s) return s;
+    const size_t smem = ski_smem_bytes((int)m, (int)k);
+    LC_REQUIRE(smem + 8192 <= ctx->smem_optin, LC_ERR_UNSUPPORTED,
+               "lc_proj_q4k_static: m*k=%u*%u activations exceed shared memory (%zu of %zu bytes)", m, k, smem,
+               ctx->smem_optin);
+    void *base = nullptr;
+    s = static_fixup_ptr(ctx, &base);
+    if (s) return s;
+    Fixup fx;
+    fx.acc = (float *)base;
+    fx.cnt = (unsigned *)((char *)base + (size_t)kStaticMaxTiles * 64 * 4);
+    const uint8_t *w = (const uint8_t *)wv + (size_t)(expert_offset / 256) * 144;
+    const int T = (int)((n + 15) / 16);
+    const long long units = (long long)T * (k / 256);
+    const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, (units + 31) / 32));
+    switch (m) {
+    case 1: s = launch_q4k_sk<1>(ctx, grid, smem, x, w, c, k, n, fx); break;
+    case 2: s = launch_q4k_sk<2>(ctx, grid, smem, x, w, c, k, n, fx); break;
+    case 3: s = launch_q4k_sk<3>(ctx, grid, smem, x, w, c, k, n, fx); break;
+    default: s = launch_q4k_sk<4>(ctx, grid, smem, x, w, c, k, n, fx); break;
+    }
+    if (s) return s;
+    return lc_after_launch(ctx, "lc_proj_q4k_static");
 }

@@ -82,6 +82,7 @@ SIGNATURES = {
     "lc_proj_q4k": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32]),
     "lc_proj_quant": (_i, [_vp, _i, _vp, _vp, _vp, _u32, _u32, _u32]),
     "lc_proj_m": (_i, [_vp, _i, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
+    "lc_proj_q4k_static": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
     "lc_dequant": (_i, [_vp, _i, _vp, _sz, _sz, _vp]),
     "lc_rmsnorm": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _f]),
     "lc_qk_norm_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _f, _u32]),
@@ -249,6 +250,10 @@ class Context:
 
     def proj_m(self, dtype, x, w, c, m, k, n, expert_offset=0):
         check(self.L.lc_proj_m(self.h, dtype, ptr(x), ptr(w), ptr(c), m, k, n, expert_offset), "lc_proj_m")
+
+    def proj_q4k_static(self, x, w, c, m, k, n, expert_offset=0):
+        check(self.L.lc_proj_q4k_static(self.h, ptr(x), ptr(w), ptr(c), m, k, n, expert_offset),
+              "lc_proj_q4k_static")
 
     def dequant(self, dtype, src, src_bytes, n, out):
         check(self.L.lc_dequant(self.h, dtype, ptr(src), src_bytes, n, ptr(out)), "lc_dequant")
