@@ -92,6 +92,11 @@ void *lc_get_stream(lc_ctx *ctx);
 int lc_synchronize(lc_ctx *ctx);
 /* 1: every compute call waits for completion (reference behaviour); 0: async. */
 int lc_set_sync(lc_ctx *ctx, int sync);
+/* Wait for the context's stream, then report (and clear) the device status
+ * word: LC_ERR_TIMEOUT if a kernel's bounded wait on its own asynchronous
+ * copies gave up (the launch's outputs are then invalid), else LC_OK.  Kernels
+ * never hang on such a wait; this call is how the host learns of it. */
+int lc_device_status(lc_ctx *ctx);
 /* LC_HALF_REF (default) or LC_HALF_IEEE for every f16 scale decode. */
 int lc_set_half_mode(lc_ctx *ctx, int mode);
 /* Device the context runs on. */

@@ -20,7 +20,13 @@ struct lc_ctx {
     // Grow-only scratch slots (see LC_SCRATCH_*).
     void *scratch[8] = {};
     size_t scratch_bytes[8] = {};
+    // Device word that kernels set (atomicOr of LC_DEV_*) when a bounded wait
+    // gives up; read and cleared by lc_device_status().  Allocated at init.
+    unsigned *dev_status = nullptr;
 };
+
+// Bits of lc_ctx::dev_status.
+enum { LC_DEV_WAIT_TIMEOUT = 1u };
 
 struct lc_buf {
     lc_ctx *ctx = nullptr;

@@ -21,10 +21,17 @@
 // order (x_pack_* kernels, a few KB); every CTA copies the part it needs into
 // shared memory.  The k-index <-> element permutation of A and B is the same,
 // so the sum is the reference's dot product in a different association order.
+#include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <map>
 #include <mutex>
 
 #include "lc_internal.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace {
 
@@ -385,26 +392,6 @@ struct Fixup {
     unsigned *cnt;    // [tiles]
 };
 
-// The raw bytes of one 256-element super-block for rows g and g+8 of a 16-row
-// tile: headers (d, dmin, 12 scale bytes) and nibble group t (bytes 32t..32t+31
-// of the 128, i.e. sub-blocks 2t -- low nibbles -- and 2t+1 -- high nibbles).
-struct Q4UnitG {
-    uint4 H0, H1, A0, B0, A1, B1;
-    __device__ __forceinline__ void load(const uint8_t *b0, const uint8_t *b1, int t) {
-        H0 = H1 = A0 = B0 = A1 = B1 = make_uint4(0, 0, 0, 0);
-        if (b0) {
-            H0 = ldg_stream(b0);
-            A0 = ldg_stream(b0 + 16 + 32 * t);
-            B0 = ldg_stream(b0 + 32 + 32 * t);
-        }
-        if (b1) {
-            H1 = ldg_stream(b1);
-            A1 = ldg_stream(b1 + 16 + 32 * t);
-            B1 = ldg_stream(b1 + 32 + 32 * t);
-        }
-    }
-};
-
 // ---------------------------------------------------------------------------
 // Integer tensor-core path (m <= 4 tokens).
 //
@@ -505,13 +492,6 @@ __device__ __forceinline__ float2 scales2_f32(uint32_t h2, uint32_t ref_mask) {
     return __half22float2(lc_u32_as_h2(fixed));
 }
 
-// Two 6-bit values in bytes 0 / 1 -> floats, exactly (PRMT to 1024 + v halves).
-__device__ __forceinline__ float2 u6pair_f32(uint32_t v2) {
-    const __half2 h = __hsub2(lc_u32_as_h2(__byte_perm(v2, 0x64646464u, 0x4140)),
-                              __half2(__float2half_rn(1024.f), __float2half_rn(1024.f)));
-    return __half22float2(h);
-}
-
 __device__ __forceinline__ void lc_imma_u8s8_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -530,67 +510,6 @@ __device__ __forceinline__ void lc_imma_s8s8_z(int (&d)[4], uint32_t a0, uint32_
 
 __device__ __forceinline__ uint32_t dig4(const int8_t *dig, size_t idx) {
     return *reinterpret_cast<const uint32_t *>(dig + idx);
-}
-
-// One Q4_K super-block of a 16-row tile, integer MMAs.  tbl: this lane's
-// entry of the super-block's table [8 MMAs][M][8] (zero block for non-owner
-// lanes); sb4: float4 (Sx, inv of sub-block 2t, Sx, inv of 2t+1) of token 0,
-// tokens sb4_stride float4 apart.
-template <int M>
-__device__ __forceinline__ void q4k_unit_int(const Q4UnitG &U, const uint2 *tbl, const float4 *sb4, int sb4_stride,
-                                             uint32_t ref_mask, int t, float (&y)[M][2]) {
-    int c[2][M][4];
-#pragma unroll
-    for (int half = 0; half < 2; half++) {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint4 &Pg = i < 2 ? U.A0 : U.B0;
-            const uint4 &Pg8 = i < 2 ? U.A1 : U.B1;
-            uint32_t w0g = (i & 1) ? Pg.z : Pg.x, w1g = (i & 1) ? Pg.w : Pg.y;
-            uint32_t w0g8 = (i & 1) ? Pg8.z : Pg8.x, w1g8 = (i & 1) ? Pg8.w : Pg8.y;
-            if (half) {
-                w0g >>= 4;
-                w1g >>= 4;
-                w0g8 >>= 4;
-                w1g8 >>= 4;
-            }
-            const uint32_t a0 = w0g & 0x0F0F0F0Fu, a2 = w1g & 0x0F0F0F0Fu;
-            const uint32_t a1 = w0g8 & 0x0F0F0F0Fu, a3 = w1g8 & 0x0F0F0F0Fu;
-#pragma unroll
-            for (int j = 0; j < M; j++) {
-                const uint2 b = tbl[((half * 4 + i) * M + j) * 8];
-                if (i == 0)
-                    lc_imma_u8s8_z(c[half][j], a0, a1, a2, a3, b.x, b.y);
-                else
-                    lc_imma_u8s8(c[half][j], a0, a1, a2, a3, b.x, b.y);
-            }
-        }
-    }
-    // per row: scales / mins of sub-blocks 2t (lo nibbles) and 2t+1 (hi nibbles)
-    // (get_scale_min_k4, proj_q4k.comp:113-125; t >= 2 uses the j >= 4 packing)
-    const int sh = 16 * (t & 1);
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-        const uint4 H = r ? U.H1 : U.H0;
-        const float2 dd = scales2_f32(H.x, ref_mask);  // (d, dmin)
-        const uint32_t yy = H.y >> sh, zz = H.z >> sh, ww = H.w >> sh;
-        const uint32_t sc_b = (ww & 0x0F0Fu) | ((yy >> 2) & 0x3030u);
-        const uint32_t mn_b = ((ww >> 4) & 0x0F0Fu) | ((zz >> 2) & 0x3030u);
-        const float2 sc = u6pair_f32(t < 2 ? (yy & 0x3F3Fu) : sc_b);
-        const float2 mn = u6pair_f32(t < 2 ? (zz & 0x3F3Fu) : mn_b);
-        const float ds_lo = dd.x * sc.x, ds_hi = dd.x * sc.y;
-        const float dm_lo = dd.y * mn.x, dm_hi = dd.y * mn.y;
-#pragma unroll
-        for (int j = 0; j < M; j++) {
-            const float4 f = sb4[j * sb4_stride];  // Sx_lo, inv_lo, Sx_hi, inv_hi
-            const float s_lo = fmaf(i2f_small(c[0][j][2 * r]), 256.f, i2f_small(c[0][j][2 * r + 1]));
-            const float s_hi = fmaf(i2f_small(c[1][j][2 * r]), 256.f, i2f_small(c[1][j][2 * r + 1]));
-            float v = fmaf(ds_lo * f.y, s_lo, y[j][r]);
-            v = fmaf(ds_hi * f.w, s_hi, v);
-            v = fmaf(-dm_lo, f.x, v);
-            y[j][r] = fmaf(-dm_hi, f.z, v);
-        }
-    }
 }
 
 // Write (or accumulate) rows g, g+8 of `tile` for the finished part
@@ -643,92 +562,365 @@ __device__ __forceinline__ void skm_flush(float (&y)[M][2], int tile, int sb_a, 
     if (lane == 0) atomicExch(fx.cnt + tile, 0u);
 }
 
-// Persistent stream-K Q4_K projection for M <= 4 tokens.  One CTA per SM
-// digitises x into shared memory and builds the B table for the whole K,
-// then its warps walk equal shares of the flattened (16-row tile,
-// super-block) unit space, prefetching the next unit's bytes while the tensor
-// cores work on the current one.  A tile whose super-blocks are split between
-// warps is summed in `fx.acc` with atomics; the warp that completes the tile's
-// count writes the rows and leaves fx.acc / fx.cnt zero for the next call.
+// ---------------------------------------------------------------------------
+// Bulk asynchronous copies into shared memory (cp.async.bulk, completion on an
+// mbarrier).  Every wait is bounded: after kWaitSpins polls the waiter records
+// LC_DEV_WAIT_TIMEOUT in the context's status word and gives up.
+
+constexpr uint32_t kWaitSpins = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase of `bar` with the given parity; false if the bound ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_test(bar, parity)) return true;
+    for (uint32_t i = 0; i < kWaitSpins; ++i)
+        if (mbar_test(bar, parity)) return true;
+    return false;
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+    return p;
+}
+
+// Orders this thread's earlier generic-proxy accesses of shared memory before
+// later async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(const void *p) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(smem_addr(p)));
+    return v;
+}
+
+// 2D tensor copy global -> shared (TMA, tile mode) of the box at element
+// coordinates (x, y) of `tm`, completing on `bar`; evict-first in L2.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, int x, int y, uint64_t *bar,
+                                            uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;\n" ::"r"(smem_addr(dst)),
+        "l"(tm), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(pol)
+        : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Q4_K GEMV for m <= 4 tokens, weights streamed by TMA.
+//
+// The weight matrix is a 2D tensor of n rows x (k/256 * 18) u64 words; one
+// TMA box is 16 rows x 18 words = one super-block of a 16-row tile (a "unit",
+// 2304 B), written to shared memory with a 144-byte row stride.
+//
+// Work split: CTAs run in clusters of kTmaCluster (one CTA per SM).  Each
+// cluster owns a contiguous range of whole 16-row tiles (balanced to one
+// tile); the cluster's units, flattened tile-major, are cut into one
+// contiguous range per CTA and per warp.  A warp keeps R units requested
+// ahead in its own ring (lane 0 issues one TMA per unit), accumulates the
+// units of one tile in registers and, when the tile changes, adds the partial
+// into the shared-memory accumulator of the tile's owner CTA in the cluster
+// (distributed shared memory, f32 atomics).  After a cluster barrier each CTA
+// stores the tiles it owns.  No split tile crosses a cluster, so nothing goes
+// through global memory but the outputs.
+//
+// Activations: one scale per (token, super-block): x ~= xi * inv with
+// xi = rint(x * 32639 / max|x|) in 16 bits, split into s8 digits
+// xi = 256 * hi + lo.  The MMAs (u8 nibbles x s8 digits -> s32) give each
+// thread the per-sub-block sums of its own two sub-blocks (2t: low nibbles,
+// 2t+1: high nibbles masked in place, i.e. 16x); the 6-bit scales and mins
+// are applied in integers:
+//   y += d*inv/16 * (256 * A_hi + A_lo) - dmin*inv * B,
+//   A_digit = 16*sc_2t*C_2t + sc_2t+1*C16_2t+1,  B = m_2t*X_2t + m_2t+1*X_2t+1,
+// with X_s the integer sum of xi over sub-block s.  All integer terms stay
+// below 2^31 (|C| <= 32*15*128, sc, m <= 63, |X| <= 32*32639).
+constexpr int kTmaUnit = 16 * 144;
+
+struct TmaLayout {
+    size_t ring, tab, xs, invs, zero, tacc, bars, total;
+};
+
+// Shared memory for NW warps, R stages each, m tokens, k, and at most `tl`
+// tiles per cluster:
+//   ring  [NW][R][16 rows][144 B]     (128-byte aligned TMA destinations)
+//   tab   uint2 [S][8 MMAs][m][8 lanes]   digit fragments (see the prologue)
+//   xs    int   [m][S][8]                 X of each sub-block
+//   invs  float [m][S]
+//   zero  uint2 [8][m][8]                 B fragment of lanes without one
+//   tacc  float [tl][16][m]               tile sums (tiles this CTA owns)
+//   bars  uint64 [NW][R]
+__host__ __device__ __forceinline__ TmaLayout q4t_layout(int nw, int m, int k, int R, int tl) {
+    TmaLayout L;
+    const size_t S = (size_t)k / 256;
+    L.ring = 0;
+    L.tab = L.ring + (size_t)nw * R * kTmaUnit;
+    L.xs = L.tab + S * 64 * m * 8;
+    L.invs = L.xs + (size_t)m * S * 32;
+    L.zero = (L.invs + (size_t)m * S * 4 + 15) & ~(size_t)15;
+    L.tacc = L.zero + (size_t)64 * m * 8;
+    L.bars = (L.tacc + (size_t)tl * 16 * m * 4 + 7) & ~(size_t)7;
+    L.total = L.bars + (size_t)nw * R * 8 + 128;  // + slack to 128-align the base
+    return L;
+}
+
+// Add a warp's partial of one tile (rows g, g+8 per thread, summed over the
+// thread's sub-blocks) into the tile's accumulator `ta` in the owner CTA's
+// shared memory (possibly this CTA's), and clear the partial.
 template <int M>
-__global__ void __launch_bounds__(kSkWarps * 32, 1) q4k_sk_kernel(const float *__restrict__ x,
-                                                                  const uint8_t *__restrict__ w,
-                                                                  float *__restrict__ y, int k, int n,
-                                                                  int half_mode, Fixup fx) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    const int S = k >> 8;  // super-blocks per row
-    float *xs = reinterpret_cast<float *>(smem);
-    uint2 *tab = reinterpret_cast<uint2 *>(smem);  // replaces xs: [S][8][M][8]
-    int8_t *dig = reinterpret_cast<int8_t *>(smem + (size_t)M * k * 4);
-    float2 *sbi = reinterpret_cast<float2 *>(smem + (size_t)M * k * 6);
-    __shared__ __align__(16) uint2 zbuf[8 * M * 8];
+__device__ __forceinline__ void q4t_tile_add(float (&acc)[M][2], float *ta, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int j = 0; j < M; j++) {
+        float a = acc[j][0], b = acc[j][1];
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        a += __shfl_xor_sync(0xffffffffu, a, 2);
+        b += __shfl_xor_sync(0xffffffffu, b, 1);
+        b += __shfl_xor_sync(0xffffffffu, b, 2);
+        if (t == j) {
+            atomicAdd(ta + g * M + j, a);
+            atomicAdd(ta + (g + 8) * M + j, b);
+        }
+        acc[j][0] = acc[j][1] = 0.f;
+    }
+}
+
+// Prologue: one warp per (token j, super-block sb).  Lane l converts elements
+// 8l..8l+7 of the super-block, which are exactly the 8 k positions of table
+// entry (MMA half*4 + i, owner t) with t = l/8, half = (l/4)&1, i = l&3; it
+// writes that entry's hi (e = 2t) and lo (e = 2t+1) digit words and, with its
+// 3 neighbours, the integer sum of sub-block l/4 = 2t + half.
+template <int M, int NW>
+__device__ __forceinline__ void q4t_prologue(const float *__restrict__ x, int k, uint2 *tab, int *xs, float *invs) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int S = k >> 8;
+    const bool vec = (((uintptr_t)x) & 15) == 0;
+    for (int it = warp; it < M * S; it += NW) {
+        const int j = it / S, sb = it - j * S;
+        const float *xp = x + (size_t)j * k + (size_t)sb * 256 + 8 * lane;
+        float v[8];
+        if (vec) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(xp));
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(xp) + 1);
+            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = __ldg(xp + e);
+        }
+        float mx = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) mx = fmaxf(mx, fabsf(v[e]));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const bool fin = mx < INFINITY;  // false for inf / nan
+        const float scale = (mx > 0.f && fin) ? 32639.f / mx : 0.f;
+        const float inv = mx > 0.f ? (fin ? mx * (1.f / 32639.f) : __int_as_float(0x7FC00000)) : 0.f;
+        uint32_t h[2] = {0u, 0u}, l[2] = {0u, 0u};
+        int sum = 0;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int xi = __float2int_rn(v[e] * scale);
+            const int hi = (xi + 128) >> 8;
+            const int lo = xi - (hi << 8);
+            sum += xi;
+            h[e >> 2] |= (uint32_t)(hi & 0xFF) << (8 * (e & 3));
+            l[e >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (e & 3));
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        const int t = lane >> 3, half = (lane >> 2) & 1, i = lane & 3;
+        uint2 *ent = tab + ((size_t)(sb * 8 + half * 4 + i) * M + j) * 8 + 2 * t;
+        ent[0] = make_uint2(h[0], h[1]);
+        ent[1] = make_uint2(l[0], l[1]);
+        // xs[(j*S + sb)*8 + 2t + half]: the pair (X_2t, X_2t+1) of owner t is one int2
+        if ((lane & 3) == 0) xs[((size_t)j * S + sb) * 8 + (lane >> 2)] = sum;
+        if (lane == 0) invs[(size_t)j * S + sb] = inv;
+    }
+}
+
+// One unit from shared memory: rows g, g+8 of the stage at `st`.
+template <int M>
+__device__ __forceinline__ void q4t_unit(const uint8_t *st, const uint2 *tbl, const int2 *xs2, const float *inv_s,
+                                         int S, uint32_t ref_mask, int g, int t, float (&y)[M][2]) {
+    const uint8_t *r0 = st + g * 144, *r1 = st + (g + 8) * 144;
+    const uint4 H0 = lds128(r0), H1 = lds128(r1);
+    const uint4 A0 = lds128(r0 + 16 + 32 * t), B0 = lds128(r0 + 32 + 32 * t);
+    const uint4 A1 = lds128(r1 + 16 + 32 * t), B1 = lds128(r1 + 32 + 32 * t);
+    int c[2][M][4];
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        const uint32_t mask = half ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint4 &Pg = i < 2 ? A0 : B0;
+            const uint4 &Pg8 = i < 2 ? A1 : B1;
+            const uint32_t a0 = ((i & 1) ? Pg.z : Pg.x) & mask, a2 = ((i & 1) ? Pg.w : Pg.y) & mask;
+            const uint32_t a1 = ((i & 1) ? Pg8.z : Pg8.x) & mask, a3 = ((i & 1) ? Pg8.w : Pg8.y) & mask;
+#pragma unroll
+            for (int j = 0; j < M; j++) {
+                const uint2 b = tbl[((half * 4 + i) * M + j) * 8];
+                if (i == 0)
+                    lc_imma_u8s8_z(c[half][j], a0, a1, a2, a3, b.x, b.y);
+                else
+                    lc_imma_u8s8(c[half][j], a0, a1, a2, a3, b.x, b.y);
+            }
+        }
+    }
+    // scales / mins of sub-blocks 2t and 2t+1 (get_scale_min_k4,
+    // proj_q4k.comp:46-58): t < 2 reads bytes q[2t], q[2t+1] (& 63) and
+    // q[2t+4], q[2t+5]; t >= 2 combines q[2t+4..] nibbles with the top bits
+    // of q[2t-4..] and q[2t..].
+    const int sh = 16 * (t & 1);
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const uint4 H = r ? H1 : H0;
+        const float2 dd = scales2_f32(H.x, ref_mask);  // (d, dmin)
+        const uint32_t yy = H.y >> sh, zz = H.z >> sh, ww = H.w >> sh;
+        const uint32_t scw = t < 2 ? (yy & 0x3F3Fu) : ((ww & 0x0F0Fu) | ((yy >> 2) & 0x3030u));
+        const uint32_t mnw = t < 2 ? (zz & 0x3F3Fu) : (((ww >> 4) & 0x0F0Fu) | ((zz >> 2) & 0x3030u));
+        const int sc0x16 = (int)(scw & 0xFFu) << 4, sc1 = (int)((scw >> 8) & 0xFFu);
+        const int mn0 = (int)(mnw & 0xFFu), mn1 = (int)((mnw >> 8) & 0xFFu);
+#pragma unroll
+        for (int j = 0; j < M; j++) {
+            const int2 X = xs2[(size_t)j * S * 4];
+            const float inv = inv_s[(size_t)j * S];
+            const int a_hi = sc0x16 * c[0][j][2 * r] + sc1 * c[1][j][2 * r];
+            const int a_lo = sc0x16 * c[0][j][2 * r + 1] + sc1 * c[1][j][2 * r + 1];
+            const int bm = mn0 * X.x + mn1 * X.y;
+            const float a = fmaf(__int2float_rn(a_hi), 256.f, __int2float_rn(a_lo));
+            float v = fmaf(dd.x * inv * 0.0625f, a, y[j][r]);
+            y[j][r] = fmaf(-dd.y * inv, __int2float_rn(bm), v);
+        }
+    }
+}
+
+template <int M, int NW, int CL>
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NW * 32, 1)
+    q4k_tma_kernel(const __grid_constant__ CUtensorMap tm, const float *__restrict__ x, float *__restrict__ y, int k,
+                   int n, int half_mode, int R, int tl, unsigned *__restrict__ status) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    // The same offset on every CTA (the dynamic window starts at the same
+    // shared address), so a partner's accumulator is at our own offset.
+    unsigned char *smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
+    cg::cluster_group cluster = cg::this_cluster();
+    const int S = k >> 8;
+    const TmaLayout L = q4t_layout(NW, M, k, R, tl);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const size_t rowbytes = (size_t)S * 144;
+    uint8_t *ring = smem + L.ring + (size_t)warp * R * kTmaUnit;
+    uint2 *tab = reinterpret_cast<uint2 *>(smem + L.tab);
+    int *xs = reinterpret_cast<int *>(smem + L.xs);
+    float *invs = reinterpret_cast<float *>(smem + L.invs);
+    uint2 *zbuf = reinterpret_cast<uint2 *>(smem + L.zero);
+    float *tacc = reinterpret_cast<float *>(smem + L.tacc);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * R;
+
+    // cluster -> whole tiles; CTA -> contiguous units; warp -> contiguous units
+    const int rank = (int)cluster.block_rank();
+    const int C = gridDim.x / CL, cid = blockIdx.x / CL;
     const int T = (n + 15) >> 4;
-    const long long TS = (long long)T * S;
-    const long long Wt = (long long)gridDim.x * kSkWarps;
-    const long long wid = (long long)blockIdx.x * kSkWarps + warp;
-    const long long u0 = TS * wid / Wt;
-    const int n_units = (int)(TS * (wid + 1) / Wt - u0);
-    int tile = (int)(u0 / S), sub = (int)(u0 % S);
+    const int tc0 = (int)((long long)T * cid / C), tc1 = (int)((long long)T * (cid + 1) / C);
+    const int uc0 = tc0 * S, ucn = (tc1 - tc0) * S;
+    const int U0 = uc0 + (int)((long long)ucn * rank / CL), U1 = uc0 + (int)((long long)ucn * (rank + 1) / CL);
+    const int w0 = U0 + (int)((long long)(U1 - U0) * warp / NW);
+    const int my_units = U0 + (int)((long long)(U1 - U0) * (warp + 1) / NW) - w0;
 
-    // Start streaming the first two units' weights before the prologue.
-    int pt = tile, ps = sub, loaded = 0;
-    auto load_next = [&](Q4UnitG &U) {
-        if (loaded >= n_units) return;
-        const int rg = pt * 16 + g, rg8 = rg + 8;
-        U.load(rg < n ? w + (size_t)rg * rowbytes + (size_t)ps * 144 : nullptr,
-               rg8 < n ? w + (size_t)rg8 * rowbytes + (size_t)ps * 144 : nullptr, t);
-        if (++ps == S) ps = 0, ++pt;
-        ++loaded;
+    if (lane < R) mbar_init(bars + lane, 1);
+    mbar_init_fence();
+    __syncwarp();
+    const uint64_t pol = l2_evict_first_policy();
+    int issued = 0, istage = 0, itile = w0 / S, isb = w0 - (w0 / S) * S;
+    auto issue = [&]() {
+        if (lane == 0) {
+            mbar_expect_tx(bars + istage, kTmaUnit);
+            tma_load_2d(ring + (size_t)istage * kTmaUnit, &tm, isb * 18, itile * 16, bars + istage, pol);
+        }
+        if (++istage == R) istage = 0;
+        if (++isb == S) isb = 0, ++itile;
+        ++issued;
     };
-    Q4UnitG A, B, C;  // three units in flight per warp
-    load_next(A);
-    load_next(B);
-    load_next(C);
+    const int first = min(R, my_units);
+    for (int q = 0; q < first; q++) issue();
 
-    for (int i = threadIdx.x; i < 8 * M * 8; i += blockDim.x) zbuf[i] = make_uint2(0u, 0u);
-    ski_prologue(x, M, k, xs, dig, sbi);
-    // Table entry (sub, mma = half*4 + i, token j, e = 2*owner + digit): the
-    // owner's 8 k positions are elements 256sub + 64owner + 32half + 8i + 0..7.
-    for (int idx = threadIdx.x; idx < S * 8 * M * 8; idx += blockDim.x) {
-        const int e = idx & 7;
-        const int j = (idx >> 3) % M;
-        const int mm = (idx / (8 * M)) & 7;
-        const int sb = idx / (64 * M);
-        const int to = e >> 1, dg = e & 1, half = mm >> 2, i = mm & 3;
-        const size_t base = ((size_t)j * 2 + dg) * k + (size_t)sb * 256 + 64 * to + 32 * half + 8 * i;
-        tab[idx] = make_uint2(dig4(dig, base), dig4(dig, base + 4));
-    }
-    __syncthreads();
+    for (int i = threadIdx.x; i < 64 * M; i += blockDim.x) zbuf[i] = make_uint2(0u, 0u);
+    for (int i = threadIdx.x; i < tl * 16 * M; i += blockDim.x) tacc[i] = 0.f;
+    q4t_prologue<M, NW>(x, k, tab, xs, invs);
+    // every CTA's accumulators are zero before any partner adds into them
+    cluster.sync();
 
-    // Lanes that carry no B fragment (g / 2 != t) read a zero block instead,
-    // so the k-step loop has no predicate.
     const bool own = (g >> 1) == t;
-    const int sb4_stride = k >> 6;  // float4 per token
+    const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
+    const int2 *xs2 = reinterpret_cast<const int2 *>(xs) + t;
     float acc[M][2];
 #pragma unroll
     for (int j = 0; j < M; j++) acc[j][0] = acc[j][1] = 0.f;
-    const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
-    int seg0 = sub, done = 0;
-    auto step = [&](Q4UnitG &U) {
-        const uint2 *tbl = own ? tab + (size_t)sub * 64 * M + g : zbuf;
-        q4k_unit_int<M>(U, tbl, reinterpret_cast<const float4 *>(sbi) + sub * 4 + t, sb4_stride, ref_mask, t, acc);
-        load_next(U);  // U's registers are free again: refill with the unit three ahead
-        ++done;
-        if (sub == S - 1 || done == n_units) {
-            skm_flush<M>(acc, tile, seg0, sub + 1, S, n, y, fx, lane);
-            seg0 = 0;
-        }
-        if (++sub == S) sub = 0, ++tile;
+    int tile = w0 / S, sb = w0 - (w0 / S) * S, s = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    auto tile_acc = [&](int tl_) {  // accumulator of cluster tile tl_ in its owner CTA
+        return cluster.map_shared_rank(tacc, tl_ % CL) + (size_t)(tl_ / CL) * 16 * M;
     };
-    while (done < n_units) {
-        step(A);
-        if (done == n_units) break;
-        step(B);
-        if (done == n_units) break;
-        step(C);
+    for (int q = 0; q < my_units; q++) {
+        // all lanes wait on the same barrier; the vote keeps the outcome warp-uniform
+        if (!__all_sync(0xffffffffu, mbar_wait(bars + s, phase))) {
+            ok = false;
+            break;
+        }
+        const uint2 *tbl = own ? tab + (size_t)sb * 64 * M + g : zbuf;
+        q4t_unit<M>(ring + (size_t)s * kTmaUnit, tbl, xs2 + (size_t)sb * 4, invs + sb, S, ref_mask, g, t, acc);
+        // the stage's bytes are consumed: hand it to the next copy
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (issued < my_units) issue();
+        if (++s == R) s = 0, phase ^= 1u;
+        if (++sb == S || q == my_units - 1) {
+            q4t_tile_add<M>(acc, tile_acc(tile - tc0), lane);
+            if (sb == S) sb = 0, ++tile;
+        }
+    }
+    if (!ok) {
+        // A wait gave up: record it, then let this warp's copies in flight
+        // land (bounded) before the CTA's shared memory is released.
+        if (lane == 0) atomicOr(status, LC_DEV_WAIT_TIMEOUT);
+        for (int st = 0; st < R; st++) {
+            const int last = issued - 1 - ((issued - 1 - st) % R + R) % R;  // newest unit issued to stage st
+            if (last >= 0) mbar_wait(bars + st, (uint32_t)(last / R) & 1u);
+        }
+    }
+    // all partials have landed in their owners' accumulators
+    cluster.sync();
+    for (int lt = rank; lt < tc1 - tc0; lt += CL) {
+        const float *ta = tacc + (size_t)(lt / CL) * 16 * M;
+        for (int idx = threadIdx.x; idx < 16 * M; idx += blockDim.x) {
+            const int r = idx / M, j = idx - r * M, row = (tc0 + lt) * 16 + r;
+            if (row < n) y[(size_t)j * n + row] = ta[idx];
+        }
     }
 }
 
@@ -1084,13 +1276,131 @@ int launch_q4k(lc_ctx *ctx, const uint2 *tab, const float *inv_scale, const uint
     return LC_OK;
 }
 
-template <int M>
-int launch_q4k_sk(lc_ctx *ctx, int grid, size_t smem, const float *x, const uint8_t *w, float *c, uint32_t k,
-                  uint32_t n, Fixup fx) {
-    int s = set_smem(q4k_sk_kernel<M>, smem);
-    if (s) return s;
-    q4k_sk_kernel<M><<<grid, kSkWarps * 32, smem, ctx->stream>>>(x, w, c, (int)k, (int)n, ctx->half_mode, fx);
+// TMA tensor maps are encoded with the driver's cuTensorMapEncodeTiled,
+// resolved once through the runtime (no link-time dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+std::once_flag g_encode_once;
+
+int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000 *out) {
+    std::call_once(g_encode_once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode_tiled = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    });
+    LC_REQUIRE(g_encode_tiled, LC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    *out = g_encode_tiled;
     return LC_OK;
+}
+
+// Q4_K weights [n rows][k/256 super-blocks] as a 2D tensor of u64 words with
+// 16-row x one-super-block boxes.  Rows past n read as zero.
+int q4k_tensor_map(CUtensorMap *tm, const void *w, uint32_t k, uint32_t n) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+    int s = tensor_map_encoder(&enc);
+    if (s) return s;
+    const cuuint64_t S = k / 256;
+    cuuint64_t dims[2] = {S * 18, (cuuint64_t)n};
+    cuuint64_t strides[1] = {S * 144};
+    cuuint32_t box[2] = {18, 16};
+    cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    LC_REQUIRE(r == CUDA_SUCCESS, LC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for k=%u n=%u", (int)r, k, n);
+    return LC_OK;
+}
+
+constexpr int kTmaWarps = 16;
+constexpr int kTmaCluster = 4;
+constexpr int kTmaMaxStages = 4;
+
+// Launch geometry of the TMA GEMV: clusters, ring depth, tiles per cluster.
+struct TmaPlan {
+    int grid = 0, R = 0, tl = 0;
+    size_t smem = 0;
+};
+
+template <int M>
+int q4k_tma_max_clusters(size_t smem) {
+    static std::mutex mu;
+    static std::map<std::pair<int, size_t>, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find({dev, smem});
+    if (it != cache.end()) return it->second;
+    int s = set_smem(q4k_tma_kernel<M, kTmaWarps, kTmaCluster>, smem);
+    if (s) return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kTmaCluster * 64, 1, 1);
+    cfg.blockDim = dim3(kTmaWarps * 32, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    int nc = 0;
+    if (cudaOccupancyMaxActiveClusters(&nc, q4k_tma_kernel<M, kTmaWarps, kTmaCluster>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        nc = 0;
+    }
+    cache[{dev, smem}] = nc;
+    return nc;
+}
+
+int q4k_tma_max_clusters_m(int m, size_t smem) {
+    switch (m) {
+    case 1: return q4k_tma_max_clusters<1>(smem);
+    case 2: return q4k_tma_max_clusters<2>(smem);
+    case 3: return q4k_tma_max_clusters<3>(smem);
+    default: return q4k_tma_max_clusters<4>(smem);
+    }
+}
+
+// R = 0 when the shapes do not fit (the caller falls back).
+TmaPlan q4k_tma_plan(const lc_ctx *ctx, int m, int k, int n) {
+    TmaPlan p;
+    const int T = (n + 15) / 16;
+    if ((long long)T * (k / 256) >= (1ll << 31)) return p;
+    const int c_sms = std::max(1, ctx->num_sms / kTmaCluster);
+    for (int R = kTmaMaxStages; R >= 2; R--) {
+        const int C0 = std::min(T, c_sms);
+        const int tl = (T + C0 - 1) / C0;
+        const size_t b = q4t_layout(kTmaWarps, m, k, R, tl).total;
+        if (b > ctx->smem_optin) continue;
+        // only as many clusters as can be resident at once (one wave)
+        const int nc = q4k_tma_max_clusters_m(m, b);
+        if (nc <= 0) return p;
+        const int C = std::min(C0, nc);
+        p.tl = (T + C - 1) / C;
+        p.smem = q4t_layout(kTmaWarps, m, k, R, p.tl).total;
+        p.grid = C * kTmaCluster;
+        p.R = R;
+        return p;
+    }
+    return p;
+}
+
+template <int M>
+int launch_q4k_tma_m(lc_ctx *ctx, const TmaPlan &p, const CUtensorMap &tm, const float *x, float *c, uint32_t k,
+                     uint32_t n) {
+    int s = set_smem(q4k_tma_kernel<M, kTmaWarps, kTmaCluster>, p.smem);
+    if (s) return s;
+    q4k_tma_kernel<M, kTmaWarps, kTmaCluster><<<p.grid, kTmaWarps * 32, p.smem, ctx->stream>>>(
+        tm, x, c, (int)k, (int)n, ctx->half_mode, p.R, p.tl, ctx->dev_status);
+    return LC_OK;
+}
+
+// The TMA GEMV for m = 1..4 tokens.
+int launch_q4k_tma(lc_ctx *ctx, const TmaPlan &p, uint32_t m, const float *x, const uint8_t *w, float *c,
+                   uint32_t k, uint32_t n) {
+    CUtensorMap tm;
+    int s = q4k_tensor_map(&tm, w, k, n);
+    if (s) return s;
+    switch (m) {
+    case 1: return launch_q4k_tma_m<1>(ctx, p, tm, x, c, k, n);
+    case 2: return launch_q4k_tma_m<2>(ctx, p, tm, x, c, k, n);
+    case 3: return launch_q4k_tma_m<3>(ctx, p, tm, x, c, k, n);
+    default: return launch_q4k_tma_m<4>(ctx, p, tm, x, c, k, n);
+    }
 }
 
 template <int M>
@@ -1123,6 +1433,10 @@ int launch_q8(lc_ctx *ctx, const uint2 *tab, const float *inv_scale, const uint8
 
 namespace lc {
 
+int proj_q4k_tiled(lc_ctx *ctx, const float *x, const uint8_t *w, float *c, uint32_t m, uint32_t k, uint32_t n,
+                   void *pack);
+size_t q4k_pack_bytes(uint32_t m_group, uint32_t k);
+
 // One launch group handles up to 16 tokens (NT = 4 n-tiles).
 int proj_q4k(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m, uint32_t k, uint32_t n,
              uint32_t expert_offset) {
@@ -1131,30 +1445,29 @@ int proj_q4k(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m, 
                expert_offset);
     LC_REQUIRE(((uintptr_t)wv & 15) == 0, LC_ERR_INVALID, "proj_q4k: weight pointer not 16-byte aligned");
     const uint8_t *w = (const uint8_t *)wv + (size_t)(expert_offset / 256) * 144;
-    const int nsb = k / 256;
     if (m <= 4) {
-        const size_t smem = ski_smem_bytes((int)m, (int)k);
-        if (smem + 8192 <= ctx->smem_optin) {  // + static shared (zero block, scales)
-            const int T = (int)((n + 15) / 16);
-            Fixup fx;
-            fx.acc = (float *)lc_scratch_zeroed(ctx, LC_SCRATCH_FIXUP, (size_t)T * 64 * 4 + (size_t)T * 4 + 256);
-            if (!fx.acc) return LC_ERR_OOM;
-            fx.cnt = (unsigned *)(fx.acc + (size_t)T * 64);
-            const long long units = (long long)T * nsb;
-            const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, (units + 31) / 32));
-            switch (m) {
-            case 1: return launch_q4k_sk<1>(ctx, grid, smem, x, w, c, k, n, fx);
-            case 2: return launch_q4k_sk<2>(ctx, grid, smem, x, w, c, k, n, fx);
-            case 3: return launch_q4k_sk<3>(ctx, grid, smem, x, w, c, k, n, fx);
-            default: return launch_q4k_sk<4>(ctx, grid, smem, x, w, c, k, n, fx);
-            }
-        }
+        const TmaPlan p = q4k_tma_plan(ctx, (int)m, (int)k, (int)n);
+        if (p.R) return launch_q4k_tma(ctx, p, m, x, w, c, k, n);
     }
+    return proj_q4k_tiled(ctx, x, w, c, m, k, n, nullptr);
+}
+
+size_t q4k_pack_bytes(uint32_t m_group, uint32_t k) {
+    const size_t nt = (m_group + 3) / 4;
+    return (size_t)(k / 256) * 17 * nt * 32 * 8 + 16 * 4;
+}
+
+// Groups of up to 16 tokens through x_pack_q4k + q4k_mma_kernel.  The packed
+// activations go to `pack` (at least q4k_pack_bytes(min(m, 16), k) bytes)
+// or, when it is null, to the context's scratch pool.
+int proj_q4k_tiled(lc_ctx *ctx, const float *x, const uint8_t *w, float *c, uint32_t m, uint32_t k, uint32_t n,
+                   void *pack) {
+    const int nsb = k / 256;
     for (uint32_t t0 = 0; t0 < m; t0 += 16) {
         const int mm = (int)std::min<uint32_t>(16, m - t0);
         const int nt = (mm + 3) / 4;
         const size_t tab_bytes = (size_t)nsb * 17 * nt * 32 * 8;
-        uint2 *tab = (uint2 *)lc_scratch(ctx, LC_SCRATCH_PACK, tab_bytes + 16 * 4);
+        uint2 *tab = (uint2 *)(pack ? pack : lc_scratch(ctx, LC_SCRATCH_PACK, tab_bytes + 16 * 4));
         if (!tab) return LC_ERR_OOM;
         float *inv = (float *)((char *)tab + tab_bytes);
         x_pack_q4k<<<nt * 4, 256, 0, ctx->stream>>>(x + (size_t)t0 * k, tab, inv, mm, (int)k, nt);
@@ -1295,26 +1608,26 @@ extern "C" int lc_proj_m(lc_ctx *ctx, int dtype, const float *x, const void *w, 
 // ---------------------------------------------------------------------------
 // Q4_K projection that allocates no device memory.
 //
-// lc_proj_q4k / lc_proj_m take their stream-K split-tile scratch from the
-// context's scratch pool, which grows with cudaMalloc on first use of a larger
-// shape.  Some callers cannot allocate on the call path: a serving loop whose
-// memory planner has already handed all of HBM to weights and the K/V cache
-// (a cudaMalloc there fails or fragments that plan), or a latency-bound decode
-// loop that must not pay cudaMalloc's implicit device-wide synchronisation,
-// which stalls every other stream on the GPU.  This variant runs the same
-// stream-K kernel with its scratch in a fixed static device array instead.
+// lc_proj_q4k / lc_proj_m put the packed activations of their tiled path
+// (m > 4 tokens) in the context's scratch pool, which grows with cudaMalloc the
+// first time a larger shape arrives.  Some callers cannot allocate on the call
+// path: a serving loop whose memory planner has already handed all of HBM to
+// weights and the K/V cache (a cudaMalloc there fails or fragments that plan),
+// or a latency-bound decode loop that must not pay cudaMalloc's implicit
+// device-wide synchronisation, which stalls every other stream on the GPU.
+// This entry point takes that scratch from a fixed static device array
+// instead; for m <= 4 it runs the cluster GEMV, which needs no scratch.
 //
-// Limits: m in 1..4 tokens, n <= kStaticMaxTiles * 16 rows, and the staged
-// activations of m * k must fit in shared memory.  The array must be all zero
-// when a launch starts; it is zero when the module loads and every completed
-// launch leaves it zero again (the last contributor to a split tile clears its
-// entries).  Calls that overlap on the GPU (two streams, or two contexts on one
-// device) share the array and race; callers serialise them.
+// Limits: m in 1..16 tokens; for m <= 4 the activation table of m * k must fit
+// in shared memory; for m > 4 the packed activations of m * k must fit in the
+// array (k <= 15360 at m = 16).  Nothing in the array needs to start at zero:
+// each call writes the part it reads.  Calls that overlap on the GPU (two
+// streams, or two contexts on one device) share the array and race; callers
+// serialise them.
 
-constexpr int kStaticMaxTiles = 4096;  // n <= 65536 rows
-constexpr size_t kStaticScratchBytes = (size_t)kStaticMaxTiles * 64 * 4 + (size_t)kStaticMaxTiles * 4;
+constexpr size_t kStaticPackBytes = (size_t)1 << 20;
 
-static __device__ __align__(256) unsigned char g_static_fixup[kStaticScratchBytes];
+static __device__ __align__(256) unsigned char g_static_pack[kStaticPackBytes];
 
 namespace {
 
@@ -1323,13 +1636,13 @@ void *g_static_ptr[64];  // per device ordinal, set up once with that device cur
 
 // Set-up on the first call per device: resolve the array's device address.
 // That first call should come before any stream capture on the device.
-int static_fixup_ptr(lc_ctx *ctx, void **out) {
+int static_pack_ptr(lc_ctx *ctx, void **out) {
     LC_REQUIRE(ctx->device >= 0 && ctx->device < 64, LC_ERR_INVALID, "static scratch: device %d out of range",
                ctx->device);
     std::lock_guard<std::mutex> lk(g_static_mu);
     if (!g_static_ptr[ctx->device]) {
         void *p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_fixup);
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_pack);
         LC_REQUIRE(e == cudaSuccess && p, LC_ERR_CUDA, "static scratch: cudaGetSymbolAddress failed: %s",
                    cudaGetErrorString(e));
         g_static_ptr[ctx->device] = p;
@@ -1345,35 +1658,30 @@ extern "C" int lc_proj_q4k_static(lc_ctx *ctx, const float *x, const void *wv, f
     LC_REQUIRE(ctx, LC_ERR_INVALID, "lc_proj_q4k_static: null ctx");
     if (m == 0 || n == 0) return LC_OK;
     LC_REQUIRE(x && wv && c, LC_ERR_INVALID, "lc_proj_q4k_static: null pointer");
-    LC_REQUIRE(m <= 4, LC_ERR_UNSUPPORTED, "lc_proj_q4k_static: m=%u tokens, at most 4", m);
+    LC_REQUIRE(m <= 16, LC_ERR_UNSUPPORTED, "lc_proj_q4k_static: m=%u tokens, at most 16", m);
     LC_REQUIRE(k > 0 && k % 256 == 0, LC_ERR_UNSUPPORTED, "lc_proj_q4k_static: k=%u is not a positive multiple of 256",
                k);
     LC_REQUIRE(expert_offset % 256 == 0, LC_ERR_UNSUPPORTED,
                "lc_proj_q4k_static: expert_offset=%u not a multiple of 256", expert_offset);
-    LC_REQUIRE(n <= (uint32_t)kStaticMaxTiles * 16, LC_ERR_UNSUPPORTED,
-               "lc_proj_q4k_static: n=%u rows exceeds the static scratch limit of %d rows", n, kStaticMaxTiles * 16);
     LC_REQUIRE(((uintptr_t)wv & 15) == 0, LC_ERR_INVALID, "lc_proj_q4k_static: weight pointer not 16-byte aligned");
     int s = lc_use_device(ctx);
     if (s) return s;
-    const size_t smem = ski_smem_bytes((int)m, (int)k);
-    LC_REQUIRE(smem + 8192 <= ctx->smem_optin, LC_ERR_UNSUPPORTED,
-               "lc_proj_q4k_static: m*k=%u*%u activations exceed shared memory (%zu of %zu bytes)", m, k, smem,
-               ctx->smem_optin);
-    void *base = nullptr;
-    s = static_fixup_ptr(ctx, &base);
-    if (s) return s;
-    Fixup fx;
-    fx.acc = (float *)base;
-    fx.cnt = (unsigned *)((char *)base + (size_t)kStaticMaxTiles * 64 * 4);
     const uint8_t *w = (const uint8_t *)wv + (size_t)(expert_offset / 256) * 144;
-    const int T = (int)((n + 15) / 16);
-    const long long units = (long long)T * (k / 256);
-    const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, (units + 31) / 32));
-    switch (m) {
-    case 1: s = launch_q4k_sk<1>(ctx, grid, smem, x, w, c, k, n, fx); break;
-    case 2: s = launch_q4k_sk<2>(ctx, grid, smem, x, w, c, k, n, fx); break;
-    case 3: s = launch_q4k_sk<3>(ctx, grid, smem, x, w, c, k, n, fx); break;
-    default: s = launch_q4k_sk<4>(ctx, grid, smem, x, w, c, k, n, fx); break;
+    if (m <= 4) {
+        const TmaPlan p = q4k_tma_plan(ctx, (int)m, (int)k, (int)n);
+        LC_REQUIRE(p.R, LC_ERR_UNSUPPORTED,
+                   "lc_proj_q4k_static: m*k=%u*%u activations exceed shared memory (%zu of %zu bytes)", m, k,
+                   q4t_layout(kTmaWarps, (int)m, (int)k, 2, 1).total, ctx->smem_optin);
+        s = launch_q4k_tma(ctx, p, m, x, w, c, k, n);
+    } else {
+        const size_t need = lc::q4k_pack_bytes(m, k);
+        LC_REQUIRE(need <= kStaticPackBytes, LC_ERR_UNSUPPORTED,
+                   "lc_proj_q4k_static: packed activations of m*k=%u*%u need %zu bytes, the static scratch has %zu", m,
+                   k, need, kStaticPackBytes);
+        void *pack = nullptr;
+        s = static_pack_ptr(ctx, &pack);
+        if (s) return s;
+        s = lc::proj_q4k_tiled(ctx, x, w, c, m, k, n, pack);
     }
     if (s) return s;
     return lc_after_launch(ctx, "lc_proj_q4k_static");

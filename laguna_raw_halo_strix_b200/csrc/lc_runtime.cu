@@ -57,8 +57,30 @@ extern "C" int lc_init(int device, lc_ctx **out) {
         return lc_fail(LC_ERR_CUDA, "lc_init: cudaStreamCreate: %s", cudaGetErrorString(e));
     }
     ctx->stream = ctx->own_stream;
+    e = cudaMalloc((void **)&ctx->dev_status, 256);
+    if (e == cudaSuccess) e = cudaMemset(ctx->dev_status, 0, 256);
+    if (e != cudaSuccess) {
+        if (ctx->dev_status) cudaFree(ctx->dev_status);
+        cudaStreamDestroy(ctx->own_stream);
+        delete ctx;
+        return lc_fail(LC_ERR_CUDA, "lc_init: status word: %s", cudaGetErrorString(e));
+    }
     *out = ctx;
     return LC_OK;
+}
+
+extern "C" int lc_device_status(lc_ctx *ctx) {
+    LC_REQUIRE(ctx, LC_ERR_INVALID, "lc_device_status: null ctx");
+    int s = lc_use_device(ctx);
+    if (s) return s;
+    unsigned v = 0;
+    LC_CUDA(cudaMemcpyAsync(&v, ctx->dev_status, sizeof(v), cudaMemcpyDeviceToHost, ctx->stream));
+    LC_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (!v) return LC_OK;
+    LC_CUDA(cudaMemsetAsync(ctx->dev_status, 0, sizeof(v), ctx->stream));
+    LC_CUDA(cudaStreamSynchronize(ctx->stream));
+    return lc_fail(LC_ERR_TIMEOUT, "a bounded device-side wait expired (status 0x%x); results of that launch are invalid",
+                   v);
 }
 
 extern "C" int lc_destroy(lc_ctx *ctx) {
@@ -68,6 +90,7 @@ extern "C" int lc_destroy(lc_ctx *ctx) {
     if (ctx->stream && ctx->stream != ctx->own_stream) cudaStreamSynchronize(ctx->stream);
     for (int i = 0; i < LC_SCRATCH_COUNT; i++)
         if (ctx->scratch[i]) cudaFree(ctx->scratch[i]);
+    if (ctx->dev_status) cudaFree(ctx->dev_status);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return LC_OK;
@@ -128,6 +151,7 @@ int lc_after_launch(lc_ctx *ctx, const char *what) {
     if (ctx->sync) {
         e = cudaStreamSynchronize(ctx->stream);
         if (e != cudaSuccess) return lc_fail(LC_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+        return lc_device_status(ctx);
     }
     return LC_OK;
 }

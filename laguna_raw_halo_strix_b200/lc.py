@@ -81,6 +81,7 @@ SIGNATURES = {
     "lc_proj_q8_0": (_i, [_vp, _vp, _vp, _vp, _u32, _u32]),
     "lc_proj_q4k": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32]),
     "lc_proj_quant": (_i, [_vp, _i, _vp, _vp, _vp, _u32, _u32, _u32]),
+    "lc_device_status": (_i, [_vp]),
     "lc_proj_m": (_i, [_vp, _i, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
     "lc_proj_q4k_static": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
     "lc_dequant": (_i, [_vp, _i, _vp, _sz, _sz, _vp]),
@@ -247,6 +248,9 @@ class Context:
 
     def proj_quant(self, dtype, x, w, c, k, n, expert_offset=0):
         check(self.L.lc_proj_quant(self.h, dtype, ptr(x), ptr(w), ptr(c), k, n, expert_offset), "lc_proj_quant")
+
+    def device_status(self):
+        check(self.L.lc_device_status(self.h), "lc_device_status")
 
     def proj_m(self, dtype, x, w, c, m, k, n, expert_offset=0):
         check(self.L.lc_proj_m(self.h, dtype, ptr(x), ptr(w), ptr(c), m, k, n, expert_offset), "lc_proj_m")

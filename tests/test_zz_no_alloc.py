@@ -1,7 +1,9 @@
-"""lc_proj_q4k_static: the Q4_K stream-K projection with its split-tile scratch
-in a static device array.  Compared through the C ABI with the existing entry
-point (lc_proj_m, LC_Q4_K) and the CPU oracle, on two calls in a row.  Named
-to be collected last; it also passes alone in a fresh process."""
+"""lc_proj_q4k_static: the Q4_K projection that allocates no device memory
+(m <= 4: the cluster GEMV, which needs no scratch; m = 5..16: the tiled path
+with its packed activations in a static device array).  Compared through the
+C ABI with the existing entry point (lc_proj_m, LC_Q4_K) and the CPU oracle,
+on two calls in a row.  Named to be collected last; it also passes alone in a
+fresh process."""
 import numpy as np
 import pytest
 
@@ -15,7 +17,8 @@ TOL = 1e-3  # max|err| <= TOL * ||ref||_inf, the projection tolerance
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 4096, 14336), (2, 1024, 777), (3, 512, 4096), (2, 14336, 4096),
-                                   (4, 4096, 4096), (1, 256, 16)])
+                                   (4, 4096, 4096), (1, 256, 16), (8, 4096, 1000), (16, 14336, 4096),
+                                   (5, 256, 40)])
 def test_static_matches_existing_entry(ctx, dev, m, k, n):
     import torch
 
@@ -57,17 +60,13 @@ def test_static_rejects_out_of_range(ctx, dev):
 
     rng = np.random.default_rng(3)
     w = to_dev(synth.q4k_blocks(16, 256, rng), dev)
-    x = to_dev(synth.activations(5, 256, rng), dev)
-    c = torch.empty(5, 16, device=dev)
-    with pytest.raises(lc.LagunaError) as e:
-        ctx.proj_q4k_static(x, w, c, 5, 256, 16)  # more than 4 tokens
-    assert e.value.status == lc.LC_ERR_UNSUPPORTED
-    with pytest.raises(lc.LagunaError) as e:
-        ctx.proj_q4k_static(x, w, c, 1, 256, 65536 + 16)  # beyond the static scratch (checked before launch)
-    assert e.value.status == lc.LC_ERR_UNSUPPORTED and "static scratch" in str(e.value)
-    with pytest.raises(lc.LagunaError) as e:
-        ctx.proj_q4k_static(x, w, c, 1, 320, 16)  # k not a multiple of 256
-    assert e.value.status == lc.LC_ERR_UNSUPPORTED
-    with pytest.raises(lc.LagunaError) as e:
-        ctx.proj_q4k_static(x, w, c, 4, 14336, 16)  # 4 x 14336 staged activations exceed shared memory
-    assert e.value.status == lc.LC_ERR_UNSUPPORTED and "shared memory" in str(e.value)
+    x = to_dev(synth.activations(17, 256, rng), dev)
+    c = torch.empty(17, 16, device=dev)
+    cases = [((17, 256, 16), "at most 16"),          # more than 16 tokens
+             ((1, 320, 16), "multiple of 256"),       # k not a multiple of 256
+             ((4, 32768, 16), "shared memory"),       # 4 x 32768 activation table exceeds shared memory
+             ((16, 16384, 16), "static scratch")]     # packed activations exceed the 1 MiB array
+    for (m, k, n), what in cases:  # all rejected on the host, before any launch
+        with pytest.raises(lc.LagunaError) as e:
+            ctx.proj_q4k_static(x, w, c, m, k, n)
+        assert e.value.status == lc.LC_ERR_UNSUPPORTED and what in str(e.value), (m, k, n, str(e.value))
