@@ -506,7 +506,7 @@ def main():
                 "unit": "GB/s",
                 "frac": achieved / hbm,
                 "traffic": traffic,
-                "kernel": (("q4k_sk_kernel" if m <= 4 else "q4k_mma_kernel + x_pack_q4k") if wl["dtype"] == "q4k"
+                "kernel": (("q4k_tma_kernel" if m <= 4 else "q4k_mma_kernel + x_pack_q4k") if wl["dtype"] == "q4k"
                            else ("q8_sk_kernel" if m <= 4 else "q8_mma_kernel + x_pack_q8")),
                 "per_launch_us": per_launch_ms * 1e3,
                 "bytes_per_launch": launch_bytes(wl),

@@ -408,7 +408,7 @@ struct Fixup {
 
 __device__ __forceinline__ void lc_imma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                              uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -494,7 +494,7 @@ __device__ __forceinline__ float2 scales2_f32(uint32_t h2, uint32_t ref_mask) {
 
 __device__ __forceinline__ void lc_imma_u8s8_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
@@ -502,7 +502,7 @@ __device__ __forceinline__ void lc_imma_u8s8_z(int (&d)[4], uint32_t a0, uint32_
 
 __device__ __forceinline__ void lc_imma_s8s8_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
@@ -608,10 +608,13 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     return p;
 }
 
-// Orders this thread's earlier generic-proxy accesses of shared memory before
-// later async-proxy (bulk copy) accesses.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+// 16-byte shared load into `v` when `pred`, else `v` keeps its value (the
+// lanes that skip it generate no shared-memory traffic).
+__device__ __forceinline__ void lds128_if(bool pred, uint4 &v, const void *p) {
+    asm volatile(
+        "{\n .reg .pred q;\n setp.ne.u32 q, %4, 0;\n @q ld.shared.v4.u32 {%0,%1,%2,%3}, [%5];\n}\n"
+        : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w)
+        : "r"((uint32_t)pred), "r"(smem_addr(p)));
 }
 
 __device__ __forceinline__ uint4 lds128(const void *p) {
@@ -633,6 +636,48 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, in
         : "memory");
 }
 
+// Lane 0 of the warp arms `bar` for one 16-row unit and issues its copy;
+// predicated rather than branched, so the warp stays converged.
+__device__ __forceinline__ void tma_unit_lane0(int lane, void *dst, const CUtensorMap *tm, int x, int y,
+                                               uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.eq.s32 p, %0, 0;\n"
+        " @p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %2;\n"
+        " @p cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%3], [%4, {%5, %6}], [%1], %7;\n}\n" ::"r"(lane),
+        "r"(smem_addr(bar)), "r"(16 * 144), "r"(smem_addr(dst)), "l"(tm), "r"(x), "r"(y), "l"(pol)
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *tm) {
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(tm) : "memory");
+}
+
+// Named barrier over the first `nthreads` threads of the CTA (id 1; id 0 is
+// __syncthreads).
+__device__ __forceinline__ void named_barrier_sync(int nthreads) {
+    asm volatile("bar.sync 1, %0;\n" ::"r"(nthreads) : "memory");
+}
+
+// Packed f32x2 arithmetic (sm_100): two fp32 lanes per instruction.
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+        " mul.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}\n"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+        " mov.b64 rc, {%6, %7};\n fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}\n"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
 // ---------------------------------------------------------------------------
 // Q4_K GEMV for m <= 4 tokens, weights streamed by TMA.
 //
@@ -643,13 +688,18 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, in
 // Work split: CTAs run in clusters of kTmaCluster (one CTA per SM).  Each
 // cluster owns a contiguous range of whole 16-row tiles (balanced to one
 // tile); the cluster's units, flattened tile-major, are cut into one
-// contiguous range per CTA and per warp.  A warp keeps R units requested
-// ahead in its own ring (lane 0 issues one TMA per unit), accumulates the
-// units of one tile in registers and, when the tile changes, adds the partial
-// into the shared-memory accumulator of the tile's owner CTA in the cluster
-// (distributed shared memory, f32 atomics).  After a cluster barrier each CTA
-// stores the tiles it owns.  No split tile crosses a cluster, so nothing goes
-// through global memory but the outputs.
+// contiguous range per CTA and per consumer warp.  A producer warp fills
+// every consumer's ring (R units) at kernel start, so the consumers do not
+// block on the TMA queue while they digitise x; after that each consumer
+// refills its own ring, one copy per unit consumed.  A consumer accumulates
+// the units of one tile in registers and, when the tile changes, adds the
+// partial into its CTA's shared-memory accumulator of that tile (f32
+// atomics).  After a cluster barrier, each tile's owner CTA sums the
+// cluster's accumulators of the tile over distributed shared memory and
+// stores the rows.  No split tile crosses a cluster, so nothing goes through
+// global memory but the outputs.  (There is no cluster barrier before the
+// main loop: its release semantics would wait for the weight copies just
+// issued.)
 //
 // Activations: one scale per (token, super-block): x ~= xi * inv with
 // xi = rint(x * 32639 / max|x|) in 16 bits, split into s8 digits
@@ -667,14 +717,15 @@ struct TmaLayout {
     size_t ring, tab, xs, invs, zero, tacc, bars, total;
 };
 
-// Shared memory for NW warps, R stages each, m tokens, k, and at most `tl`
-// tiles per cluster:
+// Shared memory for NW consumer warps, R stages each, m tokens, k, and at
+// most `tl` tiles per cluster:
 //   ring  [NW][R][16 rows][144 B]     (128-byte aligned TMA destinations)
-//   tab   uint2 [S][8 MMAs][m][8 lanes]   digit fragments (see the prologue)
+//   tab   uint2 [S][2 halves][2 MMA pairs][m][8 lanes][2]  digit fragments
+//                                          (see the prologue)
 //   xs    int   [m][S][8]                 X of each sub-block
-//   invs  float [m][S]
+//   invs  float2 [m][S]                   (inv/16, -inv)
 //   zero  uint2 [8][m][8]                 B fragment of lanes without one
-//   tacc  float [tl][16][m]               tile sums (tiles this CTA owns)
+//   tacc  float [tl][16][m]               this CTA's partial sums of the cluster's tiles
 //   bars  uint64 [NW][R]
 __host__ __device__ __forceinline__ TmaLayout q4t_layout(int nw, int m, int k, int R, int tl) {
     TmaLayout L;
@@ -683,7 +734,7 @@ __host__ __device__ __forceinline__ TmaLayout q4t_layout(int nw, int m, int k, i
     L.tab = L.ring + (size_t)nw * R * kTmaUnit;
     L.xs = L.tab + S * 64 * m * 8;
     L.invs = L.xs + (size_t)m * S * 32;
-    L.zero = (L.invs + (size_t)m * S * 4 + 15) & ~(size_t)15;
+    L.zero = (L.invs + (size_t)m * S * 8 + 15) & ~(size_t)15;
     L.tacc = L.zero + (size_t)64 * m * 8;
     L.bars = (L.tacc + (size_t)tl * 16 * m * 4 + 7) & ~(size_t)7;
     L.total = L.bars + (size_t)nw * R * 8 + 128;  // + slack to 128-align the base
@@ -691,14 +742,14 @@ __host__ __device__ __forceinline__ TmaLayout q4t_layout(int nw, int m, int k, i
 }
 
 // Add a warp's partial of one tile (rows g, g+8 per thread, summed over the
-// thread's sub-blocks) into the tile's accumulator `ta` in the owner CTA's
-// shared memory (possibly this CTA's), and clear the partial.
+// thread's sub-blocks; each a (main, min) pair) into this CTA's accumulator
+// `ta` of the tile, and clear the partial.
 template <int M>
-__device__ __forceinline__ void q4t_tile_add(float (&acc)[M][2], float *ta, int lane) {
+__device__ __forceinline__ void q4t_tile_add(float2 (&acc)[M][2], float *ta, int lane) {
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
     for (int j = 0; j < M; j++) {
-        float a = acc[j][0], b = acc[j][1];
+        float a = acc[j][0].x + acc[j][0].y, b = acc[j][1].x + acc[j][1].y;
         a += __shfl_xor_sync(0xffffffffu, a, 1);
         a += __shfl_xor_sync(0xffffffffu, a, 2);
         b += __shfl_xor_sync(0xffffffffu, b, 1);
@@ -707,121 +758,166 @@ __device__ __forceinline__ void q4t_tile_add(float (&acc)[M][2], float *ta, int 
             atomicAdd(ta + g * M + j, a);
             atomicAdd(ta + (g + 8) * M + j, b);
         }
-        acc[j][0] = acc[j][1] = 0.f;
+        acc[j][0] = acc[j][1] = make_float2(0.f, 0.f);
     }
 }
 
-// Prologue: one warp per (token j, super-block sb).  Lane l converts elements
-// 8l..8l+7 of the super-block, which are exactly the 8 k positions of table
-// entry (MMA half*4 + i, owner t) with t = l/8, half = (l/4)&1, i = l&3; it
-// writes that entry's hi (e = 2t) and lo (e = 2t+1) digit words and, with its
-// 3 neighbours, the integer sum of sub-block l/4 = 2t + half.
-template <int M, int NW>
-__device__ __forceinline__ void q4t_prologue(const float *__restrict__ x, int k, uint2 *tab, int *xs, float *invs) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int S = k >> 8;
-    const bool vec = (((uintptr_t)x) & 15) == 0;
-    for (int it = warp; it < M * S; it += NW) {
-        const int j = it / S, sb = it - j * S;
-        const float *xp = x + (size_t)j * k + (size_t)sb * 256 + 8 * lane;
-        float v[8];
-        if (vec) {
-            const float4 a = __ldg(reinterpret_cast<const float4 *>(xp));
-            const float4 b = __ldg(reinterpret_cast<const float4 *>(xp) + 1);
-            v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-        } else {
+// Prologue: one warp per item (token j, super-block sb).  Lane l converts
+// elements 8l..8l+7 of the super-block, which are exactly the 8 k positions of
+// table entry (MMA half*4 + i, owner t) with t = l/8, half = (l/4)&1, i = l&3;
+// it writes that entry's hi (e = 2t) and lo (e = 2t+1) digit words and, with
+// its 3 neighbours, the integer sum of sub-block l/4 = 2t + half.  The loads
+// are split from the conversion so a warp can issue its first items' loads
+// before anything else.
+constexpr int kXPre = 4;  // items per warp whose x loads are issued early
+
+__device__ __forceinline__ void q4t_xload(const float *__restrict__ x, int k, int S, int it, float (&v)[8]) {
+    const int lane = threadIdx.x & 31;
+    const int j = it / S, sb = it - j * S;
+    const float *xp = x + (size_t)j * k + (size_t)sb * 256 + 8 * lane;
+    if ((((uintptr_t)x) & 15) == 0) {
+        const float4 a = __ldg(reinterpret_cast<const float4 *>(xp));
+        const float4 b = __ldg(reinterpret_cast<const float4 *>(xp) + 1);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    } else {
 #pragma unroll
-            for (int e = 0; e < 8; e++) v[e] = __ldg(xp + e);
-        }
-        float mx = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; e++) mx = fmaxf(mx, fabsf(v[e]));
-#pragma unroll
-        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        const bool fin = mx < INFINITY;  // false for inf / nan
-        const float scale = (mx > 0.f && fin) ? 32639.f / mx : 0.f;
-        const float inv = mx > 0.f ? (fin ? mx * (1.f / 32639.f) : __int_as_float(0x7FC00000)) : 0.f;
-        uint32_t h[2] = {0u, 0u}, l[2] = {0u, 0u};
-        int sum = 0;
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            const int xi = __float2int_rn(v[e] * scale);
-            const int hi = (xi + 128) >> 8;
-            const int lo = xi - (hi << 8);
-            sum += xi;
-            h[e >> 2] |= (uint32_t)(hi & 0xFF) << (8 * (e & 3));
-            l[e >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (e & 3));
-        }
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        const int t = lane >> 3, half = (lane >> 2) & 1, i = lane & 3;
-        uint2 *ent = tab + ((size_t)(sb * 8 + half * 4 + i) * M + j) * 8 + 2 * t;
-        ent[0] = make_uint2(h[0], h[1]);
-        ent[1] = make_uint2(l[0], l[1]);
-        // xs[(j*S + sb)*8 + 2t + half]: the pair (X_2t, X_2t+1) of owner t is one int2
-        if ((lane & 3) == 0) xs[((size_t)j * S + sb) * 8 + (lane >> 2)] = sum;
-        if (lane == 0) invs[(size_t)j * S + sb] = inv;
+        for (int e = 0; e < 8; e++) v[e] = __ldg(xp + e);
     }
 }
 
-// One unit from shared memory: rows g, g+8 of the stage at `st`.
 template <int M>
-__device__ __forceinline__ void q4t_unit(const uint8_t *st, const uint2 *tbl, const int2 *xs2, const float *inv_s,
-                                         int S, uint32_t ref_mask, int g, int t, float (&y)[M][2]) {
+__device__ __forceinline__ void q4t_digitize(const float (&v)[8], int S, int it, uint2 *tab, int *xs, float2 *invs) {
+    const int lane = threadIdx.x & 31;
+    const int j = it / S, sb = it - j * S;
+    float mx = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) mx = fmaxf(mx, fabsf(v[e]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const bool fin = mx < INFINITY;  // false for inf / nan
+    const float scale = (mx > 0.f && fin) ? 32639.f / mx : 0.f;
+    const float inv = mx > 0.f ? (fin ? mx * (1.f / 32639.f) : __int_as_float(0x7FC00000)) : 0.f;
+    uint32_t h[2] = {0u, 0u}, l[2] = {0u, 0u};
+    int sum = 0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const int xi = __float2int_rn(v[e] * scale);
+        const int hi = (xi + 128) >> 8;
+        const int lo = xi - (hi << 8);
+        sum += xi;
+        h[e >> 2] |= (uint32_t)(hi & 0xFF) << (8 * (e & 3));
+        l[e >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (e & 3));
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    // entry (sb, half, MMA i, token j, e) at uint2 index
+    // ((((sb*2 + half)*2 + i/2)*M + j)*8 + e)*2 + i%2: MMAs i and i+1 of a
+    // lane are one 16-byte load
+    const int t = lane >> 3, half = (lane >> 2) & 1, i = lane & 3;
+    uint2 *ent = tab + ((((size_t)(sb * 2 + half) * 2 + (i >> 1)) * M + j) * 8 + 2 * t) * 2 + (i & 1);
+    ent[0] = make_uint2(h[0], h[1]);
+    ent[2] = make_uint2(l[0], l[1]);
+    // xs[(j*S + sb)*8 + 2t + half]: the pair (X_2t, X_2t+1) of owner t is one int2
+    if ((lane & 3) == 0) xs[((size_t)j * S + sb) * 8 + (lane >> 2)] = sum;
+    if (lane == 0) invs[(size_t)j * S + sb] = make_float2(inv * 0.0625f, -inv);
+}
+
+// Lane constants of the scale / min byte extraction (get_scale_min_k4,
+// proj_q4k.comp:46-58) for sub-blocks 2t, 2t+1: t < 2 takes the 6-bit
+// q[2t], q[2t+1] and q[2t+4], q[2t+5]; t >= 2 combines the low / high nibbles
+// of q[2t+4], q[2t+5] with the top two bits of q[2t-4], q[2t-3] (scales) or
+// q[2t], q[2t+1] (mins).
+struct Q4ScaleSel {
+    uint32_t perm, mlo, mhi;
+    bool lo;  // t < 2
+    __device__ __forceinline__ Q4ScaleSel(int t) {
+        perm = (t & 1) ? 0x7632u : 0x5410u;  // bytes 2u, 2u+1 of row 0, then of row 1
+        lo = t < 2;
+        mlo = lo ? 0x3F3F3F3Fu : 0x0F0F0F0Fu;
+        mhi = lo ? 0u : 0x30303030u;
+    }
+    // (sc, m) of both rows: bytes (row0 2t, row0 2t+1, row1 2t, row1 2t+1)
+    __device__ __forceinline__ void get(const uint4 &H0, const uint4 &H1, uint32_t &sc4, uint32_t &mn4) const {
+        const uint32_t py = __byte_perm(H0.y, H1.y, perm);
+        const uint32_t pz = __byte_perm(H0.z, H1.z, perm);
+        const uint32_t pw = __byte_perm(H0.w, H1.w, perm);
+        sc4 = ((lo ? py : pw) & mlo) | ((py >> 2) & mhi);
+        mn4 = ((lo ? pz : pw >> 4) & mlo) | ((pz >> 2) & mhi);
+    }
+};
+
+// One unit from shared memory: rows g, g+8 of the stage at `st`.  tbl4: this
+// lane's B fragments of the super-block (MMAs 2p, 2p+1 at tbl4[((half*2+p)*M
+// + j)*8]).  For m <= 2 only the lanes that own a fragment (`own`) load it
+// into bf and the others keep bf at zero; for m > 2 those persistent zero
+// fragments would cost too many registers, so every lane loads, the
+// non-owners from the zero block `zb`.  xs2 / iv2: (X_2t, X_2t+1) and
+// (inv/16, -inv) of token 0, tokens S*4 int2 / S float2 apart.  y[j][r]
+// accumulates the (main, min) terms of row g + 8r, summed at the end.
+template <int M>
+__device__ __forceinline__ void q4t_unit(const uint8_t *st, const uint4 *tbl4, const uint4 *zb, bool own,
+                                         uint4 (&bf)[2][2][M], const int2 *xs2, const float2 *iv2, int S,
+                                         uint32_t ref_mask, int g, int t, const Q4ScaleSel &sel, float2 (&y)[M][2]) {
     const uint8_t *r0 = st + g * 144, *r1 = st + (g + 8) * 144;
     const uint4 H0 = lds128(r0), H1 = lds128(r1);
     const uint4 A0 = lds128(r0 + 16 + 32 * t), B0 = lds128(r0 + 32 + 32 * t);
     const uint4 A1 = lds128(r1 + 16 + 32 * t), B1 = lds128(r1 + 32 + 32 * t);
+#pragma unroll
+    for (int half = 0; half < 2; half++)
+#pragma unroll
+        for (int p = 0; p < 2; p++)
+#pragma unroll
+            for (int j = 0; j < M; j++) {
+                const int o = ((half * 2 + p) * M + j) * 8;
+                if constexpr (M <= 2)
+                    lds128_if(own, bf[half][p][j], tbl4 + o);
+                else
+                    bf[half][p][j] = lds128(own ? tbl4 + o : zb + o);
+            }
     int c[2][M][4];
 #pragma unroll
     for (int half = 0; half < 2; half++) {
         const uint32_t mask = half ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint4 &Pg = i < 2 ? A0 : B0;
-            const uint4 &Pg8 = i < 2 ? A1 : B1;
-            const uint32_t a0 = ((i & 1) ? Pg.z : Pg.x) & mask, a2 = ((i & 1) ? Pg.w : Pg.y) & mask;
-            const uint32_t a1 = ((i & 1) ? Pg8.z : Pg8.x) & mask, a3 = ((i & 1) ? Pg8.w : Pg8.y) & mask;
+        for (int p = 0; p < 2; p++) {
+            const uint4 &Pg = p ? B0 : A0;
+            const uint4 &Pg8 = p ? B1 : A1;
 #pragma unroll
             for (int j = 0; j < M; j++) {
-                const uint2 b = tbl[((half * 4 + i) * M + j) * 8];
-                if (i == 0)
-                    lc_imma_u8s8_z(c[half][j], a0, a1, a2, a3, b.x, b.y);
+                const uint4 &b = bf[half][p][j];
+                if (p == 0)
+                    lc_imma_u8s8_z(c[half][j], Pg.x & mask, Pg8.x & mask, Pg.y & mask, Pg8.y & mask, b.x, b.y);
                 else
-                    lc_imma_u8s8(c[half][j], a0, a1, a2, a3, b.x, b.y);
+                    lc_imma_u8s8(c[half][j], Pg.x & mask, Pg8.x & mask, Pg.y & mask, Pg8.y & mask, b.x, b.y);
+                lc_imma_u8s8(c[half][j], Pg.z & mask, Pg8.z & mask, Pg.w & mask, Pg8.w & mask, b.z, b.w);
             }
         }
     }
-    // scales / mins of sub-blocks 2t and 2t+1 (get_scale_min_k4,
-    // proj_q4k.comp:46-58): t < 2 reads bytes q[2t], q[2t+1] (& 63) and
-    // q[2t+4], q[2t+5]; t >= 2 combines q[2t+4..] nibbles with the top bits
-    // of q[2t-4..] and q[2t..].
-    const int sh = 16 * (t & 1);
+    uint32_t sc4, mn4;
+    sel.get(H0, H1, sc4, mn4);
 #pragma unroll
     for (int r = 0; r < 2; r++) {
-        const uint4 H = r ? H1 : H0;
-        const float2 dd = scales2_f32(H.x, ref_mask);  // (d, dmin)
-        const uint32_t yy = H.y >> sh, zz = H.z >> sh, ww = H.w >> sh;
-        const uint32_t scw = t < 2 ? (yy & 0x3F3Fu) : ((ww & 0x0F0Fu) | ((yy >> 2) & 0x3030u));
-        const uint32_t mnw = t < 2 ? (zz & 0x3F3Fu) : (((ww >> 4) & 0x0F0Fu) | ((zz >> 2) & 0x3030u));
-        const int sc0x16 = (int)(scw & 0xFFu) << 4, sc1 = (int)((scw >> 8) & 0xFFu);
-        const int mn0 = (int)(mnw & 0xFFu), mn1 = (int)((mnw >> 8) & 0xFFu);
+        const float2 dd = scales2_f32(r ? H1.x : H0.x, ref_mask);  // (d, dmin)
+        const uint32_t scr = sc4 >> (16 * r), mnr = mn4 >> (16 * r);
+        const int sc0x16 = (int)((scr << 4) & 0xFF0u), sc1 = (int)((scr >> 8) & 0xFFu);
+        const int mn0 = (int)(mnr & 0xFFu), mn1 = (int)((mnr >> 8) & 0xFFu);
 #pragma unroll
         for (int j = 0; j < M; j++) {
             const int2 X = xs2[(size_t)j * S * 4];
-            const float inv = inv_s[(size_t)j * S];
+            const float2 iv = iv2[(size_t)j * S];
             const int a_hi = sc0x16 * c[0][j][2 * r] + sc1 * c[1][j][2 * r];
             const int a_lo = sc0x16 * c[0][j][2 * r + 1] + sc1 * c[1][j][2 * r + 1];
             const int bm = mn0 * X.x + mn1 * X.y;
             const float a = fmaf(__int2float_rn(a_hi), 256.f, __int2float_rn(a_lo));
-            float v = fmaf(dd.x * inv * 0.0625f, a, y[j][r]);
-            y[j][r] = fmaf(-dd.y * inv, __int2float_rn(bm), v);
+            // (main, min) += (d*inv/16, -dmin*inv) * (a, bm)
+            y[j][r] = ffma2(fmul2(dd, iv), make_float2(a, __int2float_rn(bm)), y[j][r]);
         }
     }
 }
 
+// NW consumer warps + one producer warp (warp NW) per CTA.
 template <int M, int NW, int CL>
-__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NW * 32, 1)
+__global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__((NW + 1) * 32, 1)
     q4k_tma_kernel(const __grid_constant__ CUtensorMap tm, const float *__restrict__ x, float *__restrict__ y, int k,
                    int n, int half_mode, int R, int tl, unsigned *__restrict__ status) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -833,74 +929,113 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NW * 32, 1)
     const TmaLayout L = q4t_layout(NW, M, k, R, tl);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    uint8_t *ring = smem + L.ring + (size_t)warp * R * kTmaUnit;
     uint2 *tab = reinterpret_cast<uint2 *>(smem + L.tab);
     int *xs = reinterpret_cast<int *>(smem + L.xs);
-    float *invs = reinterpret_cast<float *>(smem + L.invs);
+    float2 *invs = reinterpret_cast<float2 *>(smem + L.invs);
     uint2 *zbuf = reinterpret_cast<uint2 *>(smem + L.zero);
     float *tacc = reinterpret_cast<float *>(smem + L.tacc);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars) + warp * R;
+    uint64_t *bars_all = reinterpret_cast<uint64_t *>(smem + L.bars);
 
-    // cluster -> whole tiles; CTA -> contiguous units; warp -> contiguous units
+    // cluster -> whole tiles; CTA -> contiguous units; warp -> contiguous
+    // units.  32-bit arithmetic (the host keeps T*C and T*S*NW below 2^31);
+    // CL and NW are compile-time divisors.
     const int rank = (int)cluster.block_rank();
     const int C = gridDim.x / CL, cid = blockIdx.x / CL;
     const int T = (n + 15) >> 4;
-    const int tc0 = (int)((long long)T * cid / C), tc1 = (int)((long long)T * (cid + 1) / C);
+    const int tc0 = T * cid / C, tc1 = T * (cid + 1) / C;
     const int uc0 = tc0 * S, ucn = (tc1 - tc0) * S;
-    const int U0 = uc0 + (int)((long long)ucn * rank / CL), U1 = uc0 + (int)((long long)ucn * (rank + 1) / CL);
-    const int w0 = U0 + (int)((long long)(U1 - U0) * warp / NW);
-    const int my_units = U0 + (int)((long long)(U1 - U0) * (warp + 1) / NW) - w0;
-
-    if (lane < R) mbar_init(bars + lane, 1);
-    mbar_init_fence();
-    __syncwarp();
+    const int U0 = uc0 + ucn * rank / CL, nU = uc0 + ucn * (rank + 1) / CL - U0;
+    const int wq = warp < NW ? warp : 0;
+    const int w0 = U0 + nU * wq / NW;
+    const int my_units = warp < NW ? U0 + nU * (wq + 1) / NW - w0 : 0;
     const uint64_t pol = l2_evict_first_policy();
-    int issued = 0, istage = 0, itile = w0 / S, isb = w0 - (w0 / S) * S;
-    auto issue = [&]() {
-        if (lane == 0) {
-            mbar_expect_tx(bars + istage, kTmaUnit);
-            tma_load_2d(ring + (size_t)istage * kTmaUnit, &tm, isb * 18, itile * 16, bars + istage, pol);
+
+    float xv[kXPre][8];
+    if (warp < NW) {
+        // x loads of this warp's first prologue items go out first
+#pragma unroll
+        for (int p = 0; p < kXPre; p++)
+            if (warp + p * NW < M * S) q4t_xload(x, k, S, warp + p * NW, xv[p]);
+        if (lane < R) mbar_init(bars_all + warp * R + lane, 1);
+        mbar_init_fence();
+    } else if (lane == 0) {
+        prefetch_tensormap(&tm);
+    }
+    __syncthreads();  // barriers initialised
+
+    if (warp == NW) {
+        // producer: the first R units of every consumer, consumer w on lane w
+        if (lane < NW) {
+            const int a = U0 + nU * lane / NW, cnt = U0 + nU * (lane + 1) / NW - a;
+            int tile = a / S, sb = a - (a / S) * S;
+            uint8_t *ring = smem + L.ring + (size_t)lane * R * kTmaUnit;
+            for (int q = 0; q < R && q < cnt; q++) {
+                mbar_expect_tx(bars_all + lane * R + q, kTmaUnit);
+                tma_load_2d(ring + (size_t)q * kTmaUnit, &tm, sb * 18, tile * 16, bars_all + lane * R + q, pol);
+                if (++sb == S) sb = 0, ++tile;
+            }
         }
+    } else {
+        for (int i = threadIdx.x; i < 64 * M; i += NW * 32) zbuf[i] = make_uint2(0u, 0u);
+        for (int i = threadIdx.x; i < tl * 16 * M; i += NW * 32) tacc[i] = 0.f;
+#pragma unroll
+        for (int p = 0; p < kXPre; p++)
+            if (warp + p * NW < M * S) q4t_digitize<M>(xv[p], S, warp + p * NW, tab, xs, invs);
+        for (int it = warp + kXPre * NW; it < M * S; it += NW) {
+            float v[8];
+            q4t_xload(x, k, S, it, v);
+            q4t_digitize<M>(v, S, it, tab, xs, invs);
+        }
+        named_barrier_sync(NW * 32);  // consumers only: the table is complete
+    }
+
+    uint8_t *ring = smem + L.ring + (size_t)wq * R * kTmaUnit;
+    uint64_t *bars = bars_all + wq * R;
+    // consumer refills continue after the producer's first R units
+    int issued = min(R, my_units), istage = issued == R ? 0 : issued;
+    int itile = (w0 + issued) / S, isb = (w0 + issued) - ((w0 + issued) / S) * S;
+    auto issue = [&]() {
+        tma_unit_lane0(lane, ring + (size_t)istage * kTmaUnit, &tm, isb * 18, itile * 16, bars + istage, pol);
         if (++istage == R) istage = 0;
         if (++isb == S) isb = 0, ++itile;
         ++issued;
     };
-    const int first = min(R, my_units);
-    for (int q = 0; q < first; q++) issue();
-
-    for (int i = threadIdx.x; i < 64 * M; i += blockDim.x) zbuf[i] = make_uint2(0u, 0u);
-    for (int i = threadIdx.x; i < tl * 16 * M; i += blockDim.x) tacc[i] = 0.f;
-    q4t_prologue<M, NW>(x, k, tab, xs, invs);
-    // every CTA's accumulators are zero before any partner adds into them
-    cluster.sync();
 
     const bool own = (g >> 1) == t;
     const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
     const int2 *xs2 = reinterpret_cast<const int2 *>(xs) + t;
-    float acc[M][2];
+    const Q4ScaleSel sel(t);
+    // B fragments: own lanes load their entry of the table; the others keep zeros
+    const uint4 *tab4 = reinterpret_cast<const uint4 *>(tab) + g;
+    const uint4 *zb4 = reinterpret_cast<const uint4 *>(zbuf);
+    uint4 bf[2][2][M];
 #pragma unroll
-    for (int j = 0; j < M; j++) acc[j][0] = acc[j][1] = 0.f;
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int p = 0; p < 2; p++)
+#pragma unroll
+            for (int j = 0; j < M; j++) bf[h][p][j] = make_uint4(0u, 0u, 0u, 0u);
+    float2 acc[M][2];
+#pragma unroll
+    for (int j = 0; j < M; j++) acc[j][0] = acc[j][1] = make_float2(0.f, 0.f);
     int tile = w0 / S, sb = w0 - (w0 / S) * S, s = 0;
     uint32_t phase = 0;
     bool ok = true;
-    auto tile_acc = [&](int tl_) {  // accumulator of cluster tile tl_ in its owner CTA
-        return cluster.map_shared_rank(tacc, tl_ % CL) + (size_t)(tl_ / CL) * 16 * M;
-    };
     for (int q = 0; q < my_units; q++) {
         // all lanes wait on the same barrier; the vote keeps the outcome warp-uniform
         if (!__all_sync(0xffffffffu, mbar_wait(bars + s, phase))) {
             ok = false;
             break;
         }
-        const uint2 *tbl = own ? tab + (size_t)sb * 64 * M + g : zbuf;
-        q4t_unit<M>(ring + (size_t)s * kTmaUnit, tbl, xs2 + (size_t)sb * 4, invs + sb, S, ref_mask, g, t, acc);
-        // the stage's bytes are consumed: hand it to the next copy
-        fence_proxy_async_smem();
+        q4t_unit<M>(ring + (size_t)s * kTmaUnit, tab4 + (size_t)sb * 32 * M, zb4, own, bf, xs2 + (size_t)sb * 4,
+                    invs + sb, S, ref_mask, g, t, sel, acc);
+        // the stage's bytes are in registers and consumed (the MMAs and the
+        // epilogue above depend on them): hand the stage to the next copy
         __syncwarp();
         if (issued < my_units) issue();
         if (++s == R) s = 0, phase ^= 1u;
         if (++sb == S || q == my_units - 1) {
-            q4t_tile_add<M>(acc, tile_acc(tile - tc0), lane);
+            q4t_tile_add<M>(acc, tacc + (size_t)(tile - tc0) * 16 * M, lane);
             if (sb == S) sb = 0, ++tile;
         }
     }
@@ -913,15 +1048,25 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(NW * 32, 1)
             if (last >= 0) mbar_wait(bars + st, (uint32_t)(last / R) & 1u);
         }
     }
-    // all partials have landed in their owners' accumulators
+    // every CTA's partials are complete; each tile's owner sums the cluster's
+    // copies (distributed shared memory) and stores the rows
     cluster.sync();
-    for (int lt = rank; lt < tc1 - tc0; lt += CL) {
-        const float *ta = tacc + (size_t)(lt / CL) * 16 * M;
-        for (int idx = threadIdx.x; idx < 16 * M; idx += blockDim.x) {
-            const int r = idx / M, j = idx - r * M, row = (tc0 + lt) * 16 + r;
-            if (row < n) y[(size_t)j * n + row] = ta[idx];
+    {
+        const float *part[CL];
+#pragma unroll
+        for (int c = 0; c < CL; c++) part[c] = cluster.map_shared_rank(tacc, c);
+        const int ntile = tc1 - tc0, nown = ntile > rank ? (ntile - rank + CL - 1) / CL : 0;
+        for (int idx = threadIdx.x; idx < nown * 16 * M; idx += blockDim.x) {
+            const int q = idx / (16 * M), e = idx - q * 16 * M;
+            const int lt = rank + q * CL, r = e / M, j = e - r * M, row = (tc0 + lt) * 16 + r;
+            float v = 0.f;
+#pragma unroll
+            for (int c = 0; c < CL; c++) v += part[c][(size_t)lt * 16 * M + e];
+            if (row < n) y[(size_t)j * n + row] = v;
         }
     }
+    // partners' shared memory stays alive until every owner has read it
+    cluster.sync();
 }
 
 // ---------------------------------------------------------------------------
@@ -1110,7 +1255,8 @@ __device__ __forceinline__ void q8_unit_int(const Q8UnitI &U, const uint2 *tbl, 
     }
 }
 
-// Persistent stream-K Q8_0 projection for M <= 4 tokens (see q4k_sk_kernel);
+// Persistent stream-K Q8_0 projection for M <= 4 tokens (one CTA per SM, x
+// digitised into shared memory, warps on equal shares of the flattened units);
 // units are (16-row tile, block pair).
 template <int M>
 __global__ void __launch_bounds__(kSkWarps * 32, 1) q8_sk_kernel(const float *__restrict__ x,
@@ -1312,7 +1458,9 @@ int q4k_tensor_map(CUtensorMap *tm, const void *w, uint32_t k, uint32_t n) {
     return LC_OK;
 }
 
-constexpr int kTmaWarps = 16;
+// Consumer warps per CTA (+ 1 producer warp = 512 threads, <= 128 registers).
+// More warps (20 at <= 96 registers for one token) measured slower.
+__host__ __device__ constexpr int q4t_warps(int) { return 15; }
 constexpr int kTmaCluster = 4;
 constexpr int kTmaMaxStages = 4;
 
@@ -1331,14 +1479,15 @@ int q4k_tma_max_clusters(size_t smem) {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find({dev, smem});
     if (it != cache.end()) return it->second;
-    int s = set_smem(q4k_tma_kernel<M, kTmaWarps, kTmaCluster>, smem);
+    constexpr int NW = q4t_warps(M);
+    int s = set_smem(q4k_tma_kernel<M, NW, kTmaCluster>, smem);
     if (s) return 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kTmaCluster * 64, 1, 1);
-    cfg.blockDim = dim3(kTmaWarps * 32, 1, 1);
+    cfg.blockDim = dim3((NW + 1) * 32, 1, 1);
     cfg.dynamicSmemBytes = smem;
     int nc = 0;
-    if (cudaOccupancyMaxActiveClusters(&nc, q4k_tma_kernel<M, kTmaWarps, kTmaCluster>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&nc, q4k_tma_kernel<M, NW, kTmaCluster>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         nc = 0;
     }
@@ -1359,19 +1508,21 @@ int q4k_tma_max_clusters_m(int m, size_t smem) {
 TmaPlan q4k_tma_plan(const lc_ctx *ctx, int m, int k, int n) {
     TmaPlan p;
     const int T = (n + 15) / 16;
-    if ((long long)T * (k / 256) >= (1ll << 31)) return p;
+    const int nw = q4t_warps(m);
+    // the kernel's 32-bit range arithmetic
+    if ((long long)T * (k / 256) * nw >= (1ll << 31) || (long long)T * ctx->num_sms >= (1ll << 31)) return p;
     const int c_sms = std::max(1, ctx->num_sms / kTmaCluster);
     for (int R = kTmaMaxStages; R >= 2; R--) {
         const int C0 = std::min(T, c_sms);
         const int tl = (T + C0 - 1) / C0;
-        const size_t b = q4t_layout(kTmaWarps, m, k, R, tl).total;
+        const size_t b = q4t_layout(nw, m, k, R, tl).total;
         if (b > ctx->smem_optin) continue;
         // only as many clusters as can be resident at once (one wave)
         const int nc = q4k_tma_max_clusters_m(m, b);
         if (nc <= 0) return p;
         const int C = std::min(C0, nc);
         p.tl = (T + C - 1) / C;
-        p.smem = q4t_layout(kTmaWarps, m, k, R, p.tl).total;
+        p.smem = q4t_layout(nw, m, k, R, p.tl).total;
         p.grid = C * kTmaCluster;
         p.R = R;
         return p;
@@ -1382,9 +1533,10 @@ TmaPlan q4k_tma_plan(const lc_ctx *ctx, int m, int k, int n) {
 template <int M>
 int launch_q4k_tma_m(lc_ctx *ctx, const TmaPlan &p, const CUtensorMap &tm, const float *x, float *c, uint32_t k,
                      uint32_t n) {
-    int s = set_smem(q4k_tma_kernel<M, kTmaWarps, kTmaCluster>, p.smem);
+    constexpr int NW = q4t_warps(M);
+    int s = set_smem(q4k_tma_kernel<M, NW, kTmaCluster>, p.smem);
     if (s) return s;
-    q4k_tma_kernel<M, kTmaWarps, kTmaCluster><<<p.grid, kTmaWarps * 32, p.smem, ctx->stream>>>(
+    q4k_tma_kernel<M, NW, kTmaCluster><<<p.grid, (NW + 1) * 32, p.smem, ctx->stream>>>(
         tm, x, c, (int)k, (int)n, ctx->half_mode, p.R, p.tl, ctx->dev_status);
     return LC_OK;
 }
@@ -1671,7 +1823,7 @@ extern "C" int lc_proj_q4k_static(lc_ctx *ctx, const float *x, const void *wv, f
         const TmaPlan p = q4k_tma_plan(ctx, (int)m, (int)k, (int)n);
         LC_REQUIRE(p.R, LC_ERR_UNSUPPORTED,
                    "lc_proj_q4k_static: m*k=%u*%u activations exceed shared memory (%zu of %zu bytes)", m, k,
-                   q4t_layout(kTmaWarps, (int)m, (int)k, 2, 1).total, ctx->smem_optin);
+                   q4t_layout(q4t_warps((int)m), (int)m, (int)k, 2, 1).total, ctx->smem_optin);
         s = launch_q4k_tma(ctx, p, m, x, w, c, k, n);
     } else {
         const size_t need = lc::q4k_pack_bytes(m, k);
