@@ -147,14 +147,15 @@ int lc_proj_quant(lc_ctx *ctx, int dtype, const float *x, const void *w,
  * the reference would reach by m calls of the single-row dispatch. */
 int lc_proj_m(lc_ctx *ctx, int dtype, const float *x, const void *w, float *c,
               uint32_t m, uint32_t k, uint32_t n, uint32_t expert_offset);
-/* Q4_K projection of m = 1..4 rows of x [m, k] (same results as lc_proj_m
- * with LC_Q4_K) that allocates no device memory: its split-tile scratch is a
- * fixed static device array of about 1 MiB, so n <= 65536 rows; larger n,
- * m > 4, or m * k beyond shared memory return LC_ERR_UNSUPPORTED.  The first
- * call on a device resolves the array's address; make it before any stream
- * capture.  Calls that overlap on one GPU share the array and race: serialise
- * them.  No counterpart in the reference (its projections allocate nothing
- * per call because they keep no split-tile scratch). */
+/* Q4_K projection of m = 1..16 rows of x [m, k] (same results as lc_proj_m
+ * with LC_Q4_K) that allocates no device memory, for callers that cannot
+ * allocate on the call path.  m <= 4 needs no scratch; for m = 5..16 the
+ * packed activations live in a fixed static device array of 1 MiB (k <= 15360
+ * at m = 16).  Shapes beyond that, m > 16, or (m <= 4) m * k beyond shared
+ * memory return LC_ERR_UNSUPPORTED.  The first call on a device resolves the
+ * array's address; make it before any stream capture.  Calls that overlap on
+ * one GPU share the array and race: serialise them.  No counterpart in the
+ * reference. */
 int lc_proj_q4k_static(lc_ctx *ctx, const float *x, const void *w, float *c,
                        uint32_t m, uint32_t k, uint32_t n, uint32_t expert_offset);
 
