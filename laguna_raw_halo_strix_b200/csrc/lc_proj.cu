@@ -492,6 +492,13 @@ __device__ __forceinline__ float2 scales2_f32(uint32_t h2, uint32_t ref_mask) {
     return __half22float2(lc_u32_as_h2(fixed));
 }
 
+__device__ __forceinline__ void lc_imma_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ void lc_imma_u8s8_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
     asm(
@@ -639,13 +646,13 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, in
 // Lane 0 of the warp arms `bar` for one 16-row unit and issues its copy;
 // predicated rather than branched, so the warp stays converged.
 __device__ __forceinline__ void tma_unit_lane0(int lane, void *dst, const CUtensorMap *tm, int x, int y,
-                                               uint64_t *bar, uint64_t pol) {
+                                               uint64_t *bar, uint64_t pol, uint32_t bytes) {
     asm volatile(
         "{\n .reg .pred p;\n setp.eq.s32 p, %0, 0;\n"
         " @p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %2;\n"
         " @p cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
         " [%3], [%4, {%5, %6}], [%1], %7;\n}\n" ::"r"(lane),
-        "r"(smem_addr(bar)), "r"(16 * 144), "r"(smem_addr(dst)), "l"(tm), "r"(x), "r"(y), "l"(pol)
+        "r"(smem_addr(bar)), "r"(bytes), "r"(smem_addr(dst)), "l"(tm), "r"(x), "r"(y), "l"(pol)
         : "memory");
 }
 
@@ -727,11 +734,11 @@ struct TmaLayout {
 //   zero  uint2 [8][m][8]                 B fragment of lanes without one
 //   tacc  float [tl][16][m]               this CTA's partial sums of the cluster's tiles
 //   bars  uint64 [NW][R]
-__host__ __device__ __forceinline__ TmaLayout q4t_layout(int nw, int m, int k, int R, int tl) {
+__host__ __device__ __forceinline__ TmaLayout q4t_layout(int nw, int m, int k, int R, int tl, int unit = kTmaUnit) {
     TmaLayout L;
     const size_t S = (size_t)k / 256;
     L.ring = 0;
-    L.tab = L.ring + (size_t)nw * R * kTmaUnit;
+    L.tab = L.ring + (size_t)nw * R * unit;
     L.xs = L.tab + S * 64 * m * 8;
     L.invs = L.xs + (size_t)m * S * 32;
     L.zero = (L.invs + (size_t)m * S * 8 + 15) & ~(size_t)15;
@@ -785,7 +792,7 @@ __device__ __forceinline__ void q4t_xload(const float *__restrict__ x, int k, in
     }
 }
 
-template <int M>
+template <int M, bool Q8 = false>
 __device__ __forceinline__ void q4t_digitize(const float (&v)[8], int S, int it, uint2 *tab, int *xs, float2 *invs) {
     const int lane = threadIdx.x & 31;
     const int j = it / S, sb = it - j * S;
@@ -812,8 +819,10 @@ __device__ __forceinline__ void q4t_digitize(const float (&v)[8], int S, int it,
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     // entry (sb, half, MMA i, token j, e) at uint2 index
     // ((((sb*2 + half)*2 + i/2)*M + j)*8 + e)*2 + i%2: MMAs i and i+1 of a
-    // lane are one 16-byte load
-    const int t = lane >> 3, half = (lane >> 2) & 1, i = lane & 3;
+    // lane are one 16-byte load.  Q4_K: owner t = l/8, half (low / high
+    // nibbles) = (l/4)&1.  Q8_0: elements 8l.. are block l/4, so the owner is
+    // t = (l/4)&3 and the half (blocks 0-3 / 4-7) is l/16.
+    const int t = Q8 ? (lane >> 2) & 3 : lane >> 3, half = Q8 ? lane >> 4 : (lane >> 2) & 1, i = lane & 3;
     uint2 *ent = tab + ((((size_t)(sb * 2 + half) * 2 + (i >> 1)) * M + j) * 8 + 2 * t) * 2 + (i & 1);
     ent[0] = make_uint2(h[0], h[1]);
     ent[2] = make_uint2(l[0], l[1]);
@@ -915,18 +924,107 @@ __device__ __forceinline__ void q4t_unit(const uint8_t *st, const uint4 *tbl4, c
     }
 }
 
+// Weight formats of the TMA GEMV: one unit is 16 rows x 256 elements.
+struct FmtQ4K {
+    static constexpr int kUnit = 16 * 144;  // one super-block per row
+    static constexpr int kBoxX = 18;        // u64 words per unit row
+    static constexpr bool kQ8 = false;
+};
+struct FmtQ8_0 {
+    static constexpr int kUnit = 16 * 272;  // eight 34-byte blocks per row
+    static constexpr int kBoxX = 136;       // u16 words per unit row
+    static constexpr bool kQ8 = true;
+};
+
+__device__ __forceinline__ uint32_t lds32(const void *p) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(v) : "r"(smem_addr(p)));
+    return v;
+}
+
+// One Q8_0 unit (rows g, g+8; blocks 0..7 of the 272-byte unit rows).  Thread t
+// owns blocks t and 4+t: its k slots in MMA (h, i) are elements 8i..8i+7 of
+// block 4h+t, so after the four MMAs of a half its accumulator columns hold the
+// whole block's digit sums, and the block's f16 scale d is applied once per
+// (row, block): y += d * inv * (256 * S_hi + S_lo).  The q bytes of block b
+// start at byte 34b + 2 of the row (2 bytes off word alignment for even b):
+// nine aligned words and a funnel shift give them.
+template <int M>
+__device__ __forceinline__ void q8t_unit(const uint8_t *st, const uint4 *tbl4, const uint4 *zb, bool own,
+                                         uint4 (&bf)[2][2][M], const float2 *iv2, int S, uint32_t ref_mask, int g,
+                                         int t, float2 (&y)[M][2]) {
+#pragma unroll
+    for (int half = 0; half < 2; half++)
+#pragma unroll
+        for (int p = 0; p < 2; p++)
+#pragma unroll
+            for (int j = 0; j < M; j++) {
+                const int o = ((half * 2 + p) * M + j) * 8;
+                if constexpr (M <= 2)
+                    lds128_if(own, bf[half][p][j], tbl4 + o);
+                else
+                    bf[half][p][j] = lds128(own ? tbl4 + o : zb + o);
+            }
+    const int qsh = (t & 1) ? 0 : 16;        // bit shift of block t's q bytes
+    const int qw = (34 * t + 2) >> 2;        // first word of block t's q bytes
+    int c[2][M][4];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        uint32_t q[2][8];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const uint32_t *w = reinterpret_cast<const uint32_t *>(st + (g + 8 * r) * 272) + 34 * h + qw;
+            uint32_t W[9];
+#pragma unroll
+            for (int i = 0; i < 8; i++) W[i] = lds32(w + i);
+            W[8] = qsh ? lds32(w + 8) : 0u;  // odd t: aligned, the ninth word is not needed
+#pragma unroll
+            for (int i = 0; i < 8; i++) q[r][i] = __funnelshift_r(W[i], W[i + 1], qsh);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+#pragma unroll
+            for (int j = 0; j < M; j++) {
+                const uint4 &b = bf[h][i >> 1][j];
+                const uint32_t b0 = (i & 1) ? b.z : b.x, b1 = (i & 1) ? b.w : b.y;
+                if (i == 0)
+                    lc_imma_s8s8_z(c[h][j], q[0][2 * i], q[1][2 * i], q[0][2 * i + 1], q[1][2 * i + 1], b0, b1);
+                else
+                    lc_imma_s8s8(c[h][j], q[0][2 * i], q[1][2 * i], q[0][2 * i + 1], q[1][2 * i + 1], b0, b1);
+            }
+        }
+    }
+    // d of blocks t and 4+t: the half at byte 34t (word 34t/4, high half for
+    // odd t) and at byte 136 + 34t
+    const int dw = (34 * t) >> 2;
+    const uint32_t dperm = (t & 1) ? 0x7632u : 0x5410u;
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const uint32_t *w = reinterpret_cast<const uint32_t *>(st + (g + 8 * r) * 272);
+        const float2 dd = scales2_f32(__byte_perm(lds32(w + dw), lds32(w + 34 + dw), dperm), ref_mask);
+#pragma unroll
+        for (int j = 0; j < M; j++) {
+            const float inv = -iv2[(size_t)j * S].y;
+            const float s0 = fmaf(i2f_small(c[0][j][2 * r]), 256.f, i2f_small(c[0][j][2 * r + 1]));
+            const float s1 = fmaf(i2f_small(c[1][j][2 * r]), 256.f, i2f_small(c[1][j][2 * r + 1]));
+            y[j][r] = ffma2(fmul2(dd, make_float2(inv, inv)), make_float2(s0, s1), y[j][r]);
+        }
+    }
+}
+
 // NW consumer warps + one producer warp (warp NW) per CTA.
-template <int M, int NW, int CL>
+template <class F, int M, int NW, int CL>
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__((NW + 1) * 32, 1)
-    q4k_tma_kernel(const __grid_constant__ CUtensorMap tm, const float *__restrict__ x, float *__restrict__ y, int k,
-                   int n, int half_mode, int R, int tl, unsigned *__restrict__ status) {
+    tma_gemv_kernel(const __grid_constant__ CUtensorMap tm, const float *__restrict__ x, float *__restrict__ y, int k,
+                    int n, int half_mode, int R, int tl, unsigned *__restrict__ status) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     // The same offset on every CTA (the dynamic window starts at the same
     // shared address), so a partner's accumulator is at our own offset.
     unsigned char *smem = smem_raw + ((128u - (smem_addr(smem_raw) & 127u)) & 127u);
     cg::cluster_group cluster = cg::this_cluster();
     const int S = k >> 8;
-    const TmaLayout L = q4t_layout(NW, M, k, R, tl);
+    constexpr int kUnit = F::kUnit;
+    const TmaLayout L = q4t_layout(NW, M, k, R, tl, kUnit);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     uint2 *tab = reinterpret_cast<uint2 *>(smem + L.tab);
@@ -968,10 +1066,10 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__((NW + 1) * 32, 1)
         if (lane < NW) {
             const int a = U0 + nU * lane / NW, cnt = U0 + nU * (lane + 1) / NW - a;
             int tile = a / S, sb = a - (a / S) * S;
-            uint8_t *ring = smem + L.ring + (size_t)lane * R * kTmaUnit;
+            uint8_t *ring = smem + L.ring + (size_t)lane * R * kUnit;
             for (int q = 0; q < R && q < cnt; q++) {
-                mbar_expect_tx(bars_all + lane * R + q, kTmaUnit);
-                tma_load_2d(ring + (size_t)q * kTmaUnit, &tm, sb * 18, tile * 16, bars_all + lane * R + q, pol);
+                mbar_expect_tx(bars_all + lane * R + q, kUnit);
+                tma_load_2d(ring + (size_t)q * kUnit, &tm, sb * F::kBoxX, tile * 16, bars_all + lane * R + q, pol);
                 if (++sb == S) sb = 0, ++tile;
             }
         }
@@ -980,22 +1078,23 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__((NW + 1) * 32, 1)
         for (int i = threadIdx.x; i < tl * 16 * M; i += NW * 32) tacc[i] = 0.f;
 #pragma unroll
         for (int p = 0; p < kXPre; p++)
-            if (warp + p * NW < M * S) q4t_digitize<M>(xv[p], S, warp + p * NW, tab, xs, invs);
+            if (warp + p * NW < M * S) q4t_digitize<M, F::kQ8>(xv[p], S, warp + p * NW, tab, xs, invs);
         for (int it = warp + kXPre * NW; it < M * S; it += NW) {
             float v[8];
             q4t_xload(x, k, S, it, v);
-            q4t_digitize<M>(v, S, it, tab, xs, invs);
+            q4t_digitize<M, F::kQ8>(v, S, it, tab, xs, invs);
         }
         named_barrier_sync(NW * 32);  // consumers only: the table is complete
     }
 
-    uint8_t *ring = smem + L.ring + (size_t)wq * R * kTmaUnit;
+    uint8_t *ring = smem + L.ring + (size_t)wq * R * kUnit;
     uint64_t *bars = bars_all + wq * R;
     // consumer refills continue after the producer's first R units
     int issued = min(R, my_units), istage = issued == R ? 0 : issued;
     int itile = (w0 + issued) / S, isb = (w0 + issued) - ((w0 + issued) / S) * S;
     auto issue = [&]() {
-        tma_unit_lane0(lane, ring + (size_t)istage * kTmaUnit, &tm, isb * 18, itile * 16, bars + istage, pol);
+        tma_unit_lane0(lane, ring + (size_t)istage * kUnit, &tm, isb * F::kBoxX, itile * 16, bars + istage, pol,
+                       kUnit);
         if (++istage == R) istage = 0;
         if (++isb == S) isb = 0, ++itile;
         ++issued;
@@ -1027,8 +1126,12 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__((NW + 1) * 32, 1)
             ok = false;
             break;
         }
-        q4t_unit<M>(ring + (size_t)s * kTmaUnit, tab4 + (size_t)sb * 32 * M, zb4, own, bf, xs2 + (size_t)sb * 4,
-                    invs + sb, S, ref_mask, g, t, sel, acc);
+        if constexpr (F::kQ8)
+            q8t_unit<M>(ring + (size_t)s * kUnit, tab4 + (size_t)sb * 32 * M, zb4, own, bf, invs + sb, S, ref_mask,
+                        g, t, acc);
+        else
+            q4t_unit<M>(ring + (size_t)s * kUnit, tab4 + (size_t)sb * 32 * M, zb4, own, bf, xs2 + (size_t)sb * 4,
+                        invs + sb, S, ref_mask, g, t, sel, acc);
         // the stage's bytes are in registers and consumed (the MMAs and the
         // epilogue above depend on them): hand the stage to the next copy
         __syncwarp();
@@ -1440,20 +1543,23 @@ int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000 *out) {
     return LC_OK;
 }
 
-// Q4_K weights [n rows][k/256 super-blocks] as a 2D tensor of u64 words with
-// 16-row x one-super-block boxes.  Rows past n read as zero.
-int q4k_tensor_map(CUtensorMap *tm, const void *w, uint32_t k, uint32_t n) {
+// Quantized weights [n rows] as a 2D tensor whose box is one unit: 16 rows x
+// 256 elements (Q4_K: one 144-byte super-block = 18 u64 words; Q8_0: eight
+// 34-byte blocks = 136 u16 words).  Rows past n read as zero.
+template <class F>
+int tma_tensor_map(CUtensorMap *tm, const void *w, uint32_t k, uint32_t n) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
     int s = tensor_map_encoder(&enc);
     if (s) return s;
     const cuuint64_t S = k / 256;
-    cuuint64_t dims[2] = {S * 18, (cuuint64_t)n};
-    cuuint64_t strides[1] = {S * 144};
-    cuuint32_t box[2] = {18, 16};
+    cuuint64_t dims[2] = {S * F::kBoxX, (cuuint64_t)n};
+    cuuint64_t strides[1] = {S * (F::kUnit / 16)};
+    cuuint32_t box[2] = {(cuuint32_t)F::kBoxX, 16};
     cuuint32_t es[2] = {1, 1};
-    const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), dims, strides, box, es,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUtensorMapDataType dt = F::kQ8 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT64;
+    const CUresult r = enc(tm, dt, 2, const_cast<void *>(w), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     LC_REQUIRE(r == CUDA_SUCCESS, LC_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for k=%u n=%u", (int)r, k, n);
     return LC_OK;
 }
@@ -1470,8 +1576,8 @@ struct TmaPlan {
     size_t smem = 0;
 };
 
-template <int M>
-int q4k_tma_max_clusters(size_t smem) {
+template <class F, int M>
+int tma_max_clusters(size_t smem) {
     static std::mutex mu;
     static std::map<std::pair<int, size_t>, int> cache;
     int dev = 0;
@@ -1480,14 +1586,14 @@ int q4k_tma_max_clusters(size_t smem) {
     auto it = cache.find({dev, smem});
     if (it != cache.end()) return it->second;
     constexpr int NW = q4t_warps(M);
-    int s = set_smem(q4k_tma_kernel<M, NW, kTmaCluster>, smem);
+    int s = set_smem(tma_gemv_kernel<F, M, NW, kTmaCluster>, smem);
     if (s) return 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kTmaCluster * 64, 1, 1);
     cfg.blockDim = dim3((NW + 1) * 32, 1, 1);
     cfg.dynamicSmemBytes = smem;
     int nc = 0;
-    if (cudaOccupancyMaxActiveClusters(&nc, q4k_tma_kernel<M, NW, kTmaCluster>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&nc, tma_gemv_kernel<F, M, NW, kTmaCluster>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         nc = 0;
     }
@@ -1495,17 +1601,19 @@ int q4k_tma_max_clusters(size_t smem) {
     return nc;
 }
 
-int q4k_tma_max_clusters_m(int m, size_t smem) {
+template <class F>
+int tma_max_clusters_m(int m, size_t smem) {
     switch (m) {
-    case 1: return q4k_tma_max_clusters<1>(smem);
-    case 2: return q4k_tma_max_clusters<2>(smem);
-    case 3: return q4k_tma_max_clusters<3>(smem);
-    default: return q4k_tma_max_clusters<4>(smem);
+    case 1: return tma_max_clusters<F, 1>(smem);
+    case 2: return tma_max_clusters<F, 2>(smem);
+    case 3: return tma_max_clusters<F, 3>(smem);
+    default: return tma_max_clusters<F, 4>(smem);
     }
 }
 
 // R = 0 when the shapes do not fit (the caller falls back).
-TmaPlan q4k_tma_plan(const lc_ctx *ctx, int m, int k, int n) {
+template <class F>
+TmaPlan tma_plan(const lc_ctx *ctx, int m, int k, int n) {
     TmaPlan p;
     const int T = (n + 15) / 16;
     const int nw = q4t_warps(m);
@@ -1515,44 +1623,50 @@ TmaPlan q4k_tma_plan(const lc_ctx *ctx, int m, int k, int n) {
     for (int R = kTmaMaxStages; R >= 2; R--) {
         const int C0 = std::min(T, c_sms);
         const int tl = (T + C0 - 1) / C0;
-        const size_t b = q4t_layout(nw, m, k, R, tl).total;
+        const size_t b = q4t_layout(nw, m, k, R, tl, F::kUnit).total;
         if (b > ctx->smem_optin) continue;
         // only as many clusters as can be resident at once (one wave)
-        const int nc = q4k_tma_max_clusters_m(m, b);
+        const int nc = tma_max_clusters_m<F>(m, b);
         if (nc <= 0) return p;
         const int C = std::min(C0, nc);
         p.tl = (T + C - 1) / C;
-        p.smem = q4t_layout(nw, m, k, R, p.tl).total;
+        p.smem = q4t_layout(nw, m, k, R, p.tl, F::kUnit).total;
         p.grid = C * kTmaCluster;
         p.R = R;
         return p;
     }
     return p;
 }
+TmaPlan q4k_tma_plan(const lc_ctx *ctx, int m, int k, int n) { return tma_plan<FmtQ4K>(ctx, m, k, n); }
 
-template <int M>
-int launch_q4k_tma_m(lc_ctx *ctx, const TmaPlan &p, const CUtensorMap &tm, const float *x, float *c, uint32_t k,
-                     uint32_t n) {
+template <class F, int M>
+int launch_tma_m(lc_ctx *ctx, const TmaPlan &p, const CUtensorMap &tm, const float *x, float *c, uint32_t k,
+                 uint32_t n) {
     constexpr int NW = q4t_warps(M);
-    int s = set_smem(q4k_tma_kernel<M, NW, kTmaCluster>, p.smem);
+    int s = set_smem(tma_gemv_kernel<F, M, NW, kTmaCluster>, p.smem);
     if (s) return s;
-    q4k_tma_kernel<M, NW, kTmaCluster><<<p.grid, (NW + 1) * 32, p.smem, ctx->stream>>>(
+    tma_gemv_kernel<F, M, NW, kTmaCluster><<<p.grid, (NW + 1) * 32, p.smem, ctx->stream>>>(
         tm, x, c, (int)k, (int)n, ctx->half_mode, p.R, p.tl, ctx->dev_status);
     return LC_OK;
 }
 
 // The TMA GEMV for m = 1..4 tokens.
-int launch_q4k_tma(lc_ctx *ctx, const TmaPlan &p, uint32_t m, const float *x, const uint8_t *w, float *c,
-                   uint32_t k, uint32_t n) {
+template <class F>
+int launch_tma(lc_ctx *ctx, const TmaPlan &p, uint32_t m, const float *x, const uint8_t *w, float *c, uint32_t k,
+               uint32_t n) {
     CUtensorMap tm;
-    int s = q4k_tensor_map(&tm, w, k, n);
+    int s = tma_tensor_map<F>(&tm, w, k, n);
     if (s) return s;
     switch (m) {
-    case 1: return launch_q4k_tma_m<1>(ctx, p, tm, x, c, k, n);
-    case 2: return launch_q4k_tma_m<2>(ctx, p, tm, x, c, k, n);
-    case 3: return launch_q4k_tma_m<3>(ctx, p, tm, x, c, k, n);
-    default: return launch_q4k_tma_m<4>(ctx, p, tm, x, c, k, n);
+    case 1: return launch_tma_m<F, 1>(ctx, p, tm, x, c, k, n);
+    case 2: return launch_tma_m<F, 2>(ctx, p, tm, x, c, k, n);
+    case 3: return launch_tma_m<F, 3>(ctx, p, tm, x, c, k, n);
+    default: return launch_tma_m<F, 4>(ctx, p, tm, x, c, k, n);
     }
+}
+int launch_q4k_tma(lc_ctx *ctx, const TmaPlan &p, uint32_t m, const float *x, const uint8_t *w, float *c, uint32_t k,
+                   uint32_t n) {
+    return launch_tma<FmtQ4K>(ctx, p, m, x, w, c, k, n);
 }
 
 template <int M>
@@ -1647,6 +1761,10 @@ int proj_q8_0(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m,
         return LC_OK;
     }
     const int nblk = k / 32;
+    if (m <= 4 && k % 256 == 0 && ((uintptr_t)wv & 15) == 0) {
+        const TmaPlan p = tma_plan<FmtQ8_0>(ctx, (int)m, (int)k, (int)n);
+        if (p.R) return launch_tma<FmtQ8_0>(ctx, p, m, x, w, c, k, n);
+    }
     if (m <= 4) {
         const int S = (int)(k / 64);
         const size_t smem = ski_smem_bytes((int)m, (int)k);

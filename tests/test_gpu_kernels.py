@@ -77,7 +77,8 @@ def test_q4k_vs_oracle(ctx, dev, oracle, m, k, n):
 
 
 @pytest.mark.parametrize("m,k,n", [(1, 64, 1), (1, 256, 31), (1, 4096, 300), (2, 128, 33), (4, 4096, 16),
-                                   (7, 512, 45), (16, 4096, 130), (1, 96, 10), (3, 32, 5)])
+                                   (7, 512, 45), (16, 4096, 130), (1, 96, 10), (3, 32, 5), (2, 14336, 100),
+                                   (3, 768, 1000)])
 def test_q8_0_vs_oracle(ctx, dev, oracle, m, k, n):
     rng = np.random.default_rng(m * 7 + n)
     w = synth.q8_0_blocks(n, k, rng)
