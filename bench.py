@@ -61,6 +61,15 @@ WORKLOADS = {
 }
 
 
+# Workloads with their own drivers (below): BASELINE config 4 (lm_head, vocab
+# sharded over the ranks) and config 3 (the DFlash decoder, 16-token block).
+SPECIAL = ("lm_head_q8_0", "dflash_block")
+LM_HEAD = dict(m=1024, k=4096, vocab=128256, config=4)
+DFLASH_HP = dict(n_layers=6, n_embd=4096, n_heads=32, n_kv_heads=8, head_dim=128, rope_dim=128, n_ff=14336, n_aux=5,
+                 rope_base=500000.0, norm_eps=1e-5, qk_eps=1e-6)
+DFLASH_CTX, DFLASH_BLOCK = 2048, 16
+
+
 def weight_bytes(dtype, k, n):
     return n * (k // 256 * 144 if dtype == "q4k" else k // 32 * 34)
 
@@ -307,12 +316,331 @@ def run_reference_arm(args):
 
 
 # ---------------------------------------------------------------------------
+# Shared plumbing of the special workloads.
+def _dist_init():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    return world, rank, local_rank, dev
+
+
+def _max_over_ranks(v, dev, world):
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _graph_kernel_nodes(g):
+    """Kernel nodes of a captured torch CUDA graph (cudaGraphGetNodes +
+    cudaGraphNodeGetType through the CUDA runtime)."""
+    import ctypes as C
+
+    try:
+        import torch
+
+        rt = None
+        for name in ("libcudart.so.12", "libcudart.so"):
+            try:
+                rt = C.CDLL(name)
+                break
+            except OSError:
+                pass
+        if rt is None:
+            import glob
+
+            cands = glob.glob(os.path.join(os.path.dirname(torch.__file__), "..", "nvidia", "cuda_runtime", "lib",
+                                           "libcudart.so*"))
+            rt = C.CDLL(cands[0])
+        graph = C.c_void_p(g.raw_cuda_graph())
+        n = C.c_size_t(0)
+        rt.cudaGraphGetNodes(graph, None, C.byref(n))
+        nodes = (C.c_void_p * n.value)()
+        rt.cudaGraphGetNodes(graph, nodes, C.byref(n))
+        kinds = C.c_int(0)
+        count = 0
+        for i in range(n.value):
+            rt.cudaGraphNodeGetType(C.c_void_p(nodes[i]), C.byref(kinds))
+            count += kinds.value == 0  # cudaGraphNodeTypeKernel
+        return count
+    except Exception:
+        return None
+
+
+def _emit(line):
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+def run_lm_head(args):
+    """lm_head Q8_0 4096 -> 128256 for 1024 rows (16-token
+    blocks x 64 sequences) fused with argmax.  The vocab rows are split into
+    contiguous shards, one per rank; each rank computes its shard's keys and one
+    int64 MAX all-reduce (NCCL) gives every rank the global draft tokens.
+    Total work is fixed as ranks are added ("scaling": "strong")."""
+    import torch
+    import torch.distributed as dist
+
+    from laguna_raw_halo_strix_b200 import lc, synth
+    from laguna_raw_halo_strix_b200.lm_head import ShardedLmHead
+
+    world, rank, local_rank, dev = _dist_init()
+    stream = torch.cuda.Stream(dev)
+    ctx = lc.Context(local_rank)
+    ctx.set_stream(stream)
+    m, k, vocab = LM_HEAD["m"], LM_HEAD["k"], LM_HEAD["vocab"]
+    head = ShardedLmHead(ctx, lc.Q8_0, k, vocab, rank, world)
+    rng = np.random.default_rng(2000 + rank)
+    shard = synth.q8_0_blocks(head.n_local, k, rng)
+    shard_bytes = shard.nbytes
+    pool = max(1, -(-3 * L2_BYTES // shard_bytes))  # weight copies so each step streams from HBM
+    heads = []
+    base = torch.from_numpy(shard.reshape(-1)).to(dev)
+    for p in range(pool):
+        h = ShardedLmHead(ctx, lc.Q8_0, k, vocab, rank, world)
+        # distinct bytes per copy: flip only the int8 q bytes (the f16 scales stay valid)
+        if p:
+            w = base.view(-1, 34).clone()
+            w[:, 2:] ^= (p * 37) % 255
+            h.w = w.view(-1)
+        else:
+            h.w = base
+        heads.append(h)
+    x = torch.from_numpy(synth.activations(m, k, rng)).to(dev)
+    keys = torch.empty(m, dtype=torch.int64, device=dev)
+
+    def step(i):
+        heads[i % pool](x, m, keys)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        sampler = ClockSampler(dev) if rank == 0 else None
+        if sampler:
+            sampler.start()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        if sampler:
+            sampler.mark_begin()
+        e0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record(stream)
+        stream.synchronize()
+        if sampler:
+            sampler.mark_end()
+        if world > 1:
+            dist.barrier()
+        ms = _max_over_ranks(e0.elapsed_time(e1), dev, world)
+        clocks = sampler.stop() if sampler else None
+        # local (kernel-only) time of one shard, for the roofline figure
+        l0 = torch.cuda.Event(enable_timing=True)
+        l1 = torch.cuda.Event(enable_timing=True)
+        nl = max(3, min(args.steps, 20))
+        l0.record(stream)
+        for i in range(nl):
+            heads[i % pool].local_keys(x, m, keys)
+        l1.record(stream)
+        stream.synchronize()
+        local_ms = l0.elapsed_time(l1) / nl
+        # our kernels per step: the nodes of one captured local step
+        gl = torch.cuda.CUDAGraph(keep_graph=True)
+        with torch.cuda.graph(gl, stream=stream):
+            heads[0].local_keys(x, m, keys)
+        per_step = _graph_kernel_nodes(gl)
+        del gl
+        # e2e: x from pinned host memory, draft tokens back to the host, every step
+        x_host = torch.from_numpy(synth.activations(m, k, rng)).pin_memory()
+        k_host = torch.empty(m, dtype=torch.int64).pin_memory()
+        e2e_steps = max(3, min(args.steps, 20))
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            x.copy_(x_host, non_blocking=True)
+            step(i)
+            k_host.copy_(keys, non_blocking=True)
+            stream.synchronize()
+        e2e_s = _max_over_ranks(time.perf_counter() - t0, dev, world)
+
+    w_total = vocab * (k // 32) * 34
+    step_b = w_total + world * 4 * m * k  # every weight byte once; x read by every rank
+    value = step_b * args.steps / (ms / 1e3) / 1e9
+    hbm, _, peak_src = peaks()
+    local_b = shard_bytes + 4 * m * k
+    if rank == 0:
+        _emit({
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "q8_0*f32", "data": "synthetic (seeded; BASELINE block/activation "
+                                                               "distributions)",
+            "config": {"workload": "lm_head_q8_0", "baseline_config": LM_HEAD["config"], "m": m, "k": k,
+                       "vocab": vocab, "rows_per_rank": head.n_local, "bytes_per_step": step_b,
+                       "tokens_per_s": m * args.steps / (ms / 1e3),
+                       "l2": f"weights rotated through {pool} copies of {shard_bytes / 1e6:.1f} MB per rank",
+                       "parallelism": f"vocab-sharded x{world}, int64 MAX all-reduce of {m} keys per step"},
+            "roofline": {"bound": "hbm", "achieved": local_b / (local_ms / 1e3) / 1e9, "peak": hbm,
+                         "peak_source": peak_src, "unit": "GB/s", "frac": local_b / (local_ms / 1e3) / 1e9 / hbm,
+                         "traffic": None, "kernel": "lc_lm_head_argmax (one shard, all its kernels)",
+                         "per_launch_us": local_ms * 1e3, "bytes_per_launch": local_b},
+            "cpu_baseline": None,
+            "e2e": {"value": step_b * e2e_steps / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * m * k,
+                    "d2h_bytes_per_step": 8 * m, "steps": e2e_steps},
+            "clocks": clocks, "gpu_launches": None if per_step is None else per_step * args.steps,
+        })
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------
+def run_dflash(args):
+    """the DFlash decoder (6 layers, hidden 4096, 32 Q / 8 KV
+    heads of 128, FFN 14336, Q4_K projections) for one 16-token draft block over
+    2048 context rows of encoder output; a step is lc_dflash_decode_block.  The
+    encoder prefill (fc 5x4096 -> 4096 over 2048 rows, context K/V) runs once
+    and is timed apart.  Independent sequences on each rank ("scaling": "weak")."""
+    import torch
+    import torch.distributed as dist
+
+    from laguna_raw_halo_strix_b200 import lc, synth
+    from laguna_raw_halo_strix_b200.model import DFlash, hparams
+
+    world, rank, local_rank, dev = _dist_init()
+    stream = torch.cuda.Stream(dev)
+    ctx = lc.Context(local_rank)
+    ctx.set_stream(stream)
+    hp = DFLASH_HP
+    rng = np.random.default_rng(3000 + rank)
+    model = DFlash(ctx, hparams(**hp), max_ctx=DFLASH_CTX, max_block=DFLASH_BLOCK)
+    tensors = synth.dflash_tensors(hp, lc.Q4_K, rng, share=True)
+    wbytes = 0
+    for name, (dt, a) in tensors.items():
+        model.set_tensor(name, dt, a)
+        if name.startswith("blk."):
+            wbytes += a.nbytes
+    E, A, M = hp["n_embd"], hp["n_aux"], DFLASH_BLOCK
+    kvd = hp["n_kv_heads"] * hp["head_dim"]
+    with torch.cuda.stream(stream):
+        feats = torch.from_numpy(rng.standard_normal((DFLASH_CTX, A * E)).astype(np.float32)).to(dev)
+        enc = torch.empty(DFLASH_CTX, E, device=dev)
+        x = torch.from_numpy(rng.standard_normal((M, E)).astype(np.float32)).to(dev)
+        hid = torch.empty(M, E, device=dev)
+        model.encode(feats, DFLASH_CTX, enc)  # warm
+        p0 = torch.cuda.Event(enable_timing=True)
+        p1 = torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        model.encode(feats, DFLASH_CTX, enc)
+        model.set_context(enc, DFLASH_CTX)
+        p1.record(stream)
+        stream.synchronize()
+        prefill_ms = p0.elapsed_time(p1)
+        for i in range(args.warmup):
+            model.decode_block(x, M, hid)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph(keep_graph=True)
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(args.steps):
+                model.decode_block(x, M, hid)
+        g.replay()
+        stream.synchronize()
+        launches = _graph_kernel_nodes(g)
+        if world > 1:
+            dist.barrier()
+        sampler = ClockSampler(dev) if rank == 0 else None
+        if sampler:
+            sampler.start()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        if sampler:
+            sampler.mark_begin()
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        stream.synchronize()
+        if sampler:
+            sampler.mark_end()
+        ms = _max_over_ranks(e0.elapsed_time(e1), dev, world)
+        clocks = sampler.stop() if sampler else None
+        del g
+        # e2e: the block's token inputs from pinned host memory, hidden states back
+        x_host = torch.from_numpy(rng.standard_normal((M, E)).astype(np.float32)).pin_memory()
+        h_host = torch.empty(M, E).pin_memory()
+        e2e_steps = max(5, min(args.steps, 50))
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            x.copy_(x_host, non_blocking=True)
+            model.decode_block(x, M, hid)
+            h_host.copy_(hid, non_blocking=True)
+            stream.synchronize()
+        e2e_s = _max_over_ranks(time.perf_counter() - t0, dev, world)
+    ok = bool(torch.isfinite(hid).all().item())
+    model.close()
+    kv_bytes = hp["n_layers"] * (DFLASH_CTX + M) * kvd * 2 * 4
+    fwd_bytes = wbytes + kv_bytes
+    fwd_s = world * args.steps / (ms / 1e3)
+    hbm, _, peak_src = peaks()
+    per_fwd_s = ms / 1e3 / args.steps
+    if rank == 0:
+        _emit({
+            "metric": METRIC, "value": fwd_s, "unit": "fwd/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4k*f32",
+            "data": "synthetic (seeded; BASELINE distributions; one set of projection weights per shape, "
+                    "uploaded separately for every layer)",
+            "config": {"workload": "dflash_block", "baseline_config": 3, "layers": hp["n_layers"], "hidden": E,
+                       "heads": hp["n_heads"], "kv_heads": hp["n_kv_heads"], "ffn": hp["n_ff"],
+                       "context": DFLASH_CTX, "block": M, "bytes_per_fwd": fwd_bytes,
+                       "prefill_ms": prefill_ms, "finite": ok,
+                       "l2": f"{fwd_bytes / 1e6:.0f} MB streamed per forward (> 3x the 126 MB L2)",
+                       "parallelism": f"replicas x{world} (independent sequences, no collective)"},
+            "roofline": {"bound": "hbm", "achieved": fwd_bytes / per_fwd_s / 1e9, "peak": hbm,
+                         "peak_source": peak_src, "unit": "GB/s", "frac": fwd_bytes / per_fwd_s / 1e9 / hbm,
+                         "traffic": None, "kernel": "whole decoder step (all kernels)",
+                         "per_launch_us": per_fwd_s * 1e6, "bytes_per_launch": fwd_bytes},
+            "cpu_baseline": None,
+            "e2e": {"value": world * e2e_steps / e2e_s, "unit": "fwd/s", "h2d_bytes_per_step": 4 * M * E,
+                    "d2h_bytes_per_step": 4 * M * E, "steps": e2e_steps},
+            "clocks": clocks, "gpu_launches": launches,
+        })
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", default="ffn_q4k_m1", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="ffn_q4k_m1", choices=sorted(WORKLOADS) + list(SPECIAL))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -320,6 +648,10 @@ def main():
 
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.workload == "lm_head_q8_0":
+        return run_lm_head(args)
+    if args.workload == "dflash_block":
+        return run_dflash(args)
 
     import torch
     import torch.distributed as dist

@@ -81,3 +81,38 @@ def row_bytes(dtype: int, k: int) -> int:
 
 def activations(m: int, k: int, rng: np.random.Generator) -> np.ndarray:
     return rng.standard_normal((m, k)).astype(np.float32)
+
+
+def dflash_tensors(hp: dict, wtype: int, rng: np.random.Generator, share: bool = False):
+    """Seeded synthetic DFlash draft-model tensors, name -> (dtype, array): the
+    quantized projections in `wtype` blocks (BASELINE block distributions), the
+    norms f32 near 1.  With share=True one array per distinct projection shape
+    serves every layer (a timing model: each layer still gets its own device
+    copy, so every layer's weights stream from HBM)."""
+    from .lc import F32
+
+    E, H, KV, hd, F, A = (hp[k] for k in ("n_embd", "n_heads", "n_kv_heads", "head_dim", "n_ff", "n_aux"))
+    QD, KVD = H * hd, KV * hd
+    cache = {}
+
+    def W(rows, k):
+        if share and (rows, k) in cache:
+            return cache[(rows, k)]
+        v = (wtype, weight_blocks(wtype, rows, k, rng).reshape(-1))
+        if share:
+            cache[(rows, k)] = v
+        return v
+
+    def N(n):
+        return (F32, (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32))
+
+    t = {"fc.weight": W(E, A * E), "enc.aux_norm.weight": N(A * E), "enc.output_norm.weight": N(E),
+         "output_norm.weight": N(E)}
+    for layer in range(hp["n_layers"]):
+        p = f"blk.{layer}."
+        t.update({p + "attn_norm.weight": N(E), p + "attn_q.weight": W(QD, E), p + "attn_k.weight": W(KVD, E),
+                  p + "attn_v.weight": W(KVD, E), p + "attn_output.weight": W(E, QD),
+                  p + "attn_q_norm.weight": N(hd), p + "attn_k_norm.weight": N(hd),
+                  p + "attn_gate.weight": W(H, E), p + "ffn_norm.weight": N(E), p + "ffn_gate.weight": W(F, E),
+                  p + "ffn_up.weight": W(F, E), p + "ffn_down.weight": W(E, F)})
+    return t
