@@ -1,0 +1,686 @@
+// lc_gemm.cu -- quantized-weight GEMM on the 5th-generation tensor cores
+// (tcgen05 / TMEM) for blocks of tokens: y[t, i] = sum_j x[t, j] * W[i, j]
+// with W in raw GGUF Q4_K or Q8_0 blocks (kernels/proj_q4k.comp:60-92,
+// kernels/proj_q8_0.comp:47-67 applied to every row of x).
+//
+// One CTA per SM, warp-specialised:
+//   warp 0      producer: TMA copies of raw weight units (128 rows x 256
+//               elements), of the tokens' f16 activations and (Q4_K) of their
+//               sub-block sums;
+//   warps 1-8   converters: one weight row per thread, warps 1-4 the first
+//               half of a unit, warps 5-8 the second; they write f16 straight
+//               into the 128-byte-swizzled K-major layout the UMMA reads;
+//   warp 9      allocates the tensor memory and issues tcgen05.mma
+//               (kind::f16, M = 128 weight rows, N = 2 NT, K = 16) with f32
+//               accumulation in TMEM;
+//   warps 10-13 epilogue: tcgen05.ld of the accumulators, scales, f32 atomic
+//               adds into y (zeroed before the launch).
+// Units (128-row tile, super-block) are flattened tile-major and cut into one
+// contiguous range per CTA.
+//
+// Q4_K keeps the weights exact on the tensor cores: A holds the integers
+// sc_j * q, so each unit's product P = sum sc_j q x and min term
+// M = sum_j m_j Sx_j (Sx_j the sub-block sums of x, one extra K = 16 MMA) land
+// in their own TMEM columns, and the epilogue accumulates d P - dmin M in f32
+// per unit (four accumulator buffers in flight).  Q8_0 weights become
+// f16(d q) (one rounding) and accumulate in TMEM over a tile's run of units
+// (two buffers, the epilogue of a run overlapping the next run's MMAs).
+//
+// Activations: x [m, k] f32 times a per-token power of two (exact) becomes
+// x16 [2 NT, k] f16: rows 0..NT-1 the f16 value, rows NT..2NT-1 the f16 of the
+// remainder (rows past m zero), so the UMMA (N = 2 NT) sees x to ~22 bits and
+// the epilogue adds the two columns of a token.  k is in the order the
+// converters produce within each super-block (a fixed permutation: the dot
+// product is the same).
+//
+// Every mbarrier wait is bounded; on expiry the kernel records
+// LC_DEV_WAIT_TIMEOUT in the context's status word, stops issuing work, lets
+// the tensor-core work in flight finish (bounded) and frees the TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+
+#include "lc_internal.cuh"
+#include "lc_sm100.cuh"
+
+namespace {
+
+constexpr int kRows = 128;      // weight rows per tile (UMMA M)
+constexpr int kConvWarps = 8;
+constexpr int kMmaWarp = 1 + kConvWarps;
+constexpr int kGemmWarps = kMmaWarp + 5;  // + the MMA warp and 4 epilogue warps
+constexpr int kHalfK = 128;     // k per A / x stage (half a super-block)
+constexpr int kAStage = kRows * kHalfK * 2;  // 32 KB of f16
+
+// ---- tcgen05 ---------------------------------------------------------------
+
+// Shared-memory matrix descriptor, K-major with 128-byte swizzle: rows of
+// 128 bytes in groups of 8 (1024 bytes, SBO), 16-byte chunks XOR-swizzled by
+// the row within the group; LBO unused (1); version 1; layout type 2.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;               // LBO (16 B; unused for this layout)
+    d |= (uint64_t)(1024u >> 4) << 32;     // SBO: 8 rows x 128 B
+    d |= (uint64_t)1u << 46;               // descriptor version (sm_100)
+    d |= (uint64_t)2u << 61;               // SWIZZLE_128B
+    return d;
+}
+
+// Shared-memory matrix descriptor, K-major without swizzle, for a K = 16
+// operand in core matrices of 8 rows x 16 bytes: the two K groups 128 bytes
+// apart (LBO), 8-row groups 256 bytes apart (SBO).
+__device__ __forceinline__ uint64_t umma_desc_core16(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)(128u >> 4) << 16;
+    d |= (uint64_t)(256u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    return d;
+}
+
+// Instruction descriptor of kind::f16: D f32, A and B f16, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(dtmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// The values of every tcgen05.ld issued so far are in their registers.
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
+// Ties registers written by tcgen05.ld to a point after tmem_ld_wait(): their
+// uses depend on these (ordered) volatile statements, so none moves above the
+// wait.
+template <int N>
+__device__ __forceinline__ void tmem_regs_ready(float (&v)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; i++) asm volatile("" : "+f"(v[i])::"memory");
+}
+
+// Untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Byte offset of the 16-byte chunk `c` (k = 8c..8c+7 within a 64-wide atom
+// column) of row r in a K-major 128B-swizzled tile of 64-element columns.
+__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// ---- formats ----------------------------------------------------------------
+
+struct GQ4K {
+    static constexpr int kRowBytes = 144;  // one super-block per row and unit
+    static constexpr int kBoxX = 18;       // u64 words
+    static constexpr bool kQ8 = false;
+};
+struct GQ8_0 {
+    static constexpr int kRowBytes = 272;  // eight 34-byte blocks
+    static constexpr int kBoxX = 136;      // u16 words
+    static constexpr bool kQ8 = true;
+};
+
+// f16 bits of two halves with the reference rule for subnormals (exponent
+// field set to 1) when ref_mask is 0x04000400 (kernels/proj_q8_0.comp:27-45).
+__device__ __forceinline__ uint32_t fix_sub_h2(uint32_t h2, uint32_t ref_mask) {
+    const uint32_t man = h2 & 0x03FF03FFu, ex = h2 & 0x7C007C00u;
+    const uint32_t m_nz = (man + 0x03FF03FFu) & 0x04000400u;
+    const uint32_t e_nz = ((ex + 0x7C007C00u) & 0x80008000u) >> 5;
+    return h2 | (m_nz & ~e_nz & ref_mask);
+}
+
+__device__ __forceinline__ __half2 u2h2(uint32_t v) { return *reinterpret_cast<__half2 *>(&v); }
+__device__ __forceinline__ uint32_t h22u(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
+
+// k order within a super-block (position -> element), shared by the
+// converters and the activation packing.
+//   Q4_K: chunk c (8 positions) is qs word c (bytes 4c..4c+3, group G = c/8,
+//         p = 4(c%8)): elements 64G + [p, p+2, p+1, p+3, 32+p, 34+p, 33+p, 35+p].
+//   Q8_0: chunk c = 4b + i is q words 2i, 2i+1 of block b: elements
+//         32b + 8i + [0, 2, 1, 3, 4, 6, 5, 7].
+__host__ __device__ __forceinline__ int perm_elem(bool q8, int pos) {
+    const int c = pos >> 3, e = pos & 7;
+    const int sw = (e & 4) | ((e & 1) << 1) | ((e >> 1) & 1);  // [0,2,1,3,4,6,5,7]
+    if (q8) return 32 * (c >> 2) + 8 * (c & 3) + sw;
+    const int G = c >> 3, p = 4 * (c & 7);
+    return 64 * G + p + ((e & 4) << 3) + (sw & 3);
+}
+
+// Q4_K: half g (sub-blocks 4g..4g+3) of one row of a unit -> 16 chunks of 8
+// f16, written to row r of the A stage (two 64-column atoms).  The values are
+// the exact integers sc_j * q (at most 63 * 15): each pair comes from one
+// HFMA2 of the nibble pair biased into f16 (1024 + q, or 1024 + 16 q for the
+// high nibbles) with sc (sc / 16) and the bias term, which is exact because
+// the fused result is an integer below 2048.  d and dmin are applied in f32 by
+// the epilogue.
+template <int g>
+__device__ __forceinline__ void conv_q4k_half(const uint8_t *raw, const uint32_t (&sc)[8], uint8_t *ast, int r) {
+#pragma unroll
+    for (int gg = 0; gg < 2; gg++) {
+        const int G = 2 * g + gg;  // qs group: sub-blocks 2G (low), 2G+1 (high nibbles)
+        const __half2 slo = __float2half2_rn((float)sc[2 * G]), clo = __float2half2_rn(-1024.f * (float)sc[2 * G]);
+        const __half2 shi = __float2half2_rn((float)sc[2 * G + 1] * 0.0625f),
+                      chi = __float2half2_rn(-64.f * (float)sc[2 * G + 1]);
+#pragma unroll
+        for (int w4 = 0; w4 < 2; w4++) {
+            const uint4 Q = lds128(raw + 16 + 32 * G + 16 * w4);
+            const uint32_t qw[4] = {Q.x, Q.y, Q.z, Q.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t W = qw[i], W8 = W >> 8;
+                uint4 o;
+                o.x = h22u(__hfma2(u2h2((W & 0x000F000Fu) | 0x64006400u), slo, clo));
+                o.y = h22u(__hfma2(u2h2((W8 & 0x000F000Fu) | 0x64006400u), slo, clo));
+                o.z = h22u(__hfma2(u2h2((W & 0x00F000F0u) | 0x64006400u), shi, chi));
+                o.w = h22u(__hfma2(u2h2((W8 & 0x00F000F0u) | 0x64006400u), shi, chi));
+                const int cc = 8 * gg + 4 * w4 + i;  // chunk within the half
+                *reinterpret_cast<uint4 *>(ast + (cc >> 3) * (kRows * 128) + sw128_off(r, cc & 7)) = o;
+            }
+        }
+    }
+}
+
+// The eight 6-bit (sc, m) pairs of a Q4_K super-block from its 12 scale bytes
+// (get_scale_min_k4, kernels/proj_q4k.comp:46-58).
+__device__ __forceinline__ void q4k_scale_mins(const uint4 &H, uint32_t (&sc)[8], uint32_t (&mn)[8]) {
+    const uint32_t q[3] = {H.y, H.z, H.w};
+    auto qb = [&](int j) { return (q[j >> 2] >> (8 * (j & 3))) & 0xFFu; };
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        if (j < 4) {
+            sc[j] = qb(j) & 63u;
+            mn[j] = qb(j + 4) & 63u;
+        } else {
+            sc[j] = (qb(j + 4) & 0xFu) | ((qb(j - 4) >> 6) << 4);
+            mn[j] = (qb(j + 4) >> 4) | ((qb(j) >> 6) << 4);
+        }
+    }
+}
+
+// Q8_0: half h (blocks 4h..4h+3) of one row -> 16 chunks of f16(d * q) (one
+// rounding per weight).  Block b's q bytes start at byte 34b + 2 (two bytes
+// off word alignment for even b), its f16 d at byte 34b.
+__device__ __forceinline__ void conv_q8_half(const uint8_t *raw, int h, uint32_t ref_mask, uint8_t *ast, int r) {
+    const uint32_t *W = reinterpret_cast<const uint32_t *>(raw);
+    const __half2 k1152 = __float2half2_rn(1152.f);
+#pragma unroll
+    for (int bb = 0; bb < 4; bb++) {
+        const int b = 4 * h + bb;
+        const int wq = (17 * b + 1) >> 1, sh = (b & 1) ? 0 : 16;
+        const uint32_t dw = W[(b & 1) ? (17 * (b - 1)) / 2 + 8 : (17 * b) / 2];
+        const uint32_t dbits = fix_sub_h2((b & 1) ? (dw >> 16) : (dw & 0xFFFFu), ref_mask) & 0xFFFFu;
+        const __half2 d2 = u2h2(dbits | (dbits << 16));
+        uint32_t qw[9];
+#pragma unroll
+        for (int i = 0; i < 9; i++) qw[i] = (i < 8 || sh) ? W[wq + i] : 0u;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            uint4 o;
+            uint32_t t[2];
+#pragma unroll
+            for (int u = 0; u < 2; u++) t[u] = __funnelshift_r(qw[2 * i + u], qw[2 * i + u + 1], sh);
+            o.x = h22u(__hmul2(__hsub2(u2h2((t[0] & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
+            o.y = h22u(__hmul2(__hsub2(u2h2(((t[0] >> 8) & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
+            o.z = h22u(__hmul2(__hsub2(u2h2((t[1] & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
+            o.w = h22u(__hmul2(__hsub2(u2h2(((t[1] >> 8) & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
+            const int cc = 4 * bb + i;
+            *reinterpret_cast<uint4 *>(ast + (cc >> 3) * (kRows * 128) + sw128_off(r, cc & 7)) = o;
+        }
+    }
+}
+
+// Byte offset of element (row, kk) of a 16-wide K-major operand in the
+// no-swizzle core-matrix layout (8 rows x 16 bytes per core matrix, the two
+// K groups 128 bytes apart, 8-row groups 256 bytes apart).
+__host__ __device__ __forceinline__ uint32_t core16_off(int row, int kk) {
+    return (uint32_t)((row >> 3) * 256 + (kk >> 3) * 128 + (row & 7) * 16 + (kk & 7) * 2);
+}
+
+// x [m, k] f32 -> x16 [2 NT, k] f16 (hi rows, then lo rows) in the
+// converters' k order, times a per-token power of two (rows m..NT-1 zero);
+// inv[t] = its inverse.  For Q4_K also the sub-block sums of the scaled
+// activations divided by 32 (exact power of two, keeps them below 2^15), per
+// super-block as a 2 NT x 16 K-major operand: columns 0..7 the eight sums
+// (hi in row t, lo in row NT + t), columns 8..15 zero.  One CTA per token slot.
+__global__ void x16_pack_kernel(const float *__restrict__ x, int m, int k, int q8, int nt, __half *__restrict__ x16,
+                                uint8_t *__restrict__ sx16, float *__restrict__ inv) {
+    const int t = blockIdx.x;
+    __shared__ float red[32];
+    float mx = 0.f;
+    if (t < m)
+        for (int i = threadIdx.x; i < k; i += blockDim.x) mx = fmaxf(mx, fabsf(x[(size_t)t * k + i]));
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    float s = 0.f, iv = 0.f;
+    act_scale(red[0], s, iv);
+    if (threadIdx.x == 0) inv[t] = t < m ? iv : 0.f;
+    for (int pos = threadIdx.x; pos < k; pos += blockDim.x) {
+        const int sb = pos >> 8;
+        const float v = t < m ? x[(size_t)t * k + sb * 256 + perm_elem(q8 != 0, pos & 255)] * s : 0.f;
+        const __half hi = __float2half_rn(v);
+        x16[(size_t)t * k + pos] = hi;
+        x16[(size_t)(t + nt) * k + pos] = __float2half_rn(v - __half2float(hi));
+    }
+    if (q8) return;
+    const int S = k >> 8, blk = 2 * nt * 32;
+    for (int idx = threadIdx.x; idx < S * 16; idx += blockDim.x) {
+        const int sb = idx >> 4, kk = idx & 15;
+        float v = 0.f;
+        if (kk < 8 && t < m) {
+            const float *p = x + (size_t)t * k + sb * 256 + kk * 32;
+#pragma unroll 8
+            for (int e = 0; e < 32; e++) v += p[e];
+            v *= s * 0.03125f;
+        }
+        const __half hi = __float2half_rn(v);
+        uint8_t *b = sx16 + (size_t)sb * blk;
+        *reinterpret_cast<__half *>(b + core16_off(t, kk)) = hi;
+        *reinterpret_cast<__half *>(b + core16_off(t + nt, kk)) = __float2half_rn(v - __half2float(hi));
+    }
+}
+
+struct GemmLayout {
+    size_t a = 0, x = 0, raw = 0, sc = 0, bars = 0, tslot = 0, total = 0;
+    int AS = 0, XS = 0, RS = 0, ND = 0, astage = 0, xstage = 0;
+};
+
+// Shared memory: A stages (+ the 4 KB min-term operand for Q4_K), activation
+// stages (+ the sub-block sums for Q4_K), raw weight stages, per-unit (d, dmin)
+// slots (Q4_K), barriers.  Every stage size is a multiple of 1024 bytes.
+template <class F, int NT>
+__host__ __device__ constexpr GemmLayout gemm_layout() {
+    GemmLayout L{};
+    L.AS = 3;
+    L.XS = NT >= 32 ? 3 : 4;
+    L.RS = F::kQ8 ? 2 : 3;
+    L.ND = F::kQ8 ? 2 : 4;
+    L.astage = kAStage + (F::kQ8 ? 0 : kRows * 32);
+    L.xstage = 2 * NT * 256 + (F::kQ8 ? 0 : 2 * NT * 32);
+    L.a = 0;
+    L.x = L.a + (size_t)L.AS * L.astage;
+    L.raw = L.x + (size_t)L.XS * L.xstage;
+    L.sc = L.raw + (size_t)L.RS * kRows * F::kRowBytes;
+    L.bars = L.sc + (F::kQ8 ? 0 : (size_t)L.ND * kRows * 8);
+    L.tslot = L.bars + (size_t)(2 * L.RS + 2 * L.AS + 2 * L.XS + 3 * L.ND + 1) * 8;
+    L.total = L.tslot + 16 + 1024;  // + slack to 1024-align the base
+    return L;
+}
+
+template <class F, int NT>
+__global__ void __launch_bounds__(kGemmWarps * 32, 1)
+    dq_gemm_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+                   const uint8_t *__restrict__ sx16, const float *__restrict__ inv, float *__restrict__ y, int m,
+                   int k, int n, int half_mode, unsigned *__restrict__ status) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    constexpr GemmLayout L = gemm_layout<F, NT>();
+    constexpr bool PU = !F::kQ8;  // Q4_K: one accumulator per unit, scaled in f32
+    constexpr int NB = 2 * NT;    // UMMA N: hi and lo rows of the tokens
+    constexpr int kXTiles = NB * 256;
+    constexpr int kRawStage = kRows * F::kRowBytes;
+    constexpr int ND = L.ND;
+    constexpr int kBufCols = PU ? 2 * NB : NB;  // Q4_K: main product, then the min term
+    constexpr int kCols = ND * kBufCols;        // power of two >= 32
+    uint8_t *a_ring = smem + L.a, *x_ring = smem + L.x, *raw_ring = smem + L.raw;
+    float2 *dslot = reinterpret_cast<float2 *>(smem + L.sc);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *raw_full = bars, *raw_empty = raw_full + L.RS;
+    uint64_t *a_full = raw_empty + L.RS, *a_empty = a_full + L.AS;
+    uint64_t *x_full = a_empty + L.AS, *x_empty = x_full + L.XS;
+    uint64_t *d_full = x_empty + L.XS, *d_empty = d_full + ND, *s_full = d_empty + ND, *drain = s_full + ND;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + L.tslot);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = k >> 8, T = (n + kRows - 1) / kRows;
+    const long long TS = (long long)T * S;
+    const int U0 = (int)(TS * blockIdx.x / gridDim.x), U1 = (int)(TS * (blockIdx.x + 1) / gridDim.x);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < L.RS; i++) mbar_init(raw_full + i, 1), mbar_init(raw_empty + i, kConvWarps);
+        for (int i = 0; i < L.AS; i++) mbar_init(a_full + i, 4), mbar_init(a_empty + i, 1);
+        for (int i = 0; i < L.XS; i++) mbar_init(x_full + i, 1), mbar_init(x_empty + i, 1);
+        for (int i = 0; i < ND; i++) mbar_init(d_full + i, 1), mbar_init(d_empty + i, 4), mbar_init(s_full + i, 4);
+        mbar_init(drain, 1);
+        mbar_init_fence();
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tslot)),
+                     "r"(kCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    bool ok = true;
+    auto fail = [&]() {
+        ok = false;
+        atomicOr(status, LC_DEV_WAIT_TIMEOUT);
+    };
+    auto seg_last = [&](int u) { return u == U1 - 1 || (u + 1) / S != u / S; };
+
+    if (warp == 0) {
+        if (lane == 0) {  // producer
+            const uint64_t pol = l2_evict_first_policy();  // weights: read once
+            uint64_t xpol;                                  // activations: read by every CTA
+            asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(xpol));
+            for (int u = U0; u < U1 && ok; u++) {
+                const int j = u - U0, tile = u / S, sb = u - tile * S;
+                const int rs = j % L.RS;
+                if (!mbar_wait(raw_empty + rs, ((j / L.RS) & 1) ^ 1)) { fail(); break; }
+                mbar_expect_tx(raw_full + rs, kRawStage);
+                tma_load_2d(raw_ring + (size_t)rs * kRawStage, &tmw, sb * F::kBoxX, tile * kRows, raw_full + rs, pol);
+                for (int h = 0; h < 2 && ok; h++) {
+                    const int xi = 2 * j + h, xs = xi % L.XS;
+                    if (!mbar_wait(x_empty + xs, ((xi / L.XS) & 1) ^ 1)) { fail(); break; }
+                    uint8_t *xst = x_ring + (size_t)xs * L.xstage;
+                    const bool mins = PU && h == 0;
+                    mbar_expect_tx(x_full + xs, kXTiles + (mins ? NB * 32 : 0));
+#pragma unroll
+                    for (int kc = 0; kc < 2; kc++)
+                        tma_load_2d(xst + kc * NB * 128, &tmx, sb * 256 + h * 128 + kc * 64, 0, x_full + xs, xpol);
+                    if (mins) bulk_load(xst + kXTiles, sx16 + (size_t)sb * NB * 32, NB * 32, x_full + xs, xpol);
+                }
+            }
+        }
+    } else if (warp <= kConvWarps) {  // converters: group g converts half g of row r of every unit
+        const int g = (warp - 1) >> 2, r = ((warp - 1) & 3) * 32 + lane;
+        const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
+        if (PU && g == 0)  // columns 8..15 of the min-term operand stay zero
+            for (int i = 0; i < L.AS; i++)
+                *reinterpret_cast<uint4 *>(a_ring + (size_t)i * L.astage + kAStage + core16_off(r, 8)) =
+                    make_uint4(0u, 0u, 0u, 0u);
+        for (int u = U0; u < U1 && ok; u++) {
+            const int j = u - U0, rs = j % L.RS;
+            if (!mbar_wait(raw_full + rs, (j / L.RS) & 1)) { fail(); break; }
+            const uint8_t *raw = raw_ring + (size_t)rs * kRawStage + (size_t)r * F::kRowBytes;
+            const int ai = 2 * j + g, as = ai % L.AS;
+            if (!mbar_wait(a_empty + as, ((ai / L.AS) & 1) ^ 1)) { fail(); break; }
+            uint8_t *ast = a_ring + (size_t)as * L.astage;
+            if constexpr (PU) {
+                const uint4 H = lds128(raw);
+                uint32_t sc[8], mn[8];
+                q4k_scale_mins(H, sc, mn);
+                if (g == 0)
+                    conv_q4k_half<0>(raw, sc, ast, r);
+                else
+                    conv_q4k_half<1>(raw, sc, ast, r);
+                if (g == 0) {
+                    // min-term operand: m_j (exact in f16) in columns 0..7 of row r
+                    uint4 o;
+                    o.x = h22u(__floats2half2_rn((float)mn[0], (float)mn[1]));
+                    o.y = h22u(__floats2half2_rn((float)mn[2], (float)mn[3]));
+                    o.z = h22u(__floats2half2_rn((float)mn[4], (float)mn[5]));
+                    o.w = h22u(__floats2half2_rn((float)mn[6], (float)mn[7]));
+                    *reinterpret_cast<uint4 *>(ast + kAStage + core16_off(r, 0)) = o;
+                    // (d, 32 dmin) of the unit for the epilogue, once its slot is free
+                    const int db = j % ND;
+                    if (!mbar_wait(d_empty + db, ((j / ND) & 1) ^ 1)) { fail(); break; }
+                    const float2 dd = scales2_f32(H.x, ref_mask);
+                    dslot[db * kRows + r] = make_float2(dd.x, 32.f * dd.y);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(s_full + db);
+                }
+            } else {
+                conv_q8_half(raw, g, ref_mask, ast, r);
+            }
+            fence_proxy_async_smem();  // generic-proxy writes -> the tensor cores' reads
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(a_full + as);
+                mbar_arrive(raw_empty + rs);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = umma_idesc_f16(kRows, NB);
+            const uint32_t a0 = smem_addr(a_ring), x0 = smem_addr(x_ring);
+            int run = 0;  // Q8_0: accumulator runs started
+            for (int u = U0; u < U1 && ok; u++) {
+                const int j = u - U0;
+                const bool first_seg = u == U0 || u / S != (u - 1) / S;
+                int db;
+                if constexpr (PU) {
+                    db = j % ND;
+                    if (!mbar_wait(d_empty + db, ((j / ND) & 1) ^ 1)) { fail(); break; }
+                    tc_fence_after();
+                } else {
+                    db = run % ND;
+                    if (first_seg) {
+                        if (!mbar_wait(d_empty + db, ((run / ND) & 1) ^ 1)) { fail(); break; }
+                        tc_fence_after();
+                    }
+                }
+                const uint32_t dcol = tbase + db * kBufCols;
+                for (int h = 0; h < 2 && ok; h++) {
+                    const int ai = 2 * j + h, as = ai % L.AS, xs = ai % L.XS;
+                    if (!mbar_wait(a_full + as, (ai / L.AS) & 1) || !mbar_wait(x_full + xs, (ai / L.XS) & 1)) {
+                        fail();
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t ab = a0 + as * L.astage, xb = x0 + xs * L.xstage;
+                    const bool fresh = PU || first_seg;
+#pragma unroll
+                    for (int kk = 0; kk < 8; kk++) {
+                        const uint64_t ad = umma_desc_sw128(ab + (kk >> 2) * (kRows * 128) + (kk & 3) * 32);
+                        const uint64_t bd = umma_desc_sw128(xb + (kk >> 2) * (NB * 128) + (kk & 3) * 32);
+                        umma_f16(dcol, ad, bd, idesc, (fresh && h == 0 && kk == 0) ? 0u : 1u);
+                    }
+                    if (PU && h == 0)  // min term: sum_j m_j * (sub-block sum of x) / 32
+                        umma_f16(dcol + NB, umma_desc_core16(ab + kAStage), umma_desc_core16(xb + kXTiles), idesc,
+                                 0u);
+                    umma_commit(a_empty + as);
+                    umma_commit(x_empty + xs);
+                }
+                if (!ok) break;
+                if (PU) {
+                    umma_commit(d_full + db);
+                } else if (seg_last(u)) {
+                    umma_commit(d_full + db);
+                    run++;
+                }
+            }
+            // everything issued has completed before the TMEM is freed
+            umma_commit(drain);
+            if (!mbar_wait(drain, 0)) atomicOr(status, LC_DEV_WAIT_TIMEOUT);
+        }
+    } else {  // epilogue: TMEM lanes 32q..32q+31 = tile rows
+        const int q = warp & 3;
+        const uint32_t lanes = (uint32_t)(32 * q) << 16;
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = 0.f;
+        int run = 0;
+        for (int u = U0; u < U1 && ok; u++) {
+            const int j = u - U0;
+            const bool last = seg_last(u);
+            if (!PU && !last) continue;
+            const int db = PU ? j % ND : run % ND;
+            const uint32_t par = PU ? (j / ND) & 1 : (run / ND) & 1;
+            if (!mbar_wait(d_full + db, par)) { fail(); break; }
+            tc_fence_after();
+            const uint32_t col = tbase + lanes + db * kBufCols;
+            if constexpr (PU) {
+                if (!mbar_wait(s_full + db, par)) { fail(); break; }
+                const float2 dd = dslot[db * kRows + 32 * q + lane];
+#pragma unroll
+                for (int c = 0; c < NT / 16; c++) {
+                    float ph[16], pl[16], mh[16], ml[16];
+                    tmem_ld16(col + 16 * c, ph);
+                    tmem_ld16(col + NT + 16 * c, pl);
+                    tmem_ld16(col + NB + 16 * c, mh);
+                    tmem_ld16(col + NB + NT + 16 * c, ml);
+                    tmem_ld_wait();
+                    tmem_regs_ready(ph), tmem_regs_ready(pl), tmem_regs_ready(mh), tmem_regs_ready(ml);
+#pragma unroll
+                    for (int i = 0; i < 16; i++)
+                        acc[16 * c + i] += dd.x * (ph[i] + pl[i]) - dd.y * (mh[i] + ml[i]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < NT / 16; c++) {
+                    float ph[16], pl[16];
+                    tmem_ld16(col + 16 * c, ph);
+                    tmem_ld16(col + NT + 16 * c, pl);
+                    tmem_ld_wait();
+                    tmem_regs_ready(ph), tmem_regs_ready(pl);
+#pragma unroll
+                    for (int i = 0; i < 16; i++) acc[16 * c + i] = ph[i] + pl[i];
+                }
+                run++;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d_empty + db);
+            if (last) {
+                const int row = (u / S) * kRows + 32 * q + lane;
+                if (row < n)
+#pragma unroll
+                    for (int t = 0; t < NT; t++)
+                        if (t < m) atomicAdd(y + (size_t)t * n + row, acc[t] * inv[t]);
+#pragma unroll
+                for (int t = 0; t < NT; t++) acc[t] = 0.f;
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(kCols) : "memory");
+    }
+}
+
+// ---- host -------------------------------------------------------------------
+
+template <class F>
+int weight_map_rows128(CUtensorMap *tm, const void *w, uint32_t k, uint32_t n) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+    int s = lc_tensor_map_encoder(&enc);
+    if (s) return s;
+    const cuuint64_t S = k / 256;
+    cuuint64_t dims[2] = {S * F::kBoxX, (cuuint64_t)n};
+    cuuint64_t strides[1] = {S * F::kRowBytes};
+    cuuint32_t box[2] = {(cuuint32_t)F::kBoxX, (cuuint32_t)kRows};
+    cuuint32_t es[2] = {1, 1};
+    const CUtensorMapDataType dt = F::kQ8 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT64;
+    const CUresult r = enc(tm, dt, 2, const_cast<void *>(w), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    LC_REQUIRE(r == CUDA_SUCCESS, LC_ERR_CUDA, "cuTensorMapEncodeTiled (weights) failed (%d)", (int)r);
+    return LC_OK;
+}
+
+int x16_map(CUtensorMap *tm, const void *x16, uint32_t k, int nt) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+    int s = lc_tensor_map_encoder(&enc);
+    if (s) return s;
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)nt};
+    cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)nt};
+    cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(x16), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    LC_REQUIRE(r == CUDA_SUCCESS, LC_ERR_CUDA, "cuTensorMapEncodeTiled (activations) failed (%d)", (int)r);
+    return LC_OK;
+}
+
+template <class F, int NT>
+int launch_dq_gemm(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
+    constexpr GemmLayout L = gemm_layout<F, NT>();
+    LC_REQUIRE(L.total <= ctx->smem_optin, LC_ERR_UNSUPPORTED, "dq_gemm: %zu bytes of shared memory needed", L.total);
+    const size_t x16_bytes = (size_t)2 * NT * k * 2;
+    const size_t sx_bytes = F::kQ8 ? 0 : (size_t)(k / 256) * 2 * NT * 32;  // multiple of 16
+    uint8_t *scr = (uint8_t *)lc_scratch(ctx, LC_SCRATCH_PACK, x16_bytes + sx_bytes + NT * 4 + 256);
+    if (!scr) return LC_ERR_OOM;
+    __half *x16 = reinterpret_cast<__half *>(scr);
+    uint8_t *sx16 = scr + x16_bytes;
+    float *inv = reinterpret_cast<float *>(scr + x16_bytes + sx_bytes);
+    CUtensorMap tmw, tmx;
+    int s = weight_map_rows128<F>(&tmw, w, k, n);
+    if (s) return s;
+    s = x16_map(&tmx, x16, k, 2 * NT);
+    if (s) return s;
+    LC_CUDA(cudaMemsetAsync(y, 0, (size_t)m * n * 4, ctx->stream));
+    x16_pack_kernel<<<NT, 256, 0, ctx->stream>>>(x, (int)m, (int)k, F::kQ8 ? 1 : 0, NT, x16, sx16, inv);
+    s = lc_set_smem_attr((const void *)dq_gemm_kernel<F, NT>, L.total);
+    if (s) return s;
+    const long long TS = (long long)((n + kRows - 1) / kRows) * (k / 256);
+    const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, TS));
+    dq_gemm_kernel<F, NT><<<grid, kGemmWarps * 32, L.total, ctx->stream>>>(tmw, tmx, sx16, inv, y, (int)m, (int)k,
+                                                                           (int)n, ctx->half_mode, ctx->dev_status);
+    return LC_OK;
+}
+
+}  // namespace
+
+namespace lc {
+
+// Quantized GEMM on tcgen05 for 5..32 tokens; LC_ERR_UNSUPPORTED when the
+// shape is not covered (the caller falls back).
+int gemm_dq(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
+    if (m == 0 || m > 32 || k % 256 != 0 || ((uintptr_t)w & 15) != 0 || (long long)k * 32 >= (1ll << 31))
+        return LC_ERR_UNSUPPORTED;
+    const uint8_t *wb = (const uint8_t *)w;
+    if (dtype == LC_Q4_K)
+        return m <= 16 ? launch_dq_gemm<GQ4K, 16>(ctx, x, wb, y, m, k, n) : launch_dq_gemm<GQ4K, 32>(ctx, x, wb, y, m, k, n);
+    if (dtype == LC_Q8_0)
+        return m <= 16 ? launch_dq_gemm<GQ8_0, 16>(ctx, x, wb, y, m, k, n)
+                       : launch_dq_gemm<GQ8_0, 32>(ctx, x, wb, y, m, k, n);
+    return LC_ERR_UNSUPPORTED;
+}
+
+}  // namespace lc

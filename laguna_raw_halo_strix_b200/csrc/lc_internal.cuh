@@ -17,6 +17,9 @@ struct lc_ctx {
     cudaStream_t stream = nullptr;
     int sync = 0;
     int half_mode = LC_HALF_REF;
+    // 1: 5..32-token Q4_K / Q8_0 projections run the tcgen05 GEMM (lc_gemm.cu);
+    // 0: the mma.sync tiled kernels.  Set from LC_GEMM_TC at lc_init (default 1).
+    int gemm_tc = 1;
     // Grow-only scratch slots (see LC_SCRATCH_*).
     void *scratch[8] = {};
     size_t scratch_bytes[8] = {};
@@ -144,4 +147,7 @@ int proj_q4k(lc_ctx *ctx, const float *x, const void *w, float *c, uint32_t m, u
 int proj_q8_0(lc_ctx *ctx, const float *x, const void *w, float *c, uint32_t m, uint32_t k, uint32_t n);
 int proj_f32(lc_ctx *ctx, const float *x, const float *w, float *c, uint32_t m, uint32_t k, uint32_t n,
              uint32_t row_major);
+// tcgen05 GEMM for 5..32 tokens (lc_gemm.cu); LC_ERR_UNSUPPORTED when the
+// shape is not covered.
+int gemm_dq(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n);
 }  // namespace lc

@@ -1567,6 +1567,9 @@ int proj_q4k(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m, 
     if (m <= 4) {
         const TmaPlan p = q4k_tma_plan(ctx, (int)m, (int)k, (int)n);
         if (p.R) return launch_q4k_tma(ctx, p, m, x, w, c, k, n);
+    } else if (ctx->gemm_tc) {
+        const int s = gemm_dq(ctx, LC_Q4_K, x, w, c, m, k, n);
+        if (s != LC_ERR_UNSUPPORTED) return s;
     }
     return proj_q4k_tiled(ctx, x, w, c, m, k, n, nullptr);
 }
@@ -1617,6 +1620,9 @@ int proj_q8_0(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m,
     if (m <= 4 && k % 256 == 0 && ((uintptr_t)wv & 15) == 0) {
         const TmaPlan p = tma_plan<FmtQ8_0>(ctx, (int)m, (int)k, (int)n);
         if (p.R) return launch_tma<FmtQ8_0>(ctx, p, m, x, w, c, k, n);
+    } else if (m > 4 && ctx->gemm_tc) {
+        const int s = gemm_dq(ctx, LC_Q8_0, x, w, c, m, k, n);
+        if (s != LC_ERR_UNSUPPORTED) return s;
     }
     if (m <= 4) {
         const int S = (int)(k / 64);

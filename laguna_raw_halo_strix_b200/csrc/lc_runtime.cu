@@ -6,6 +6,8 @@
 #include <map>
 #include <mutex>
 
+#include <stdlib.h>
+
 #include "lc_internal.cuh"
 
 static thread_local char g_err[1024] = "";
@@ -51,6 +53,7 @@ extern "C" int lc_init(int device, lc_ctx **out) {
     ctx->device = device;
     ctx->num_sms = prop.multiProcessorCount;
     ctx->smem_optin = prop.sharedMemPerBlockOptin;
+    if (const char *e = getenv("LC_GEMM_TC")) ctx->gemm_tc = e[0] != '0';
     cudaError_t e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         delete ctx;
