@@ -5,33 +5,41 @@
 //
 // One CTA per SM, warp-specialised:
 //   warp 0      producer: TMA copies of raw weight units (128 rows x 256
-//               elements), of the tokens' f16 activations and (Q4_K) of their
-//               sub-block sums;
-//   warps 1-8   converters: one weight row per thread, warps 1-4 the first
-//               half of a unit, warps 5-8 the second; they write f16 straight
-//               into the 128-byte-swizzled K-major layout the UMMA reads;
+//               elements) and of the tokens' f16 activations (+ their Q4_K
+//               sub-block sums);
+//   warps 1-8   converters: one weight row per thread (the row is the TMEM
+//               lane the warp may access), warps 1-4 the first half of a unit,
+//               warps 5-8 the second; they dequantise to f16 in registers and
+//               store it into tensor memory with tcgen05.st;
 //   warp 9      allocates the tensor memory and issues tcgen05.mma
-//               (kind::f16, M = 128 weight rows, N = 2 NT, K = 16) with f32
-//               accumulation in TMEM;
-//   warps 10-13 epilogue: tcgen05.ld of the accumulators, scales, f32 atomic
-//               adds into y (zeroed before the launch).
+//               (kind::f16, A = weights from TMEM, M = 128 rows, B = tokens
+//               from shared memory, N = 2 NT, K = 16) with f32 accumulation in
+//               TMEM;
+//   warps 10-13 epilogue: tcgen05.ld of each unit's accumulators, scales, and
+//               at the end of a tile's run f32 atomic adds into y (zeroed by
+//               the packing kernel).
 // Units (128-row tile, super-block) are flattened tile-major and cut into one
 // contiguous range per CTA.
 //
+// With only 2 NT token columns per MMA, an A operand in shared memory would
+// cost 4 KB of shared-memory reads per 16-cycle MMA plus the converters'
+// writes: shared-memory bandwidth, not the tensor cores, would bound the
+// kernel.  Tensor memory takes that traffic instead (columns 0-255: four A
+// half-unit stages of 64 columns; columns 256-511: accumulators).
+//
 // Q4_K keeps the weights exact on the tensor cores: A holds the integers
 // sc_j * q, so each unit's product P = sum sc_j q x and min term
-// M = sum_j m_j Sx_j (Sx_j the sub-block sums of x, one extra K = 16 MMA) land
-// in their own TMEM columns, and the epilogue accumulates d P - dmin M in f32
-// per unit (four accumulator buffers in flight).  Q8_0 weights become
-// f16(d q) (one rounding) and accumulate in TMEM over a tile's run of units
-// (two buffers, the epilogue of a run overlapping the next run's MMAs).
+// M = sum_j m_j Sx_j (Sx_j the sub-block sums of x, one extra K = 16 MMA with
+// both operands in shared memory) land in their own TMEM columns, and the
+// epilogue accumulates d P - dmin M in f32.  Q8_0 weights become f16(d q) (one
+// rounding).
 //
-// Activations: x [m, k] f32 times a per-token power of two (exact) becomes
-// x16 [2 NT, k] f16: rows 0..NT-1 the f16 value, rows NT..2NT-1 the f16 of the
-// remainder (rows past m zero), so the UMMA (N = 2 NT) sees x to ~22 bits and
-// the epilogue adds the two columns of a token.  k is in the order the
-// converters produce within each super-block (a fixed permutation: the dot
-// product is the same).
+// Activations: x [m, k] f32 times a power of two per (token, super-block)
+// (exact) becomes x16 [2 NT, k] f16: rows 0..NT-1 the f16 value, rows
+// NT..2NT-1 the f16 of the remainder (rows past m zero), so the UMMA sees x to
+// ~22 bits; the epilogue adds the two columns of a token and multiplies by the
+// inverse scale.  Within each super-block k is in the order the converters
+// produce (a fixed permutation; the dot product is the same).
 //
 // Every mbarrier wait is bounded; on expiry the kernel records
 // LC_DEV_WAIT_TIMEOUT in the context's status word, stops issuing work, lets
@@ -40,20 +48,21 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
-#include <map>
-#include <mutex>
 
 #include "lc_internal.cuh"
 #include "lc_sm100.cuh"
 
 namespace {
 
-constexpr int kRows = 128;      // weight rows per tile (UMMA M)
+constexpr int kRows = 128;  // weight rows per tile (UMMA M)
 constexpr int kConvWarps = 8;
 constexpr int kMmaWarp = 1 + kConvWarps;
 constexpr int kGemmWarps = kMmaWarp + 5;  // + the MMA warp and 4 epilogue warps
-constexpr int kHalfK = 128;     // k per A / x stage (half a super-block)
-constexpr int kAStage = kRows * kHalfK * 2;  // 32 KB of f16
+constexpr int kTmemCols = 512;
+constexpr int kAStages = 4;     // TMEM A stages of half a unit (K = 128)
+constexpr int kACols = 64;      // 128 f16 per lane
+constexpr int kAccBase = kAStages * kACols;
+constexpr int kMinBytes = kRows * 32;  // Q4_K min-term operand: 128 rows x 16 f16
 
 // ---- tcgen05 ---------------------------------------------------------------
 
@@ -87,12 +96,23 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
     return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
+// D (TMEM) (+)= A (shared memory) * B (shared memory)^T.
+__device__ __forceinline__ void umma_f16_ss(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(dtmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D (TMEM) (+)= A (TMEM: row i in lane i, two f16 per column) * B (shared memory)^T.
+__device__ __forceinline__ void umma_f16_ts(uint32_t dtmem, uint32_t atmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(dtmem),
+        "r"(atmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -106,6 +126,8 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 
+// 16 consecutive 32-bit TMEM columns of this thread's lane -> registers
+// (complete after tmem_ld_wait).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
     asm volatile(
@@ -129,14 +151,18 @@ __device__ __forceinline__ void tmem_regs_ready(float (&v)[N]) {
     for (int i = 0; i < N; i++) asm volatile("" : "+f"(v[i])::"memory");
 }
 
-// Untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16).
-__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t pol) {
+// Registers -> 16 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
     asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n" ::"r"(
-            smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
 }
+
+// Every tcgen05.st this thread issued has written the tensor memory.
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
@@ -146,10 +172,13 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
 }
 
-// Byte offset of the 16-byte chunk `c` (k = 8c..8c+7 within a 64-wide atom
-// column) of row r in a K-major 128B-swizzled tile of 64-element columns.
-__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
-    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + (((c & 7) ^ (r & 7)) << 4));
+// Untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
+        : "memory");
 }
 
 // ---- formats ----------------------------------------------------------------
@@ -177,29 +206,21 @@ __device__ __forceinline__ uint32_t fix_sub_h2(uint32_t h2, uint32_t ref_mask) {
 __device__ __forceinline__ __half2 u2h2(uint32_t v) { return *reinterpret_cast<__half2 *>(&v); }
 __device__ __forceinline__ uint32_t h22u(__half2 v) { return *reinterpret_cast<uint32_t *>(&v); }
 
-// k order within a super-block (position -> element), shared by the
-// converters and the activation packing.
-//   Q4_K: chunk c (8 positions) is qs word c (bytes 4c..4c+3, group G = c/8,
-//         p = 4(c%8)): elements 64G + [p, p+2, p+1, p+3, 32+p, 34+p, 33+p, 35+p].
-//   Q8_0: chunk c = 4b + i is q words 2i, 2i+1 of block b: elements
-//         32b + 8i + [0, 2, 1, 3, 4, 6, 5, 7].
-__host__ __device__ __forceinline__ int perm_elem(bool q8, int pos) {
-    const int c = pos >> 3, e = pos & 7;
-    const int sw = (e & 4) | ((e & 1) << 1) | ((e >> 1) & 1);  // [0,2,1,3,4,6,5,7]
-    if (q8) return 32 * (c >> 2) + 8 * (c & 3) + sw;
-    const int G = c >> 3, p = 4 * (c & 7);
-    return 64 * G + p + ((e & 4) << 3) + (sw & 3);
-}
+// k order within a super-block.  Position chunk c (8 positions, 4 TMEM
+// columns) holds elements
+//   Q4_K: qs word c (G = c/8, p = 4(c%8)): 64G + [p, p+2, p+1, p+3, 32+p, 34+p, 33+p, 35+p]
+//   Q8_0: block b = c/4, words 2i, 2i+1 (i = c%4): 32b + 8i + [0, 2, 1, 3, 4, 6, 5, 7]
+// i.e. two runs of four consecutive elements e0..e0+3 and e1..e1+3, each in
+// the order [0, 2, 1, 3] (what the byte-pair extraction yields).
 
-// Q4_K: half g (sub-blocks 4g..4g+3) of one row of a unit -> 16 chunks of 8
-// f16, written to row r of the A stage (two 64-column atoms).  The values are
-// the exact integers sc_j * q (at most 63 * 15): each pair comes from one
-// HFMA2 of the nibble pair biased into f16 (1024 + q, or 1024 + 16 q for the
-// high nibbles) with sc (sc / 16) and the bias term, which is exact because
-// the fused result is an integer below 2048.  d and dmin are applied in f32 by
-// the epilogue.
+// Q4_K: half g (sub-blocks 4g..4g+3) of one row of a unit -> 64 TMEM columns
+// at taddr.  The values are the exact integers sc_j * q (at most 63 * 15): each
+// pair comes from one HFMA2 of the nibble pair biased into f16 (1024 + q, or
+// 1024 + 16 q for the high nibbles) with sc (sc / 16) and the bias term, which
+// is exact because the fused result is an integer below 2048.  d and dmin are
+// applied in f32 by the epilogue.
 template <int g>
-__device__ __forceinline__ void conv_q4k_half(const uint8_t *raw, const uint32_t (&sc)[8], uint8_t *ast, int r) {
+__device__ __forceinline__ void conv_q4k_half(const uint8_t *raw, const uint32_t (&sc)[8], uint32_t taddr) {
 #pragma unroll
     for (int gg = 0; gg < 2; gg++) {
         const int G = 2 * g + gg;  // qs group: sub-blocks 2G (low), 2G+1 (high nibbles)
@@ -210,17 +231,16 @@ __device__ __forceinline__ void conv_q4k_half(const uint8_t *raw, const uint32_t
         for (int w4 = 0; w4 < 2; w4++) {
             const uint4 Q = lds128(raw + 16 + 32 * G + 16 * w4);
             const uint32_t qw[4] = {Q.x, Q.y, Q.z, Q.w};
+            uint32_t o[16];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const uint32_t W = qw[i], W8 = W >> 8;
-                uint4 o;
-                o.x = h22u(__hfma2(u2h2((W & 0x000F000Fu) | 0x64006400u), slo, clo));
-                o.y = h22u(__hfma2(u2h2((W8 & 0x000F000Fu) | 0x64006400u), slo, clo));
-                o.z = h22u(__hfma2(u2h2((W & 0x00F000F0u) | 0x64006400u), shi, chi));
-                o.w = h22u(__hfma2(u2h2((W8 & 0x00F000F0u) | 0x64006400u), shi, chi));
-                const int cc = 8 * gg + 4 * w4 + i;  // chunk within the half
-                *reinterpret_cast<uint4 *>(ast + (cc >> 3) * (kRows * 128) + sw128_off(r, cc & 7)) = o;
+                o[4 * i + 0] = h22u(__hfma2(u2h2((W & 0x000F000Fu) | 0x64006400u), slo, clo));
+                o[4 * i + 1] = h22u(__hfma2(u2h2((W8 & 0x000F000Fu) | 0x64006400u), slo, clo));
+                o[4 * i + 2] = h22u(__hfma2(u2h2((W & 0x00F000F0u) | 0x64006400u), shi, chi));
+                o[4 * i + 3] = h22u(__hfma2(u2h2((W8 & 0x00F000F0u) | 0x64006400u), shi, chi));
             }
+            tmem_st16(taddr + 32 * gg + 16 * w4, o);  // chunks 8gg + 4w4 .. +3
         }
     }
 }
@@ -242,10 +262,10 @@ __device__ __forceinline__ void q4k_scale_mins(const uint4 &H, uint32_t (&sc)[8]
     }
 }
 
-// Q8_0: half h (blocks 4h..4h+3) of one row -> 16 chunks of f16(d * q) (one
-// rounding per weight).  Block b's q bytes start at byte 34b + 2 (two bytes
-// off word alignment for even b), its f16 d at byte 34b.
-__device__ __forceinline__ void conv_q8_half(const uint8_t *raw, int h, uint32_t ref_mask, uint8_t *ast, int r) {
+// Q8_0: half h (blocks 4h..4h+3) of one row -> 64 TMEM columns of f16(d * q)
+// (one rounding per weight).  Block b's q bytes start at byte 34b + 2 (two
+// bytes off word alignment for even b), its f16 d at byte 34b.
+__device__ __forceinline__ void conv_q8_half(const uint8_t *raw, int h, uint32_t ref_mask, uint32_t taddr) {
     const uint32_t *W = reinterpret_cast<const uint32_t *>(raw);
     const __half2 k1152 = __float2half2_rn(1152.f);
 #pragma unroll
@@ -258,19 +278,18 @@ __device__ __forceinline__ void conv_q8_half(const uint8_t *raw, int h, uint32_t
         uint32_t qw[9];
 #pragma unroll
         for (int i = 0; i < 9; i++) qw[i] = (i < 8 || sh) ? W[wq + i] : 0u;
+        uint32_t o[16];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            uint4 o;
             uint32_t t[2];
 #pragma unroll
             for (int u = 0; u < 2; u++) t[u] = __funnelshift_r(qw[2 * i + u], qw[2 * i + u + 1], sh);
-            o.x = h22u(__hmul2(__hsub2(u2h2((t[0] & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
-            o.y = h22u(__hmul2(__hsub2(u2h2(((t[0] >> 8) & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
-            o.z = h22u(__hmul2(__hsub2(u2h2((t[1] & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
-            o.w = h22u(__hmul2(__hsub2(u2h2(((t[1] >> 8) & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
-            const int cc = 4 * bb + i;
-            *reinterpret_cast<uint4 *>(ast + (cc >> 3) * (kRows * 128) + sw128_off(r, cc & 7)) = o;
+            o[4 * i + 0] = h22u(__hmul2(__hsub2(u2h2((t[0] & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
+            o[4 * i + 1] = h22u(__hmul2(__hsub2(u2h2(((t[0] >> 8) & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
+            o[4 * i + 2] = h22u(__hmul2(__hsub2(u2h2((t[1] & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
+            o[4 * i + 3] = h22u(__hmul2(__hsub2(u2h2(((t[1] >> 8) & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
         }
+        tmem_st16(taddr + 16 * bb, o);  // chunks 4bb .. 4bb+3
     }
 }
 
@@ -281,79 +300,99 @@ __host__ __device__ __forceinline__ uint32_t core16_off(int row, int kk) {
     return (uint32_t)((row >> 3) * 256 + (kk >> 3) * 128 + (row & 7) * 16 + (kk & 7) * 2);
 }
 
-// x [m, k] f32 -> x16 [2 NT, k] f16 (hi rows, then lo rows) in the
-// converters' k order, times a per-token power of two (rows m..NT-1 zero);
-// inv[t] = its inverse.  For Q4_K also the sub-block sums of the scaled
-// activations divided by 32 (exact power of two, keeps them below 2^15), per
-// super-block as a 2 NT x 16 K-major operand: columns 0..7 the eight sums
-// (hi in row t, lo in row NT + t), columns 8..15 zero.  One CTA per token slot.
+// Activation packing, one warp per (token slot t, super-block sb), grid
+// (S, NT / 8) x 256 threads: lane c converts position chunk c.
+//   x16[t] / x16[NT + t]: hi / lo f16 of x * s, s = 2^e per (t, sb) putting
+//                         max |x * s| in [2^13, 2^14);
+//   inv[sb * NT + t]:     1 / s (0 for rows past m);
+//   sx16 (Q4_K):          per super-block a 2 NT x 16 K-major operand in the
+//                         core-matrix layout: columns 0..7 the sub-block sums
+//                         of x * s / 32 (hi in row t, lo in row NT + t),
+//                         columns 8..15 zero.
+// The CTAs also zero y [m, n] for the GEMM's atomic adds.
 __global__ void x16_pack_kernel(const float *__restrict__ x, int m, int k, int q8, int nt, __half *__restrict__ x16,
-                                uint8_t *__restrict__ sx16, float *__restrict__ inv) {
-    const int t = blockIdx.x;
-    __shared__ float red[32];
-    float mx = 0.f;
-    if (t < m)
-        for (int i = threadIdx.x; i < k; i += blockDim.x) mx = fmaxf(mx, fabsf(x[(size_t)t * k + i]));
+                                uint8_t *__restrict__ sx16, float *__restrict__ inv, float *__restrict__ y,
+                                long long ny) {
+    const long long nthreads = (long long)gridDim.x * gridDim.y * blockDim.x;
+    for (long long i = ((long long)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x; i < ny;
+         i += nthreads)
+        y[i] = 0.f;
+    const int sb = blockIdx.x, t = blockIdx.y * 8 + (threadIdx.x >> 5), c = threadIdx.x & 31;
+    int e0, e1;
+    if (q8) {
+        e0 = 32 * (c >> 2) + 8 * (c & 3);
+        e1 = e0 + 4;
+    } else {
+        e0 = 64 * (c >> 3) + 4 * (c & 7);
+        e1 = e0 + 32;
+    }
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (t < m) {
+        const float *xr = x + (size_t)t * k + (size_t)sb * 256;
+        a = *reinterpret_cast<const float4 *>(xr + e0);
+        b = *reinterpret_cast<const float4 *>(xr + e1);
+    }
+    float mx = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
+                     fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+#pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-        for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (threadIdx.x == 0) red[0] = v;
+    float s, iv;
+    act_scale(mx, s, iv);
+    if (c == 0) inv[sb * nt + t] = t < m ? iv : 0.f;
+    const float v[8] = {a.x * s, a.z * s, a.y * s, a.w * s, b.x * s, b.z * s, b.y * s, b.w * s};
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        const float2 hf = __half22float2(h);
+        hi[i] = h22u(h);
+        lo[i] = h22u(__floats2half2_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y));
     }
-    __syncthreads();
-    float s = 0.f, iv = 0.f;
-    act_scale(red[0], s, iv);
-    if (threadIdx.x == 0) inv[t] = t < m ? iv : 0.f;
-    for (int pos = threadIdx.x; pos < k; pos += blockDim.x) {
-        const int sb = pos >> 8;
-        const float v = t < m ? x[(size_t)t * k + sb * 256 + perm_elem(q8 != 0, pos & 255)] * s : 0.f;
-        const __half hi = __float2half_rn(v);
-        x16[(size_t)t * k + pos] = hi;
-        x16[(size_t)(t + nt) * k + pos] = __float2half_rn(v - __half2float(hi));
-    }
+    const size_t pos = (size_t)sb * 256 + 8 * c;
+    *reinterpret_cast<uint4 *>(x16 + (size_t)t * k + pos) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4 *>(x16 + (size_t)(t + nt) * k + pos) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     if (q8) return;
-    const int S = k >> 8, blk = 2 * nt * 32;
-    for (int idx = threadIdx.x; idx < S * 16; idx += blockDim.x) {
-        const int sb = idx >> 4, kk = idx & 15;
-        float v = 0.f;
-        if (kk < 8 && t < m) {
-            const float *p = x + (size_t)t * k + sb * 256 + kk * 32;
-#pragma unroll 8
-            for (int e = 0; e < 32; e++) v += p[e];
-            v *= s * 0.03125f;
-        }
-        const __half hi = __float2half_rn(v);
-        uint8_t *b = sx16 + (size_t)sb * blk;
-        *reinterpret_cast<__half *>(b + core16_off(t, kk)) = hi;
-        *reinterpret_cast<__half *>(b + core16_off(t + nt, kk)) = __float2half_rn(v - __half2float(hi));
+    // sub-block 2G (the a runs) and 2G+1 (the b runs) of lanes 8G..8G+7
+    float s0 = (a.x + a.y) + (a.z + a.w), s1 = (b.x + b.y) + (b.z + b.w);
+#pragma unroll
+    for (int o = 4; o; o >>= 1) {
+        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    }
+    const int kk = c & 15, src = 8 * ((kk & 7) >> 1);
+    const float g0 = __shfl_sync(0xffffffffu, s0, src), g1 = __shfl_sync(0xffffffffu, s1, src);
+    if (c < 16) {
+        const float sum = kk < 8 ? ((kk & 1) ? g1 : g0) * (s * 0.03125f) : 0.f;
+        const __half h = __float2half_rn(sum);
+        uint8_t *blk = sx16 + (size_t)sb * (2 * nt * 32);
+        *reinterpret_cast<__half *>(blk + core16_off(t, kk)) = h;
+        *reinterpret_cast<__half *>(blk + core16_off(t + nt, kk)) = __float2half_rn(sum - __half2float(h));
     }
 }
 
 struct GemmLayout {
-    size_t a = 0, x = 0, raw = 0, sc = 0, bars = 0, tslot = 0, total = 0;
-    int AS = 0, XS = 0, RS = 0, ND = 0, astage = 0, xstage = 0;
+    size_t amin = 0, x = 0, raw = 0, sc = 0, bars = 0, tslot = 0, total = 0;
+    int XS = 0, RS = 0, ND = 0, xstage = 0, bufcols = 0;
 };
 
-// Shared memory: A stages (+ the 4 KB min-term operand for Q4_K), activation
-// stages (+ the sub-block sums for Q4_K), raw weight stages, per-unit (d, dmin)
-// slots (Q4_K), barriers.  Every stage size is a multiple of 1024 bytes.
+// Shared memory: Q4_K min-term operands (one per TMEM A stage), activation
+// stages (+ the sub-block sums for Q4_K), raw weight stages, per-unit
+// (d, dmin) slots (Q4_K), barriers.  Every stage size is a multiple of 1024
+// bytes.  TMEM: accumulator buffers of `bufcols` columns from column 256.
 template <class F, int NT>
 __host__ __device__ constexpr GemmLayout gemm_layout() {
     GemmLayout L{};
-    L.AS = 3;
-    L.XS = NT >= 32 ? 3 : 4;
-    L.RS = F::kQ8 ? 2 : 3;
-    L.ND = F::kQ8 ? 2 : 4;
-    L.astage = kAStage + (F::kQ8 ? 0 : kRows * 32);
+    L.XS = NT >= 32 ? 6 : 8;
+    L.RS = F::kQ8 ? (NT >= 32 ? 3 : 4) : (NT >= 32 ? 5 : 6);
+    L.bufcols = F::kQ8 ? 2 * NT : 4 * NT;  // hi / lo columns (+ the Q4_K min term)
+    L.ND = (kTmemCols - kAccBase) / L.bufcols < 4 ? (kTmemCols - kAccBase) / L.bufcols : 4;
     L.xstage = 2 * NT * 256 + (F::kQ8 ? 0 : 2 * NT * 32);
-    L.a = 0;
-    L.x = L.a + (size_t)L.AS * L.astage;
+    L.amin = 0;
+    L.x = L.amin + (F::kQ8 ? 0 : (size_t)kAStages * kMinBytes);
     L.raw = L.x + (size_t)L.XS * L.xstage;
     L.sc = L.raw + (size_t)L.RS * kRows * F::kRowBytes;
     L.bars = L.sc + (F::kQ8 ? 0 : (size_t)L.ND * kRows * 8);
-    L.tslot = L.bars + (size_t)(2 * L.RS + 2 * L.AS + 2 * L.XS + 3 * L.ND + 1) * 8;
+    L.tslot = L.bars + (size_t)(2 * L.RS + 2 * kAStages + 2 * L.XS + 3 * L.ND + 1) * 8;
     L.total = L.tslot + 16 + 1024;  // + slack to 1024-align the base
     return L;
 }
@@ -366,19 +405,17 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     constexpr GemmLayout L = gemm_layout<F, NT>();
-    constexpr bool PU = !F::kQ8;  // Q4_K: one accumulator per unit, scaled in f32
-    constexpr int NB = 2 * NT;    // UMMA N: hi and lo rows of the tokens
+    constexpr bool Q4 = !F::kQ8;
+    constexpr int NB = 2 * NT;  // UMMA N: hi and lo rows of the tokens
     constexpr int kXTiles = NB * 256;
     constexpr int kRawStage = kRows * F::kRowBytes;
     constexpr int ND = L.ND;
-    constexpr int kBufCols = PU ? 2 * NB : NB;  // Q4_K: main product, then the min term
-    constexpr int kCols = ND * kBufCols;        // power of two >= 32
-    uint8_t *a_ring = smem + L.a, *x_ring = smem + L.x, *raw_ring = smem + L.raw;
+    uint8_t *amin_ring = smem + L.amin, *x_ring = smem + L.x, *raw_ring = smem + L.raw;
     float2 *dslot = reinterpret_cast<float2 *>(smem + L.sc);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *raw_full = bars, *raw_empty = raw_full + L.RS;
-    uint64_t *a_full = raw_empty + L.RS, *a_empty = a_full + L.AS;
-    uint64_t *x_full = a_empty + L.AS, *x_empty = x_full + L.XS;
+    uint64_t *a_full = raw_empty + L.RS, *a_empty = a_full + kAStages;
+    uint64_t *x_full = a_empty + kAStages, *x_empty = x_full + L.XS;
     uint64_t *d_full = x_empty + L.XS, *d_empty = d_full + ND, *s_full = d_empty + ND, *drain = s_full + ND;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + L.tslot);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -388,7 +425,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < L.RS; i++) mbar_init(raw_full + i, 1), mbar_init(raw_empty + i, kConvWarps);
-        for (int i = 0; i < L.AS; i++) mbar_init(a_full + i, 4), mbar_init(a_empty + i, 1);
+        for (int i = 0; i < kAStages; i++) mbar_init(a_full + i, 4), mbar_init(a_empty + i, 1);
         for (int i = 0; i < L.XS; i++) mbar_init(x_full + i, 1), mbar_init(x_empty + i, 1);
         for (int i = 0; i < ND; i++) mbar_init(d_full + i, 1), mbar_init(d_empty + i, 4), mbar_init(s_full + i, 4);
         mbar_init(drain, 1);
@@ -396,7 +433,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
     }
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tslot)),
-                     "r"(kCols)
+                     "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
         tc_fence_before();
@@ -409,7 +446,6 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
         ok = false;
         atomicOr(status, LC_DEV_WAIT_TIMEOUT);
     };
-    auto seg_last = [&](int u) { return u == U1 - 1 || (u + 1) / S != u / S; };
 
     if (warp == 0) {
         if (lane == 0) {  // producer
@@ -426,7 +462,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
                     const int xi = 2 * j + h, xs = xi % L.XS;
                     if (!mbar_wait(x_empty + xs, ((xi / L.XS) & 1) ^ 1)) { fail(); break; }
                     uint8_t *xst = x_ring + (size_t)xs * L.xstage;
-                    const bool mins = PU && h == 0;
+                    const bool mins = Q4 && h == 0;
                     mbar_expect_tx(x_full + xs, kXTiles + (mins ? NB * 32 : 0));
 #pragma unroll
                     for (int kc = 0; kc < 2; kc++)
@@ -436,27 +472,28 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
             }
         }
     } else if (warp <= kConvWarps) {  // converters: group g converts half g of row r of every unit
-        const int g = (warp - 1) >> 2, r = ((warp - 1) & 3) * 32 + lane;
+        const int g = (warp - 1) >> 2, quad = warp & 3, r = 32 * quad + lane;
+        const uint32_t tlane = tbase + ((uint32_t)(32 * quad) << 16);
         const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
-        if (PU && g == 0)  // columns 8..15 of the min-term operand stay zero
-            for (int i = 0; i < L.AS; i++)
-                *reinterpret_cast<uint4 *>(a_ring + (size_t)i * L.astage + kAStage + core16_off(r, 8)) =
-                    make_uint4(0u, 0u, 0u, 0u);
+        if (Q4 && g == 0)  // columns 8..15 of the min-term operands stay zero
+            for (int i = 0; i < kAStages; i++)
+                *reinterpret_cast<uint4 *>(amin_ring + i * kMinBytes + core16_off(r, 8)) = make_uint4(0u, 0u, 0u, 0u);
         for (int u = U0; u < U1 && ok; u++) {
             const int j = u - U0, rs = j % L.RS;
             if (!mbar_wait(raw_full + rs, (j / L.RS) & 1)) { fail(); break; }
             const uint8_t *raw = raw_ring + (size_t)rs * kRawStage + (size_t)r * F::kRowBytes;
-            const int ai = 2 * j + g, as = ai % L.AS;
-            if (!mbar_wait(a_empty + as, ((ai / L.AS) & 1) ^ 1)) { fail(); break; }
-            uint8_t *ast = a_ring + (size_t)as * L.astage;
-            if constexpr (PU) {
+            const int ai = 2 * j + g, as = ai % kAStages;
+            if (!mbar_wait(a_empty + as, ((ai / kAStages) & 1) ^ 1)) { fail(); break; }
+            tc_fence_after();
+            const uint32_t ta = tlane + as * kACols;
+            if constexpr (Q4) {
                 const uint4 H = lds128(raw);
                 uint32_t sc[8], mn[8];
                 q4k_scale_mins(H, sc, mn);
                 if (g == 0)
-                    conv_q4k_half<0>(raw, sc, ast, r);
+                    conv_q4k_half<0>(raw, sc, ta);
                 else
-                    conv_q4k_half<1>(raw, sc, ast, r);
+                    conv_q4k_half<1>(raw, sc, ta);
                 if (g == 0) {
                     // min-term operand: m_j (exact in f16) in columns 0..7 of row r
                     uint4 o;
@@ -464,7 +501,8 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
                     o.y = h22u(__floats2half2_rn((float)mn[2], (float)mn[3]));
                     o.z = h22u(__floats2half2_rn((float)mn[4], (float)mn[5]));
                     o.w = h22u(__floats2half2_rn((float)mn[6], (float)mn[7]));
-                    *reinterpret_cast<uint4 *>(ast + kAStage + core16_off(r, 0)) = o;
+                    *reinterpret_cast<uint4 *>(amin_ring + as * kMinBytes + core16_off(r, 0)) = o;
+                    fence_proxy_async_smem();  // generic-proxy writes -> the tensor cores' reads
                     // (d, 32 dmin) of the unit for the epilogue, once its slot is free
                     const int db = j % ND;
                     if (!mbar_wait(d_empty + db, ((j / ND) & 1) ^ 1)) { fail(); break; }
@@ -474,9 +512,10 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
                     if (lane == 0) mbar_arrive(s_full + db);
                 }
             } else {
-                conv_q8_half(raw, g, ref_mask, ast, r);
+                conv_q8_half(raw, g, ref_mask, ta);
             }
-            fence_proxy_async_smem();  // generic-proxy writes -> the tensor cores' reads
+            tmem_st_wait();
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(a_full + as);
@@ -486,52 +525,33 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
     } else if (warp == kMmaWarp) {
         if (lane == 0) {  // MMA issuer
             constexpr uint32_t idesc = umma_idesc_f16(kRows, NB);
-            const uint32_t a0 = smem_addr(a_ring), x0 = smem_addr(x_ring);
-            int run = 0;  // Q8_0: accumulator runs started
+            const uint32_t x0 = smem_addr(x_ring), m0 = smem_addr(amin_ring);
             for (int u = U0; u < U1 && ok; u++) {
-                const int j = u - U0;
-                const bool first_seg = u == U0 || u / S != (u - 1) / S;
-                int db;
-                if constexpr (PU) {
-                    db = j % ND;
-                    if (!mbar_wait(d_empty + db, ((j / ND) & 1) ^ 1)) { fail(); break; }
-                    tc_fence_after();
-                } else {
-                    db = run % ND;
-                    if (first_seg) {
-                        if (!mbar_wait(d_empty + db, ((run / ND) & 1) ^ 1)) { fail(); break; }
-                        tc_fence_after();
-                    }
-                }
-                const uint32_t dcol = tbase + db * kBufCols;
+                const int j = u - U0, db = j % ND;
+                if (!mbar_wait(d_empty + db, ((j / ND) & 1) ^ 1)) { fail(); break; }
+                tc_fence_after();
+                const uint32_t dcol = tbase + kAccBase + db * L.bufcols;
                 for (int h = 0; h < 2 && ok; h++) {
-                    const int ai = 2 * j + h, as = ai % L.AS, xs = ai % L.XS;
-                    if (!mbar_wait(a_full + as, (ai / L.AS) & 1) || !mbar_wait(x_full + xs, (ai / L.XS) & 1)) {
+                    const int ai = 2 * j + h, as = ai % kAStages, xs = ai % L.XS;
+                    if (!mbar_wait(a_full + as, (ai / kAStages) & 1) || !mbar_wait(x_full + xs, (ai / L.XS) & 1)) {
                         fail();
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t ab = a0 + as * L.astage, xb = x0 + xs * L.xstage;
-                    const bool fresh = PU || first_seg;
+                    const uint32_t xb = x0 + xs * L.xstage;
 #pragma unroll
                     for (int kk = 0; kk < 8; kk++) {
-                        const uint64_t ad = umma_desc_sw128(ab + (kk >> 2) * (kRows * 128) + (kk & 3) * 32);
                         const uint64_t bd = umma_desc_sw128(xb + (kk >> 2) * (NB * 128) + (kk & 3) * 32);
-                        umma_f16(dcol, ad, bd, idesc, (fresh && h == 0 && kk == 0) ? 0u : 1u);
+                        umma_f16_ts(dcol, tbase + as * kACols + 8 * kk, bd, idesc, (h == 0 && kk == 0) ? 0u : 1u);
                     }
-                    if (PU && h == 0)  // min term: sum_j m_j * (sub-block sum of x) / 32
-                        umma_f16(dcol + NB, umma_desc_core16(ab + kAStage), umma_desc_core16(xb + kXTiles), idesc,
-                                 0u);
+                    if (Q4 && h == 0)  // min term: sum_j m_j * (sub-block sum of x) / 32
+                        umma_f16_ss(dcol + NB, umma_desc_core16(m0 + as * kMinBytes), umma_desc_core16(xb + kXTiles),
+                                    idesc, 0u);
                     umma_commit(a_empty + as);
                     umma_commit(x_empty + xs);
                 }
                 if (!ok) break;
-                if (PU) {
-                    umma_commit(d_full + db);
-                } else if (seg_last(u)) {
-                    umma_commit(d_full + db);
-                    run++;
-                }
+                umma_commit(d_full + db);
             }
             // everything issued has completed before the TMEM is freed
             umma_commit(drain);
@@ -543,54 +563,52 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
         float acc[NT];
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[t] = 0.f;
-        int run = 0;
         for (int u = U0; u < U1 && ok; u++) {
-            const int j = u - U0;
-            const bool last = seg_last(u);
-            if (!PU && !last) continue;
-            const int db = PU ? j % ND : run % ND;
-            const uint32_t par = PU ? (j / ND) & 1 : (run / ND) & 1;
+            const int j = u - U0, db = j % ND, tile = u / S, sb = u - tile * S;
+            const uint32_t par = (j / ND) & 1;
             if (!mbar_wait(d_full + db, par)) { fail(); break; }
             tc_fence_after();
-            const uint32_t col = tbase + lanes + db * kBufCols;
-            if constexpr (PU) {
+            const uint32_t col = tbase + lanes + kAccBase + db * L.bufcols;
+            float2 dd = make_float2(1.f, 0.f);
+            if constexpr (Q4) {
                 if (!mbar_wait(s_full + db, par)) { fail(); break; }
-                const float2 dd = dslot[db * kRows + 32 * q + lane];
+                dd = dslot[db * kRows + 32 * q + lane];
+            }
 #pragma unroll
-                for (int c = 0; c < NT / 16; c++) {
-                    float ph[16], pl[16], mh[16], ml[16];
-                    tmem_ld16(col + 16 * c, ph);
-                    tmem_ld16(col + NT + 16 * c, pl);
+            for (int c = 0; c < NT / 16; c++) {
+                float iv[16], ph[16], pl[16];
+#pragma unroll
+                for (int t = 0; t < 16; t += 4) {
+                    const float4 f = __ldg(reinterpret_cast<const float4 *>(inv + sb * NT + 16 * c + t));
+                    iv[t] = f.x, iv[t + 1] = f.y, iv[t + 2] = f.z, iv[t + 3] = f.w;
+                }
+                tmem_ld16(col + 16 * c, ph);
+                tmem_ld16(col + NT + 16 * c, pl);
+                if constexpr (Q4) {
+                    float mh[16], ml[16];
                     tmem_ld16(col + NB + 16 * c, mh);
                     tmem_ld16(col + NB + NT + 16 * c, ml);
                     tmem_ld_wait();
                     tmem_regs_ready(ph), tmem_regs_ready(pl), tmem_regs_ready(mh), tmem_regs_ready(ml);
 #pragma unroll
                     for (int i = 0; i < 16; i++)
-                        acc[16 * c + i] += dd.x * (ph[i] + pl[i]) - dd.y * (mh[i] + ml[i]);
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < NT / 16; c++) {
-                    float ph[16], pl[16];
-                    tmem_ld16(col + 16 * c, ph);
-                    tmem_ld16(col + NT + 16 * c, pl);
+                        acc[16 * c + i] += iv[i] * (dd.x * (ph[i] + pl[i]) - dd.y * (mh[i] + ml[i]));
+                } else {
                     tmem_ld_wait();
                     tmem_regs_ready(ph), tmem_regs_ready(pl);
 #pragma unroll
-                    for (int i = 0; i < 16; i++) acc[16 * c + i] = ph[i] + pl[i];
+                    for (int i = 0; i < 16; i++) acc[16 * c + i] += iv[i] * (ph[i] + pl[i]);
                 }
-                run++;
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(d_empty + db);
-            if (last) {
-                const int row = (u / S) * kRows + 32 * q + lane;
+            if (u == U1 - 1 || sb == S - 1) {  // end of this CTA's run over the tile
+                const int row = tile * kRows + 32 * q + lane;
                 if (row < n)
 #pragma unroll
                     for (int t = 0; t < NT; t++)
-                        if (t < m) atomicAdd(y + (size_t)t * n + row, acc[t] * inv[t]);
+                        if (t < m) atomicAdd(y + (size_t)t * n + row, acc[t]);
 #pragma unroll
                 for (int t = 0; t < NT; t++) acc[t] = 0.f;
             }
@@ -599,7 +617,8 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
     __syncthreads();
     if (warp == kMmaWarp) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(kCols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(kTmemCols)
+                     : "memory");
     }
 }
 
@@ -642,9 +661,11 @@ template <class F, int NT>
 int launch_dq_gemm(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
     constexpr GemmLayout L = gemm_layout<F, NT>();
     LC_REQUIRE(L.total <= ctx->smem_optin, LC_ERR_UNSUPPORTED, "dq_gemm: %zu bytes of shared memory needed", L.total);
+    const uint32_t S = k / 256;
     const size_t x16_bytes = (size_t)2 * NT * k * 2;
-    const size_t sx_bytes = F::kQ8 ? 0 : (size_t)(k / 256) * 2 * NT * 32;  // multiple of 16
-    uint8_t *scr = (uint8_t *)lc_scratch(ctx, LC_SCRATCH_PACK, x16_bytes + sx_bytes + NT * 4 + 256);
+    const size_t sx_bytes = F::kQ8 ? 0 : (size_t)S * 2 * NT * 32;  // multiple of 16
+    const size_t inv_bytes = (size_t)S * NT * 4;
+    uint8_t *scr = (uint8_t *)lc_scratch(ctx, LC_SCRATCH_PACK, x16_bytes + sx_bytes + inv_bytes + 256);
     if (!scr) return LC_ERR_OOM;
     __half *x16 = reinterpret_cast<__half *>(scr);
     uint8_t *sx16 = scr + x16_bytes;
@@ -654,11 +675,11 @@ int launch_dq_gemm(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint
     if (s) return s;
     s = x16_map(&tmx, x16, k, 2 * NT);
     if (s) return s;
-    LC_CUDA(cudaMemsetAsync(y, 0, (size_t)m * n * 4, ctx->stream));
-    x16_pack_kernel<<<NT, 256, 0, ctx->stream>>>(x, (int)m, (int)k, F::kQ8 ? 1 : 0, NT, x16, sx16, inv);
+    x16_pack_kernel<<<dim3(S, NT / 8), 256, 0, ctx->stream>>>(x, (int)m, (int)k, F::kQ8 ? 1 : 0, NT, x16, sx16, inv,
+                                                                y, (long long)m * n);
     s = lc_set_smem_attr((const void *)dq_gemm_kernel<F, NT>, L.total);
     if (s) return s;
-    const long long TS = (long long)((n + kRows - 1) / kRows) * (k / 256);
+    const long long TS = (long long)((n + kRows - 1) / kRows) * S;
     const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, TS));
     dq_gemm_kernel<F, NT><<<grid, kGemmWarps * 32, L.total, ctx->stream>>>(tmw, tmx, sx16, inv, y, (int)m, (int)k,
                                                                            (int)n, ctx->half_mode, ctx->dev_status);
@@ -672,7 +693,8 @@ namespace lc {
 // Quantized GEMM on tcgen05 for 5..32 tokens; LC_ERR_UNSUPPORTED when the
 // shape is not covered (the caller falls back).
 int gemm_dq(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
-    if (m == 0 || m > 32 || k % 256 != 0 || ((uintptr_t)w & 15) != 0 || (long long)k * 32 >= (1ll << 31))
+    if (m == 0 || m > 32 || k % 256 != 0 || ((uintptr_t)w & 15) != 0 || ((uintptr_t)x & 15) != 0 ||
+        (long long)k * 32 >= (1ll << 31))
         return LC_ERR_UNSUPPORTED;
     const uint8_t *wb = (const uint8_t *)w;
     if (dtype == LC_Q4_K)
