@@ -11,11 +11,12 @@
 //               lane the warp may access), warps 1-4 the first half of a unit,
 //               warps 5-8 the second; they dequantise to f16 in registers and
 //               store it into tensor memory with tcgen05.st;
-//   warp 9      allocates the tensor memory and issues tcgen05.mma
-//               (kind::f16, A = weights from TMEM, M = 128 rows, B = tokens
-//               from shared memory, N = 2 NT, K = 16) with f32 accumulation in
-//               TMEM;
-//   warps 10-13 epilogue: tcgen05.ld of each unit's accumulators, scales, and
+//   warps 9-10  issue tcgen05.mma for the even / odd units (kind::f16,
+//               A = weights from TMEM, M = 128 rows, B = tokens from shared
+//               memory, N = 2 NT, K = 16) with f32 accumulation in TMEM; two
+//               issuers overlap one unit's barrier waits and commits with the
+//               other's MMAs; warp 9 also allocates the tensor memory;
+//   warps 11-14 epilogue: tcgen05.ld of each unit's accumulators, scales, and
 //               at the end of a tile's run f32 atomic adds into y (zeroed by
 //               the packing kernel).
 // Units (128-row tile, super-block) are flattened tile-major and cut into one
@@ -56,12 +57,13 @@ namespace {
 
 constexpr int kRows = 128;  // weight rows per tile (UMMA M)
 constexpr int kConvWarps = 8;
-constexpr int kMmaWarp = 1 + kConvWarps;
-constexpr int kGemmWarps = kMmaWarp + 5;  // + the MMA warp and 4 epilogue warps
+constexpr int kMmaWarp = 1 + kConvWarps;  // first of the two MMA warps (even / odd units)
+constexpr int kMmaWarps = 2;
+constexpr int kGemmWarps = kMmaWarp + kMmaWarps + 4;  // + 4 epilogue warps
 constexpr int kTmemCols = 512;
-constexpr int kAStages = 4;     // TMEM A stages of half a unit (K = 128)
-constexpr int kACols = 64;      // 128 f16 per lane
-constexpr int kAccBase = kAStages * kACols;
+constexpr int kASlots = 2;      // TMEM A slots of one unit (K = 256)
+constexpr int kACols = 128;     // 256 f16 per lane; half h at column 64 h
+constexpr int kAccBase = kASlots * kACols;
 constexpr int kMinBytes = kRows * 32;  // Q4_K min-term operand: 128 rows x 16 f16
 
 // ---- tcgen05 ---------------------------------------------------------------
@@ -221,6 +223,13 @@ __device__ __forceinline__ uint32_t h22u(__half2 v) { return *reinterpret_cast<u
 // applied in f32 by the epilogue.
 template <int g>
 __device__ __forceinline__ void conv_q4k_half(const uint8_t *raw, const uint32_t (&sc)[8], uint32_t taddr) {
+    // All 64 qs bytes of the half are loaded before the first tcgen05.st:
+    // the stores are volatile asm with a memory clobber, so loads written
+    // between them could not be hoisted and each round would pay the full
+    // shared-memory latency.
+    uint4 Qa[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) Qa[i] = lds128(raw + 16 + 64 * g + 16 * i);
 #pragma unroll
     for (int gg = 0; gg < 2; gg++) {
         const int G = 2 * g + gg;  // qs group: sub-blocks 2G (low), 2G+1 (high nibbles)
@@ -229,7 +238,7 @@ __device__ __forceinline__ void conv_q4k_half(const uint8_t *raw, const uint32_t
                       chi = __float2half2_rn(-64.f * (float)sc[2 * G + 1]);
 #pragma unroll
         for (int w4 = 0; w4 < 2; w4++) {
-            const uint4 Q = lds128(raw + 16 + 32 * G + 16 * w4);
+            const uint4 Q = Qa[2 * gg + w4];
             const uint32_t qw[4] = {Q.x, Q.y, Q.z, Q.w};
             uint32_t o[16];
 #pragma unroll
@@ -265,25 +274,34 @@ __device__ __forceinline__ void q4k_scale_mins(const uint4 &H, uint32_t (&sc)[8]
 // Q8_0: half h (blocks 4h..4h+3) of one row -> 64 TMEM columns of f16(d * q)
 // (one rounding per weight).  Block b's q bytes start at byte 34b + 2 (two
 // bytes off word alignment for even b), its f16 d at byte 34b.
-__device__ __forceinline__ void conv_q8_half(const uint8_t *raw, int h, uint32_t ref_mask, uint32_t taddr) {
-    const uint32_t *W = reinterpret_cast<const uint32_t *>(raw);
+template <int h>
+__device__ __forceinline__ void conv_q8_half(const uint8_t *raw, uint32_t ref_mask, uint32_t taddr) {
+    // The half's blocks span row bytes 136h .. 136h + 135; the 9 aligned
+    // 16-byte chunks from byte 128h cover them and are all loaded before the
+    // first tcgen05.st (see conv_q4k_half).  Word i of Wd is row word 32h + i.
+    uint32_t Wd[36];
+#pragma unroll
+    for (int i = 0; i < 9; i++) {
+        const uint4 v = lds128(raw + 128 * h + 16 * i);
+        Wd[4 * i] = v.x, Wd[4 * i + 1] = v.y, Wd[4 * i + 2] = v.z, Wd[4 * i + 3] = v.w;
+    }
     const __half2 k1152 = __float2half2_rn(1152.f);
 #pragma unroll
     for (int bb = 0; bb < 4; bb++) {
         const int b = 4 * h + bb;
-        const int wq = (17 * b + 1) >> 1, sh = (b & 1) ? 0 : 16;
-        const uint32_t dw = W[(b & 1) ? (17 * (b - 1)) / 2 + 8 : (17 * b) / 2];
+        const int wq = (17 * b + 1) / 2 - 32 * h, sh = (b & 1) ? 0 : 16;
+        const uint32_t dw = Wd[((b & 1) ? (17 * (b - 1)) / 2 + 8 : (17 * b) / 2) - 32 * h];
         const uint32_t dbits = fix_sub_h2((b & 1) ? (dw >> 16) : (dw & 0xFFFFu), ref_mask) & 0xFFFFu;
         const __half2 d2 = u2h2(dbits | (dbits << 16));
-        uint32_t qw[9];
-#pragma unroll
-        for (int i = 0; i < 9; i++) qw[i] = (i < 8 || sh) ? W[wq + i] : 0u;
         uint32_t o[16];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             uint32_t t[2];
 #pragma unroll
-            for (int u = 0; u < 2; u++) t[u] = __funnelshift_r(qw[2 * i + u], qw[2 * i + u + 1], sh);
+            for (int u = 0; u < 2; u++) {
+                const int wi = wq + 2 * i + u;
+                t[u] = __funnelshift_r(Wd[wi], (sh && wi + 1 < 36) ? Wd[wi + 1] : 0u, sh);
+            }
             o[4 * i + 0] = h22u(__hmul2(__hsub2(u2h2((t[0] & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
             o[4 * i + 1] = h22u(__hmul2(__hsub2(u2h2(((t[0] >> 8) & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
             o[4 * i + 2] = h22u(__hmul2(__hsub2(u2h2((t[1] & 0x00FF00FFu) ^ 0x64806480u), k1152), d2));
@@ -382,17 +400,17 @@ struct GemmLayout {
 template <class F, int NT>
 __host__ __device__ constexpr GemmLayout gemm_layout() {
     GemmLayout L{};
-    L.XS = NT >= 32 ? 6 : 8;
+    L.XS = NT >= 32 ? 3 : 4;
     L.RS = F::kQ8 ? (NT >= 32 ? 3 : 4) : (NT >= 32 ? 5 : 6);
     L.bufcols = F::kQ8 ? 2 * NT : 4 * NT;  // hi / lo columns (+ the Q4_K min term)
     L.ND = (kTmemCols - kAccBase) / L.bufcols < 4 ? (kTmemCols - kAccBase) / L.bufcols : 4;
-    L.xstage = 2 * NT * 256 + (F::kQ8 ? 0 : 2 * NT * 32);
+    L.xstage = 2 * NT * 512 + (F::kQ8 ? 0 : 2 * NT * 32);  // both halves of a unit
     L.amin = 0;
-    L.x = L.amin + (F::kQ8 ? 0 : (size_t)kAStages * kMinBytes);
+    L.x = L.amin + (F::kQ8 ? 0 : (size_t)kASlots * kMinBytes);
     L.raw = L.x + (size_t)L.XS * L.xstage;
     L.sc = L.raw + (size_t)L.RS * kRows * F::kRowBytes;
     L.bars = L.sc + (F::kQ8 ? 0 : (size_t)L.ND * kRows * 8);
-    L.tslot = L.bars + (size_t)(2 * L.RS + 2 * kAStages + 2 * L.XS + 3 * L.ND + 1) * 8;
+    L.tslot = L.bars + (size_t)(2 * L.RS + 2 * kASlots + 2 * L.XS + 3 * L.ND + 1) * 8;
     L.total = L.tslot + 16 + 1024;  // + slack to 1024-align the base
     return L;
 }
@@ -407,15 +425,15 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
     constexpr GemmLayout L = gemm_layout<F, NT>();
     constexpr bool Q4 = !F::kQ8;
     constexpr int NB = 2 * NT;  // UMMA N: hi and lo rows of the tokens
-    constexpr int kXTiles = NB * 256;
+    constexpr int kXTiles = NB * 512;  // activations of one unit: two halves of two 64-column boxes
     constexpr int kRawStage = kRows * F::kRowBytes;
     constexpr int ND = L.ND;
     uint8_t *amin_ring = smem + L.amin, *x_ring = smem + L.x, *raw_ring = smem + L.raw;
     float2 *dslot = reinterpret_cast<float2 *>(smem + L.sc);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *raw_full = bars, *raw_empty = raw_full + L.RS;
-    uint64_t *a_full = raw_empty + L.RS, *a_empty = a_full + kAStages;
-    uint64_t *x_full = a_empty + kAStages, *x_empty = x_full + L.XS;
+    uint64_t *a_full = raw_empty + L.RS, *a_empty = a_full + kASlots;
+    uint64_t *x_full = a_empty + kASlots, *x_empty = x_full + L.XS;
     uint64_t *d_full = x_empty + L.XS, *d_empty = d_full + ND, *s_full = d_empty + ND, *drain = s_full + ND;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + L.tslot);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -425,10 +443,10 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < L.RS; i++) mbar_init(raw_full + i, 1), mbar_init(raw_empty + i, kConvWarps);
-        for (int i = 0; i < kAStages; i++) mbar_init(a_full + i, 4), mbar_init(a_empty + i, 1);
+        for (int i = 0; i < kASlots; i++) mbar_init(a_full + i, kConvWarps), mbar_init(a_empty + i, 1);
         for (int i = 0; i < L.XS; i++) mbar_init(x_full + i, 1), mbar_init(x_empty + i, 1);
         for (int i = 0; i < ND; i++) mbar_init(d_full + i, 1), mbar_init(d_empty + i, 4), mbar_init(s_full + i, 4);
-        mbar_init(drain, 1);
+        mbar_init(drain, kMmaWarps);
         mbar_init_fence();
     }
     if (warp == kMmaWarp) {
@@ -458,17 +476,14 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
                 if (!mbar_wait(raw_empty + rs, ((j / L.RS) & 1) ^ 1)) { fail(); break; }
                 mbar_expect_tx(raw_full + rs, kRawStage);
                 tma_load_2d(raw_ring + (size_t)rs * kRawStage, &tmw, sb * F::kBoxX, tile * kRows, raw_full + rs, pol);
-                for (int h = 0; h < 2 && ok; h++) {
-                    const int xi = 2 * j + h, xs = xi % L.XS;
-                    if (!mbar_wait(x_empty + xs, ((xi / L.XS) & 1) ^ 1)) { fail(); break; }
-                    uint8_t *xst = x_ring + (size_t)xs * L.xstage;
-                    const bool mins = Q4 && h == 0;
-                    mbar_expect_tx(x_full + xs, kXTiles + (mins ? NB * 32 : 0));
+                const int xs = j % L.XS;
+                if (!mbar_wait(x_empty + xs, ((j / L.XS) & 1) ^ 1)) { fail(); break; }
+                uint8_t *xst = x_ring + (size_t)xs * L.xstage;
+                mbar_expect_tx(x_full + xs, kXTiles + (Q4 ? NB * 32 : 0));
 #pragma unroll
-                    for (int kc = 0; kc < 2; kc++)
-                        tma_load_2d(xst + kc * NB * 128, &tmx, sb * 256 + h * 128 + kc * 64, 0, x_full + xs, xpol);
-                    if (mins) bulk_load(xst + kXTiles, sx16 + (size_t)sb * NB * 32, NB * 32, x_full + xs, xpol);
-                }
+                for (int kc = 0; kc < 4; kc++)  // half kc / 2, 64-column box kc % 2
+                    tma_load_2d(xst + kc * NB * 128, &tmx, sb * 256 + kc * 64, 0, x_full + xs, xpol);
+                if (Q4) bulk_load(xst + kXTiles, sx16 + (size_t)sb * NB * 32, NB * 32, x_full + xs, xpol);
             }
         }
     } else if (warp <= kConvWarps) {  // converters: group g converts half g of row r of every unit
@@ -476,16 +491,16 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
         const uint32_t tlane = tbase + ((uint32_t)(32 * quad) << 16);
         const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
         if (Q4 && g == 0)  // columns 8..15 of the min-term operands stay zero
-            for (int i = 0; i < kAStages; i++)
+            for (int i = 0; i < kASlots; i++)
                 *reinterpret_cast<uint4 *>(amin_ring + i * kMinBytes + core16_off(r, 8)) = make_uint4(0u, 0u, 0u, 0u);
         for (int u = U0; u < U1 && ok; u++) {
             const int j = u - U0, rs = j % L.RS;
             if (!mbar_wait(raw_full + rs, (j / L.RS) & 1)) { fail(); break; }
             const uint8_t *raw = raw_ring + (size_t)rs * kRawStage + (size_t)r * F::kRowBytes;
-            const int ai = 2 * j + g, as = ai % kAStages;
-            if (!mbar_wait(a_empty + as, ((ai / kAStages) & 1) ^ 1)) { fail(); break; }
+            const int as = j % kASlots;
+            if (!mbar_wait(a_empty + as, ((j / kASlots) & 1) ^ 1)) { fail(); break; }
             tc_fence_after();
-            const uint32_t ta = tlane + as * kACols;
+            const uint32_t ta = tlane + as * kACols + g * 64;
             if constexpr (Q4) {
                 const uint4 H = lds128(raw);
                 uint32_t sc[8], mn[8];
@@ -512,7 +527,10 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
                     if (lane == 0) mbar_arrive(s_full + db);
                 }
             } else {
-                conv_q8_half(raw, g, ref_mask, ta);
+                if (g == 0)
+                    conv_q8_half<0>(raw, ref_mask, ta);
+                else
+                    conv_q8_half<1>(raw, ref_mask, ta);
             }
             tmem_st_wait();
             tc_fence_before();
@@ -522,35 +540,40 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
                 mbar_arrive(raw_empty + rs);
             }
         }
-    } else if (warp == kMmaWarp) {
+    } else if (warp < kMmaWarp + kMmaWarps) {
         if (lane == 0) {  // MMA issuer
             constexpr uint32_t idesc = umma_idesc_f16(kRows, NB);
-            const uint32_t x0 = smem_addr(x_ring), m0 = smem_addr(amin_ring);
-            for (int u = U0; u < U1 && ok; u++) {
-                const int j = u - U0, db = j % ND;
-                if (!mbar_wait(d_empty + db, ((j / ND) & 1) ^ 1)) { fail(); break; }
+            // Descriptors of x stage 0 and of the min-term operand stage 0; the
+            // start-address field is the low 14 bits (address / 16, below
+            // 2^14 for any shared-memory address), so stage and K offsets are
+            // plain additions.
+            const uint64_t xdesc0 = umma_desc_sw128(smem_addr(x_ring));
+            const uint64_t mdesc0 = umma_desc_core16(smem_addr(amin_ring));
+            const uint64_t sdesc0 = umma_desc_core16(smem_addr(x_ring) + kXTiles);  // sub-block sums, x stage 0
+            // One synchronisation point per unit: the accumulator buffer, the
+            // unit's A slot (both converter groups) and its activations, one
+            // fence, 16 (+1) MMAs, three commits.
+            for (int u = U0 + (warp - kMmaWarp); u < U1 && ok; u += kMmaWarps) {
+                const int j = u - U0, db = j % ND, as = j % kASlots, xs = j % L.XS;
+                if (!mbar_wait(d_empty + db, ((j / ND) & 1) ^ 1) || !mbar_wait(a_full + as, (j / kASlots) & 1) ||
+                    !mbar_wait(x_full + xs, (j / L.XS) & 1)) {
+                    fail();
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t dcol = tbase + kAccBase + db * L.bufcols;
-                for (int h = 0; h < 2 && ok; h++) {
-                    const int ai = 2 * j + h, as = ai % kAStages, xs = ai % L.XS;
-                    if (!mbar_wait(a_full + as, (ai / kAStages) & 1) || !mbar_wait(x_full + xs, (ai / L.XS) & 1)) {
-                        fail();
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t xb = x0 + xs * L.xstage;
+                const uint64_t xd = xdesc0 + (uint64_t)((xs * L.xstage) >> 4);
+                const uint32_t ta = tbase + as * kACols;
+                umma_f16_ts(dcol, ta, xd, idesc, 0u);
 #pragma unroll
-                    for (int kk = 0; kk < 8; kk++) {
-                        const uint64_t bd = umma_desc_sw128(xb + (kk >> 2) * (NB * 128) + (kk & 3) * 32);
-                        umma_f16_ts(dcol, tbase + as * kACols + 8 * kk, bd, idesc, (h == 0 && kk == 0) ? 0u : 1u);
-                    }
-                    if (Q4 && h == 0)  // min term: sum_j m_j * (sub-block sum of x) / 32
-                        umma_f16_ss(dcol + NB, umma_desc_core16(m0 + as * kMinBytes), umma_desc_core16(xb + kXTiles),
-                                    idesc, 0u);
-                    umma_commit(a_empty + as);
-                    umma_commit(x_empty + xs);
-                }
-                if (!ok) break;
+                for (int kk = 1; kk < 16; kk++)  // half kk / 8 at column 64 (kk / 8) + 8 (kk % 8)
+                    umma_f16_ts(dcol, ta + 8 * kk, xd + (uint64_t)(((kk >> 2) * (NB * 128) + (kk & 3) * 32) >> 4), idesc,
+                                1u);
+                if (Q4)  // min term: sum_j m_j * (sub-block sum of x) / 32
+                    umma_f16_ss(dcol + NB, mdesc0 + (uint64_t)((as * kMinBytes) >> 4),
+                                sdesc0 + (uint64_t)((xs * L.xstage) >> 4), idesc, 0u);
+                umma_commit(a_empty + as);
+                umma_commit(x_empty + xs);
                 umma_commit(d_full + db);
             }
             // everything issued has completed before the TMEM is freed
