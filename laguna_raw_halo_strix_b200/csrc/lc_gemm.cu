@@ -645,6 +645,325 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
     }
 }
 
+// ---- lm_head: logits of 128-token tiles fused with argmax -------------------
+//
+// TargetModel::project_normalized_hidden (src/target.rs:580-605) for many
+// hidden rows at once, followed by the argmax of src/lib.rs:456-464.  A tile is
+// 128 vocab rows x 256 tokens (N = 256: every MMA at the tensor cores' full
+// rate).  The activations are one f16 per element after a per-token power of
+// two (no hi / lo split: the logits only feed an argmax, and the split would
+// double both the MMAs and the activation reads from L2, which bound the
+// kernel: each weight tile re-reads its token tile).  Weights are f16 in TMEM
+// (Q8_0: f16(d q); Q4_K: the exact integer sc q, then one HFMA2 with d and
+// f16(-dmin m)); the accumulator holds the whole K loop (activation scale per
+// token).  Persistent CTAs walk the tiles token-tile fastest, so the CTAs that
+// share a weight tile run together and read it from L2.  The epilogue writes
+// the logits (optional) and reduces each token's best (logit, row) over the
+// warp's 32 rows with redux.sync / ballot, then one atomicMax per warp and
+// token on the order-preserving int64 key.
+
+constexpr int kLmTok = 256;           // tokens per tile
+constexpr int kLmN = kLmTok;          // UMMA N
+constexpr int kLmChunk = kLmN * 128;  // one 64-column activation chunk, 32 KB
+constexpr int kLmXS = 4;              // activation chunks in flight: the stream that bounds the kernel
+constexpr int kLmWarps = 15;          // weight producer, 8 converters, MMA, 4 epilogue, activation producer
+constexpr int kLmMma = 9;
+constexpr int kLmXProd = 14;
+constexpr unsigned long long kKeyMin = 0x8000000000000000ull;
+
+// Element of position e (0..7) of position chunk c within a super-block (the
+// order listed above conv_q4k_half).
+__host__ __device__ __forceinline__ int chunk_elem(bool q8, int c, int e) {
+    const int base = q8 ? 32 * (c >> 2) + 8 * (c & 3) : 64 * (c >> 3) + 4 * (c & 7);
+    return base + (e >> 2) * (q8 ? 4 : 32) + (((e & 1) << 1) | ((e >> 1) & 1));
+}
+
+// Q4_K for the lm_head: half g of one row -> 64 TMEM columns of
+// f16(d * (sc q) - f16(dmin m)) (sc q exact, one fused rounding).
+template <int g>
+__device__ __forceinline__ void conv_q4k_half_w(const uint8_t *raw, const uint32_t (&sc)[8], const uint32_t (&mn)[8],
+                                                float d, float dmin, uint32_t taddr) {
+    uint4 Qa[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) Qa[i] = lds128(raw + 16 + 64 * g + 16 * i);
+    const __half2 d2 = __float2half2_rn(d);  // d is an f16 value: exact
+#pragma unroll
+    for (int gg = 0; gg < 2; gg++) {
+        const int G = 2 * g + gg;
+        const __half2 slo = __float2half2_rn((float)sc[2 * G]), clo = __float2half2_rn(-1024.f * (float)sc[2 * G]);
+        const __half2 shi = __float2half2_rn((float)sc[2 * G + 1] * 0.0625f),
+                      chi = __float2half2_rn(-64.f * (float)sc[2 * G + 1]);
+        const __half2 mlo = __float2half2_rn(-dmin * (float)mn[2 * G]), mhi = __float2half2_rn(-dmin * (float)mn[2 * G + 1]);
+#pragma unroll
+        for (int w4 = 0; w4 < 2; w4++) {
+            const uint4 Q = Qa[2 * gg + w4];
+            const uint32_t qw[4] = {Q.x, Q.y, Q.z, Q.w};
+            uint32_t o[16];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t W = qw[i], W8 = W >> 8;
+                o[4 * i + 0] = h22u(__hfma2(__hfma2(u2h2((W & 0x000F000Fu) | 0x64006400u), slo, clo), d2, mlo));
+                o[4 * i + 1] = h22u(__hfma2(__hfma2(u2h2((W8 & 0x000F000Fu) | 0x64006400u), slo, clo), d2, mlo));
+                o[4 * i + 2] = h22u(__hfma2(__hfma2(u2h2((W & 0x00F000F0u) | 0x64006400u), shi, chi), d2, mhi));
+                o[4 * i + 3] = h22u(__hfma2(__hfma2(u2h2((W8 & 0x00F000F0u) | 0x64006400u), shi, chi), d2, mhi));
+            }
+            tmem_st16(taddr + 32 * gg + 16 * w4, o);
+        }
+    }
+}
+
+// lm_head activation packing, one CTA per token slot (m rounded up to 256):
+// x16 [TT * 256][k] f16 (row t: token t) in the converters' k order, x scaled
+// by a power of two per token; inv[t] its inverse (0 past m); keys[t] (t < m)
+// reset to the smallest key.
+__global__ void lmh_pack_kernel(const float *__restrict__ x, int m, int k, int q8, __half *__restrict__ x16,
+                                float *__restrict__ inv, unsigned long long *__restrict__ keys) {
+    const int t = blockIdx.x;
+    __shared__ float red[32];
+    float mx = 0.f;
+    if (t < m)
+        for (int i = threadIdx.x; i < k; i += blockDim.x) mx = fmaxf(mx, fabsf(x[(size_t)t * k + i]));
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    float s, iv;
+    act_scale(red[0], s, iv);
+    if (threadIdx.x == 0) {
+        inv[t] = t < m ? iv : 0.f;
+        if (t < m) keys[t] = kKeyMin;
+    }
+    __half *xr16 = x16 + (size_t)t * k;
+    for (int q = threadIdx.x; q < k / 8; q += blockDim.x) {  // position chunk c of super-block sb
+        const int sb = q >> 5, c = q & 31;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+        if (t < m) {
+            const float *xr = x + (size_t)t * k + (size_t)sb * 256;
+            a = *reinterpret_cast<const float4 *>(xr + chunk_elem(q8 != 0, c, 0));
+            b = *reinterpret_cast<const float4 *>(xr + chunk_elem(q8 != 0, c, 4));
+        }
+        const float v[8] = {a.x * s, a.z * s, a.y * s, a.w * s, b.x * s, b.z * s, b.y * s, b.w * s};
+        uint32_t h[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) h[i] = h22u(__floats2half2_rn(v[2 * i], v[2 * i + 1]));
+        *reinterpret_cast<uint4 *>(xr16 + (size_t)q * 8) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+}
+
+struct LmhLayout {
+    size_t x = 0, raw = 0, bars = 0, tslot = 0, total = 0;
+    int RS = 0;
+};
+
+template <class F>
+__host__ __device__ constexpr LmhLayout lmh_layout() {
+    LmhLayout L{};
+    L.RS = F::kQ8 ? 2 : 3;  // raw weight units (34 / 18 KB) in flight
+    L.x = 0;
+    L.raw = (size_t)kLmXS * kLmChunk;
+    L.bars = L.raw + (size_t)L.RS * kRows * F::kRowBytes;
+    L.tslot = L.bars + (size_t)(2 * L.RS + 2 * kASlots + 2 * kLmXS + 2 + 1) * 8;
+    L.total = L.tslot + 16 + 1024;
+    return L;
+}
+
+template <class F>
+__global__ void __launch_bounds__(kLmWarps * 32, 1)
+    lmh_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+               const float *__restrict__ inv, int m, int k, int n, uint32_t row_offset,
+               unsigned long long *__restrict__ keys, float *__restrict__ logits, int half_mode,
+               unsigned *__restrict__ status) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    constexpr LmhLayout L = lmh_layout<F>();
+    constexpr int kLmRS = L.RS;
+    constexpr int kRawStage = kRows * F::kRowBytes;
+    uint8_t *x_ring = smem + L.x, *raw_ring = smem + L.raw;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *raw_full = bars, *raw_empty = raw_full + kLmRS;
+    uint64_t *a_full = raw_empty + kLmRS, *a_empty = a_full + kASlots;
+    uint64_t *x_full = a_empty + kASlots, *x_empty = x_full + kLmXS;
+    uint64_t *d_full = x_empty + kLmXS, *d_empty = d_full + 1, *drain = d_empty + 1;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + L.tslot);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = k >> 8, RT = (n + kRows - 1) / kRows, TT = (m + kLmTok - 1) / kLmTok;
+    const int ntiles = RT * TT;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kLmRS; i++) mbar_init(raw_full + i, 1), mbar_init(raw_empty + i, kConvWarps);
+        for (int i = 0; i < kASlots; i++) mbar_init(a_full + i, kConvWarps), mbar_init(a_empty + i, 1);
+        for (int i = 0; i < kLmXS; i++) mbar_init(x_full + i, 1), mbar_init(x_empty + i, 1);
+        mbar_init(d_full, 1), mbar_init(d_empty, 4), mbar_init(drain, 1);
+        mbar_init_fence();
+    }
+    if (warp == kLmMma) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tslot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot, dacc = tbase + kAccBase;
+    bool ok = true;
+    auto fail = [&]() {
+        ok = false;
+        atomicOr(status, LC_DEV_WAIT_TIMEOUT);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {  // weight producer
+            const uint64_t pol = l2_evict_first_policy();
+            int j = 0;
+            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+                const int rt = tile / TT;
+                for (int sb = 0; sb < S && ok; sb++, j++) {
+                    const int rs = j % kLmRS;
+                    if (!mbar_wait(raw_empty + rs, ((j / kLmRS) & 1) ^ 1)) { fail(); break; }
+                    mbar_expect_tx(raw_full + rs, kRawStage);
+                    tma_load_2d(raw_ring + (size_t)rs * kRawStage, &tmw, sb * F::kBoxX, rt * kRows, raw_full + rs, pol);
+                }
+            }
+        }
+    } else if (warp == kLmXProd) {
+        if (lane == 0) {  // activation producer: 64-column chunks of the tile's tokens
+            uint64_t xpol;
+            asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(xpol));
+            int xc = 0;
+            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+                const int tt = tile % TT;
+                for (int kc = 0; kc < 4 * S && ok; kc++, xc++) {
+                    const int xs = xc % kLmXS;
+                    if (!mbar_wait(x_empty + xs, ((xc / kLmXS) & 1) ^ 1)) { fail(); break; }
+                    mbar_expect_tx(x_full + xs, kLmChunk);
+                    tma_load_2d(x_ring + (size_t)xs * kLmChunk, &tmx, kc * 64, tt * kLmN, x_full + xs, xpol);
+                }
+            }
+        }
+    } else if (warp <= kConvWarps) {  // converters: group g converts half g of row r
+        const int g = (warp - 1) >> 2, quad = warp & 3, r = 32 * quad + lane;
+        const uint32_t tlane = tbase + ((uint32_t)(32 * quad) << 16);
+        const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
+        int j = 0;
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            for (int sb = 0; sb < S; sb++, j++) {
+                const int rs = j % kLmRS, as = j % kASlots;
+                if (!mbar_wait(raw_full + rs, (j / kLmRS) & 1) || !mbar_wait(a_empty + as, ((j / kASlots) & 1) ^ 1)) {
+                    fail();
+                    break;
+                }
+                tc_fence_after();
+                const uint8_t *raw = raw_ring + (size_t)rs * kRawStage + (size_t)r * F::kRowBytes;
+                const uint32_t ta = tlane + as * kACols + g * 64;
+                if constexpr (F::kQ8) {
+                    if (g == 0)
+                        conv_q8_half<0>(raw, ref_mask, ta);
+                    else
+                        conv_q8_half<1>(raw, ref_mask, ta);
+                } else {
+                    const uint4 H = lds128(raw);
+                    uint32_t sc[8], mn[8];
+                    q4k_scale_mins(H, sc, mn);
+                    const float2 dd = scales2_f32(H.x, ref_mask);
+                    if (g == 0)
+                        conv_q4k_half_w<0>(raw, sc, mn, dd.x, dd.y, ta);
+                    else
+                        conv_q4k_half_w<1>(raw, sc, mn, dd.x, dd.y, ta);
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(a_full + as);
+                    mbar_arrive(raw_empty + rs);
+                }
+            }
+        }
+    } else if (warp == kLmMma) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = umma_idesc_f16(kRows, kLmN);
+            const uint64_t xdesc0 = umma_desc_sw128(smem_addr(x_ring));
+            int j = 0, xc = 0, tc = 0;
+            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, tc++) {
+                if (!mbar_wait(d_empty, (tc & 1) ^ 1)) { fail(); break; }
+                tc_fence_after();
+                for (int sb = 0; sb < S && ok; sb++, j++) {
+                    const int as = j % kASlots;
+                    if (!mbar_wait(a_full + as, (j / kASlots) & 1)) { fail(); break; }
+                    for (int kc = 0; kc < 4; kc++, xc++) {
+                        const int xs = xc % kLmXS;
+                        if (!mbar_wait(x_full + xs, (xc / kLmXS) & 1)) { fail(); break; }
+                        tc_fence_after();
+                        const uint64_t xd = xdesc0 + (uint64_t)((xs * kLmChunk) >> 4);
+                        const uint32_t ta = tbase + as * kACols + kc * 32;
+#pragma unroll
+                        for (int kk = 0; kk < 4; kk++)
+                            umma_f16_ts(dacc, ta + 8 * kk, xd + (uint64_t)(2 * kk), idesc, (sb | kc | kk) ? 1u : 0u);
+                        umma_commit(x_empty + xs);
+                    }
+                    umma_commit(a_empty + as);
+                }
+                if (!ok) break;
+                umma_commit(d_full);
+            }
+            umma_commit(drain);
+            if (!mbar_wait(drain, 0)) atomicOr(status, LC_DEV_WAIT_TIMEOUT);
+        }
+    } else {  // epilogue: TMEM lanes 32q..32q+31 = tile rows
+        const int q = warp & 3;
+        const uint32_t lanes = (uint32_t)(32 * q) << 16;
+        int tc = 0;
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, tc++) {
+            const int rt = tile / TT, tt = tile - rt * TT;
+            if (!mbar_wait(d_full, tc & 1)) { fail(); break; }
+            tc_fence_after();
+            const int row = rt * kRows + 32 * q + lane;
+            const bool valid = row < n;
+            const uint32_t gidx = row_offset + (uint32_t)row;
+#pragma unroll 1
+            for (int c = 0; c < kLmTok / 16; c++) {
+                float ph[16], iv[16];
+                const int t0 = tt * kLmTok + 16 * c;
+#pragma unroll
+                for (int i = 0; i < 16; i += 4) {
+                    const float4 f = __ldg(reinterpret_cast<const float4 *>(inv + t0 + i));
+                    iv[i] = f.x, iv[i + 1] = f.y, iv[i + 2] = f.z, iv[i + 3] = f.w;
+                }
+                tmem_ld16(dacc + lanes + 16 * c, ph);
+                tmem_ld_wait();
+                tmem_regs_ready(ph);
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const int t = t0 + i;
+                    const float v = ph[i] * iv[i];
+                    if (logits && valid && t < m) logits[(size_t)t * n + row] = v;
+                    const uint32_t b = __float_as_uint(v);
+                    const uint32_t o = valid ? ((b & 0x80000000u) ? ~b : (b | 0x80000000u)) : 0u;
+                    const uint32_t mo = __reduce_max_sync(0xffffffffu, o);
+                    const uint32_t win = __ballot_sync(0xffffffffu, valid && o == mo);
+                    if (t < m && win && lane == 31 - __clz(win))
+                        atomicMax(reinterpret_cast<long long *>(keys) + t, (long long)lc_make_key(v, gidx));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d_empty);
+        }
+    }
+    __syncthreads();
+    if (warp == kLmMma) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
 // ---- host -------------------------------------------------------------------
 
 template <class F>
@@ -665,13 +984,14 @@ int weight_map_rows128(CUtensorMap *tm, const void *w, uint32_t k, uint32_t n) {
     return LC_OK;
 }
 
-int x16_map(CUtensorMap *tm, const void *x16, uint32_t k, int nt) {
+// f16 activation rows [rows][k], boxes of 64 columns x box_rows rows, 128-byte swizzle.
+int x16_map(CUtensorMap *tm, const void *x16, uint32_t k, int rows, int box_rows) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
     int s = lc_tensor_map_encoder(&enc);
     if (s) return s;
-    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)nt};
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-    cuuint32_t box[2] = {64, (cuuint32_t)nt};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     cuuint32_t es[2] = {1, 1};
     const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(x16), dims, strides, box, es,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -696,7 +1016,7 @@ int launch_dq_gemm(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint
     CUtensorMap tmw, tmx;
     int s = weight_map_rows128<F>(&tmw, w, k, n);
     if (s) return s;
-    s = x16_map(&tmx, x16, k, 2 * NT);
+    s = x16_map(&tmx, x16, k, 2 * NT, 2 * NT);
     if (s) return s;
     x16_pack_kernel<<<dim3(S, NT / 8), 256, 0, ctx->stream>>>(x, (int)m, (int)k, F::kQ8 ? 1 : 0, NT, x16, sx16, inv,
                                                                 y, (long long)m * n);
@@ -706,6 +1026,34 @@ int launch_dq_gemm(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint
     const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, TS));
     dq_gemm_kernel<F, NT><<<grid, kGemmWarps * 32, L.total, ctx->stream>>>(tmw, tmx, sx16, inv, y, (int)m, (int)k,
                                                                            (int)n, ctx->half_mode, ctx->dev_status);
+    return LC_OK;
+}
+
+template <class F>
+int launch_lmh(lc_ctx *ctx, const float *x, const uint8_t *w, uint32_t m, uint32_t k, uint32_t n,
+               uint32_t row_offset, uint64_t *keys, float *logits) {
+    constexpr LmhLayout L = lmh_layout<F>();
+    LC_REQUIRE(L.total <= ctx->smem_optin, LC_ERR_UNSUPPORTED, "lm_head: %zu bytes of shared memory needed", L.total);
+    const uint32_t TT = (m + kLmTok - 1) / kLmTok, RT = (n + kRows - 1) / kRows;
+    const size_t x16_bytes = (size_t)TT * kLmN * k * 2, inv_bytes = (size_t)TT * kLmTok * 4;
+    uint8_t *scr = (uint8_t *)lc_scratch(ctx, LC_SCRATCH_PACK, x16_bytes + inv_bytes + 256);
+    if (!scr) return LC_ERR_OOM;
+    __half *x16 = reinterpret_cast<__half *>(scr);
+    float *inv = reinterpret_cast<float *>(scr + x16_bytes);
+    CUtensorMap tmw, tmx;
+    int s = weight_map_rows128<F>(&tmw, w, k, n);
+    if (s) return s;
+    s = x16_map(&tmx, x16, k, (int)(TT * kLmN), kLmN);
+    if (s) return s;
+    lmh_pack_kernel<<<TT * kLmTok, 256, 0, ctx->stream>>>(x, (int)m, (int)k, F::kQ8 ? 1 : 0, x16, inv,
+                                                           reinterpret_cast<unsigned long long *>(keys));
+    s = lc_set_smem_attr((const void *)lmh_kernel<F>, L.total);
+    if (s) return s;
+    const long long tiles = (long long)RT * TT;
+    const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, tiles));
+    lmh_kernel<F><<<grid, kLmWarps * 32, L.total, ctx->stream>>>(tmw, tmx, inv, (int)m, (int)k, (int)n, row_offset,
+                                                                 reinterpret_cast<unsigned long long *>(keys), logits,
+                                                                 ctx->half_mode, ctx->dev_status);
     return LC_OK;
 }
 
@@ -725,6 +1073,20 @@ int gemm_dq(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uin
     if (dtype == LC_Q8_0)
         return m <= 16 ? launch_dq_gemm<GQ8_0, 16>(ctx, x, wb, y, m, k, n)
                        : launch_dq_gemm<GQ8_0, 32>(ctx, x, wb, y, m, k, n);
+    return LC_ERR_UNSUPPORTED;
+}
+
+// lm_head logits + argmax on tcgen05 for a vocab shard (rows [0, n) of w,
+// global index row_offset + row); LC_ERR_UNSUPPORTED when the shape is not
+// covered.  keys[t] is reset and then receives the shard's best key.
+int lm_head_tc(lc_ctx *ctx, int dtype, const float *x, const void *w, uint32_t m, uint32_t k, uint32_t n,
+               uint32_t row_offset, uint64_t *keys, float *logits) {
+    if (m == 0 || n == 0 || k % 256 != 0 || ((uintptr_t)w & 15) != 0 || ((uintptr_t)x & 15) != 0 ||
+        (long long)k * 32 >= (1ll << 31))
+        return LC_ERR_UNSUPPORTED;
+    const uint8_t *wb = (const uint8_t *)w;
+    if (dtype == LC_Q8_0) return launch_lmh<GQ8_0>(ctx, x, wb, m, k, n, row_offset, keys, logits);
+    if (dtype == LC_Q4_K) return launch_lmh<GQ4K>(ctx, x, wb, m, k, n, row_offset, keys, logits);
     return LC_ERR_UNSUPPORTED;
 }
 

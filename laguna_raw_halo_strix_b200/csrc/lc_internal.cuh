@@ -150,4 +150,8 @@ int proj_f32(lc_ctx *ctx, const float *x, const float *w, float *c, uint32_t m, 
 // tcgen05 GEMM for 5..32 tokens (lc_gemm.cu); LC_ERR_UNSUPPORTED when the
 // shape is not covered.
 int gemm_dq(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n);
+// lm_head logits + argmax keys on tcgen05 (lc_gemm.cu); LC_ERR_UNSUPPORTED when
+// the shape is not covered.
+int lm_head_tc(lc_ctx *ctx, int dtype, const float *x, const void *w, uint32_t m, uint32_t k, uint32_t n,
+               uint32_t row_offset, uint64_t *keys, float *logits);
 }  // namespace lc

@@ -360,6 +360,13 @@ extern "C" int lc_lm_head_argmax(lc_ctx *ctx, int dtype, const float *x, const v
     if (m == 0) return LC_OK;
     LC_REQUIRE(x && w && keys, LC_ERR_INVALID, "lc_lm_head_argmax: null pointer");
     LC_REQUIRE(n_local > 0, LC_ERR_INVALID, "lc_lm_head_argmax: n_local must be > 0");
+    // Blocks of more than 32 rows: tensor-core tiles with the argmax fused in
+    // the epilogue (the choice depends on m only, so every vocab shard of a
+    // call computes its logits the same way).
+    if (ctx->gemm_tc && m > 32) {
+        const int s = lc::lm_head_tc(ctx, dtype, x, w, m, k, n_local, row_offset, keys, logits);
+        if (s != LC_ERR_UNSUPPORTED) return s ? s : lc_after_launch(ctx, "lc_lm_head_argmax");
+    }
     float *lg = logits;
     if (!lg) {
         lg = (float *)lc_scratch(ctx, LC_SCRATCH_LOGITS, (size_t)m * n_local * 4);

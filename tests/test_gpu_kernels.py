@@ -347,6 +347,41 @@ def test_lm_head_argmax(ctx, dev, oracle, dtype):
             assert srt[-1] - srt[-2] <= 2e-3 * np.abs(ref[r]).max()
 
 
+@pytest.mark.parametrize("dtype", [lc.Q8_0, lc.Q4_K])
+def test_lm_head_argmax_tiles(ctx, dev, oracle, dtype):
+    """More than 32 rows: the tensor-core tiles with the argmax in the epilogue
+    (200 rows = a full and a partial 128-token tile; 3000 vocab rows = 23 full
+    128-row tiles and a partial one; a shard offset)."""
+    import torch
+
+    rng = np.random.default_rng(13)
+    m, k, n, off = 200, 512, 3000, 777
+    w = synth.q8_0_blocks(n, k, rng) if dtype == lc.Q8_0 else synth.q4k_blocks(n, k, rng)
+    x = synth.activations(m, k, rng)
+    xd, wd = to_dev(x, dev), to_dev(w, dev)
+    keys = torch.empty(m, dtype=torch.int64, device=dev)
+    logits = torch.full((m, n), float("nan"), device=dev)
+    ctx.lm_head_argmax(dtype, xd, wd, m, k, n, off, keys, logits)
+    keys2 = torch.empty(m, dtype=torch.int64, device=dev)
+    ctx.lm_head_argmax(dtype, xd, wd, m, k, n, off, keys2)  # without the logits output
+    torch.cuda.synchronize()
+    ctx.device_status()
+    ref = oracle.proj(dtype, x, w, k, n).reshape(m, n)
+    lg = logits.cpu().numpy()
+    assert np.array_equal(keys.cpu().numpy(), keys2.cpu().numpy())
+    for r in range(m):
+        check_tol(lg[r], ref[r], 1e-3, "lm_head logits")
+        kk = int(np.int64(keys[r].item()).view(np.uint64))
+        idx = lc.key_index(kk)
+        j = n - 1 - int(np.argmax(lg[r][::-1]))  # last maximum of the returned logits
+        assert idx == off + j
+        assert lc.key_value(kk) == lg[r][j]
+        o = oracle.argmax(ref[r])
+        if idx != off + o:
+            srt = np.sort(ref[r])
+            assert srt[-1] - srt[-2] <= 2e-3 * np.abs(ref[r]).max()
+
+
 @pytest.mark.parametrize("dtype", [lc.Q4_K, lc.Q8_0])
 def test_repeat_calls_consistent(ctx, dev, oracle, dtype):
     # The stream-K kernels sum split tiles in a scratch that each call must

@@ -92,12 +92,13 @@ def test_two_rank_gloo_reduction(tmp_path):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("m", [9, 150])  # 150: the tensor-core tiles (m > 32), a partial token tile
 @pytest.mark.parametrize("dtype", [lc.Q8_0, lc.Q4_K])
-def test_shards_on_one_gpu_combine(ctx, dev, oracle, dtype):
+def test_shards_on_one_gpu_combine(ctx, dev, oracle, dtype, m):
     import torch
 
     rng = np.random.default_rng(17)
-    m, k, n = 9, 512, 2051
+    k, n = 512, 2051
     w = synth.weight_blocks(dtype, n, k, rng)
     x = synth.activations(m, k, rng)
     xd = torch.from_numpy(x).to(dev)
