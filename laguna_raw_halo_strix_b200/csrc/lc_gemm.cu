@@ -896,10 +896,14 @@ __global__ void __launch_bounds__(kLmWarps * 32, 1)
                 for (int sb = 0; sb < S && ok; sb++, j++) {
                     const int as = j % kASlots;
                     if (!mbar_wait(a_full + as, (j / kASlots) & 1)) { fail(); break; }
+                    // A was written by other threads' tcgen05.st: fence after that
+                    // synchronisation.  The activation chunks arrive by TMA and are
+                    // read by the MMA through the same async proxy, ordered by
+                    // their mbarrier alone.
+                    tc_fence_after();
                     for (int kc = 0; kc < 4; kc++, xc++) {
                         const int xs = xc % kLmXS;
                         if (!mbar_wait(x_full + xs, (xc / kLmXS) & 1)) { fail(); break; }
-                        tc_fence_after();
                         const uint64_t xd = xdesc0 + (uint64_t)((xs * kLmChunk) >> 4);
                         const uint32_t ta = tbase + as * kACols + kc * 32;
 #pragma unroll
@@ -925,7 +929,6 @@ __global__ void __launch_bounds__(kLmWarps * 32, 1)
             tc_fence_after();
             const int row = rt * kRows + 32 * q + lane;
             const bool valid = row < n;
-            const uint32_t gidx = row_offset + (uint32_t)row;
 #pragma unroll 1
             for (int c = 0; c < kLmTok / 16; c++) {
                 float ph[16], iv[16];
@@ -938,6 +941,10 @@ __global__ void __launch_bounds__(kLmWarps * 32, 1)
                 tmem_ld16(dacc + lanes + 16 * c, ph);
                 tmem_ld_wait();
                 tmem_regs_ready(ph);
+                // All 16 tokens' warp maxima first (independent redux / ballot
+                // pairs), then lane i builds token i's key from the warp-uniform
+                // maximum and winning lane: one predicated atomic per lane.
+                uint32_t my_o = 0u, my_win = 0u;
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
                     const int t = t0 + i;
@@ -947,8 +954,14 @@ __global__ void __launch_bounds__(kLmWarps * 32, 1)
                     const uint32_t o = valid ? ((b & 0x80000000u) ? ~b : (b | 0x80000000u)) : 0u;
                     const uint32_t mo = __reduce_max_sync(0xffffffffu, o);
                     const uint32_t win = __ballot_sync(0xffffffffu, valid && o == mo);
-                    if (t < m && win && lane == 31 - __clz(win))
-                        atomicMax(reinterpret_cast<long long *>(keys) + t, (long long)lc_make_key(v, gidx));
+                    if (lane == i) my_o = mo, my_win = win;
+                }
+                const int t = t0 + lane;
+                if (lane < 16 && t < m && my_win) {
+                    const uint32_t wrow = (uint32_t)(rt * kRows + 32 * q + 31 - __clz(my_win));
+                    const unsigned long long key =
+                        (((unsigned long long)my_o << 32) | (row_offset + wrow)) ^ kKeyMin;  // lc_make_key
+                    atomicMax(reinterpret_cast<long long *>(keys) + t, (long long)key);
                 }
             }
             tc_fence_before();
