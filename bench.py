@@ -37,6 +37,16 @@ L2_BYTES = 126 * 1024 * 1024
 METRIC = "Q4_K/Q8_0 GEMV HBM GB/s (% of peak); DFlash 16-token draft-block fwd/s"
 
 
+def _traffic(workload):
+    """DRAM bytes (read + write) of one launch of the workload's dominant kernel,
+    from the ncu capture summarised in profiles/ (None if not recorded)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(workload)
+    except Exception:
+        return None
+
+
 def peaks():
     try:
         with open(MEASURED_PEAKS) as f:
@@ -401,7 +411,7 @@ def run_lm_head(args):
     stream = torch.cuda.Stream(dev)
     ctx = lc.Context(local_rank)
     ctx.set_stream(stream)
-    m, k, vocab = LM_HEAD["m"], LM_HEAD["k"], LM_HEAD["vocab"]
+    m, k, vocab = LM_HEAD["m"], LM_HEAD["k"], args.vocab or LM_HEAD["vocab"]
     head = ShardedLmHead(ctx, lc.Q8_0, k, vocab, rank, world)
     rng = np.random.default_rng(2000 + rank)
     shard = synth.q8_0_blocks(head.n_local, k, rng)
@@ -485,8 +495,9 @@ def run_lm_head(args):
     w_total = vocab * (k // 32) * 34
     step_b = w_total + world * 4 * m * k  # every weight byte once; x read by every rank
     value = step_b * args.steps / (ms / 1e3) / 1e9
-    hbm, _, peak_src = peaks()
+    hbm, tflops, peak_src = peaks()
     local_b = shard_bytes + 4 * m * k
+    local_f = 2.0 * m * k * head.n_local
     if rank == 0:
         _emit({
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -498,10 +509,13 @@ def run_lm_head(args):
                        "tokens_per_s": m * args.steps / (ms / 1e3),
                        "l2": f"weights rotated through {pool} copies of {shard_bytes / 1e6:.1f} MB per rank",
                        "parallelism": f"vocab-sharded x{world}, int64 MAX all-reduce of {m} keys per step"},
-            "roofline": {"bound": "hbm", "achieved": local_b / (local_ms / 1e3) / 1e9, "peak": hbm,
-                         "peak_source": peak_src, "unit": "GB/s", "frac": local_b / (local_ms / 1e3) / 1e9 / hbm,
-                         "traffic": None, "kernel": "lc_lm_head_argmax (one shard, all its kernels)",
-                         "per_launch_us": local_ms * 1e3, "bytes_per_launch": local_b},
+            # tensor-bound: 2 m k n_local useful flops per launch (the tcgen05 tiles)
+            "roofline": {"bound": "tensor", "achieved": local_f / (local_ms / 1e3) / 1e12, "peak": tflops,
+                         "peak_source": peak_src + " (dense bf16 burst)", "unit": "TFLOP/s",
+                         "frac": local_f / (local_ms / 1e3) / 1e12 / tflops, "traffic": _traffic("lm_head_q8_0"),
+                         "kernel": "lc_lm_head_argmax (one shard: packing + lmh_kernel)",
+                         "per_launch_us": local_ms * 1e3, "flops_per_launch": local_f,
+                         "hbm_gbs_per_launch": local_b / (local_ms / 1e3) / 1e9},
             "cpu_baseline": None,
             "e2e": {"value": step_b * e2e_steps / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * m * k,
                     "d2h_bytes_per_step": 8 * m, "steps": e2e_steps},
@@ -643,6 +657,9 @@ def main():
     ap.add_argument("--workload", default="ffn_q4k_m1", choices=sorted(WORKLOADS) + list(SPECIAL))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--vocab", type=int, default=0,
+                    help="lm_head_q8_0 only: vocab rows (default: BASELINE config 4's 128256); a smaller vocab "
+                         "keeps an ncu capture short")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -808,12 +825,7 @@ def main():
         if not args.no_cpu_baseline and world == 1:
             v, kind, cores, sample = cpu_baseline(wl, 10.0, np.random.default_rng(7))
             cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample}
-        traffic = None
-        try:
-            with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-                traffic = json.load(f).get(args.workload)
-        except Exception:
-            pass
+        traffic = _traffic(args.workload)
         line = {
             "metric": METRIC,
             "value": value,
@@ -838,8 +850,9 @@ def main():
                 "unit": "GB/s",
                 "frac": achieved / hbm,
                 "traffic": traffic,
-                "kernel": (("q4k_tma_kernel" if m <= 4 else "q4k_mma_kernel + x_pack_q4k") if wl["dtype"] == "q4k"
-                           else ("q8_sk_kernel" if m <= 4 else "q8_mma_kernel + x_pack_q8")),
+                "kernel": ((f"tma_gemv_kernel<FmtQ4K,{m}>" if wl["dtype"] == "q4k" else f"tma_gemv_kernel<FmtQ8_0,{m}>")
+                           if m <= 4 else ("dq_gemm_kernel + x16_pack_kernel" if m <= 32 else
+                                           "q4k_mma_kernel / q8_mma_kernel + x_pack")),
                 "per_launch_us": per_launch_ms * 1e3,
                 "bytes_per_launch": launch_bytes(wl),
             },

@@ -226,9 +226,17 @@ class Context:
             pass
 
     def set_stream(self, stream) -> None:
-        """stream: torch.cuda.Stream, raw cudaStream_t int, or None (own stream)."""
-        raw = getattr(stream, "cuda_stream", stream)
-        check(self.L.lc_set_stream(self.h, raw or None), "lc_set_stream")
+        """stream: torch.cuda.Stream, raw cudaStream_t int, or None (the context's
+        own stream).  A torch stream whose handle is 0 (torch's default stream) maps
+        to cudaStreamLegacy, so the work really runs on that stream: a NULL handle
+        would select the context's own stream instead."""
+        if stream is None:
+            raw = None
+        elif hasattr(stream, "cuda_stream"):
+            raw = stream.cuda_stream or 0x1  # cudaStreamLegacy
+        else:
+            raw = stream or None
+        check(self.L.lc_set_stream(self.h, raw), "lc_set_stream")
 
     def synchronize(self) -> None:
         check(self.L.lc_synchronize(self.h), "lc_synchronize")
