@@ -174,6 +174,15 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// Programmatic dependent launch: the dependent grid may start once every CTA
+// of this grid has executed launch_dependents (or exited); griddep_wait blocks
+// until the prerequisite grid has completed and its writes are visible (a no-op
+// in a grid launched without the attribute).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 // Untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t pol) {
     asm volatile(
@@ -645,6 +654,382 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
     }
 }
 
+// ---- the int8 GEMV: 1..4 tokens ----------------------------------------------
+//
+// kernels/proj_q4k.comp:60-92 and proj_q8_0.comp:47-67 for up to 4 rows of x on
+// the tensor cores' 8-bit path (tcgen05.mma kind::i8, K = 32): one MMA covers
+// exactly one 32-element Q4_K sub-block / Q8_0 block of 128 weight rows, so the
+// weights go to TMEM as their raw integers (Q4_K nibbles as u8, Q8_0 bytes as s8;
+// a mask and a shift per 8 weights) and each block's scale is applied by the
+// epilogue to that block's own accumulator columns.  The activations are
+// X = round(x * s) (|X| <= 16256, s per (token, super-block)) in two s8 digits,
+// X = 128 hi + lo, hi in B row t and lo in B row 8 + t (N = 16); the sums are
+// exact integers until the epilogue's f32 scaling.  Q4_K's min term uses the
+// integer sub-block sums of X.
+
+constexpr int kG8Rows = 16;          // B rows (N): hi digits 0..7, lo digits 8..15
+constexpr int kG8XStage = kG8Rows * 256;  // one unit's digits, 4 KB
+constexpr int kG8ACols = 64;          // one unit of 8-bit weights: 256 per lane
+constexpr int kG8ASlots = 4;
+constexpr int kG8DCols = 128;         // 8 blocks x 16 columns
+constexpr int kG8ND = 2;
+
+// Activation digits, one CTA per super-block, warp t = token slot t (0..7):
+//   x8 [16][k] s8: row t the hi digit, row 8 + t the lo digit (zero past m);
+//   inv[sb * 8 + t] = 1 / s; sx[(sb * 8 + j) * 8 + t] = the integer sum of X over
+//   sub-block j (Q4_K).  The CTAs also zero y [m, n].
+__global__ void x8_pack_kernel(const float *__restrict__ x, int m, int k, int8_t *__restrict__ x8,
+                               float *__restrict__ inv, int *__restrict__ sx, float *__restrict__ y, long long ny) {
+    griddep_launch_dependents();  // the GEMV may start streaming its weights now
+    const long long nthreads = (long long)gridDim.x * blockDim.x;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < ny; i += nthreads) y[i] = 0.f;
+    const int sb = blockIdx.x, t = threadIdx.x >> 5, c = threadIdx.x & 31;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (t < m) {
+        const float4 a = *reinterpret_cast<const float4 *>(x + (size_t)t * k + (size_t)sb * 256 + 8 * c);
+        const float4 b = *reinterpret_cast<const float4 *>(x + (size_t)t * k + (size_t)sb * 256 + 8 * c + 4);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    }
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) mx = fmaxf(mx, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float s = mx > 0.f && mx < INFINITY ? 16256.f / mx : 0.f;
+    uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int X = __float2int_rn(v[i] * s);  // |X| <= 16256
+        const int hi = (X + 64) >> 7, lo = X - 128 * hi;
+        sum += X;
+        hw[i >> 2] |= (uint32_t)(hi & 0xFF) << (8 * (i & 3));
+        lw[i >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (i & 3));
+    }
+    *reinterpret_cast<uint2 *>(x8 + (size_t)t * k + (size_t)sb * 256 + 8 * c) = make_uint2(hw[0], hw[1]);
+    *reinterpret_cast<uint2 *>(x8 + (size_t)(8 + t) * k + (size_t)sb * 256 + 8 * c) = make_uint2(lw[0], lw[1]);
+    if (c == 0) inv[sb * 8 + t] = s > 0.f ? 1.f / s : 0.f;
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (sx && (c & 3) == 0) sx[(sb * 8 + (c >> 2)) * 8 + t] = sum;
+}
+
+struct G8Layout {
+    size_t x = 0, raw = 0, sc = 0, bars = 0, tslot = 0, total = 0;
+    int XS = 0, RS = 0;
+};
+
+template <class F>
+__host__ __device__ constexpr G8Layout g8_layout() {
+    G8Layout L{};
+    L.XS = 8;
+    L.RS = F::kQ8 ? 5 : 9;
+    L.x = 0;
+    L.raw = (size_t)L.XS * kG8XStage;
+    L.sc = L.raw + (size_t)L.RS * kRows * F::kRowBytes;
+    L.bars = L.sc + (size_t)kG8ND * kRows * 64;
+    L.tslot = L.bars + (size_t)(2 * L.RS + 2 * kG8ASlots + 2 * L.XS + 3 * kG8ND + 1) * 8;
+    L.total = L.tslot + 16 + 1024;
+    return L;
+}
+
+// Instruction descriptor of kind::i8: D s32, A u8 (a_signed = 0) or s8, B s8, K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_i8(int m, int n, bool a_signed) {
+    return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_i8_ts(uint32_t dtmem, uint32_t atmem, uint64_t bdesc, uint32_t idesc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.u32 p, 0, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(dtmem),
+        "r"(atmem), "l"(bdesc), "r"(idesc)
+        : "memory");
+}
+
+// N consecutive 32-bit TMEM columns of this thread's lane (s32), N = 4 or 8.
+template <int N>
+__device__ __forceinline__ void tmem_ld_s32(uint32_t taddr, int (&v)[N]) {
+    if constexpr (N == 4)
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\n"
+                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                     : "r"(taddr));
+    else
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                       "=r"(v[7])
+                     : "r"(taddr));
+}
+
+template <int N>
+__device__ __forceinline__ void tmem_regs_ready_i(int (&v)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; i++) asm volatile("" : "+r"(v[i])::"memory");
+}
+
+// One converter thread's half of a unit for the int8 GEMV: blocks 4g..4g+3 of its
+// row as raw integers into TMEM at ta (block b at column 8b), and their f32 scales
+// (Q4_K: d sc_j and dmin m_j; Q8_0: d).
+template <class F, int g>
+__device__ __forceinline__ void g8_convert(const uint8_t *raw, uint32_t ta, uint32_t ref_mask, float (&scl)[4],
+                                           float (&mns)[4]) {
+    if constexpr (!F::kQ8) {
+        // qs groups G = 2g, 2g+1: low nibbles = sub-block 2G, high = 2G+1
+        uint4 Qa[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) Qa[i] = lds128(raw + 16 + 64 * g + 16 * i);
+        const uint4 H = lds128(raw);
+#pragma unroll
+        for (int gg = 0; gg < 2; gg++) {
+            const uint4 A = Qa[2 * gg], B = Qa[2 * gg + 1];
+            const uint32_t qw[8] = {A.x, A.y, A.z, A.w, B.x, B.y, B.z, B.w};
+            uint32_t o[16];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                o[i] = qw[i] & 0x0F0F0F0Fu;
+                o[8 + i] = (qw[i] >> 4) & 0x0F0F0F0Fu;
+            }
+            tmem_st16(ta + 16 * gg, o);
+        }
+        uint32_t sc[8], mn[8];
+        q4k_scale_mins(H, sc, mn);
+        const float2 dd = scales2_f32(H.x, ref_mask);
+#pragma unroll
+        for (int i = 0; i < 4; i++) scl[i] = dd.x * (float)sc[4 * g + i], mns[i] = dd.y * (float)mn[4 * g + i];
+    } else {
+        // blocks 4g..4g+3 span row bytes 136g .. 136g + 135 (see conv_q8_half)
+        uint32_t Wd[36];
+#pragma unroll
+        for (int i = 0; i < 9; i++) {
+            const uint4 v = lds128(raw + 128 * g + 16 * i);
+            Wd[4 * i] = v.x, Wd[4 * i + 1] = v.y, Wd[4 * i + 2] = v.z, Wd[4 * i + 3] = v.w;
+        }
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+            uint32_t o[16];
+#pragma unroll
+            for (int bh = 0; bh < 2; bh++) {
+                const int bb = 2 * half + bh, b = 4 * g + bb;
+                const int wq = (17 * b + 1) / 2 - 32 * g, sh = (b & 1) ? 0 : 16;
+                const uint32_t dw = Wd[((b & 1) ? (17 * (b - 1)) / 2 + 8 : (17 * b) / 2) - 32 * g];
+                const uint32_t dbits = fix_sub_h2((b & 1) ? (dw >> 16) : (dw & 0xFFFFu), ref_mask) & 0xFFFFu;
+                scl[bb] = __half2float(__ushort_as_half((unsigned short)dbits));
+                mns[bb] = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int wi = wq + i;
+                    o[8 * bh + i] = __funnelshift_r(Wd[wi], (sh && wi + 1 < 36) ? Wd[wi + 1] : 0u, sh);
+                }
+            }
+            tmem_st16(ta + 16 * half, o);
+        }
+    }
+}
+
+template <class F, int MT>
+__global__ void __launch_bounds__(kGemmWarps * 32, 1)
+    gemv_i8_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+                   const float *__restrict__ inv, const int *__restrict__ sx, float *__restrict__ y, int m, int k,
+                   int n, int half_mode, unsigned *__restrict__ status) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    constexpr G8Layout L = g8_layout<F>();
+    constexpr bool Q4 = !F::kQ8;
+    constexpr int kRawStage = kRows * F::kRowBytes;
+    uint8_t *x_ring = smem + L.x, *raw_ring = smem + L.raw;
+    float *dslot = reinterpret_cast<float *>(smem + L.sc);  // [ND][128 rows][16]: 8 block scales (+ 8 mins)
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *raw_full = bars, *raw_empty = raw_full + L.RS;
+    uint64_t *a_full = raw_empty + L.RS, *a_empty = a_full + kG8ASlots;
+    uint64_t *x_full = a_empty + kG8ASlots, *x_empty = x_full + L.XS;
+    uint64_t *d_full = x_empty + L.XS, *d_empty = d_full + kG8ND, *s_full = d_empty + kG8ND, *drain = s_full + kG8ND;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + L.tslot);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = k >> 8, T = (n + kRows - 1) / kRows;
+    const long long TS = (long long)T * S;
+    const int U0 = (int)(TS * blockIdx.x / gridDim.x), U1 = (int)(TS * (blockIdx.x + 1) / gridDim.x);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < L.RS; i++) mbar_init(raw_full + i, 1), mbar_init(raw_empty + i, kConvWarps);
+        for (int i = 0; i < kG8ASlots; i++) mbar_init(a_full + i, kConvWarps), mbar_init(a_empty + i, 1);
+        for (int i = 0; i < L.XS; i++) mbar_init(x_full + i, 1), mbar_init(x_empty + i, 1);
+        for (int i = 0; i < kG8ND; i++)
+            mbar_init(d_full + i, 1), mbar_init(d_empty + i, 4), mbar_init(s_full + i, kConvWarps);
+        mbar_init(drain, kMmaWarps);
+        mbar_init_fence();
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tslot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    bool ok = true;
+    auto fail = [&]() {
+        ok = false;
+        atomicOr(status, LC_DEV_WAIT_TIMEOUT);
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {  // producer: raw weight units and the unit's activation digits
+            const uint64_t pol = l2_evict_first_policy();
+            uint64_t xpol;
+            asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(xpol));
+            for (int u = U0; u < U1 && ok; u++) {
+                const int j = u - U0, tile = u / S, sb = u - tile * S;
+                const int rs = j % L.RS, xs = j % L.XS;
+                if (!mbar_wait(raw_empty + rs, ((j / L.RS) & 1) ^ 1)) { fail(); break; }
+                mbar_expect_tx(raw_full + rs, kRawStage);
+                tma_load_2d(raw_ring + (size_t)rs * kRawStage, &tmw, sb * F::kBoxX, tile * kRows, raw_full + rs, pol);
+                if (j == 0) griddep_wait();  // the digits come from the packing kernel
+                if (!mbar_wait(x_empty + xs, ((j / L.XS) & 1) ^ 1)) { fail(); break; }
+                mbar_expect_tx(x_full + xs, kG8XStage);
+#pragma unroll
+                for (int c = 0; c < 2; c++)
+                    tma_load_2d(x_ring + (size_t)xs * kG8XStage + c * (kG8Rows * 128), &tmx, sb * 256 + c * 128, 0,
+                                x_full + xs, xpol);
+            }
+        }
+    } else if (warp <= kConvWarps) {  // converters: group g = blocks 4g..4g+3 of row r
+        const int g = (warp - 1) >> 2, quad = warp & 3, r = 32 * quad + lane;
+        const uint32_t tlane = tbase + ((uint32_t)(32 * quad) << 16);
+        const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
+        for (int u = U0; u < U1 && ok; u++) {
+            const int j = u - U0, rs = j % L.RS, as = j % kG8ASlots, db = j % kG8ND;
+            if (!mbar_wait(raw_full + rs, (j / L.RS) & 1) || !mbar_wait(a_empty + as, ((j / kG8ASlots) & 1) ^ 1)) {
+                fail();
+                break;
+            }
+            tc_fence_after();
+            const uint8_t *raw = raw_ring + (size_t)rs * kRawStage + (size_t)r * F::kRowBytes;
+            const uint32_t ta = tlane + as * kG8ACols + 32 * g;  // block b at columns 8b
+            float scl[4], mns[4];
+            if (g == 0)
+                g8_convert<F, 0>(raw, ta, ref_mask, scl, mns);
+            else
+                g8_convert<F, 1>(raw, ta, ref_mask, scl, mns);
+            // the unit's block scales for the epilogue, once its slot is free
+            if (!mbar_wait(d_empty + db, ((j / kG8ND) & 1) ^ 1)) { fail(); break; }
+            float4 *ds = reinterpret_cast<float4 *>(dslot + ((size_t)db * kRows + r) * 16);
+            ds[g] = make_float4(scl[0], scl[1], scl[2], scl[3]);
+            if (Q4) ds[2 + g] = make_float4(mns[0], mns[1], mns[2], mns[3]);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(a_full + as);
+                mbar_arrive(raw_empty + rs);
+                mbar_arrive(s_full + db);
+            }
+        }
+    } else if (warp < kMmaWarp + kMmaWarps) {
+        if (lane == 0) {  // MMA issuers: even / odd units, one MMA per 32-element block
+            constexpr uint32_t idesc = umma_idesc_i8(kRows, kG8Rows, F::kQ8);
+            const uint64_t xdesc0 = umma_desc_sw128(smem_addr(x_ring));
+            for (int u = U0 + (warp - kMmaWarp); u < U1 && ok; u += kMmaWarps) {
+                const int j = u - U0, db = j % kG8ND, as = j % kG8ASlots, xs = j % L.XS;
+                if (!mbar_wait(d_empty + db, ((j / kG8ND) & 1) ^ 1) || !mbar_wait(a_full + as, (j / kG8ASlots) & 1) ||
+                    !mbar_wait(x_full + xs, (j / L.XS) & 1)) {
+                    fail();
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t dcol = tbase + kAccBase + db * kG8DCols;
+                const uint64_t xd = xdesc0 + (uint64_t)((xs * kG8XStage) >> 4);
+                const uint32_t ta = tbase + as * kG8ACols;
+#pragma unroll
+                for (int b = 0; b < 8; b++)  // block b: K bytes 32b of the unit
+                    umma_i8_ts(dcol + 16 * b, ta + 8 * b,
+                               xd + (uint64_t)(((b >> 2) * (kG8Rows * 128) + (b & 3) * 32) >> 4), idesc);
+                umma_commit(a_empty + as);
+                umma_commit(x_empty + xs);
+                umma_commit(d_full + db);
+            }
+            umma_commit(drain);
+            if (!mbar_wait(drain, 0)) atomicOr(status, LC_DEV_WAIT_TIMEOUT);
+        }
+    } else {  // epilogue: TMEM lanes 32q..32q+31 = tile rows
+        griddep_wait();  // scales, sums and the zeroed y come from the packing kernel
+        const int q = warp & 3;
+        const uint32_t lanes = (uint32_t)(32 * q) << 16;
+        float acc[MT];
+#pragma unroll
+        for (int t = 0; t < MT; t++) acc[t] = 0.f;
+        for (int u = U0; u < U1 && ok; u++) {
+            const int j = u - U0, db = j % kG8ND, tile = u / S, sb = u - tile * S;
+            const uint32_t par = (j / kG8ND) & 1;
+            // the unit's activation scales and (Q4_K) integer sub-block sums, loaded
+            // before the wait so their latency overlaps it
+            float iv[MT], sxf[8][MT];
+#pragma unroll
+            for (int t = 0; t < MT; t++) iv[t] = __ldg(inv + sb * 8 + t);
+            if constexpr (Q4) {
+#pragma unroll
+                for (int jb = 0; jb < 8; jb++)
+#pragma unroll
+                    for (int t = 0; t < MT; t++) sxf[jb][t] = (float)__ldg(sx + (sb * 8 + jb) * 8 + t);
+            }
+            if (!mbar_wait(d_full + db, par) || !mbar_wait(s_full + db, par)) { fail(); break; }
+            tc_fence_after();
+            const uint32_t col = tbase + lanes + kAccBase + db * kG8DCols;
+            const float4 *ds = reinterpret_cast<const float4 *>(dslot + ((size_t)db * kRows + 32 * q + lane) * 16);
+            const float4 s0 = ds[0], s1 = ds[1];
+            const float scl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            float au[MT];
+#pragma unroll
+            for (int t = 0; t < MT; t++) au[t] = 0.f;
+#pragma unroll
+            for (int b = 0; b < 8; b += 2) {
+                constexpr int NL = MT <= 4 ? 4 : 8;  // columns read per digit
+                int h0[NL], l0[NL], h1[NL], l1[NL];
+                tmem_ld_s32<NL>(col + 16 * b, h0);
+                tmem_ld_s32<NL>(col + 16 * b + 8, l0);
+                tmem_ld_s32<NL>(col + 16 * (b + 1), h1);
+                tmem_ld_s32<NL>(col + 16 * (b + 1) + 8, l1);
+                tmem_ld_wait();
+                tmem_regs_ready_i(h0), tmem_regs_ready_i(l0), tmem_regs_ready_i(h1), tmem_regs_ready_i(l1);
+#pragma unroll
+                for (int t = 0; t < MT; t++) {
+                    au[t] += scl[b] * (float)(128 * h0[t] + l0[t]);
+                    au[t] += scl[b + 1] * (float)(128 * h1[t] + l1[t]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d_empty + db);
+            if constexpr (Q4) {
+                const float4 m0 = ds[2], m1 = ds[3];
+                const float mns[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+#pragma unroll
+                for (int jb = 0; jb < 8; jb++)
+#pragma unroll
+                    for (int t = 0; t < MT; t++) au[t] -= mns[jb] * sxf[jb][t];
+            }
+#pragma unroll
+            for (int t = 0; t < MT; t++) acc[t] += iv[t] * au[t];
+            if (u == U1 - 1 || sb == S - 1) {
+                const int row = tile * kRows + 32 * q + lane;
+                if (row < n)
+#pragma unroll
+                    for (int t = 0; t < MT; t++)
+                        if (t < m) atomicAdd(y + (size_t)t * n + row, acc[t]);
+#pragma unroll
+                for (int t = 0; t < MT; t++) acc[t] = 0.f;
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
 // ---- lm_head: logits of 128-token tiles fused with argmax -------------------
 //
 // TargetModel::project_normalized_hidden (src/target.rs:580-605) for many
@@ -1042,6 +1427,61 @@ int launch_dq_gemm(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint
     return LC_OK;
 }
 
+// s8 activation digits [16][k], boxes of 128 columns x 16 rows, 128-byte swizzle.
+int x8_map(CUtensorMap *tm, const void *x8, uint32_t k) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+    int s = lc_tensor_map_encoder(&enc);
+    if (s) return s;
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)kG8Rows};
+    cuuint64_t strides[1] = {(cuuint64_t)k};
+    cuuint32_t box[2] = {128, (cuuint32_t)kG8Rows};
+    cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(x8), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    LC_REQUIRE(r == CUDA_SUCCESS, LC_ERR_CUDA, "cuTensorMapEncodeTiled (activation digits) failed (%d)", (int)r);
+    return LC_OK;
+}
+
+template <class F, int MT>
+int launch_gemv_i8(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
+    constexpr G8Layout L = g8_layout<F>();
+    LC_REQUIRE(L.total <= ctx->smem_optin, LC_ERR_UNSUPPORTED, "gemv_i8: %zu bytes of shared memory needed", L.total);
+    const uint32_t S = k / 256;
+    const size_t x8_bytes = (size_t)kG8Rows * k, inv_bytes = (size_t)S * 8 * 4;
+    const size_t sx_bytes = F::kQ8 ? 0 : (size_t)S * 64 * 4;
+    uint8_t *scr = (uint8_t *)lc_scratch(ctx, LC_SCRATCH_PACK, x8_bytes + inv_bytes + sx_bytes + 256);
+    if (!scr) return LC_ERR_OOM;
+    int8_t *x8 = reinterpret_cast<int8_t *>(scr);
+    float *inv = reinterpret_cast<float *>(scr + x8_bytes);
+    int *sx = F::kQ8 ? nullptr : reinterpret_cast<int *>(scr + x8_bytes + inv_bytes);
+    CUtensorMap tmw, tmx;
+    int s = weight_map_rows128<F>(&tmw, w, k, n);
+    if (s) return s;
+    s = x8_map(&tmx, x8, k);
+    if (s) return s;
+    x8_pack_kernel<<<S, 256, 0, ctx->stream>>>(x, (int)m, (int)k, x8, inv, sx, y, (long long)m * n);
+    s = lc_set_smem_attr((const void *)gemv_i8_kernel<F, MT>, L.total);
+    if (s) return s;
+    const long long TS = (long long)((n + kRows - 1) / kRows) * S;
+    const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, TS));
+    // launched as a programmatic dependent of the packing kernel: weights stream
+    // while the activations are digitised
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemmWarps * 32);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    LC_CUDA(cudaLaunchKernelEx(&cfg, gemv_i8_kernel<F, MT>, tmw, tmx, (const float *)inv, (const int *)sx, y, (int)m,
+                               (int)k, (int)n, ctx->half_mode, ctx->dev_status));
+    return LC_OK;
+}
+
 template <class F>
 int launch_lmh(lc_ctx *ctx, const float *x, const uint8_t *w, uint32_t m, uint32_t k, uint32_t n,
                uint32_t row_offset, uint64_t *keys, float *logits) {
@@ -1100,6 +1540,22 @@ int lm_head_tc(lc_ctx *ctx, int dtype, const float *x, const void *w, uint32_t m
     const uint8_t *wb = (const uint8_t *)w;
     if (dtype == LC_Q8_0) return launch_lmh<GQ8_0>(ctx, x, wb, m, k, n, row_offset, keys, logits);
     if (dtype == LC_Q4_K) return launch_lmh<GQ4K>(ctx, x, wb, m, k, n, row_offset, keys, logits);
+    return LC_ERR_UNSUPPORTED;
+}
+
+// 3..8-token projections on the 8-bit tensor-core path (1 and 2 tokens stream
+// faster through the TMA GEMV of lc_proj.cu); LC_ERR_UNSUPPORTED when the
+// shape is not covered (the caller falls back).
+int gemv_i8(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
+    if (m < 3 || m > 8 || k % 256 != 0 || ((uintptr_t)w & 15) != 0 || ((uintptr_t)x & 15) != 0 ||
+        (long long)k * 16 >= (1ll << 31))
+        return LC_ERR_UNSUPPORTED;
+    const uint8_t *wb = (const uint8_t *)w;
+    if (dtype == LC_Q4_K)
+        return m <= 4 ? launch_gemv_i8<GQ4K, 4>(ctx, x, wb, y, m, k, n) : launch_gemv_i8<GQ4K, 8>(ctx, x, wb, y, m, k, n);
+    if (dtype == LC_Q8_0)
+        return m <= 4 ? launch_gemv_i8<GQ8_0, 4>(ctx, x, wb, y, m, k, n)
+                      : launch_gemv_i8<GQ8_0, 8>(ctx, x, wb, y, m, k, n);
     return LC_ERR_UNSUPPORTED;
 }
 

@@ -150,6 +150,9 @@ int proj_f32(lc_ctx *ctx, const float *x, const float *w, float *c, uint32_t m, 
 // tcgen05 GEMM for 5..32 tokens (lc_gemm.cu); LC_ERR_UNSUPPORTED when the
 // shape is not covered.
 int gemm_dq(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n);
+// 1..4-token projections on tcgen05 kind::i8 (lc_gemm.cu); LC_ERR_UNSUPPORTED when
+// the shape is not covered.
+int gemv_i8(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n);
 // lm_head logits + argmax keys on tcgen05 (lc_gemm.cu); LC_ERR_UNSUPPORTED when
 // the shape is not covered.
 int lm_head_tc(lc_ctx *ctx, int dtype, const float *x, const void *w, uint32_t m, uint32_t k, uint32_t n,
