@@ -200,7 +200,8 @@ int lc_enc_aux_norm(lc_ctx *ctx, const float *x, const float *w, float *y,
                     float eps);
 /* dispatch_mha_attn_seq (src/dflash.rs:1160-1198), kernels/mha_attn.comp, for
  * m query rows q [m, n_q_heads*head_dim] over k, v [seq_len, n_kv_heads*head_dim];
- * query r sits at position q_pos0 + r (key p is visible iff !causal || p <= pos). */
+ * query r sits at position q_pos0 + r (key p is visible iff !causal || p <= pos).
+ * head_dim 128; q, k and v 16-byte aligned. */
 int lc_mha_attn(lc_ctx *ctx, const float *q, const float *k, const float *v,
                 float *out, uint32_t m, uint32_t n_q_heads, uint32_t n_kv_heads,
                 uint32_t head_dim, uint32_t seq_len, float scale,

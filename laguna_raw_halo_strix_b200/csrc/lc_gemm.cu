@@ -1543,19 +1543,24 @@ int lm_head_tc(lc_ctx *ctx, int dtype, const float *x, const void *w, uint32_t m
     return LC_ERR_UNSUPPORTED;
 }
 
-// 3..8-token projections on the 8-bit tensor-core path (1 and 2 tokens stream
-// faster through the TMA GEMV of lc_proj.cu); LC_ERR_UNSUPPORTED when the
-// shape is not covered (the caller falls back).
+// ctx->gemv_i8_min..8-token projections on the 8-bit tensor-core path (by
+// default 3: 1 and 2 tokens stream faster through the TMA GEMV of lc_proj.cu);
+// LC_ERR_UNSUPPORTED when the shape is not covered (the caller falls back).
 int gemv_i8(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
-    if (m < 3 || m > 8 || k % 256 != 0 || ((uintptr_t)w & 15) != 0 || ((uintptr_t)x & 15) != 0 ||
+    if ((int)m < ctx->gemv_i8_min || m > 8 || k % 256 != 0 || ((uintptr_t)w & 15) != 0 || ((uintptr_t)x & 15) != 0 ||
         (long long)k * 16 >= (1ll << 31))
         return LC_ERR_UNSUPPORTED;
     const uint8_t *wb = (const uint8_t *)w;
     if (dtype == LC_Q4_K)
-        return m <= 4 ? launch_gemv_i8<GQ4K, 4>(ctx, x, wb, y, m, k, n) : launch_gemv_i8<GQ4K, 8>(ctx, x, wb, y, m, k, n);
+        return m == 1   ? launch_gemv_i8<GQ4K, 1>(ctx, x, wb, y, m, k, n)
+               : m == 2 ? launch_gemv_i8<GQ4K, 2>(ctx, x, wb, y, m, k, n)
+               : m <= 4 ? launch_gemv_i8<GQ4K, 4>(ctx, x, wb, y, m, k, n)
+                        : launch_gemv_i8<GQ4K, 8>(ctx, x, wb, y, m, k, n);
     if (dtype == LC_Q8_0)
-        return m <= 4 ? launch_gemv_i8<GQ8_0, 4>(ctx, x, wb, y, m, k, n)
-                      : launch_gemv_i8<GQ8_0, 8>(ctx, x, wb, y, m, k, n);
+        return m == 1   ? launch_gemv_i8<GQ8_0, 1>(ctx, x, wb, y, m, k, n)
+               : m == 2 ? launch_gemv_i8<GQ8_0, 2>(ctx, x, wb, y, m, k, n)
+               : m <= 4 ? launch_gemv_i8<GQ8_0, 4>(ctx, x, wb, y, m, k, n)
+                        : launch_gemv_i8<GQ8_0, 8>(ctx, x, wb, y, m, k, n);
     return LC_ERR_UNSUPPORTED;
 }
 

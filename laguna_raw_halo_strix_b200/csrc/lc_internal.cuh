@@ -20,6 +20,8 @@ struct lc_ctx {
     // 1: 5..32-token Q4_K / Q8_0 projections run the tcgen05 GEMM (lc_gemm.cu);
     // 0: the mma.sync tiled kernels.  Set from LC_GEMM_TC at lc_init (default 1).
     int gemm_tc = 1;
+    // Smallest token count sent to the int8 tcgen05 GEMV (LC_GEMV_I8_MIN, default 3).
+    int gemv_i8_min = 3;
     // Grow-only scratch slots (see LC_SCRATCH_*).
     void *scratch[8] = {};
     size_t scratch_bytes[8] = {};

@@ -1565,7 +1565,7 @@ int proj_q4k(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m, 
     LC_REQUIRE(((uintptr_t)wv & 15) == 0, LC_ERR_INVALID, "proj_q4k: weight pointer not 16-byte aligned");
     const uint8_t *w = (const uint8_t *)wv + (size_t)(expert_offset / 256) * 144;
     // 1-2 tokens: the TMA GEMV; 3-8: the int8 tcgen05 GEMV; 9-32: the f16 tcgen05 GEMM
-    if (ctx->gemm_tc && m >= 3 && m <= 8) {
+    if (ctx->gemm_tc && (int)m >= ctx->gemv_i8_min && m <= 8) {
         const int s = gemv_i8(ctx, LC_Q4_K, x, w, c, m, k, n);
         if (s != LC_ERR_UNSUPPORTED) return s;
     }
@@ -1622,7 +1622,7 @@ int proj_q8_0(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m,
         return LC_OK;
     }
     const int nblk = k / 32;
-    if (ctx->gemm_tc && m >= 3 && m <= 8) {  // as proj_q4k
+    if (ctx->gemm_tc && (int)m >= ctx->gemv_i8_min && m <= 8) {  // as proj_q4k
         const int s = gemv_i8(ctx, LC_Q8_0, x, w, c, m, k, n);
         if (s != LC_ERR_UNSUPPORTED) return s;
     }
