@@ -46,6 +46,73 @@ __global__ void rmsnorm_kernel(const float *__restrict__ w, const float *x, floa
     for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = xr[i] * w[i] * rms;
 }
 
+// rmsnorm for rows of n % 4 == 0, n <= 16 * blockDim: the row stays in
+// registers (4 float4 per thread at most), one read of x.
+__global__ void rmsnorm4_kernel(const float *__restrict__ w, const float *x, float *y, int n, float eps) {
+    __shared__ float sh[32];
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * n);
+    float4 *yr = reinterpret_cast<float4 *>(y + (size_t)blockIdx.x * n);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    const int n4 = n >> 2;
+    float4 v[4];
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        v[j] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        s += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+    }
+    s = block_sum(s, sh);
+    const float rms = rsqrtf(s / (float)n + eps);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < n4) {
+            const float4 ww = w4[i];
+            yr[i] = make_float4(v[j].x * ww.x * rms, v[j].y * ww.y * rms, v[j].z * ww.z * rms, v[j].w * ww.w * rms);
+        }
+    }
+}
+
+// qk_norm_rope.comp:29-67 for head_dim 128 and rope_dim 0 or 128: one CTA per
+// (row, 4 heads), one warp per head, lane l holding dims 4l..4l+3.  The rope
+// partner of dim d (d +/- 64) sits in lane l ^ 16, fetched with a shuffle, so
+// the head is read once into registers and out may alias x.  The row's 64
+// (cos, sin) pairs are computed once per CTA (the same sincosf of the same
+// argument as the per-element form) instead of once per element.
+__global__ void qk_norm_rope128_kernel(const float *x, const float *__restrict__ w, const float *__restrict__ freq,
+                                       float *y, int n_heads, int rope, float eps, uint32_t pos0) {
+    __shared__ float2 cs[64];
+    const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.y * 4 + warp;
+    const uint32_t pos = pos0 + row;
+    if (rope && threadIdx.x < 64) {
+        float sf, cf;
+        sincosf(freq[threadIdx.x] * (float)pos, &sf, &cf);
+        cs[threadIdx.x] = make_float2(cf, sf);
+    }
+    __syncthreads();
+    if (h >= n_heads) return;
+    const size_t base = ((size_t)row * n_heads + h) * 128 + 4 * lane;
+    const float4 v = *reinterpret_cast<const float4 *>(x + base);
+    const float sq = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    const float r = rsqrtf(warp_sum(sq) / 128.f + eps);
+    const float4 wv = *reinterpret_cast<const float4 *>(w + 4 * lane);
+    const float nv[4] = {v.x * wv.x * r, v.y * wv.y * r, v.z * wv.z * r, v.w * wv.w * r};
+    float o[4];
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const float pn = __shfl_xor_sync(0xffffffffu, nv[c], 16);  // dim +/- 64
+        if (!rope) {
+            o[c] = nv[c];
+        } else {
+            const float2 t = cs[4 * (lane & 15) + c];
+            o[c] = lane < 16 ? nv[c] * t.x - pn * t.y : nv[c] * t.x + pn * t.y;
+        }
+    }
+    *reinterpret_cast<float4 *>(y + base) = make_float4(o[0], o[1], o[2], o[3]);
+}
+
 // qk_norm_rope.comp:29-67 for one row (n_heads*head_dim) per CTA at position
 // pos0 + row.  The row is staged in shared memory first so out may alias x.
 __global__ void qk_norm_rope_kernel(const float *x, const float *__restrict__ w, const float *__restrict__ freq,
@@ -262,7 +329,11 @@ extern "C" int lc_rmsnorm(lc_ctx *ctx, const float *w, const float *x, float *ou
     LC_BEGIN(ctx, "lc_rmsnorm");
     if (m == 0 || n == 0) return LC_OK;
     LC_REQUIRE(w && x && out, LC_ERR_INVALID, "lc_rmsnorm: null pointer");
-    rmsnorm_kernel<<<m, n >= 4096 ? 1024 : 256, 0, ctx->stream>>>(w, x, out, (int)n, eps);
+    const int bd = n > 4096 ? 1024 : 256;
+    if (n % 4 == 0 && n <= 16u * bd && (((uintptr_t)w | (uintptr_t)x | (uintptr_t)out) & 15) == 0)
+        rmsnorm4_kernel<<<m, bd, 0, ctx->stream>>>(w, x, out, (int)n, eps);
+    else
+        rmsnorm_kernel<<<m, n >= 4096 ? 1024 : 256, 0, ctx->stream>>>(w, x, out, (int)n, eps);
     return lc_after_launch(ctx, "lc_rmsnorm");
 }
 
@@ -280,6 +351,11 @@ extern "C" int lc_qk_norm_rope(lc_ctx *ctx, const float *x, const float *w, cons
     // frequency table past its end.  Only the well-defined forms are accepted.
     LC_REQUIRE(rope_dim == 0 || rope_dim == head_dim, LC_ERR_UNSUPPORTED,
                "lc_qk_norm_rope: rope_dim %u must be 0 or head_dim %u", rope_dim, head_dim);
+    if (head_dim == 128 && (((uintptr_t)x | (uintptr_t)w | (uintptr_t)out) & 15) == 0) {
+        qk_norm_rope128_kernel<<<dim3(m, (n_heads + 3) / 4), 128, 0, ctx->stream>>>(x, w, freq, out, (int)n_heads,
+                                                                                    rope_dim ? 1 : 0, eps, pos0);
+        return lc_after_launch(ctx, "lc_qk_norm_rope");
+    }
     const size_t smem = ((size_t)n_heads * head_dim + n_heads) * 4;
     LC_REQUIRE(smem <= ctx->smem_optin, LC_ERR_UNSUPPORTED, "lc_qk_norm_rope: row of %u values too large",
                n_heads * head_dim);
