@@ -340,6 +340,7 @@ __host__ __device__ __forceinline__ uint32_t core16_off(int row, int kk) {
 __global__ void x16_pack_kernel(const float *__restrict__ x, int m, int k, int q8, int nt, __half *__restrict__ x16,
                                 uint8_t *__restrict__ sx16, float *__restrict__ inv, float *__restrict__ y,
                                 long long ny) {
+    griddep_launch_dependents();  // the GEMM may start streaming its weights now
     const long long nthreads = (long long)gridDim.x * gridDim.y * blockDim.x;
     for (long long i = ((long long)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x; i < ny;
          i += nthreads)
@@ -485,6 +486,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
                 if (!mbar_wait(raw_empty + rs, ((j / L.RS) & 1) ^ 1)) { fail(); break; }
                 mbar_expect_tx(raw_full + rs, kRawStage);
                 tma_load_2d(raw_ring + (size_t)rs * kRawStage, &tmw, sb * F::kBoxX, tile * kRows, raw_full + rs, pol);
+                if (j == 0) griddep_wait();  // activations come from the packing kernel
                 const int xs = j % L.XS;
                 if (!mbar_wait(x_empty + xs, ((j / L.XS) & 1) ^ 1)) { fail(); break; }
                 uint8_t *xst = x_ring + (size_t)xs * L.xstage;
@@ -590,6 +592,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
             if (!mbar_wait(drain, 0)) atomicOr(status, LC_DEV_WAIT_TIMEOUT);
         }
     } else {  // epilogue: TMEM lanes 32q..32q+31 = tile rows
+        griddep_wait();  // scales and the zeroed y come from the packing kernel
         const int q = warp & 3;
         const uint32_t lanes = (uint32_t)(32 * q) << 16;
         float acc[NT];
@@ -1422,8 +1425,20 @@ int launch_dq_gemm(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint
     if (s) return s;
     const long long TS = (long long)((n + kRows - 1) / kRows) * S;
     const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, TS));
-    dq_gemm_kernel<F, NT><<<grid, kGemmWarps * 32, L.total, ctx->stream>>>(tmw, tmx, sx16, inv, y, (int)m, (int)k,
-                                                                           (int)n, ctx->half_mode, ctx->dev_status);
+    // a programmatic dependent of the packing kernel: weights stream while the
+    // activations are packed
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemmWarps * 32);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    LC_CUDA(cudaLaunchKernelEx(&cfg, dq_gemm_kernel<F, NT>, tmw, tmx, (const uint8_t *)sx16, (const float *)inv, y,
+                               (int)m, (int)k, (int)n, ctx->half_mode, ctx->dev_status));
     return LC_OK;
 }
 
