@@ -657,32 +657,42 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
     }
 }
 
-// ---- the int8 GEMV: 1..4 tokens ----------------------------------------------
+// ---- the int8 GEMV: 3..16 tokens ---------------------------------------------
 //
-// kernels/proj_q4k.comp:60-92 and proj_q8_0.comp:47-67 for up to 4 rows of x on
+// kernels/proj_q4k.comp:60-92 and proj_q8_0.comp:47-67 for up to 16 rows of x on
 // the tensor cores' 8-bit path (tcgen05.mma kind::i8, K = 32): one MMA covers
 // exactly one 32-element Q4_K sub-block / Q8_0 block of 128 weight rows, so the
 // weights go to TMEM as their raw integers (Q4_K nibbles as u8, Q8_0 bytes as s8;
 // a mask and a shift per 8 weights) and each block's scale is applied by the
 // epilogue to that block's own accumulator columns.  The activations are
 // X = round(x * s) (|X| <= 16256, s per (token, super-block)) in two s8 digits,
-// X = 128 hi + lo, hi in B row t and lo in B row 8 + t (N = 16); the sums are
-// exact integers until the epilogue's f32 scaling.  Q4_K's min term uses the
-// integer sub-block sums of X.
+// X = 128 hi + lo, hi in B row t and lo in B row NR/2 + t (N = NR = 16 for up
+// to 8 tokens, 32 for up to 16); the sums are exact integers until the
+// epilogue's f32 scaling.  Q4_K's min term uses the integer sub-block sums of X.
+// Accumulators are per half unit (4 blocks x NR columns); TMEM holds
+// 512 / NR... : NR = 16: four A unit slots + four half-unit buffers, NR = 32:
+// two A slots + three half-unit buffers.
 
-constexpr int kG8Rows = 16;          // B rows (N): hi digits 0..7, lo digits 8..15
-constexpr int kG8XStage = kG8Rows * 256;  // one unit's digits, 4 KB
 constexpr int kG8ACols = 64;          // one unit of 8-bit weights: 256 per lane
-constexpr int kG8ASlots = 4;
-constexpr int kG8DCols = 128;         // 8 blocks x 16 columns
-constexpr int kG8ND = 2;
+constexpr int kG8NU = 2;              // per-unit scale slots
 
-// Activation digits, one CTA per super-block, warp t = token slot t (0..7):
-//   x8 [16][k] s8: row t the hi digit, row 8 + t the lo digit (zero past m);
-//   inv[sb * 8 + t] = 1 / s; sx[(sb * 8 + j) * 8 + t] = the integer sum of X over
+template <int NR>
+struct G8Cfg {
+    static constexpr int kXStage = NR * 256;                   // one unit's digits
+    static constexpr int kASlots = NR == 16 ? 4 : 2;
+    static constexpr int kHCols = 4 * NR;                      // one half-unit buffer
+    static constexpr int kNH = (kTmemCols - kASlots * kG8ACols) / kHCols;  // half-unit buffers
+    static constexpr int kDBase = kASlots * kG8ACols;
+};
+
+// Activation digits, one CTA per super-block, warp t = token slot t (0..T-1,
+// T = blockDim / 32 = NR / 2):
+//   x8 [NR][k] s8: row t the hi digit, row T + t the lo digit (zero past m);
+//   inv[sb * T + t] = 1 / s; sx[(sb * 8 + j) * T + t] = the integer sum of X over
 //   sub-block j (Q4_K).  The CTAs also zero y [m, n].
 __global__ void x8_pack_kernel(const float *__restrict__ x, int m, int k, int8_t *__restrict__ x8,
                                float *__restrict__ inv, int *__restrict__ sx, float *__restrict__ y, long long ny) {
+    const int T = blockDim.x >> 5;
     griddep_launch_dependents();  // the GEMV may start streaming its weights now
     const long long nthreads = (long long)gridDim.x * blockDim.x;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < ny; i += nthreads) y[i] = 0.f;
@@ -710,11 +720,11 @@ __global__ void x8_pack_kernel(const float *__restrict__ x, int m, int k, int8_t
         lw[i >> 2] |= (uint32_t)(lo & 0xFF) << (8 * (i & 3));
     }
     *reinterpret_cast<uint2 *>(x8 + (size_t)t * k + (size_t)sb * 256 + 8 * c) = make_uint2(hw[0], hw[1]);
-    *reinterpret_cast<uint2 *>(x8 + (size_t)(8 + t) * k + (size_t)sb * 256 + 8 * c) = make_uint2(lw[0], lw[1]);
-    if (c == 0) inv[sb * 8 + t] = s > 0.f ? 1.f / s : 0.f;
+    *reinterpret_cast<uint2 *>(x8 + (size_t)(T + t) * k + (size_t)sb * 256 + 8 * c) = make_uint2(lw[0], lw[1]);
+    if (c == 0) inv[sb * T + t] = s > 0.f ? 1.f / s : 0.f;
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    if (sx && (c & 3) == 0) sx[(sb * 8 + (c >> 2)) * 8 + t] = sum;
+    if (sx && (c & 3) == 0) sx[(sb * 8 + (c >> 2)) * T + t] = sum;
 }
 
 struct G8Layout {
@@ -722,16 +732,17 @@ struct G8Layout {
     int XS = 0, RS = 0;
 };
 
-template <class F>
+template <class F, int NR>
 __host__ __device__ constexpr G8Layout g8_layout() {
+    using C = G8Cfg<NR>;
     G8Layout L{};
-    L.XS = 8;
-    L.RS = F::kQ8 ? 5 : 9;
+    L.XS = NR == 16 ? 8 : 6;
+    L.RS = F::kQ8 ? (NR == 16 ? 5 : 4) : (NR == 16 ? 9 : 8);
     L.x = 0;
-    L.raw = (size_t)L.XS * kG8XStage;
+    L.raw = (size_t)L.XS * C::kXStage;
     L.sc = L.raw + (size_t)L.RS * kRows * F::kRowBytes;
-    L.bars = L.sc + (size_t)kG8ND * kRows * 64;
-    L.tslot = L.bars + (size_t)(2 * L.RS + 2 * kG8ASlots + 2 * L.XS + 3 * kG8ND + 1) * 8;
+    L.bars = L.sc + (size_t)kG8NU * kRows * 64;
+    L.tslot = L.bars + (size_t)(2 * L.RS + 2 * C::kASlots + 2 * L.XS + 2 * C::kNH + 2 * kG8NU + 1) * 8;
     L.total = L.tslot + 16 + 1024;
     return L;
 }
@@ -750,10 +761,16 @@ __device__ __forceinline__ void umma_i8_ts(uint32_t dtmem, uint32_t atmem, uint6
         : "memory");
 }
 
-// N consecutive 32-bit TMEM columns of this thread's lane (s32), N = 4 or 8.
+// N consecutive 32-bit TMEM columns of this thread's lane (s32), N = 4, 8 or 16.
 template <int N>
 __device__ __forceinline__ void tmem_ld_s32(uint32_t taddr, int (&v)[N]) {
-    if constexpr (N == 4)
+    if constexpr (N == 16)
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+            : "r"(taddr));
+    else if constexpr (N == 4)
         asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\n"
                      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
                      : "r"(taddr));
@@ -834,30 +851,33 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
     gemv_i8_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
                    const float *__restrict__ inv, const int *__restrict__ sx, float *__restrict__ y, int m, int k,
                    int n, int half_mode, unsigned *__restrict__ status) {
+    constexpr int NR = MT <= 8 ? 16 : 32, T = NR / 2;  // B rows, token slots
+    using C = G8Cfg<NR>;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-    constexpr G8Layout L = g8_layout<F>();
+    constexpr G8Layout L = g8_layout<F, NR>();
     constexpr bool Q4 = !F::kQ8;
     constexpr int kRawStage = kRows * F::kRowBytes;
     uint8_t *x_ring = smem + L.x, *raw_ring = smem + L.raw;
-    float *dslot = reinterpret_cast<float *>(smem + L.sc);  // [ND][128 rows][16]: 8 block scales (+ 8 mins)
+    float *dslot = reinterpret_cast<float *>(smem + L.sc);  // [NU][128 rows][16]: 8 block scales (+ 8 mins)
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *raw_full = bars, *raw_empty = raw_full + L.RS;
-    uint64_t *a_full = raw_empty + L.RS, *a_empty = a_full + kG8ASlots;
-    uint64_t *x_full = a_empty + kG8ASlots, *x_empty = x_full + L.XS;
-    uint64_t *d_full = x_empty + L.XS, *d_empty = d_full + kG8ND, *s_full = d_empty + kG8ND, *drain = s_full + kG8ND;
+    uint64_t *a_full = raw_empty + L.RS, *a_empty = a_full + C::kASlots;
+    uint64_t *x_full = a_empty + C::kASlots, *x_empty = x_full + L.XS;
+    uint64_t *d_full = x_empty + L.XS, *d_empty = d_full + C::kNH;  // half-unit accumulator buffers
+    uint64_t *s_full = d_empty + C::kNH, *s_empty = s_full + kG8NU, *drain = s_empty + kG8NU;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + L.tslot);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int S = k >> 8, T = (n + kRows - 1) / kRows;
-    const long long TS = (long long)T * S;
+    const int S = k >> 8, Tt = (n + kRows - 1) / kRows;
+    const long long TS = (long long)Tt * S;
     const int U0 = (int)(TS * blockIdx.x / gridDim.x), U1 = (int)(TS * (blockIdx.x + 1) / gridDim.x);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < L.RS; i++) mbar_init(raw_full + i, 1), mbar_init(raw_empty + i, kConvWarps);
-        for (int i = 0; i < kG8ASlots; i++) mbar_init(a_full + i, kConvWarps), mbar_init(a_empty + i, 1);
+        for (int i = 0; i < C::kASlots; i++) mbar_init(a_full + i, kConvWarps), mbar_init(a_empty + i, 1);
         for (int i = 0; i < L.XS; i++) mbar_init(x_full + i, 1), mbar_init(x_empty + i, 1);
-        for (int i = 0; i < kG8ND; i++)
-            mbar_init(d_full + i, 1), mbar_init(d_empty + i, 4), mbar_init(s_full + i, kConvWarps);
+        for (int i = 0; i < C::kNH; i++) mbar_init(d_full + i, 1), mbar_init(d_empty + i, 4);
+        for (int i = 0; i < kG8NU; i++) mbar_init(s_full + i, kConvWarps), mbar_init(s_empty + i, 4);
         mbar_init(drain, kMmaWarps);
         mbar_init_fence();
     }
@@ -890,10 +910,10 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
                 tma_load_2d(raw_ring + (size_t)rs * kRawStage, &tmw, sb * F::kBoxX, tile * kRows, raw_full + rs, pol);
                 if (j == 0) griddep_wait();  // the digits come from the packing kernel
                 if (!mbar_wait(x_empty + xs, ((j / L.XS) & 1) ^ 1)) { fail(); break; }
-                mbar_expect_tx(x_full + xs, kG8XStage);
+                mbar_expect_tx(x_full + xs, C::kXStage);
 #pragma unroll
                 for (int c = 0; c < 2; c++)
-                    tma_load_2d(x_ring + (size_t)xs * kG8XStage + c * (kG8Rows * 128), &tmx, sb * 256 + c * 128, 0,
+                    tma_load_2d(x_ring + (size_t)xs * C::kXStage + c * (NR * 128), &tmx, sb * 256 + c * 128, 0,
                                 x_full + xs, xpol);
             }
         }
@@ -902,8 +922,8 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
         const uint32_t tlane = tbase + ((uint32_t)(32 * quad) << 16);
         const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
         for (int u = U0; u < U1 && ok; u++) {
-            const int j = u - U0, rs = j % L.RS, as = j % kG8ASlots, db = j % kG8ND;
-            if (!mbar_wait(raw_full + rs, (j / L.RS) & 1) || !mbar_wait(a_empty + as, ((j / kG8ASlots) & 1) ^ 1)) {
+            const int j = u - U0, rs = j % L.RS, as = j % C::kASlots, su = j % kG8NU;
+            if (!mbar_wait(raw_full + rs, (j / L.RS) & 1) || !mbar_wait(a_empty + as, ((j / C::kASlots) & 1) ^ 1)) {
                 fail();
                 break;
             }
@@ -916,8 +936,8 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
             else
                 g8_convert<F, 1>(raw, ta, ref_mask, scl, mns);
             // the unit's block scales for the epilogue, once its slot is free
-            if (!mbar_wait(d_empty + db, ((j / kG8ND) & 1) ^ 1)) { fail(); break; }
-            float4 *ds = reinterpret_cast<float4 *>(dslot + ((size_t)db * kRows + r) * 16);
+            if (!mbar_wait(s_empty + su, ((j / kG8NU) & 1) ^ 1)) { fail(); break; }
+            float4 *ds = reinterpret_cast<float4 *>(dslot + ((size_t)su * kRows + r) * 16);
             ds[g] = make_float4(scl[0], scl[1], scl[2], scl[3]);
             if (Q4) ds[2 + g] = make_float4(mns[0], mns[1], mns[2], mns[3]);
             tmem_st_wait();
@@ -926,31 +946,37 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
             if (lane == 0) {
                 mbar_arrive(a_full + as);
                 mbar_arrive(raw_empty + rs);
-                mbar_arrive(s_full + db);
+                mbar_arrive(s_full + su);
             }
         }
     } else if (warp < kMmaWarp + kMmaWarps) {
         if (lane == 0) {  // MMA issuers: even / odd units, one MMA per 32-element block
-            constexpr uint32_t idesc = umma_idesc_i8(kRows, kG8Rows, F::kQ8);
+            constexpr uint32_t idesc = umma_idesc_i8(kRows, NR, F::kQ8);
             const uint64_t xdesc0 = umma_desc_sw128(smem_addr(x_ring));
             for (int u = U0 + (warp - kMmaWarp); u < U1 && ok; u += kMmaWarps) {
-                const int j = u - U0, db = j % kG8ND, as = j % kG8ASlots, xs = j % L.XS;
-                if (!mbar_wait(d_empty + db, ((j / kG8ND) & 1) ^ 1) || !mbar_wait(a_full + as, (j / kG8ASlots) & 1) ||
-                    !mbar_wait(x_full + xs, (j / L.XS) & 1)) {
+                const int j = u - U0, as = j % C::kASlots, xs = j % L.XS;
+                if (!mbar_wait(a_full + as, (j / C::kASlots) & 1) || !mbar_wait(x_full + xs, (j / L.XS) & 1)) {
                     fail();
                     break;
                 }
-                tc_fence_after();
-                const uint32_t dcol = tbase + kAccBase + db * kG8DCols;
-                const uint64_t xd = xdesc0 + (uint64_t)((xs * kG8XStage) >> 4);
+                const uint64_t xd = xdesc0 + (uint64_t)((xs * C::kXStage) >> 4);
                 const uint32_t ta = tbase + as * kG8ACols;
+                for (int h = 0; h < 2 && ok; h++) {  // half-unit buffer hj = 2j + h
+                    const int hj = 2 * j + h, hb = hj % C::kNH;
+                    if (!mbar_wait(d_empty + hb, ((hj / C::kNH) & 1) ^ 1)) { fail(); break; }
+                    tc_fence_after();
+                    const uint32_t dcol = tbase + C::kDBase + hb * C::kHCols;
 #pragma unroll
-                for (int b = 0; b < 8; b++)  // block b: K bytes 32b of the unit
-                    umma_i8_ts(dcol + 16 * b, ta + 8 * b,
-                               xd + (uint64_t)(((b >> 2) * (kG8Rows * 128) + (b & 3) * 32) >> 4), idesc);
+                    for (int bb = 0; bb < 4; bb++) {  // block b = 4h + bb: K bytes 32b of the unit
+                        const int b = 4 * h + bb;
+                        umma_i8_ts(dcol + NR * bb, ta + 8 * b,
+                                   xd + (uint64_t)(((b >> 2) * (NR * 128) + (b & 3) * 32) >> 4), idesc);
+                    }
+                    umma_commit(d_full + hb);
+                }
+                if (!ok) break;
                 umma_commit(a_empty + as);
                 umma_commit(x_empty + xs);
-                umma_commit(d_full + db);
             }
             umma_commit(drain);
             if (!mbar_wait(drain, 0)) atomicOr(status, LC_DEV_WAIT_TIMEOUT);
@@ -959,58 +985,55 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
         griddep_wait();  // scales, sums and the zeroed y come from the packing kernel
         const int q = warp & 3;
         const uint32_t lanes = (uint32_t)(32 * q) << 16;
+        constexpr int NL = MT <= 4 ? 4 : MT <= 8 ? 8 : 16;  // columns read per digit
         float acc[MT];
 #pragma unroll
         for (int t = 0; t < MT; t++) acc[t] = 0.f;
         for (int u = U0; u < U1 && ok; u++) {
-            const int j = u - U0, db = j % kG8ND, tile = u / S, sb = u - tile * S;
-            const uint32_t par = (j / kG8ND) & 1;
-            // the unit's activation scales and (Q4_K) integer sub-block sums, loaded
-            // before the wait so their latency overlaps it
-            float iv[MT], sxf[8][MT];
+            const int j = u - U0, su = j % kG8NU, tile = u / S, sb = u - tile * S;
+            float iv[MT];
 #pragma unroll
-            for (int t = 0; t < MT; t++) iv[t] = __ldg(inv + sb * 8 + t);
-            if constexpr (Q4) {
-#pragma unroll
-                for (int jb = 0; jb < 8; jb++)
-#pragma unroll
-                    for (int t = 0; t < MT; t++) sxf[jb][t] = (float)__ldg(sx + (sb * 8 + jb) * 8 + t);
-            }
-            if (!mbar_wait(d_full + db, par) || !mbar_wait(s_full + db, par)) { fail(); break; }
-            tc_fence_after();
-            const uint32_t col = tbase + lanes + kAccBase + db * kG8DCols;
-            const float4 *ds = reinterpret_cast<const float4 *>(dslot + ((size_t)db * kRows + 32 * q + lane) * 16);
+            for (int t = 0; t < MT; t++) iv[t] = __ldg(inv + sb * T + t);
+            if (!mbar_wait(s_full + su, (j / kG8NU) & 1)) { fail(); break; }
+            const float4 *ds = reinterpret_cast<const float4 *>(dslot + ((size_t)su * kRows + 32 * q + lane) * 16);
             const float4 s0 = ds[0], s1 = ds[1];
             const float scl[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            float mns[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if constexpr (Q4) {
+                const float4 m0 = ds[2], m1 = ds[3];
+                mns[0] = m0.x, mns[1] = m0.y, mns[2] = m0.z, mns[3] = m0.w;
+                mns[4] = m1.x, mns[5] = m1.y, mns[6] = m1.z, mns[7] = m1.w;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_empty + su);
             float au[MT];
 #pragma unroll
             for (int t = 0; t < MT; t++) au[t] = 0.f;
+            for (int h = 0; h < 2 && ok; h++) {
+                const int hj = 2 * j + h, hb = hj % C::kNH;
+                if (!mbar_wait(d_full + hb, (hj / C::kNH) & 1)) { fail(); break; }
+                tc_fence_after();
+                const uint32_t col = tbase + lanes + C::kDBase + hb * C::kHCols;
 #pragma unroll
-            for (int b = 0; b < 8; b += 2) {
-                constexpr int NL = MT <= 4 ? 4 : 8;  // columns read per digit
-                int h0[NL], l0[NL], h1[NL], l1[NL];
-                tmem_ld_s32<NL>(col + 16 * b, h0);
-                tmem_ld_s32<NL>(col + 16 * b + 8, l0);
-                tmem_ld_s32<NL>(col + 16 * (b + 1), h1);
-                tmem_ld_s32<NL>(col + 16 * (b + 1) + 8, l1);
-                tmem_ld_wait();
-                tmem_regs_ready_i(h0), tmem_regs_ready_i(l0), tmem_regs_ready_i(h1), tmem_regs_ready_i(l1);
+                for (int bb = 0; bb < 4; bb++) {
+                    int hi[NL], lo[NL];
+                    tmem_ld_s32<NL>(col + NR * bb, hi);
+                    tmem_ld_s32<NL>(col + NR * bb + T, lo);
+                    tmem_ld_wait();
+                    tmem_regs_ready_i(hi), tmem_regs_ready_i(lo);
 #pragma unroll
-                for (int t = 0; t < MT; t++) {
-                    au[t] += scl[b] * (float)(128 * h0[t] + l0[t]);
-                    au[t] += scl[b + 1] * (float)(128 * h1[t] + l1[t]);
+                    for (int t = 0; t < MT; t++) au[t] += scl[4 * h + bb] * (float)(128 * hi[t] + lo[t]);
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(d_empty + hb);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(d_empty + db);
+            if (!ok) break;
             if constexpr (Q4) {
-                const float4 m0 = ds[2], m1 = ds[3];
-                const float mns[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
 #pragma unroll
                 for (int jb = 0; jb < 8; jb++)
 #pragma unroll
-                    for (int t = 0; t < MT; t++) au[t] -= mns[jb] * sxf[jb][t];
+                    for (int t = 0; t < MT; t++) au[t] -= mns[jb] * (float)__ldg(sx + (sb * 8 + jb) * T + t);
             }
 #pragma unroll
             for (int t = 0; t < MT; t++) acc[t] += iv[t] * au[t];
@@ -1124,7 +1147,7 @@ __global__ void lmh_pack_kernel(const float *__restrict__ x, int m, int k, int q
     act_scale(red[0], s, iv);
     if (threadIdx.x == 0) {
         inv[t] = t < m ? iv : 0.f;
-        if (t < m) keys[t] = kKeyMin;
+        if (keys && t < m) keys[t] = kKeyMin;
     }
     __half *xr16 = x16 + (size_t)t * k;
     for (int q = threadIdx.x; q < k / 8; q += blockDim.x) {  // position chunk c of super-block sb
@@ -1338,6 +1361,7 @@ __global__ void __launch_bounds__(kLmWarps * 32, 1)
                     const int t = t0 + i;
                     const float v = ph[i] * iv[i];
                     if (logits && valid && t < m) logits[(size_t)t * n + row] = v;
+                    if (!keys) continue;  // a plain projection: y = logits, no argmax
                     const uint32_t b = __float_as_uint(v);
                     const uint32_t o = valid ? ((b & 0x80000000u) ? ~b : (b | 0x80000000u)) : 0u;
                     const uint32_t mo = __reduce_max_sync(0xffffffffu, o);
@@ -1345,7 +1369,7 @@ __global__ void __launch_bounds__(kLmWarps * 32, 1)
                     if (lane == i) my_o = mo, my_win = win;
                 }
                 const int t = t0 + lane;
-                if (lane < 16 && t < m && my_win) {
+                if (keys && lane < 16 && t < m && my_win) {
                     const uint32_t wrow = (uint32_t)(rt * kRows + 32 * q + 31 - __clz(my_win));
                     const unsigned long long key =
                         (((unsigned long long)my_o << 32) | (row_offset + wrow)) ^ kKeyMin;  // lc_make_key
@@ -1442,14 +1466,14 @@ int launch_dq_gemm(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint
     return LC_OK;
 }
 
-// s8 activation digits [16][k], boxes of 128 columns x 16 rows, 128-byte swizzle.
-int x8_map(CUtensorMap *tm, const void *x8, uint32_t k) {
+// s8 activation digits [nr][k], boxes of 128 columns x nr rows, 128-byte swizzle.
+int x8_map(CUtensorMap *tm, const void *x8, uint32_t k, int nr) {
     PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
     int s = lc_tensor_map_encoder(&enc);
     if (s) return s;
-    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)kG8Rows};
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)nr};
     cuuint64_t strides[1] = {(cuuint64_t)k};
-    cuuint32_t box[2] = {128, (cuuint32_t)kG8Rows};
+    cuuint32_t box[2] = {128, (cuuint32_t)nr};
     cuuint32_t es[2] = {1, 1};
     const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(x8), dims, strides, box, es,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1460,11 +1484,12 @@ int x8_map(CUtensorMap *tm, const void *x8, uint32_t k) {
 
 template <class F, int MT>
 int launch_gemv_i8(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
-    constexpr G8Layout L = g8_layout<F>();
+    constexpr int NR = MT <= 8 ? 16 : 32, T = NR / 2;
+    constexpr G8Layout L = g8_layout<F, NR>();
     LC_REQUIRE(L.total <= ctx->smem_optin, LC_ERR_UNSUPPORTED, "gemv_i8: %zu bytes of shared memory needed", L.total);
     const uint32_t S = k / 256;
-    const size_t x8_bytes = (size_t)kG8Rows * k, inv_bytes = (size_t)S * 8 * 4;
-    const size_t sx_bytes = F::kQ8 ? 0 : (size_t)S * 64 * 4;
+    const size_t x8_bytes = (size_t)NR * k, inv_bytes = (size_t)S * T * 4;
+    const size_t sx_bytes = F::kQ8 ? 0 : (size_t)S * 8 * T * 4;
     uint8_t *scr = (uint8_t *)lc_scratch(ctx, LC_SCRATCH_PACK, x8_bytes + inv_bytes + sx_bytes + 256);
     if (!scr) return LC_ERR_OOM;
     int8_t *x8 = reinterpret_cast<int8_t *>(scr);
@@ -1473,9 +1498,9 @@ int launch_gemv_i8(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint
     CUtensorMap tmw, tmx;
     int s = weight_map_rows128<F>(&tmw, w, k, n);
     if (s) return s;
-    s = x8_map(&tmx, x8, k);
+    s = x8_map(&tmx, x8, k, NR);
     if (s) return s;
-    x8_pack_kernel<<<S, 256, 0, ctx->stream>>>(x, (int)m, (int)k, x8, inv, sx, y, (long long)m * n);
+    x8_pack_kernel<<<S, 32 * T, 0, ctx->stream>>>(x, (int)m, (int)k, x8, inv, sx, y, (long long)m * n);
     s = lc_set_smem_attr((const void *)gemv_i8_kernel<F, MT>, L.total);
     if (s) return s;
     const long long TS = (long long)((n + kRows - 1) / kRows) * S;
@@ -1558,25 +1583,35 @@ int lm_head_tc(lc_ctx *ctx, int dtype, const float *x, const void *w, uint32_t m
     return LC_ERR_UNSUPPORTED;
 }
 
-// ctx->gemv_i8_min..8-token projections on the 8-bit tensor-core path (by
-// default 3: 1 and 2 tokens stream faster through the TMA GEMV of lc_proj.cu);
-// LC_ERR_UNSUPPORTED when the shape is not covered (the caller falls back).
+// ctx->gemv_i8_min..ctx->gemv_i8_max-token projections (at most 16) on the
+// 8-bit tensor-core path (by default 3..8: 1 and 2 tokens stream faster through
+// the TMA GEMV of lc_proj.cu); LC_ERR_UNSUPPORTED when the shape is not
+// covered (the caller falls back).
 int gemv_i8(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
-    if ((int)m < ctx->gemv_i8_min || m > 8 || k % 256 != 0 || ((uintptr_t)w & 15) != 0 || ((uintptr_t)x & 15) != 0 ||
-        (long long)k * 16 >= (1ll << 31))
+    if ((int)m < ctx->gemv_i8_min || (int)m > ctx->gemv_i8_max || m > 16 || k % 256 != 0 ||
+        ((uintptr_t)w & 15) != 0 || ((uintptr_t)x & 15) != 0 || (long long)k * 32 >= (1ll << 31))
         return LC_ERR_UNSUPPORTED;
     const uint8_t *wb = (const uint8_t *)w;
     if (dtype == LC_Q4_K)
         return m == 1   ? launch_gemv_i8<GQ4K, 1>(ctx, x, wb, y, m, k, n)
                : m == 2 ? launch_gemv_i8<GQ4K, 2>(ctx, x, wb, y, m, k, n)
                : m <= 4 ? launch_gemv_i8<GQ4K, 4>(ctx, x, wb, y, m, k, n)
-                        : launch_gemv_i8<GQ4K, 8>(ctx, x, wb, y, m, k, n);
+               : m <= 8 ? launch_gemv_i8<GQ4K, 8>(ctx, x, wb, y, m, k, n)
+                        : launch_gemv_i8<GQ4K, 16>(ctx, x, wb, y, m, k, n);
     if (dtype == LC_Q8_0)
         return m == 1   ? launch_gemv_i8<GQ8_0, 1>(ctx, x, wb, y, m, k, n)
                : m == 2 ? launch_gemv_i8<GQ8_0, 2>(ctx, x, wb, y, m, k, n)
                : m <= 4 ? launch_gemv_i8<GQ8_0, 4>(ctx, x, wb, y, m, k, n)
-                        : launch_gemv_i8<GQ8_0, 8>(ctx, x, wb, y, m, k, n);
+               : m <= 8 ? launch_gemv_i8<GQ8_0, 8>(ctx, x, wb, y, m, k, n)
+                        : launch_gemv_i8<GQ8_0, 16>(ctx, x, wb, y, m, k, n);
     return LC_ERR_UNSUPPORTED;
+}
+
+// Projections of more than 32 rows (the context prefill) through the lm_head
+// tiles with the argmax off: y [m, n] = x . W^T.  LC_ERR_UNSUPPORTED when the
+// shape is not covered.
+int gemm_large(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
+    return lm_head_tc(ctx, dtype, x, w, m, k, n, 0, nullptr, y);
 }
 
 }  // namespace lc

@@ -20,8 +20,10 @@ struct lc_ctx {
     // 1: 5..32-token Q4_K / Q8_0 projections run the tcgen05 GEMM (lc_gemm.cu);
     // 0: the mma.sync tiled kernels.  Set from LC_GEMM_TC at lc_init (default 1).
     int gemm_tc = 1;
-    // Smallest token count sent to the int8 tcgen05 GEMV (LC_GEMV_I8_MIN, default 3).
+    // Token counts sent to the int8 tcgen05 GEMV: gemv_i8_min..gemv_i8_max
+    // (LC_GEMV_I8_MIN, default 3; LC_GEMV_I8_MAX, default 8, at most 16).
     int gemv_i8_min = 3;
+    int gemv_i8_max = 8;
     // Grow-only scratch slots (see LC_SCRATCH_*).
     void *scratch[8] = {};
     size_t scratch_bytes[8] = {};
@@ -155,6 +157,9 @@ int gemm_dq(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uin
 // 1..4-token projections on tcgen05 kind::i8 (lc_gemm.cu); LC_ERR_UNSUPPORTED when
 // the shape is not covered.
 int gemv_i8(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n);
+// y = x . W^T for more than 32 rows on the lm_head tiles (lc_gemm.cu);
+// LC_ERR_UNSUPPORTED when the shape is not covered.
+int gemm_large(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n);
 // lm_head logits + argmax keys on tcgen05 (lc_gemm.cu); LC_ERR_UNSUPPORTED when
 // the shape is not covered.
 int lm_head_tc(lc_ctx *ctx, int dtype, const float *x, const void *w, uint32_t m, uint32_t k, uint32_t n,

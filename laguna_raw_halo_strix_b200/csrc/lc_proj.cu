@@ -1564,8 +1564,9 @@ int proj_q4k(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m, 
                expert_offset);
     LC_REQUIRE(((uintptr_t)wv & 15) == 0, LC_ERR_INVALID, "proj_q4k: weight pointer not 16-byte aligned");
     const uint8_t *w = (const uint8_t *)wv + (size_t)(expert_offset / 256) * 144;
-    // 1-2 tokens: the TMA GEMV; 3-8: the int8 tcgen05 GEMV; 9-32: the f16 tcgen05 GEMM
-    if (ctx->gemm_tc && (int)m >= ctx->gemv_i8_min && m <= 8) {
+    // 1-2 tokens: the TMA GEMV; 3-8: the int8 tcgen05 GEMV; 9-32: the f16 tcgen05
+    // GEMM; more: the lm_head tiles
+    if (ctx->gemm_tc && (int)m >= ctx->gemv_i8_min && (int)m <= ctx->gemv_i8_max) {
         const int s = gemv_i8(ctx, LC_Q4_K, x, w, c, m, k, n);
         if (s != LC_ERR_UNSUPPORTED) return s;
     }
@@ -1573,7 +1574,7 @@ int proj_q4k(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m, 
         const TmaPlan p = q4k_tma_plan(ctx, (int)m, (int)k, (int)n);
         if (p.R) return launch_q4k_tma(ctx, p, m, x, w, c, k, n);
     } else if (ctx->gemm_tc) {
-        const int s = gemm_dq(ctx, LC_Q4_K, x, w, c, m, k, n);
+        const int s = m <= 32 ? gemm_dq(ctx, LC_Q4_K, x, w, c, m, k, n) : gemm_large(ctx, LC_Q4_K, x, w, c, m, k, n);
         if (s != LC_ERR_UNSUPPORTED) return s;
     }
     return proj_q4k_tiled(ctx, x, w, c, m, k, n, nullptr);
@@ -1622,7 +1623,7 @@ int proj_q8_0(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m,
         return LC_OK;
     }
     const int nblk = k / 32;
-    if (ctx->gemm_tc && (int)m >= ctx->gemv_i8_min && m <= 8) {  // as proj_q4k
+    if (ctx->gemm_tc && (int)m >= ctx->gemv_i8_min && (int)m <= ctx->gemv_i8_max) {  // as proj_q4k
         const int s = gemv_i8(ctx, LC_Q8_0, x, w, c, m, k, n);
         if (s != LC_ERR_UNSUPPORTED) return s;
     }
@@ -1630,7 +1631,7 @@ int proj_q8_0(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m,
         const TmaPlan p = tma_plan<FmtQ8_0>(ctx, (int)m, (int)k, (int)n);
         if (p.R) return launch_tma<FmtQ8_0>(ctx, p, m, x, w, c, k, n);
     } else if (m > 4 && ctx->gemm_tc) {
-        const int s = gemm_dq(ctx, LC_Q8_0, x, w, c, m, k, n);
+        const int s = m <= 32 ? gemm_dq(ctx, LC_Q8_0, x, w, c, m, k, n) : gemm_large(ctx, LC_Q8_0, x, w, c, m, k, n);
         if (s != LC_ERR_UNSUPPORTED) return s;
     }
     if (m <= 4) {

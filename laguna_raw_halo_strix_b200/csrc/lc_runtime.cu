@@ -55,6 +55,7 @@ extern "C" int lc_init(int device, lc_ctx **out) {
     ctx->smem_optin = prop.sharedMemPerBlockOptin;
     if (const char *e = getenv("LC_GEMM_TC")) ctx->gemm_tc = e[0] != '0';
     if (const char *e = getenv("LC_GEMV_I8_MIN")) ctx->gemv_i8_min = atoi(e) < 1 ? 1 : atoi(e);
+    if (const char *e = getenv("LC_GEMV_I8_MAX")) ctx->gemv_i8_max = atoi(e) < 0 ? 0 : atoi(e) > 16 ? 16 : atoi(e);
     cudaError_t e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         delete ctx;

@@ -416,3 +416,48 @@ def test_activation_range(ctx, dev, oracle, dtype, m, scale):
     assert np.isfinite(c).all()
     for r in range(m):
         check_tol(c[r], ref[r], 1e-3, f"range m={m} scale={scale} row {r}")
+
+
+# ---- every projection route at every token count ------------------------------------
+
+def _ctx_with_env(env):
+    """A context created while the routing variables in `env` are set (they are
+    read once, at lc_init)."""
+    import os
+
+    import torch
+
+    old = {key: os.environ.get(key) for key in env}
+    os.environ.update(env)
+    try:
+        c = lc.Context(0)
+    finally:
+        for key, v in old.items():
+            if v is None:
+                os.environ.pop(key, None)
+            else:
+                os.environ[key] = v
+    c.set_stream(torch.cuda.current_stream())
+    return c
+
+
+@pytest.mark.parametrize("route", ["i8_all", "i8_none"])
+@pytest.mark.parametrize("dtype", [lc.Q4_K, lc.Q8_0])
+def test_proj_routes_all_m(dev, oracle, dtype, route):
+    # i8_all: 1..16 tokens on the int8 tcgen05 GEMV; i8_none: 1..4 on the TMA
+    # GEMV, 5..32 on the f16 tcgen05 GEMM, 33+ on the lm_head tiles.
+    env = {"LC_GEMV_I8_MIN": "1", "LC_GEMV_I8_MAX": "16"} if route == "i8_all" else {"LC_GEMV_I8_MAX": "0"}
+    c = _ctx_with_env(env)
+    try:
+        k, n = 2048, 300
+        rng = np.random.default_rng(11 + (dtype == lc.Q8_0))
+        w = synth.q4k_blocks(n, k, rng) if dtype == lc.Q4_K else synth.q8_0_blocks(n, k, rng)
+        x_all = synth.activations(40, k, rng)
+        ref_all = oracle.proj(dtype, x_all, w, k, n).reshape(40, n)
+        for m in (list(range(1, 17)) if route == "i8_all" else [1, 4, 5, 9, 16, 32, 33, 40]):
+            out = run_proj(c, dev, dtype, x_all[:m], w, m, k, n)
+            for r in range(m):
+                check_tol(out[r], ref_all[r], 1e-3, f"{route} m={m} row {r}")
+        c.device_status()
+    finally:
+        c.close()
