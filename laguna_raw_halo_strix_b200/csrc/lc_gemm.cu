@@ -327,6 +327,13 @@ __host__ __device__ __forceinline__ uint32_t core16_off(int row, int kk) {
     return (uint32_t)((row >> 3) * 256 + (kk >> 3) * 128 + (row & 7) * 16 + (kk & 7) * 2);
 }
 
+// Outputs the packing kernel zeroes for the GEMM's atomic adds.
+struct ZeroList {
+    float *p[lc::kGroupMax];
+    long long n[lc::kGroupMax];
+    int cnt;
+};
+
 // Activation packing, one warp per (token slot t, super-block sb), grid
 // (S, NT / 8) x 256 threads: lane c converts position chunk c.
 //   x16[t] / x16[NT + t]: hi / lo f16 of x * s, s = 2^e per (t, sb) putting
@@ -336,15 +343,21 @@ __host__ __device__ __forceinline__ uint32_t core16_off(int row, int kk) {
 //                         core-matrix layout: columns 0..7 the sub-block sums
 //                         of x * s / 32 (hi in row t, lo in row NT + t),
 //                         columns 8..15 zero.
-// The CTAs also zero y [m, n] for the GEMM's atomic adds.
-__global__ void x16_pack_kernel(const float *__restrict__ x, int m, int k, int q8, int nt, __half *__restrict__ x16,
-                                uint8_t *__restrict__ sx16, float *__restrict__ inv, float *__restrict__ y,
-                                long long ny) {
+// x is the projection input, or (OP) the SwiGLU product / the softplus head
+// gate of two inputs, formed here with the element-wise kernels' own functions.
+// The CTAs also zero the outputs in `zl`.
+template <int OP>
+__global__ void x16_pack_kernel(const float *__restrict__ x, const float *__restrict__ x2, int head_dim, int m, int k,
+                                int q8, int nt, __half *__restrict__ x16, uint8_t *__restrict__ sx16,
+                                float *__restrict__ inv, const __grid_constant__ ZeroList zl) {
     griddep_launch_dependents();  // the GEMM may start streaming its weights now
     const long long nthreads = (long long)gridDim.x * gridDim.y * blockDim.x;
-    for (long long i = ((long long)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x; i < ny;
-         i += nthreads)
-        y[i] = 0.f;
+    const long long tid0 = ((long long)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x;
+    const ZeroList *Z = &zl;
+    for (int z = 0; z < Z->cnt; z++) {
+        float *p = Z->p[z];
+        for (long long i = tid0; i < Z->n[z]; i += nthreads) p[i] = 0.f;
+    }
     const int sb = blockIdx.x, t = blockIdx.y * 8 + (threadIdx.x >> 5), c = threadIdx.x & 31;
     int e0, e1;
     if (q8) {
@@ -359,6 +372,19 @@ __global__ void x16_pack_kernel(const float *__restrict__ x, int m, int k, int q
         const float *xr = x + (size_t)t * k + (size_t)sb * 256;
         a = *reinterpret_cast<const float4 *>(xr + e0);
         b = *reinterpret_cast<const float4 *>(xr + e1);
+        if constexpr (OP == lc::LC_PACK_SWIGLU) {
+            const float *ur = x2 + (size_t)t * k + (size_t)sb * 256;
+            const float4 ua = *reinterpret_cast<const float4 *>(ur + e0), ub = *reinterpret_cast<const float4 *>(ur + e1);
+            a = make_float4(lc_swiglu(a.x, ua.x), lc_swiglu(a.y, ua.y), lc_swiglu(a.z, ua.z), lc_swiglu(a.w, ua.w));
+            b = make_float4(lc_swiglu(b.x, ub.x), lc_swiglu(b.y, ub.y), lc_swiglu(b.z, ub.z), lc_swiglu(b.w, ub.w));
+        } else if constexpr (OP == lc::LC_PACK_HEADGATE) {
+            // a 4-run lies inside one head (head_dim % 4 == 0)
+            const float *gr = x2 + (size_t)t * (k / head_dim);
+            const float ga = lc_softplus_f(gr[(sb * 256 + e0) / head_dim]);
+            const float gb = lc_softplus_f(gr[(sb * 256 + e1) / head_dim]);
+            a = make_float4(a.x * ga, a.y * ga, a.z * ga, a.w * ga);
+            b = make_float4(b.x * gb, b.y * gb, b.z * gb, b.w * gb);
+        }
     }
     float mx = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
                      fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
@@ -425,11 +451,30 @@ __host__ __device__ constexpr GemmLayout gemm_layout() {
     return L;
 }
 
+// Up to kGroupMax weight matrices sharing one activation block: matrix i owns
+// the global row tiles [tile_end[i - 1], tile_end[i]).
+struct DqGroup {
+    CUtensorMap tmw[lc::kGroupMax];
+    float *y[lc::kGroupMax];
+    int n[lc::kGroupMax];
+    int tile_end[lc::kGroupMax];
+    int ng;
+};
+
+// The matrix of global row tile `tile` and the tile's index inside it.
+__device__ __forceinline__ int group_of(const DqGroup *G, int tile, int &ltile) {
+    int gi = 0;
+    while (gi + 1 < G->ng && tile >= G->tile_end[gi]) gi++;
+    ltile = tile - (gi ? G->tile_end[gi - 1] : 0);
+    return gi;
+}
+
 template <class F, int NT>
 __global__ void __launch_bounds__(kGemmWarps * 32, 1)
-    dq_gemm_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
-                   const uint8_t *__restrict__ sx16, const float *__restrict__ inv, float *__restrict__ y, int m,
-                   int k, int n, int half_mode, unsigned *__restrict__ status) {
+    dq_gemm_kernel(const __grid_constant__ DqGroup grp, const __grid_constant__ CUtensorMap tmx,
+                   const uint8_t *__restrict__ sx16, const float *__restrict__ inv, int m, int k, int half_mode,
+                   unsigned *__restrict__ status) {
+    const DqGroup *G = &grp;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     constexpr GemmLayout L = gemm_layout<F, NT>();
@@ -447,7 +492,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
     uint64_t *d_full = x_empty + L.XS, *d_empty = d_full + ND, *s_full = d_empty + ND, *drain = s_full + ND;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + L.tslot);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int S = k >> 8, T = (n + kRows - 1) / kRows;
+    const int S = k >> 8, T = G->tile_end[G->ng - 1];
     const long long TS = (long long)T * S;
     const int U0 = (int)(TS * blockIdx.x / gridDim.x), U1 = (int)(TS * (blockIdx.x + 1) / gridDim.x);
 
@@ -483,9 +528,12 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
             for (int u = U0; u < U1 && ok; u++) {
                 const int j = u - U0, tile = u / S, sb = u - tile * S;
                 const int rs = j % L.RS;
+                int ltile;
+                const int gi = group_of(G, tile, ltile);
                 if (!mbar_wait(raw_empty + rs, ((j / L.RS) & 1) ^ 1)) { fail(); break; }
                 mbar_expect_tx(raw_full + rs, kRawStage);
-                tma_load_2d(raw_ring + (size_t)rs * kRawStage, &tmw, sb * F::kBoxX, tile * kRows, raw_full + rs, pol);
+                tma_load_2d(raw_ring + (size_t)rs * kRawStage, &G->tmw[gi], sb * F::kBoxX, ltile * kRows, raw_full + rs,
+                            pol);
                 if (j == 0) griddep_wait();  // activations come from the packing kernel
                 const int xs = j % L.XS;
                 if (!mbar_wait(x_empty + xs, ((j / L.XS) & 1) ^ 1)) { fail(); break; }
@@ -639,7 +687,10 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(d_empty + db);
             if (u == U1 - 1 || sb == S - 1) {  // end of this CTA's run over the tile
-                const int row = tile * kRows + 32 * q + lane;
+                int ltile;
+                const int gi = group_of(G, tile, ltile);
+                const int n = G->n[gi], row = ltile * kRows + 32 * q + lane;
+                float *y = G->y[gi];
                 if (row < n)
 #pragma unroll
                     for (int t = 0; t < NT; t++)
@@ -1426,7 +1477,7 @@ int x16_map(CUtensorMap *tm, const void *x16, uint32_t k, int rows, int box_rows
 }
 
 template <class F, int NT>
-int launch_dq_gemm(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
+int launch_dq_gemm(lc_ctx *ctx, const lc::PackSrc &src, const lc::ProjOut *outs, int ng, uint32_t m, uint32_t k) {
     constexpr GemmLayout L = gemm_layout<F, NT>();
     LC_REQUIRE(L.total <= ctx->smem_optin, LC_ERR_UNSUPPORTED, "dq_gemm: %zu bytes of shared memory needed", L.total);
     const uint32_t S = k / 256;
@@ -1438,16 +1489,39 @@ int launch_dq_gemm(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint
     __half *x16 = reinterpret_cast<__half *>(scr);
     uint8_t *sx16 = scr + x16_bytes;
     float *inv = reinterpret_cast<float *>(scr + x16_bytes + sx_bytes);
-    CUtensorMap tmw, tmx;
-    int s = weight_map_rows128<F>(&tmw, w, k, n);
+    DqGroup grp = {};
+    ZeroList zl = {};
+    int tiles = 0;
+    for (int i = 0; i < ng; i++) {
+        int s = weight_map_rows128<F>(&grp.tmw[i], outs[i].w, k, outs[i].n);
+        if (s) return s;
+        grp.y[i] = outs[i].y;
+        grp.n[i] = (int)outs[i].n;
+        tiles += (int)((outs[i].n + kRows - 1) / kRows);
+        grp.tile_end[i] = tiles;
+        if (!outs[i].accumulate) {
+            zl.p[zl.cnt] = outs[i].y;
+            zl.n[zl.cnt++] = (long long)m * outs[i].n;
+        }
+    }
+    grp.ng = ng;
+    CUtensorMap tmx;
+    int s = x16_map(&tmx, x16, k, 2 * NT, 2 * NT);
     if (s) return s;
-    s = x16_map(&tmx, x16, k, 2 * NT, 2 * NT);
-    if (s) return s;
-    x16_pack_kernel<<<dim3(S, NT / 8), 256, 0, ctx->stream>>>(x, (int)m, (int)k, F::kQ8 ? 1 : 0, NT, x16, sx16, inv,
-                                                                y, (long long)m * n);
+    const dim3 pgrid(S, NT / 8);
+    const int q8 = F::kQ8 ? 1 : 0;
+    if (src.op == lc::LC_PACK_SWIGLU)
+        x16_pack_kernel<lc::LC_PACK_SWIGLU><<<pgrid, 256, 0, ctx->stream>>>(src.x, src.x2, 0, (int)m, (int)k, q8, NT,
+                                                                           x16, sx16, inv, zl);
+    else if (src.op == lc::LC_PACK_HEADGATE)
+        x16_pack_kernel<lc::LC_PACK_HEADGATE><<<pgrid, 256, 0, ctx->stream>>>(src.x, src.x2, src.head_dim, (int)m,
+                                                                             (int)k, q8, NT, x16, sx16, inv, zl);
+    else
+        x16_pack_kernel<lc::LC_PACK_PLAIN><<<pgrid, 256, 0, ctx->stream>>>(src.x, nullptr, 0, (int)m, (int)k, q8, NT,
+                                                                          x16, sx16, inv, zl);
     s = lc_set_smem_attr((const void *)dq_gemm_kernel<F, NT>, L.total);
     if (s) return s;
-    const long long TS = (long long)((n + kRows - 1) / kRows) * S;
+    const long long TS = (long long)tiles * S;
     const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, TS));
     // a programmatic dependent of the packing kernel: weights stream while the
     // activations are packed
@@ -1461,8 +1535,8 @@ int launch_dq_gemm(lc_ctx *ctx, const float *x, const uint8_t *w, float *y, uint
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    LC_CUDA(cudaLaunchKernelEx(&cfg, dq_gemm_kernel<F, NT>, tmw, tmx, (const uint8_t *)sx16, (const float *)inv, y,
-                               (int)m, (int)k, (int)n, ctx->half_mode, ctx->dev_status));
+    LC_CUDA(cudaLaunchKernelEx(&cfg, dq_gemm_kernel<F, NT>, grp, tmx, (const uint8_t *)sx16, (const float *)inv, (int)m,
+                               (int)k, ctx->half_mode, ctx->dev_status));
     return LC_OK;
 }
 
@@ -1557,16 +1631,39 @@ namespace lc {
 // Quantized GEMM on tcgen05 for 5..32 tokens; LC_ERR_UNSUPPORTED when the
 // shape is not covered (the caller falls back).
 int gemm_dq(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n) {
-    if (m == 0 || m > 32 || k % 256 != 0 || ((uintptr_t)w & 15) != 0 || ((uintptr_t)x & 15) != 0 ||
+    PackSrc src;
+    src.x = x;
+    ProjOut out;
+    out.w = w;
+    out.y = y;
+    out.n = n;
+    return gemm_dq_group(ctx, dtype, src, &out, 1, m, k);
+}
+
+int gemm_dq_group(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *outs, int ng, uint32_t m, uint32_t k) {
+    if (m == 0 || m > 32 || ng < 1 || ng > kGroupMax || k % 256 != 0 || ((uintptr_t)src.x & 15) != 0 ||
         (long long)k * 32 >= (1ll << 31))
         return LC_ERR_UNSUPPORTED;
-    const uint8_t *wb = (const uint8_t *)w;
+    if (src.op == LC_PACK_SWIGLU && ((uintptr_t)src.x2 & 15) != 0) return LC_ERR_UNSUPPORTED;
+    if (src.op == LC_PACK_HEADGATE && (src.head_dim <= 0 || src.head_dim % 4 != 0 || k % src.head_dim != 0))
+        return LC_ERR_UNSUPPORTED;
+    long long tiles = 0;
+    for (int i = 0; i < ng; i++) {
+        if (((uintptr_t)outs[i].w & 15) != 0 || outs[i].n == 0) return LC_ERR_UNSUPPORTED;
+        tiles += (outs[i].n + kRows - 1) / kRows;
+    }
+    if (tiles * (k / 256) >= (1ll << 31)) return LC_ERR_UNSUPPORTED;
     if (dtype == LC_Q4_K)
-        return m <= 16 ? launch_dq_gemm<GQ4K, 16>(ctx, x, wb, y, m, k, n) : launch_dq_gemm<GQ4K, 32>(ctx, x, wb, y, m, k, n);
+        return m <= 16 ? launch_dq_gemm<GQ4K, 16>(ctx, src, outs, ng, m, k)
+                       : launch_dq_gemm<GQ4K, 32>(ctx, src, outs, ng, m, k);
     if (dtype == LC_Q8_0)
-        return m <= 16 ? launch_dq_gemm<GQ8_0, 16>(ctx, x, wb, y, m, k, n)
-                       : launch_dq_gemm<GQ8_0, 32>(ctx, x, wb, y, m, k, n);
+        return m <= 16 ? launch_dq_gemm<GQ8_0, 16>(ctx, src, outs, ng, m, k)
+                       : launch_dq_gemm<GQ8_0, 32>(ctx, src, outs, ng, m, k);
     return LC_ERR_UNSUPPORTED;
+}
+
+bool routes_to_gemm_dq(const lc_ctx *ctx, uint32_t m) {
+    return ctx->gemm_tc && m > 4 && m <= 32 && !((int)m >= ctx->gemv_i8_min && (int)m <= ctx->gemv_i8_max);
 }
 
 // lm_head logits + argmax on tcgen05 for a vocab shard (rows [0, n) of w,

@@ -144,6 +144,12 @@ __device__ __forceinline__ void lc_mma1688(float (&d)[4], uint32_t a0, uint32_t 
         : "r"(a0), "r"(a1), "r"(b0));
 }
 
+// Element-wise functions shared by the stand-alone kernels and the fused
+// activation packing: kernels/activation.comp (SiLU(g) * up) and the host
+// softplus of src/dflash.rs:956-958 (log(1 + e^v), identity above 20).
+__device__ __forceinline__ float lc_swiglu(float g, float up) { return g * (1.0f / (1.0f + expf(-g))) * up; }
+__device__ __forceinline__ float lc_softplus_f(float v) { return v > 20.0f ? v : logf(1.0f + expf(v)); }
+
 // Host-side launch helpers defined in the kernel files.
 namespace lc {
 int proj_q4k(lc_ctx *ctx, const float *x, const void *w, float *c, uint32_t m, uint32_t k, uint32_t n,
@@ -154,7 +160,36 @@ int proj_f32(lc_ctx *ctx, const float *x, const float *w, float *c, uint32_t m, 
 // tcgen05 GEMM for 5..32 tokens (lc_gemm.cu); LC_ERR_UNSUPPORTED when the
 // shape is not covered.
 int gemm_dq(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n);
-// 1..4-token projections on tcgen05 kind::i8 (lc_gemm.cu); LC_ERR_UNSUPPORTED when
+// Projections that read one activation block: up to kGroupMax weight matrices
+// of one dtype and one k in a single packing launch and a single tcgen05 GEMM
+// launch (lc_gemm.cu).  The packed activation is src.x, or a function of two
+// inputs applied while packing:
+//   LC_PACK_SWIGLU:   x * sigmoid(x) * x2                (activation.comp)
+//   LC_PACK_HEADGATE: x * softplus(x2[row * k / hd + col / hd])  (softplus, gate_mul.comp)
+// Each output is y = src . W^T, or y += src . W^T when `accumulate` (the residual
+// add of the decoder).  LC_ERR_UNSUPPORTED when the shape is not covered.
+enum { LC_PACK_PLAIN = 0, LC_PACK_SWIGLU = 1, LC_PACK_HEADGATE = 2 };
+constexpr int kGroupMax = 4;
+struct PackSrc {
+    const float *x = nullptr;
+    const float *x2 = nullptr;
+    int op = LC_PACK_PLAIN;
+    int head_dim = 0;
+};
+struct ProjOut {
+    const void *w = nullptr;
+    float *y = nullptr;
+    uint32_t n = 0;
+    bool accumulate = false;
+};
+int gemm_dq_group(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *outs, int ng, uint32_t m, uint32_t k);
+// lc_qk_norm_rope of the block's Q and K in one launch where possible (lc_ops.cu).
+int qk_norm_rope_pair(lc_ctx *ctx, const float *xa, const float *wa, float *ya, uint32_t n_heads_a, const float *xb,
+                      const float *wb, float *yb, uint32_t n_heads_b, const float *freq, uint32_t m,
+                      uint32_t head_dim, uint32_t rope_dim, float eps, uint32_t pos0);
+// True when a projection of m rows would run the tcgen05 GEMM (gemm_dq).
+bool routes_to_gemm_dq(const lc_ctx *ctx, uint32_t m);
+// 3..16-token projections on tcgen05 kind::i8 (lc_gemm.cu); LC_ERR_UNSUPPORTED when
 // the shape is not covered.
 int gemv_i8(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uint32_t m, uint32_t k, uint32_t n);
 // y = x . W^T for more than 32 rows on the lm_head tiles (lc_gemm.cu);

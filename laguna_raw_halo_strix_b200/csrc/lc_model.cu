@@ -123,6 +123,50 @@ static int proj(lc_dflash *m, const Weight &w, const char *what, const float *x,
     return lc_proj_m(m->ctx, w.dtype, x, w.ptr, y, rows, k, n, 0);
 }
 
+// Projections of one activation block (lc::gemm_dq_group): one packing and one
+// tcgen05 GEMM launch when every weight has the same quantized dtype and the
+// block size runs that GEMM.  Otherwise one projection per weight, with the
+// element-wise input op and the residual adds as their own launches, in the
+// reference's order; `materialized` (rows x k) receives the op's result there.
+static int proj_block(lc_dflash *m, const lc::PackSrc &src, float *materialized, lc::ProjOut *outs,
+                      const Weight *const *ws, const char *const *names, int ng, uint32_t rows, uint32_t k) {
+    lc_ctx *c = m->ctx;
+    bool grouped = lc::routes_to_gemm_dq(c, rows);
+    for (int i = 0; i < ng; i++) {
+        if (!ws[i]->ptr) return lc_fail(LC_ERR_INVALID, "lc_dflash: missing tensor %s", names[i]);
+        if (ws[i]->n_el < (uint64_t)k * outs[i].n)
+            return lc_fail(LC_ERR_INVALID, "lc_dflash: %s has %llu elements, need %u x %u", names[i],
+                           (unsigned long long)ws[i]->n_el, outs[i].n, k);
+        outs[i].w = ws[i]->ptr;
+        if (ws[i]->dtype != ws[0]->dtype) grouped = false;
+    }
+    const int dtype = ws[0]->dtype;
+    if (grouped && (dtype == LC_Q4_K || dtype == LC_Q8_0)) {
+        const int s = lc::gemm_dq_group(c, dtype, src, outs, ng, rows, k);
+        if (s != LC_ERR_UNSUPPORTED) return s;
+    }
+    const float *x = src.x;
+    if (src.op == lc::LC_PACK_SWIGLU) {
+        LC_TRY(lc_activation(c, src.x, src.x2, materialized, rows * k));
+        x = materialized;
+    } else if (src.op == lc::LC_PACK_HEADGATE) {
+        const uint32_t heads = k / (uint32_t)src.head_dim;
+        float *gate = const_cast<float *>(src.x2);  // the block's own gate buffer
+        LC_TRY(lc_softplus(c, gate, gate, rows * heads));
+        LC_TRY(lc_gate_mul(c, src.x, gate, materialized, rows * k, heads, (uint32_t)src.head_dim));
+        x = materialized;
+    }
+    for (int i = 0; i < ng; i++) {
+        if (!outs[i].accumulate) {
+            LC_TRY(proj(m, *ws[i], names[i], x, outs[i].y, rows, k, outs[i].n));
+        } else {
+            LC_TRY(proj(m, *ws[i], names[i], x, m->tmp, rows, k, outs[i].n));
+            LC_TRY(lc_add(c, outs[i].y, m->tmp, outs[i].y, rows * outs[i].n));
+        }
+    }
+    return LC_OK;
+}
+
 static const float *need(const Weight &w, const char *what, int *status) {
     if (!w.ptr || w.dtype != LC_F32) {
         *status = lc_fail(LC_ERR_INVALID, "lc_dflash: missing f32 tensor %s", what);
@@ -337,29 +381,54 @@ extern "C" int lc_dflash_decode_block(lc_dflash *m, const float *x_in, uint32_t 
         const float *fn = need(L.ffn_norm, "ffn_norm.weight", &s);
         if (s) return s;
         float *kblk = m->kl(l) + (size_t)pos0 * KVD, *vblk = m->vl(l) + (size_t)pos0 * KVD;
-        // src/dflash.rs:938-943
+        // src/dflash.rs:938-943 (+ the head-gate projection of :955, which reads
+        // the same normalised block): one activation block, four projections
         LC_TRY(lc_rmsnorm(c, an, m->x, m->nx, mt, E, h.norm_eps));
-        LC_TRY(proj(m, L.q, "attn_q.weight", m->nx, m->q, mt, E, QD));
-        LC_TRY(proj(m, L.k, "attn_k.weight", m->nx, kblk, mt, E, KVD));
-        LC_TRY(proj(m, L.v, "attn_v.weight", m->nx, vblk, mt, E, KVD));
-        LC_TRY(lc_qk_norm_rope(c, m->q, qn, m->freq, m->q, mt, h.n_heads, h.head_dim, h.rope_dim, h.qk_eps, pos0));
-        LC_TRY(lc_qk_norm_rope(c, kblk, kn, m->freq, kblk, mt, h.n_kv_heads, h.head_dim, h.rope_dim, h.qk_eps, pos0));
+        {
+            lc::PackSrc src;
+            src.x = m->nx;
+            lc::ProjOut outs[4] = {{nullptr, m->q, QD, false}, {nullptr, kblk, KVD, false},
+                                   {nullptr, vblk, KVD, false}, {nullptr, m->gate, h.n_heads, false}};
+            const Weight *ws[4] = {&L.q, &L.k, &L.v, &L.gate_attn};
+            const char *names[4] = {"attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_gate.weight"};
+            LC_TRY(proj_block(m, src, nullptr, outs, ws, names, 4, mt, E));
+        }
+        LC_TRY(lc::qk_norm_rope_pair(c, m->q, qn, m->q, h.n_heads, kblk, kn, kblk, h.n_kv_heads, m->freq, mt,
+                                     h.head_dim, h.rope_dim, h.qk_eps, pos0));
         // :945-954 -- K/V rows [context; block] are already adjacent in the cache
         LC_TRY(lc_mha_attn(c, m->q, m->kl(l), m->vl(l), m->attn, mt, h.n_heads, h.n_kv_heads, h.head_dim,
                            pos0 + mt, scale, pos0, 1));
-        // :955-959 -- softplus head gate on the device
-        LC_TRY(proj(m, L.gate_attn, "attn_gate.weight", m->nx, m->gate, mt, E, h.n_heads));
-        LC_TRY(lc_softplus(c, m->gate, m->gate, mt * h.n_heads));
-        LC_TRY(lc_gate_mul(c, m->attn, m->gate, m->attn, mt * QD, h.n_heads, h.head_dim));
-        // :961-969
-        LC_TRY(proj(m, L.o, "attn_output.weight", m->attn, m->tmp, mt, QD, E));
-        LC_TRY(lc_add(c, m->x, m->tmp, m->x, mt * E));
+        // :955-969 -- attn * softplus(head gate), output projection, residual add
+        {
+            lc::PackSrc src;
+            src.x = m->attn;
+            src.x2 = m->gate;
+            src.op = lc::LC_PACK_HEADGATE;
+            src.head_dim = (int)h.head_dim;
+            lc::ProjOut outs[1] = {{nullptr, m->x, E, true}};
+            const Weight *ws[1] = {&L.o};
+            const char *names[1] = {"attn_output.weight"};
+            LC_TRY(proj_block(m, src, m->attn, outs, ws, names, 1, mt, QD));
+        }
         LC_TRY(lc_rmsnorm(c, fn, m->x, m->nx, mt, E, h.norm_eps));
-        LC_TRY(proj(m, L.gate, "ffn_gate.weight", m->nx, m->ffg, mt, E, F));
-        LC_TRY(proj(m, L.up, "ffn_up.weight", m->nx, m->ffu, mt, E, F));
-        LC_TRY(lc_activation(c, m->ffg, m->ffu, m->ffh, mt * F));
-        LC_TRY(proj(m, L.down, "ffn_down.weight", m->ffh, m->tmp, mt, F, E));
-        LC_TRY(lc_add(c, m->x, m->tmp, m->x, mt * E));
+        {
+            lc::PackSrc src;
+            src.x = m->nx;
+            lc::ProjOut outs[2] = {{nullptr, m->ffg, F, false}, {nullptr, m->ffu, F, false}};
+            const Weight *ws[2] = {&L.gate, &L.up};
+            const char *names[2] = {"ffn_gate.weight", "ffn_up.weight"};
+            LC_TRY(proj_block(m, src, nullptr, outs, ws, names, 2, mt, E));
+        }
+        {
+            lc::PackSrc src;
+            src.x = m->ffg;
+            src.x2 = m->ffu;
+            src.op = lc::LC_PACK_SWIGLU;
+            lc::ProjOut outs[1] = {{nullptr, m->x, E, true}};
+            const Weight *ws[1] = {&L.down};
+            const char *names[1] = {"ffn_down.weight"};
+            LC_TRY(proj_block(m, src, m->ffh, outs, ws, names, 1, mt, F));
+        }
     }
     // :972-975
     int s = LC_OK;

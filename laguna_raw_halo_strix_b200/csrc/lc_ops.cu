@@ -79,12 +79,27 @@ __global__ void rmsnorm4_kernel(const float *__restrict__ w, const float *x, flo
 // partner of dim d (d +/- 64) sits in lane l ^ 16, fetched with a shuffle, so
 // the head is read once into registers and out may alias x.  The row's 64
 // (cos, sin) pairs are computed once per CTA (the same sincosf of the same
-// argument as the per-element form) instead of once per element.
-__global__ void qk_norm_rope128_kernel(const float *x, const float *__restrict__ w, const float *__restrict__ freq,
-                                       float *y, int n_heads, int rope, float eps, uint32_t pos0) {
+// argument as the per-element form) instead of once per element.  Two
+// tensors of the same rows (the block's Q and K) go in one launch: CTAs with
+// blockIdx.y < nb0 take set 0, the rest set 1.
+struct QkPair {
+    const float *x[2];
+    const float *w[2];
+    float *y[2];
+    int n_heads[2];
+    int nb0;
+};
+
+__global__ void qk_norm_rope128_kernel(const QkPair p, const float *__restrict__ freq, int rope, float eps,
+                                       uint32_t pos0) {
     __shared__ float2 cs[64];
     const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.y * 4 + warp;
+    const bool second = (int)blockIdx.y >= p.nb0;
+    const float *x = second ? p.x[1] : p.x[0];
+    const float *__restrict__ w = second ? p.w[1] : p.w[0];
+    float *y = second ? p.y[1] : p.y[0];
+    const int n_heads = second ? p.n_heads[1] : p.n_heads[0];
+    const int h = ((int)blockIdx.y - (second ? p.nb0 : 0)) * 4 + warp;
     const uint32_t pos = pos0 + row;
     if (rope && threadIdx.x < 64) {
         float sf, cf;
@@ -162,8 +177,7 @@ __global__ void qk_norm_rope_kernel(const float *x, const float *__restrict__ w,
 
 __global__ void activation_kernel(const float *gate, const float *up, float *h, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const float g = gate[i];
-        h[i] = g * (1.0f / (1.0f + expf(-g))) * up[i];
+        h[i] = lc_swiglu(gate[i], up[i]);
     }
 }
 
@@ -178,8 +192,7 @@ __global__ void gate_mul_kernel(const float *v, const float *gate, float *out, i
 
 __global__ void softplus_kernel(const float *g, float *out, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const float v = g[i];
-        out[i] = v > 20.0f ? v : logf(1.0f + expf(v));
+        out[i] = lc_softplus_f(g[i]);
     }
 }
 
@@ -352,8 +365,8 @@ extern "C" int lc_qk_norm_rope(lc_ctx *ctx, const float *x, const float *w, cons
     LC_REQUIRE(rope_dim == 0 || rope_dim == head_dim, LC_ERR_UNSUPPORTED,
                "lc_qk_norm_rope: rope_dim %u must be 0 or head_dim %u", rope_dim, head_dim);
     if (head_dim == 128 && (((uintptr_t)x | (uintptr_t)w | (uintptr_t)out) & 15) == 0) {
-        qk_norm_rope128_kernel<<<dim3(m, (n_heads + 3) / 4), 128, 0, ctx->stream>>>(x, w, freq, out, (int)n_heads,
-                                                                                    rope_dim ? 1 : 0, eps, pos0);
+        QkPair p = {{x, x}, {w, w}, {out, out}, {(int)n_heads, 0}, (int)(n_heads + 3) / 4};
+        qk_norm_rope128_kernel<<<dim3(m, p.nb0), 128, 0, ctx->stream>>>(p, freq, rope_dim ? 1 : 0, eps, pos0);
         return lc_after_launch(ctx, "lc_qk_norm_rope");
     }
     const size_t smem = ((size_t)n_heads * head_dim + n_heads) * 4;
@@ -365,6 +378,31 @@ extern "C" int lc_qk_norm_rope(lc_ctx *ctx, const float *x, const float *w, cons
                                                         eps, pos0);
     return lc_after_launch(ctx, "lc_qk_norm_rope");
 }
+
+namespace lc {
+// lc_qk_norm_rope of two tensors over the same m rows (the block's Q with
+// n_heads_a heads and K with n_heads_b), in one launch when both take the
+// head_dim 128 kernel.
+int qk_norm_rope_pair(lc_ctx *ctx, const float *xa, const float *wa, float *ya, uint32_t n_heads_a, const float *xb,
+                      const float *wb, float *yb, uint32_t n_heads_b, const float *freq, uint32_t m,
+                      uint32_t head_dim, uint32_t rope_dim, float eps, uint32_t pos0) {
+    const bool fused = m > 0 && n_heads_a > 0 && n_heads_b > 0 && head_dim == 128 &&
+                       (rope_dim == 0 || rope_dim == head_dim) && xa && wa && ya && xb && wb && yb &&
+                       (freq || rope_dim == 0) &&
+                       (((uintptr_t)xa | (uintptr_t)wa | (uintptr_t)ya | (uintptr_t)xb | (uintptr_t)wb |
+                         (uintptr_t)yb) & 15) == 0;
+    if (!fused) {
+        const int s = lc_qk_norm_rope(ctx, xa, wa, freq, ya, m, n_heads_a, head_dim, rope_dim, eps, pos0);
+        if (s) return s;
+        return lc_qk_norm_rope(ctx, xb, wb, freq, yb, m, n_heads_b, head_dim, rope_dim, eps, pos0);
+    }
+    LC_BEGIN(ctx, "lc_qk_norm_rope");
+    const int nb0 = (int)(n_heads_a + 3) / 4, nb1 = (int)(n_heads_b + 3) / 4;
+    QkPair p = {{xa, xb}, {wa, wb}, {ya, yb}, {(int)n_heads_a, (int)n_heads_b}, nb0};
+    qk_norm_rope128_kernel<<<dim3(m, nb0 + nb1), 128, 0, ctx->stream>>>(p, freq, rope_dim ? 1 : 0, eps, pos0);
+    return lc_after_launch(ctx, "lc_qk_norm_rope");
+}
+}  // namespace lc
 
 extern "C" int lc_activation(lc_ctx *ctx, const float *gate, const float *up, float *h, uint32_t n) {
     LC_BEGIN(ctx, "lc_activation");

@@ -139,3 +139,49 @@ def test_gguf_load_forward_token_and_cli(ctx, dev, tmp_path):
                         (["encode", path], "encode+decode complete"), (["draft", path, "6", "3"], "finite 1")):
         r = subprocess.run([cli] + cmd, capture_output=True, text=True, timeout=120)
         assert r.returncode == 0 and expect in r.stdout, (cmd, r.stdout, r.stderr)
+
+
+@pytest.mark.parametrize("dtype", [orc.Q4_K, orc.Q8_0])
+@pytest.mark.parametrize("env", [{"LC_GEMV_I8_MAX": "16"}, {"LC_GEMM_TC": "0"}])
+def test_block_decode_unfused_routes(dev, dtype, env):
+    # With the 9..16-token projections on the int8 GEMV (or every tcgen05 kernel
+    # off), the decoder runs one projection per weight with the element-wise
+    # ops and residual adds as separate launches: same results.
+    import torch
+
+    old = {key: os.environ.get(key) for key in env}
+    os.environ.update(env)
+    try:
+        c = lc.Context(0)
+    finally:
+        for key, v in old.items():
+            if v is None:
+                os.environ.pop(key, None)
+            else:
+                os.environ[key] = v
+    c.set_stream(torch.cuda.current_stream())
+    try:
+        rng = np.random.default_rng(7)
+        t = make_model(HP, dtype, rng)
+        om = DFlashOracle(HP, t)
+        gm = build(c, t)
+        E, A, n_ctx = HP["n_embd"], HP["n_aux"], 24
+        feats = rng.standard_normal((n_ctx, A * E)).astype(np.float32)
+        enc_ref = om.encode(feats)
+        kv = om.context_kv(enc_ref)
+        enc = torch.empty(n_ctx, E, device=dev)
+        gm.encode(to_dev(feats, dev), n_ctx, enc)
+        gm.set_context(enc, n_ctx)
+        for m in (9, 16):
+            toks = rng.standard_normal((m, E)).astype(np.float32)
+            hid_ref = om.decode_block(toks, kv)
+            hid = torch.empty(m, E, device=dev)
+            gm.decode_block(to_dev(toks, dev), m, hid)
+            torch.cuda.synchronize()
+            got = hid.cpu().numpy()
+            for r in range(m):
+                assert rel_l2(got[r], hid_ref[r]) <= 2e-3, (m, r)
+        c.device_status()
+        gm.close()
+    finally:
+        c.close()
