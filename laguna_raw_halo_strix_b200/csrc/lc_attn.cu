@@ -1,5 +1,5 @@
 // lc_attn.cu -- GQA attention of kernels/mha_attn.comp:31-72 for a block of
-// query rows.  attn_tc_kernel (tensor cores, 3xTF32) is the default;
+// query rows.  attn_tc5_kernel (tcgen05, f16 hi / lo operands) is the default;
 // attn_partial_kernel (f32 FMA) runs with LC_GEMM_TC=0.
 //
 // The reference runs one invocation per (head, dim) and walks all positions
@@ -8,10 +8,13 @@
 // staged in shared memory once and reused by all query heads of the group and
 // all query rows (up to 64 query vectors per CTA): the CTA grid is
 // (kv head, key split, query chunk) and a second kernel merges the split
-// partial softmax states.  Arithmetic is fp32 throughout.
+// partial softmax states.  The f32 kernel computes in fp32 throughout; the
+// tcgen05 kernel multiplies f16 hi / lo parts of the fp32 values (about 22
+// significant bits) with fp32 accumulation and keeps the softmax in fp32.
 #include <algorithm>
 
 #include "lc_internal.cuh"
+#include "lc_sm100.cuh"
 
 namespace {
 
@@ -184,266 +187,355 @@ __global__ void __launch_bounds__(kThreads) attn_partial_kernel(const float *__r
     if (sub == 0) ml_part[base] = make_float2(run_m, run_l);
 }
 
-// ---- tensor-core form (head_dim 128) ----------------------------------------
+// ---- tcgen05 form (head_dim 128) --------------------------------------------
 //
-// The same partial softmax states as attn_partial_kernel, computed with
-// mma.sync m16n8k8 TF32 in the 3xTF32 form (a = a_hi + a_lo, b = b_hi + b_lo,
-// a b ~ a_hi b_hi + a_hi b_lo + a_lo b_hi with f32 accumulation: about f32
-// accuracy).  One CTA per (KV head, key split, chunk of 64 query vectors), 8
-// warps: warp w takes query vectors 16 (w % 4) .. +15 against keys 32 (w / 4)
-// .. +31 of every 64-key tile (two warps per scheduler), with its own online
-// softmax state; the two key halves are merged in shared memory at the end.
-// Per tile S = Q K^T (16 x 32 per warp) in registers, the softmax on its
-// fragments, P through shared memory into A-fragment layout, O += P V (16 x 128
-// per warp).  K / V tiles double-buffered with cp.async.
+// One CTA per (KV head, 128-key tile, 64 query vectors).  Q, K and V go to
+// shared memory as f16 hi / lo planes (x * 2^e = hi + lo, e per query row, per
+// key row and per V tile, so no value leaves the f16 range and about 22
+// significant bits survive), K-major with the 128-byte swizzle the UMMA
+// descriptors read.  V is stored transposed (row = head dim, K = key) so both
+// products read K-major operands:
+//   S = Q K^T  (M 128, N 128 keys, K 128 dims):  Ql Kh + Qh Kl + Qh Kh
+//   O = P V    (M 128, N 128 dims, K 128 keys), P in tensor memory: Pl Vh + Ph Vl + Ph Vh
+// The MMAs run M = 128 over the 64 query rows: A rows 64..127 read whatever
+// follows the Q rows of a box, and their S / P / O lanes are never used.  A
+// query row's softmax runs in the two warps that share its TMEM lane (one per
+// 64-key half); the CTA writes the unnormalised (O, m, l) of its key tile for
+// attn_combine_kernel.  TMEM columns: S 0..127, P 128..255 (hi 128..191, lo
+// 192..255), O 256..383.
+constexpr int kAtRows = 64, kAtKeys = 128;
+constexpr int kAtThreads = 256;
+constexpr uint32_t kAtQBox = 64 * 128;   // 64 rows x 64 f16 (one 128-byte swizzle span)
+constexpr uint32_t kAtBox = 128 * 128;   // 128 rows x 64 f16
+constexpr uint32_t kAtQh = 0, kAtQl = 2 * kAtQBox;                          // Q: 64 rows x 128 dims
+constexpr uint32_t kAtKh = 4 * kAtQBox, kAtKl = kAtKh + 2 * kAtBox;          // K: 128 keys x 128 dims
+constexpr uint32_t kAtVh = kAtKl + 2 * kAtBox, kAtVl = kAtVh + 2 * kAtBox;   // V^T: 128 dims x 128 keys
+constexpr uint32_t kAtRawV = kAtVl + 2 * kAtBox;                             // raw f32 V tile (64 KB)
+constexpr uint32_t kAtInvQ = kAtRawV + kAtKeys * 512, kAtInvK = kAtInvQ + 256, kAtRed = kAtInvK + 512,
+                   kAtMisc = kAtRed + 1024;
+constexpr uint32_t kAtSmem = kAtMisc + 64 + 1024;  // + slack to 1024-align the base
+constexpr uint32_t kAtColS = 0, kAtColP = 128, kAtColO = 256, kAtTmemCols = 512;
 
-constexpr int kTcKeys = 64;              // keys per tile
-constexpr int kTcWarps = 8;
-constexpr int kTcQS = kHD + 4;           // sQ / sK row stride: fragment loads conflict-free
-constexpr int kTcVS = kHD + 8;           // sV row stride (B fragments of P V read down columns)
-constexpr int kTcPS = kTcKeys / 2 + 4;   // sP row stride (32 keys per warp)
-
-__device__ __forceinline__ uint32_t tf32_bits(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
-    return r;
+// Byte offset of f16 element (row, k) in an operand plane of two boxes of 64
+// K-elements (box_bytes apart): rows 128 bytes apart in 8-row groups of 1024
+// bytes, 16-byte chunks XOR-ed with the row within its group (the 128-byte
+// swizzle of the UMMA descriptor).
+__device__ __forceinline__ uint32_t at_off(int row, int k, uint32_t box_bytes) {
+    const uint32_t byte = (uint32_t)(k & 63) * 2;
+    return (uint32_t)(k >> 6) * box_bytes + (uint32_t)(row >> 3) * 1024 + (uint32_t)(row & 7) * 128 +
+           ((((byte >> 4) ^ (uint32_t)(row & 7)) << 4) | (byte & 15));
 }
-// x ~ hi + lo, both TF32
-__device__ __forceinline__ void tf32_split(float x, uint32_t &hi, uint32_t &lo) {
-    hi = tf32_bits(x);
-    lo = tf32_bits(x - __uint_as_float(hi));
+
+// hi / lo f16 pairs of (a, b): a ~ hi.x + lo.x, b ~ hi.y + lo.y.
+__device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
 }
 
-__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+__device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
+    asm volatile("st.shared.v2.u32 [%0], {%1, %2};\n" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t a) {
+    asm volatile("st.shared.u32 [%0], %1;\n" ::"r"(addr), "r"(a) : "memory");
 }
 
-// An A fragment split once into its TF32 hi / lo parts.
-struct Tf32Frag {
-    uint32_t h[4], l[4];
-};
-__device__ __forceinline__ Tf32Frag tf32_frag(const float (&a)[4]) {
-    Tf32Frag f;
+// Rows [0, nrows) of a raw f32 [rows][128] block in shared memory -> hi / lo
+// planes: warp w converts rows w, w + 8, ..., lane l dims 4l..4l+3, eight rows
+// per pass.  inv[row] = 1 / scale of the row.
+__device__ __forceinline__ void at_rows_to_planes(const unsigned char *raw, int nrows, int warp, int lane,
+                                                  uint32_t hi_plane, uint32_t lo_plane, uint32_t box_bytes,
+                                                  float *inv) {
+#pragma unroll 1
+    for (int r0 = warp; r0 < nrows; r0 += 64) {
+        float4 x[8];
 #pragma unroll
-    for (int i = 0; i < 4; i++) tf32_split(a[i], f.h[i], f.l[i]);
-    return f;
-}
-
-// d += a b with b given as f32: three TF32 products (small terms first).
-__device__ __forceinline__ void mma_3xtf32(float (&d)[4], const Tf32Frag &a, float b0f, float b1f) {
-    uint32_t bh0, bl0, bh1, bl1;
-    tf32_split(b0f, bh0, bl0);
-    tf32_split(b1f, bh1, bl1);
-    mma_tf32(d, a.l, bh0, bh1);
-    mma_tf32(d, a.h, bl0, bl1);
-    mma_tf32(d, a.h, bh0, bh1);
-}
-
-__global__ void __launch_bounds__(kTcWarps * 32, 1)
-    attn_tc_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
-                   float *__restrict__ o_part, float2 *__restrict__ ml_part, int m, int n_q, int n_kv, int seq_len,
-                   int keys_per_split, float scale, uint32_t q_pos0, int causal) {
-    extern __shared__ __align__(16) float sm[];
-    float *sQ = sm;                                // [64][kTcQS]
-    float *sK0 = sQ + kQV * kTcQS;                 // 2 x [64][kTcQS]
-    float *sV0 = sK0 + 2 * kTcKeys * kTcQS;        // 2 x [64][kTcVS]
-    float *sP = sV0 + 2 * kTcKeys * kTcVS;         // [8 warps][16][kTcPS]
-    const int hk = blockIdx.x, split = blockIdx.y, chunk = blockIdx.z;
-    const int G = n_q / n_kv, qv_total = m * G, qv0 = chunk * kQV;
-    const int nqv = min(kQV, qv_total - qv0);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-    const int qg = warp & 3, kh = warp >> 2;  // query group, key half
-    const int p_begin = split * keys_per_split, p_end = min(seq_len, p_begin + keys_per_split);
-    const int ldq = n_q * kHD, ldk = n_kv * kHD;
-
-    // stage the 64 query vectors (rows past nqv zero): 32 threads per vector
-    for (int qi = tid >> 5; qi < kQV; qi += kTcWarps) {
-        float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (qi < nqv) {
-            const int gq = qv0 + qi, r = gq / G, h = hk * G + gq % G;
-            val = *reinterpret_cast<const float4 *>(q + (size_t)r * ldq + h * kHD + 4 * lane);
+        for (int u = 0; u < 8; u++) {
+            const int row = min(r0 + 8 * u, 127);  // rows past nrows: loaded, not used
+            x[u] = *reinterpret_cast<const float4 *>(raw + row * 512 + 16 * lane);
         }
-        *reinterpret_cast<float4 *>(sQ + qi * kTcQS + 4 * lane) = val;
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int row = r0 + 8 * u;
+            float mx = fmaxf(fmaxf(fabsf(x[u].x), fabsf(x[u].y)), fmaxf(fabsf(x[u].z), fabsf(x[u].w)));
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (row >= nrows) continue;
+            float s, iv;
+            act_scale(mx, s, iv);
+            if (lane == 0) inv[row] = iv;
+            uint32_t h0, l0, h1, l1;
+            split2(x[u].x * s, x[u].y * s, h0, l0);
+            split2(x[u].z * s, x[u].w * s, h1, l1);
+            const uint32_t off = at_off(row, 4 * lane, box_bytes);
+            st_shared_v2(hi_plane + off, h0, h1);
+            st_shared_v2(lo_plane + off, l0, l1);
+        }
     }
-    auto load_tile = [&](int t0, int buf) {
-        const int nk = min(kTcKeys, p_end - t0);
-        float *sK = sK0 + buf * kTcKeys * kTcQS, *sV = sV0 + buf * kTcKeys * kTcVS;
-        for (int i = tid; i < kTcKeys * (kHD / 4); i += kTcWarps * 32) {
-            const int kk = i / (kHD / 4), d4 = i % (kHD / 4);
-            const size_t off = (size_t)(t0 + (kk < nk ? kk : 0)) * ldk + hk * kHD + 4 * d4;
-            const uint32_t nb = kk < nk ? 16u : 0u;
-            cp_async16(sK + kk * kTcQS + 4 * d4, k + off, nb);
-            cp_async16(sV + kk * kTcVS + 4 * d4, v + off, nb);
-        }
-        cp_async_commit();
-    };
+}
 
-    // this thread's two query rows in the warp's 16: g and g + 8
-    const int qa = qg * 16 + g, qb = qa + 8;
-    const long long pos_a = (long long)q_pos0 + (qv0 + qa) / G, pos_b = (long long)q_pos0 + (qv0 + qb) / G;
-    const bool act_a = qa < nqv, act_b = qb < nqv;
-    float o[16][4];  // O[16 rows x 128 dims]: n-tile j = dims 8j..8j+7
+__global__ void __launch_bounds__(kAtThreads, 1)
+    attn_tc5_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
+                    float *__restrict__ o_part, float2 *__restrict__ ml_part, int m, int n_q, int n_kv, int seq_len,
+                    float scale, uint32_t q_pos0, int causal, unsigned *__restrict__ status) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    const uint32_t sbase = smem_addr(smem);
+    float *inv_q = reinterpret_cast<float *>(smem + kAtInvQ), *inv_k = reinterpret_cast<float *>(smem + kAtInvK);
+    float *red_m = reinterpret_cast<float *>(smem + kAtRed), *red_l = red_m + 2 * kAtRows;
+    unsigned *vmax = reinterpret_cast<unsigned *>(smem + kAtMisc);
+    uint64_t *bar_s = reinterpret_cast<uint64_t *>(smem + kAtMisc + 8), *bar_o = bar_s + 1;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + kAtMisc + 24);
+    const int hk = blockIdx.x, split = blockIdx.y, chunk = blockIdx.z;
+    const int G = n_q / n_kv, qv_total = m * G, qv0 = chunk * kAtRows;
+    const int nqv = min(kAtRows, qv_total - qv0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int p_begin = split * kAtKeys, p_end = min(seq_len, p_begin + kAtKeys), nk = max(0, p_end - p_begin);
+    const int ldq = n_q * 128, ldk = n_kv * 128;
+
+    griddep_launch_dependents();  // the combine kernel may be scheduled now
+    if (threadIdx.x == 0) {
+        mbar_init(bar_s, 1);
+        mbar_init(bar_o, 1);
+        *vmax = 0u;
+        mbar_init_fence();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tslot)),
+                     "r"(kAtTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+        tc_fence_before();
+    }
+    // raw rows by cp.async, all in flight at once: Q -> the K planes' space,
+    // K -> the V planes' space (both converted before their space is written),
+    // V -> its own staging
+#pragma unroll 1
+    for (int idx = threadIdx.x; idx < kAtKeys * 32; idx += kAtThreads) {
+        const int row = idx >> 5, ch = idx & 31;
+        if (row < nqv) {
+            const int gq = qv0 + row, r = gq / G, h = hk * G + gq % G;
+            cp_async16(smem + kAtKh + row * 512 + 16 * ch, q + (size_t)r * ldq + h * 128 + 4 * ch, 16u);
+        }
+        if (row < nk) {
+            const size_t src = (size_t)(p_begin + row) * ldk + hk * 128 + 4 * ch;
+            cp_async16(smem + kAtVh + row * 512 + 16 * ch, k + src, 16u);
+            cp_async16(smem + kAtRawV + row * 512 + 16 * ch, v + src, 16u);
+        }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    at_rows_to_planes(smem + kAtKh, nqv, warp, lane, sbase + kAtQh, sbase + kAtQl, kAtQBox, inv_q);
+    __syncthreads();  // raw Q consumed before the K planes are written
+    at_rows_to_planes(smem + kAtVh, nk, warp, lane, sbase + kAtKh, sbase + kAtKl, kAtBox, inv_k);
+    fence_proxy_async_smem();  // generic-proxy stores -> the tensor cores' reads
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    constexpr uint32_t idesc = umma_idesc_f16(128, 128);
+    if (threadIdx.x == 0) {  // S = Q K^T, small products first
+        const uint64_t qh = umma_desc_sw128(sbase + kAtQh), ql = umma_desc_sw128(sbase + kAtQl);
+        const uint64_t kh = umma_desc_sw128(sbase + kAtKh), kl = umma_desc_sw128(sbase + kAtKl);
+        const uint32_t ds = tbase + kAtColS;
 #pragma unroll
-    for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-    float m_a = kNegInit, m_b = kNegInit, l_a = 0.f, l_b = 0.f;
-
-    if (p_begin < p_end) load_tile(p_begin, 0);
-    int buf = 0;
-    for (int t0 = p_begin; t0 < p_end; t0 += kTcKeys, buf ^= 1) {
-        if (t0 + kTcKeys < p_end) {
-            load_tile(t0 + kTcKeys, buf ^ 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
+        for (int t = 0; t < 3; t++) {
+            const uint64_t qa = t == 0 ? ql : qh, kb = t == 1 ? kl : kh;
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) {
+                const uint64_t qo = ((kk >> 2) * kAtQBox + (kk & 3) * 32) >> 4;
+                const uint64_t ko = ((kk >> 2) * kAtBox + (kk & 3) * 32) >> 4;
+                umma_f16_ss(ds, qa + qo, kb + ko, idesc, (t | kk) ? 1u : 0u);
+            }
         }
+        umma_commit(bar_s);
+    }
+    // V, transposed, into the V planes (their space held raw K, converted
+    // above): one scale for the tile, then f16x2 of key pairs (2p, 2p + 1) per dim
+    float v_iv;
+    {
+        const unsigned char *raw = smem + kAtRawV;
+        float mx = 0.f;
+#pragma unroll 4
+        for (int i = 0; i < 16; i++) {
+            const int idx = threadIdx.x + kAtThreads * i;  // float4 index; key idx / 32
+            if ((idx >> 5) < nk) {
+                const float4 x = *reinterpret_cast<const float4 *>(raw + 16 * idx);
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+            }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) atomicMax(vmax, __float_as_uint(mx));  // non-negative floats order as integers
         __syncthreads();
-        const float *sK = sK0 + buf * kTcKeys * kTcQS, *sV = sV0 + buf * kTcKeys * kTcVS;
-        // S = Q K^T: 4 n-tiles of 8 keys (this warp's half), 16 k-steps of 8 dims
-        float sc[4][4];
+        float s;
+        act_scale(__uint_as_float(*vmax), s, v_iv);
+#pragma unroll 4
+        for (int i = 0; i < 32; i++) {
+            const int idx = threadIdx.x + kAtThreads * i, k0 = 2 * (idx >> 7), d = idx & 127;
+            const float a = k0 < nk ? *reinterpret_cast<const float *>(raw + k0 * 512 + 4 * d) : 0.f;
+            const float b = k0 + 1 < nk ? *reinterpret_cast<const float *>(raw + (k0 + 1) * 512 + 4 * d) : 0.f;
+            uint32_t hi, lo;
+            split2(a * s, b * s, hi, lo);
+            const uint32_t off = at_off(d, k0, kAtBox);
+            st_shared_u32(sbase + kAtVh + off, hi);
+            st_shared_u32(sbase + kAtVl + off, lo);
+        }
+    }
+    fence_proxy_async_smem();
+    // softmax: warps w and w + 4 (w = 0, 1) share query row 32 w + lane (its TMEM
+    // lane) and take keys 64 (warp >> 2) .. +63; the halves exchange maxima and
+    // sums through shared memory.  Scores are in log2 units (exp2).
+    const bool sw = (warp & 3) < 2;
+    const int srow = 32 * (warp & 3) + lane, shalf = warp >> 2;
+    const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
+    float sv[64];
+    float tmax = kNegInit, row_m = kNegInit, row_l = 0.f;
+    int klim = 0;
+    if (sw) {
+        const bool real = srow < nqv;
+        const long long pos = (long long)q_pos0 + (qv0 + srow) / G;
+        long long lim = real ? nk : 0;  // keys [0, lim) of the tile are visible to the row
+        if (causal) lim = min(lim, max(0ll, pos - p_begin + 1));
+        klim = (int)lim - 64 * shalf;
+        const float fq = inv_q[srow] * (scale * 1.4426950408889634f);  // log2(e)
+        if (!mbar_wait(bar_s, 0)) atomicOr(status, LC_DEV_WAIT_TIMEOUT);
+        tc_fence_after();
 #pragma unroll
-        for (int j = 0; j < 4; j++) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
-        const float *qw = sQ + (qg * 16) * kTcQS;
-        const int key0 = 32 * kh;
-#pragma unroll 2
-        for (int kk = 0; kk < kHD; kk += 8) {
-            const float a[4] = {qw[g * kTcQS + kk + t], qw[(g + 8) * kTcQS + kk + t], qw[g * kTcQS + kk + t + 4],
-                                qw[(g + 8) * kTcQS + kk + t + 4]};
-            const Tf32Frag af = tf32_frag(a);
+        for (int c = 0; c < 4; c++) {
+            float t[16];
+            tmem_ld16(tbase + lanes + kAtColS + 64 * shalf + 16 * c, t);
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float *kr = sK + (key0 + 8 * j + g) * kTcQS + kk;
-                mma_3xtf32(sc[j], af, kr[t], kr[t + 4]);
+            for (int j = 0; j < 16; j++) sv[16 * c + j] = t[j];
+        }
+        tmem_ld_wait();
+        tmem_regs_ready(sv);
+#pragma unroll
+        for (int j = 0; j < 64; j += 4) {
+            const float4 ik = *reinterpret_cast<const float4 *>(inv_k + 64 * shalf + j);
+            sv[j] *= ik.x * fq, sv[j + 1] *= ik.y * fq, sv[j + 2] *= ik.z * fq, sv[j + 3] *= ik.w * fq;
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (j + u < klim) tmax = fmaxf(tmax, sv[j + u]);
+        }
+        red_m[kAtRows * shalf + srow] = tmax;
+    }
+    named_barrier_sync(kAtThreads);
+    if (sw) {
+        tmax = fmaxf(tmax, red_m[kAtRows * (shalf ^ 1) + srow]);
+        float lsum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 2; c++) {  // 32 keys -> 16 columns of hi and 16 of lo
+            uint32_t ph[16], pl[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int k0 = 32 * c + 2 * j;
+                const float p0 = k0 < klim ? exp2f(sv[k0] - tmax) : 0.f;
+                const float p1 = k0 + 1 < klim ? exp2f(sv[k0 + 1] - tmax) : 0.f;
+                lsum += p0 + p1;
+                split2(p0, p1, ph[j], pl[j]);
+            }
+            tmem_st16(tbase + lanes + kAtColP + 32 * shalf + 16 * c, ph);
+            tmem_st16(tbase + lanes + kAtColP + 64 + 32 * shalf + 16 * c, pl);
+        }
+        red_l[kAtRows * shalf + srow] = lsum;
+        row_m = tmax == kNegInit ? kNegInit : tmax * 0.6931471805599453f;  // natural-log units
+        row_l = lsum;
+        tmem_st_wait();
+        tc_fence_before();
+    }
+    __syncthreads();  // V planes and P complete
+    tc_fence_after();
+    if (threadIdx.x == 0) {  // O = P V
+        const uint64_t vh = umma_desc_sw128(sbase + kAtVh), vl = umma_desc_sw128(sbase + kAtVl);
+        const uint32_t d_o = tbase + kAtColO, pa = tbase + kAtColP;
+#pragma unroll
+        for (int t = 0; t < 3; t++) {
+            const uint32_t pc = t == 0 ? pa + 64 : pa;
+            const uint64_t vb = t == 1 ? vl : vh;
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) {
+                const uint64_t vo = ((kk >> 2) * kAtBox + (kk & 3) * 32) >> 4;
+                umma_f16_ts(d_o, pc + 8 * kk, vb + vo, idesc, (t | kk) ? 1u : 0u);
             }
         }
-        // online softmax over this tile (rows g, g + 8 of the warp)
-        float tmax_a = kNegInit, tmax_b = kNegInit;
+        umma_commit(bar_o);
+    }
+    if (sw) {  // partial states: columns 64 shalf.. of the row's O
+        if (!mbar_wait(bar_o, 0)) atomicOr(status, LC_DEV_WAIT_TIMEOUT);
+        tc_fence_after();
+        float o[64];
 #pragma unroll
-        for (int j = 0; j < 4; j++)
+        for (int c = 0; c < 4; c++) {
+            float t[16];
+            tmem_ld16(tbase + lanes + kAtColO + 64 * shalf + 16 * c, t);
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const int key = t0 + key0 + 8 * j + 2 * t + (c & 1);
-                const bool rb = c >= 2;
-                const bool vis = (rb ? act_b : act_a) && key < p_end && (!causal || key <= (rb ? pos_b : pos_a));
-                sc[j][c] = vis ? sc[j][c] * scale : -INFINITY;
-                if (vis) {
-                    if (rb) tmax_b = fmaxf(tmax_b, sc[j][c]);
-                    else tmax_a = fmaxf(tmax_a, sc[j][c]);
-                }
-            }
-#pragma unroll
-        for (int o2 = 1; o2 <= 2; o2 <<= 1) {
-            tmax_a = fmaxf(tmax_a, __shfl_xor_sync(0xffffffffu, tmax_a, o2));
-            tmax_b = fmaxf(tmax_b, __shfl_xor_sync(0xffffffffu, tmax_b, o2));
+            for (int j = 0; j < 16; j++) o[16 * c + j] = t[j];
         }
-        const float mn_a = fmaxf(m_a, tmax_a), mn_b = fmaxf(m_b, tmax_b);
-        const float cr_a = expf(m_a - mn_a), cr_b = expf(m_b - mn_b);
-        float ps_a = 0.f, ps_b = 0.f;
-        float *pw = sP + (warp * 16) * kTcPS;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const float p0 = sc[j][0] == -INFINITY ? 0.f : expf(sc[j][0] - mn_a);
-            const float p1 = sc[j][1] == -INFINITY ? 0.f : expf(sc[j][1] - mn_a);
-            const float p2 = sc[j][2] == -INFINITY ? 0.f : expf(sc[j][2] - mn_b);
-            const float p3 = sc[j][3] == -INFINITY ? 0.f : expf(sc[j][3] - mn_b);
-            ps_a += p0 + p1;
-            ps_b += p2 + p3;
-            *reinterpret_cast<float2 *>(pw + g * kTcPS + 8 * j + 2 * t) = make_float2(p0, p1);
-            *reinterpret_cast<float2 *>(pw + (g + 8) * kTcPS + 8 * j + 2 * t) = make_float2(p2, p3);
-        }
-#pragma unroll
-        for (int o2 = 1; o2 <= 2; o2 <<= 1) {
-            ps_a += __shfl_xor_sync(0xffffffffu, ps_a, o2);
-            ps_b += __shfl_xor_sync(0xffffffffu, ps_b, o2);
-        }
-        l_a = l_a * cr_a + ps_a;
-        l_b = l_b * cr_b + ps_b;
-        m_a = mn_a;
-        m_b = mn_b;
-#pragma unroll
-        for (int j = 0; j < 16; j++) o[j][0] *= cr_a, o[j][1] *= cr_a, o[j][2] *= cr_b, o[j][3] *= cr_b;
-        __syncwarp();
-        // O += P V: 16 n-tiles of 8 dims, 4 k-steps of 8 keys (this warp's half)
-#pragma unroll 2
-        for (int kk = 0; kk < kTcKeys / 2; kk += 8) {
-            const float a[4] = {pw[g * kTcPS + kk + t], pw[(g + 8) * kTcPS + kk + t], pw[g * kTcPS + kk + t + 4],
-                                pw[(g + 8) * kTcPS + kk + t + 4]};
-            const Tf32Frag af = tf32_frag(a);
+        tmem_ld_wait();
+        tmem_regs_ready(o);
+        if (srow < nqv) {
+            const int gq = qv0 + srow, r = gq / G, h = hk * G + gq % G;
+            const size_t base = ((size_t)split * m + r) * n_q + h;
+            float4 *op = reinterpret_cast<float4 *>(o_part + base * 128 + 64 * shalf);
 #pragma unroll
             for (int j = 0; j < 16; j++)
-                mma_3xtf32(o[j], af, sV[(key0 + kk + t) * kTcVS + 8 * j + g],
-                           sV[(key0 + kk + t + 4) * kTcVS + 8 * j + g]);
+                op[j] = make_float4(o[4 * j] * v_iv, o[4 * j + 1] * v_iv, o[4 * j + 2] * v_iv, o[4 * j + 3] * v_iv);
+            if (shalf == 0) ml_part[base] = make_float2(row_m, row_l + red_l[kAtRows + srow]);
         }
-        __syncthreads();  // done with this K / V buffer before it is refilled
     }
-    // merge the two key halves: warps 4..7 hand (m, l, O) to warps 0..3 through
-    // shared memory (the K buffers, free after the loop's final barrier)
-    float *xch = sK0 + (size_t)(qg * 32 + lane) * 68;
-    if (kh == 1) {
-#pragma unroll
-        for (int j = 0; j < 16; j++)
-            *reinterpret_cast<float4 *>(xch + 4 * j) = make_float4(o[j][0], o[j][1], o[j][2], o[j][3]);
-        *reinterpret_cast<float4 *>(xch + 64) = make_float4(m_a, m_b, l_a, l_b);
-    }
+    tc_fence_before();
     __syncthreads();
-    if (kh == 1) return;
-    {
-        const float4 ml = *reinterpret_cast<const float4 *>(xch + 64);
-        const float Ma = fmaxf(m_a, ml.x), Mb = fmaxf(m_b, ml.y);
-        const float a0 = expf(m_a - Ma), a1 = expf(ml.x - Ma), b0 = expf(m_b - Mb), b1 = expf(ml.y - Mb);
-        l_a = l_a * a0 + ml.z * a1;
-        l_b = l_b * b0 + ml.w * b1;
-        m_a = Ma;
-        m_b = Mb;
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-            const float4 u = *reinterpret_cast<const float4 *>(xch + 4 * j);
-            o[j][0] = o[j][0] * a0 + u.x * a1;
-            o[j][1] = o[j][1] * a0 + u.y * a1;
-            o[j][2] = o[j][2] * b0 + u.z * b1;
-            o[j][3] = o[j][3] * b0 + u.w * b1;
-        }
-    }
-    // partial states, as attn_partial_kernel: o_part[split][row][head][d], ml_part = (m, l)
-#pragma unroll
-    for (int half = 0; half < 2; half++) {
-        const int qi = half ? qb : qa;
-        if (qi >= nqv) continue;
-        const int gq = qv0 + qi, r = gq / G, h = hk * G + gq % G;
-        const size_t base = ((size_t)split * m + r) * n_q + h;
-        float *op = o_part + base * kHD;
-#pragma unroll
-        for (int j = 0; j < 16; j++)
-            *reinterpret_cast<float2 *>(op + 8 * j + 2 * t) = make_float2(o[j][2 * half], o[j][2 * half + 1]);
-        if (t == 0) ml_part[base] = half ? make_float2(m_b, l_b) : make_float2(m_a, l_a);
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(kAtTmemCols)
+                     : "memory");
     }
 }
 
-
-// out[r][h][d] = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s  (0 if no key visible),
-// merged in one pass with a running maximum so each split's loads are
-// independent of the others.
+// out[r][h][d] = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s (0 if no key is
+// visible), M the largest m_s of the splits that saw a key.  One warp per
+// (row, head), lane l owning dims 4l..4l+3; the split states are read
+// lane-parallel (split s by lane s % 32) and M and the weights formed with
+// shuffles, so every split's loads are independent of the others.  Launched as
+// a programmatic dependent of the partial kernel.
 __global__ void attn_combine_kernel(const float *__restrict__ o_part, const float2 *__restrict__ ml_part,
                                     float *__restrict__ out, int m, int n_q, int splits) {
-    const int rh = blockIdx.x;  // r * n_q + h
-    const int d = threadIdx.x;  // kHD threads
+    griddep_wait();  // the partial states
+    const int rh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (rh >= m * n_q) return;
     const size_t stride = (size_t)m * n_q;
-    float M = kNegInit, L = 0.f, O = 0.f;
+    float M = kNegInit;
+    for (int s0 = 0; s0 < splits; s0 += 32)
+        if (s0 + lane < splits) {
+            const float2 ml = ml_part[(s0 + lane) * stride + rh];
+            if (ml.y != 0.f) M = fmaxf(M, ml.x);
+        }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < splits; s0 += 32) {
+        float w = 0.f;
+        if (s0 + lane < splits) {
+            const float2 ml = ml_part[(s0 + lane) * stride + rh];
+            w = ml.y != 0.f ? expf(ml.x - M) : 0.f;
+            L += ml.y * w;
+        }
+        const int ns = min(32, splits - s0);
 #pragma unroll 8
-    for (int s = 0; s < splits; s++) {
-        const float2 ml = ml_part[s * stride + rh];
-        const float o = o_part[(s * stride + rh) * kHD + d];
-        if (ml.y == 0.f) continue;
-        const float Mn = fmaxf(M, ml.x);
-        const float a = expf(M - Mn), b = expf(ml.x - Mn);
-        L = L * a + ml.y * b;
-        O = O * a + o * b;
-        M = Mn;
+        for (int j = 0; j < ns; j++) {
+            const float b = __shfl_sync(0xffffffffu, w, j);
+            const float4 o = *reinterpret_cast<const float4 *>(o_part + ((s0 + j) * stride + rh) * kHD + 4 * lane);
+            O.x += o.x * b, O.y += o.y * b, O.z += o.z * b, O.w += o.w * b;
+        }
     }
-    out[(size_t)rh * kHD + d] = L > 0.f ? O / L : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    *reinterpret_cast<float4 *>(out + (size_t)rh * kHD + 4 * lane) =
+        L > 0.f ? make_float4(O.x / L, O.y / L, O.z / L, O.w / L) : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 }  // namespace
@@ -472,11 +564,11 @@ extern "C" int lc_mha_attn(lc_ctx *ctx, const float *q, const float *k, const fl
         const int max_splits = (int)((seq_len + kTK - 1) / kTK);
         splits = std::min(want, max_splits);
     }
-    // the tensor-core kernel (default) works in tiles of 64 keys, the f32 one in 32
+    // the tcgen05 kernel (default) takes one tile of 128 keys per CTA; the f32
+    // one about one CTA per SM, in tiles of 32 keys
     const bool tc = ctx->gemm_tc != 0;
-    const int tile = tc ? kTcKeys : kTK;
     int kps = seq_len > 0 ? (int)((seq_len + splits - 1) / splits) : 1;
-    kps = ((kps + tile - 1) / tile) * tile;
+    kps = tc ? kAtKeys : ((kps + kTK - 1) / kTK) * kTK;
     splits = seq_len > 0 ? (int)((seq_len + kps - 1) / kps) : 1;
     const size_t o_bytes = (size_t)splits * m * n_q_heads * kHD * 4;
     const size_t ml_bytes = (size_t)splits * m * n_q_heads * 8;
@@ -484,15 +576,14 @@ extern "C" int lc_mha_attn(lc_ctx *ctx, const float *q, const float *k, const fl
     if (!scr) return LC_ERR_OOM;
     float *o_part = (float *)scr;
     float2 *ml_part = (float2 *)(scr + ((o_bytes + 255) & ~(size_t)255));
+    static_assert(kAtRows == kQV, "both kernels take chunks of the same query vectors");
     dim3 grid(n_kv_heads, splits, chunks);
     if (tc) {
-        const size_t smem =
-            (size_t)(kQV * kTcQS + 2 * kTcKeys * kTcQS + 2 * kTcKeys * kTcVS + kTcWarps * 16 * kTcPS) * 4;
-        s = lc_set_smem_attr((const void *)attn_tc_kernel, smem);
+        s = lc_set_smem_attr((const void *)attn_tc5_kernel, kAtSmem);
         if (s) return s;
-        attn_tc_kernel<<<grid, kTcWarps * 32, smem, ctx->stream>>>(q, seq_len ? k : q, seq_len ? v : q, o_part,
-                                                                   ml_part, (int)m, (int)n_q_heads, (int)n_kv_heads,
-                                                                   (int)seq_len, kps, scale, q_pos0, (int)causal);
+        attn_tc5_kernel<<<grid, kAtThreads, kAtSmem, ctx->stream>>>(
+            q, seq_len ? k : q, seq_len ? v : q, o_part, ml_part, (int)m, (int)n_q_heads, (int)n_kv_heads,
+            (int)seq_len, scale, q_pos0, (int)causal, ctx->dev_status);
     } else {
         const size_t smem = (size_t)(kQV * kQS + 2 * kTK * kKS + 2 * kTK * kHD + kQV * kPS) * 4;
         s = lc_set_smem_attr((const void *)attn_partial_kernel, smem);
@@ -501,7 +592,18 @@ extern "C" int lc_mha_attn(lc_ctx *ctx, const float *q, const float *k, const fl
                                                                    ml_part, (int)m, (int)n_q_heads, (int)n_kv_heads,
                                                                    (int)seq_len, kps, scale, q_pos0, (int)causal);
     }
-    attn_combine_kernel<<<m * n_q_heads, kHD, 0, ctx->stream>>>(o_part, ml_part, out, (int)m, (int)n_q_heads,
-                                                                 splits);
+    // a programmatic dependent of the partial kernel: its CTAs are resident
+    // before the partial states are complete and wait for them on the device
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((m * n_q_heads + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    LC_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_kernel, (const float *)o_part, (const float2 *)ml_part, out, (int)m,
+                               (int)n_q_heads, splits));
     return lc_after_launch(ctx, "lc_mha_attn");
 }

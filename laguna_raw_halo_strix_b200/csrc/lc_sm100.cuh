@@ -1,6 +1,7 @@
 // lc_sm100.cuh -- device helpers shared by the sm_100a kernels (not installed):
 // bounded mbarrier waits, TMA tensor copies, shared-memory loads, packed f32x2
-// arithmetic, the activation scale and the f16 scale decode.
+// arithmetic, the activation scale, the f16 scale decode, tcgen05 descriptors,
+// MMAs and tensor-memory access, programmatic dependent launch.
 #pragma once
 
 #include <cuda.h>
@@ -17,14 +18,12 @@ namespace {
 // its f16 hi / lo split cannot overflow (f16 max 65504) however large the
 // activations grow; outputs are multiplied by 2^-e.  Both steps are exact.
 __device__ __forceinline__ void act_scale(float maxabs, float &s, float &inv) {
+    // maxabs = f * 2^x with f in [0.5, 1): x = E - 126 for the biased exponent E of
+    // a normal float; a subnormal (E = 0) gives e above 100 either way.
     int e = 0;
-    if (maxabs > 0.f && maxabs < INFINITY) {
-        int x;
-        frexpf(maxabs, &x);  // maxabs = f * 2^x, f in [0.5, 1)
-        e = min(max(14 - x, -100), 100);
-    }
-    s = ldexpf(1.f, e);
-    inv = ldexpf(1.f, -e);
+    if (maxabs > 0.f && maxabs < INFINITY) e = min(max(140 - (int)(__float_as_uint(maxabs) >> 23), -100), 100);
+    s = __uint_as_float((uint32_t)(e + 127) << 23);
+    inv = __uint_as_float((uint32_t)(127 - e) << 23);
 }
 
 // (d, dmin) of a header word -> two floats.  The reference rule for subnormal
@@ -159,6 +158,132 @@ __device__ __forceinline__ uint32_t lds32(const void *p) {
     uint32_t v;
     asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(v) : "r"(smem_addr(p)));
     return v;
+}
+
+// ---- tcgen05 ---------------------------------------------------------------
+
+// Shared-memory matrix descriptor, K-major with 128-byte swizzle: rows of
+// 128 bytes in groups of 8 (1024 bytes, SBO), 16-byte chunks XOR-swizzled by
+// the row within the group; LBO unused (1); version 1; layout type 2.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;               // LBO (16 B; unused for this layout)
+    d |= (uint64_t)(1024u >> 4) << 32;     // SBO: 8 rows x 128 B
+    d |= (uint64_t)1u << 46;               // descriptor version (sm_100)
+    d |= (uint64_t)2u << 61;               // SWIZZLE_128B
+    return d;
+}
+
+// Shared-memory matrix descriptor, K-major without swizzle, for a K = 16
+// operand in core matrices of 8 rows x 16 bytes: the two K groups 128 bytes
+// apart (LBO), 8-row groups 256 bytes apart (SBO).
+__device__ __forceinline__ uint64_t umma_desc_core16(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)(128u >> 4) << 16;
+    d |= (uint64_t)(256u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    return d;
+}
+
+// Instruction descriptor of kind::f16: D f32, A and B f16, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// D (TMEM) (+)= A (shared memory) * B (shared memory)^T.
+__device__ __forceinline__ void umma_f16_ss(uint32_t dtmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(dtmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D (TMEM) (+)= A (TMEM: row i in lane i, two f16 per column) * B (shared memory)^T.
+__device__ __forceinline__ void umma_f16_ts(uint32_t dtmem, uint32_t atmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(dtmem),
+        "r"(atmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane -> registers
+// (complete after tmem_ld_wait).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// The values of every tcgen05.ld issued so far are in their registers.
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
+// Ties registers written by tcgen05.ld to a point after tmem_ld_wait(): their
+// uses depend on these (ordered) volatile statements, so none moves above the
+// wait.
+template <int N>
+__device__ __forceinline__ void tmem_regs_ready(float (&v)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; i++) asm volatile("" : "+f"(v[i])::"memory");
+}
+
+// Registers -> 16 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+// Every tcgen05.st this thread issued has written the tensor memory.
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Programmatic dependent launch: the dependent grid may start once every CTA
+// of this grid has executed launch_dependents (or exited); griddep_wait blocks
+// until the prerequisite grid has completed and its writes are visible (a no-op
+// in a grid launched without the attribute).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+// Untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
+        : "memory");
 }
 
 }  // namespace
