@@ -210,8 +210,8 @@ constexpr uint32_t kAtBox = 128 * 128;   // 128 rows x 64 f16
 constexpr uint32_t kAtQh = 0, kAtQl = 2 * kAtQBox;                          // Q: 64 rows x 128 dims
 constexpr uint32_t kAtKh = 4 * kAtQBox, kAtKl = kAtKh + 2 * kAtBox;          // K: 128 keys x 128 dims
 constexpr uint32_t kAtVh = kAtKl + 2 * kAtBox, kAtVl = kAtVh + 2 * kAtBox;   // V^T: 128 dims x 128 keys
-constexpr uint32_t kAtRawV = kAtVl + 2 * kAtBox;                             // raw f32 V tile (64 KB)
-constexpr uint32_t kAtInvQ = kAtRawV + kAtKeys * 512, kAtInvK = kAtInvQ + 256, kAtRed = kAtInvK + 512,
+constexpr uint32_t kAtRaw = kAtVl + 2 * kAtBox;                              // raw f32 Q rows (32 KB)
+constexpr uint32_t kAtInvQ = kAtRaw + kAtRows * 512, kAtInvK = kAtInvQ + 256, kAtRed = kAtInvK + 512,
                    kAtMisc = kAtRed + 1024;
 constexpr uint32_t kAtSmem = kAtMisc + 64 + 1024;  // + slack to 1024-align the base
 constexpr uint32_t kAtColS = 0, kAtColP = 128, kAtColO = 256, kAtTmemCols = 512;
@@ -233,6 +233,14 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t 
     const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
     hi = *reinterpret_cast<const uint32_t *>(&h);
     lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+// Global load issued where it stands (a volatile asm keeps its place among the
+// cp.async staging copies): the V tile's latency overlaps theirs.
+__device__ __forceinline__ float ldg_stream(const float *p) {
+    float x;
+    asm volatile("ld.global.nc.f32 %0, [%1];\n" : "=f"(x) : "l"(p));
+    return x;
 }
 
 __device__ __forceinline__ void st_shared_v2(uint32_t addr, uint32_t a, uint32_t b) {
@@ -309,28 +317,48 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
         tc_fence_before();
     }
-    // raw rows by cp.async, all in flight at once: Q -> the K planes' space,
-    // K -> the V planes' space (both converted before their space is written),
-    // V -> its own staging
+    // V rows into registers (loads issued here, in program order): warp w takes
+    // key pairs (2p, 2p + 1), p = w + 8 i, lane l dims l + 32 c
+    float vv[8][2][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int key = 2 * (warp + 8 * i) + e;
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                vv[i][e][c] = key < nk ? ldg_stream(v + (size_t)(p_begin + key) * ldk + hk * 128 + lane + 32 * c) : 0.f;
+        }
+    // raw Q and K rows by cp.async (Q -> the staging space, K -> the V planes'
+    // space, converted before V is written there)
 #pragma unroll 1
     for (int idx = threadIdx.x; idx < kAtKeys * 32; idx += kAtThreads) {
         const int row = idx >> 5, ch = idx & 31;
         if (row < nqv) {
             const int gq = qv0 + row, r = gq / G, h = hk * G + gq % G;
-            cp_async16(smem + kAtKh + row * 512 + 16 * ch, q + (size_t)r * ldq + h * 128 + 4 * ch, 16u);
+            cp_async16(smem + kAtRaw + row * 512 + 16 * ch, q + (size_t)r * ldq + h * 128 + 4 * ch, 16u);
         }
-        if (row < nk) {
-            const size_t src = (size_t)(p_begin + row) * ldk + hk * 128 + 4 * ch;
-            cp_async16(smem + kAtVh + row * 512 + 16 * ch, k + src, 16u);
-            cp_async16(smem + kAtRawV + row * 512 + 16 * ch, v + src, 16u);
-        }
+        if (row < nk)
+            cp_async16(smem + kAtVh + row * 512 + 16 * ch, k + (size_t)(p_begin + row) * ldk + hk * 128 + 4 * ch, 16u);
     }
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-    at_rows_to_planes(smem + kAtKh, nqv, warp, lane, sbase + kAtQh, sbase + kAtQl, kAtQBox, inv_q);
-    __syncthreads();  // raw Q consumed before the K planes are written
+    // Q and K planes, and the V tile's maximum, in one phase
+    at_rows_to_planes(smem + kAtRaw, nqv, warp, lane, sbase + kAtQh, sbase + kAtQl, kAtQBox, inv_q);
     at_rows_to_planes(smem + kAtVh, nk, warp, lane, sbase + kAtKh, sbase + kAtKl, kAtBox, inv_k);
+    {
+        float mx = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int e = 0; e < 2; e++)
+#pragma unroll
+                for (int c = 0; c < 4; c++) mx = fmaxf(mx, fabsf(vv[i][e][c]));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) atomicMax(vmax, __float_as_uint(mx));  // non-negative floats order as integers
+    }
     fence_proxy_async_smem();  // generic-proxy stores -> the tensor cores' reads
     __syncthreads();
     tc_fence_after();
@@ -353,35 +381,22 @@ __global__ void __launch_bounds__(kAtThreads, 1)
         umma_commit(bar_s);
     }
     // V, transposed, into the V planes (their space held raw K, converted
-    // above): one scale for the tile, then f16x2 of key pairs (2p, 2p + 1) per dim
+    // above): one scale for the tile, f16x2 of key pairs (2p, 2p + 1) per dim
     float v_iv;
     {
-        const unsigned char *raw = smem + kAtRawV;
-        float mx = 0.f;
-#pragma unroll 4
-        for (int i = 0; i < 16; i++) {
-            const int idx = threadIdx.x + kAtThreads * i;  // float4 index; key idx / 32
-            if ((idx >> 5) < nk) {
-                const float4 x = *reinterpret_cast<const float4 *>(raw + 16 * idx);
-                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
-            }
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) atomicMax(vmax, __float_as_uint(mx));  // non-negative floats order as integers
-        __syncthreads();
         float s;
         act_scale(__uint_as_float(*vmax), s, v_iv);
-#pragma unroll 4
-        for (int i = 0; i < 32; i++) {
-            const int idx = threadIdx.x + kAtThreads * i, k0 = 2 * (idx >> 7), d = idx & 127;
-            const float a = k0 < nk ? *reinterpret_cast<const float *>(raw + k0 * 512 + 4 * d) : 0.f;
-            const float b = k0 + 1 < nk ? *reinterpret_cast<const float *>(raw + (k0 + 1) * 512 + 4 * d) : 0.f;
-            uint32_t hi, lo;
-            split2(a * s, b * s, hi, lo);
-            const uint32_t off = at_off(d, k0, kAtBox);
-            st_shared_u32(sbase + kAtVh + off, hi);
-            st_shared_u32(sbase + kAtVl + off, lo);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int k0 = 2 * (warp + 8 * i);
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                uint32_t hi, lo;
+                split2(vv[i][0][c] * s, vv[i][1][c] * s, hi, lo);
+                const uint32_t off = at_off(lane + 32 * c, k0, kAtBox);
+                st_shared_u32(sbase + kAtVh + off, hi);
+                st_shared_u32(sbase + kAtVl + off, lo);
+            }
         }
     }
     fence_proxy_async_smem();
@@ -525,7 +540,7 @@ __global__ void attn_combine_kernel(const float *__restrict__ o_part, const floa
             L += ml.y * w;
         }
         const int ns = min(32, splits - s0);
-#pragma unroll 8
+#pragma unroll 16
         for (int j = 0; j < ns; j++) {
             const float b = __shfl_sync(0xffffffffu, w, j);
             const float4 o = *reinterpret_cast<const float4 *>(o_part + ((s0 + j) * stride + rh) * kHD + 4 * lane);
@@ -595,8 +610,8 @@ extern "C" int lc_mha_attn(lc_ctx *ctx, const float *q, const float *k, const fl
     // a programmatic dependent of the partial kernel: its CTAs are resident
     // before the partial states are complete and wait for them on the device
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((m * n_q_heads + 7) / 8);
-    cfg.blockDim = dim3(256);
+    cfg.gridDim = dim3((m * n_q_heads + 1) / 2);
+    cfg.blockDim = dim3(64);
     cfg.stream = ctx->stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
