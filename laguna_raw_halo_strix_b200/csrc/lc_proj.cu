@@ -901,14 +901,8 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__((NW + 1) * 32, 1)
     const int my_units = warp < NW ? U0 + nU * (wq + 1) / NW - w0 : 0;
     const uint64_t pol = l2_evict_first_policy();
 
-    // Launched as a programmatic dependent: the weights (never written by an
-    // earlier kernel) stream at once; x is read, and y written, only after the
-    // prerequisite grid has completed.  Dependents of this grid may be scheduled
-    // as its CTAs retire.
-    griddep_launch_dependents();
     float xv[kXPre][8];
     if (warp < NW) {
-        griddep_wait();
         // x loads of this warp's first prologue items go out first
 #pragma unroll
         for (int p = 0; p < kXPre; p++)
@@ -1504,18 +1498,8 @@ int launch_tma_m(lc_ctx *ctx, const TmaPlan &p, const CUtensorMap &tm, const flo
     constexpr int NW = q4t_warps(M);
     int s = set_smem(tma_gemv_kernel<F, M, NW, kTmaCluster>, p.smem);
     if (s) return s;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.grid);
-    cfg.blockDim = dim3((NW + 1) * 32);
-    cfg.dynamicSmemBytes = p.smem;
-    cfg.stream = ctx->stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    LC_CUDA(cudaLaunchKernelEx(&cfg, tma_gemv_kernel<F, M, NW, kTmaCluster>, tm, x, c, (int)k, (int)n, ctx->half_mode,
-                               p.R, p.tl, ctx->dev_status));
+    tma_gemv_kernel<F, M, NW, kTmaCluster><<<p.grid, (NW + 1) * 32, p.smem, ctx->stream>>>(
+        tm, x, c, (int)k, (int)n, ctx->half_mode, p.R, p.tl, ctx->dev_status);
     return LC_OK;
 }
 
