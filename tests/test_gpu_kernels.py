@@ -461,3 +461,37 @@ def test_proj_routes_all_m(dev, oracle, dtype, route):
         c.device_status()
     finally:
         c.close()
+
+
+@pytest.mark.parametrize("m,seq,q_pos0,causal,nq,nkv,mag", [
+    (16, 300, 284, 1, 32, 8, 1.0),      # partial last key tile
+    (8, 129, 121, 1, 32, 8, 1.0),       # one key past a tile boundary
+    (32, 200, 168, 1, 32, 8, 1.0),      # 128 query vectors: two query chunks
+    (16, 257, 241, 1, 64, 8, 1.0),      # 8 query heads per KV head, two chunks
+    (5, 70, 65, 1, 8, 8, 1.0),          # one query head per KV head
+    (16, 150, 134, 0, 32, 8, 3e4),      # values far beyond the f16 range
+    (16, 150, 134, 1, 32, 8, 1e-5),     # and deep in its subnormals
+])
+def test_mha_attn_shapes(ctx, dev, oracle, m, seq, q_pos0, causal, nq, nkv, mag):
+    # The tensor-core kernel splits keys into 128-key tiles and query vectors
+    # into chunks of 64, and scales rows / tiles by powers of two before its
+    # f16 hi / lo split; tolerance 1e-5 of max|ref| per row, as above.  q, k, v
+    # of magnitude `mag` leave the f16 range; the softmax scale divides by mag^2
+    # so the logits stay O(1) (its scores carry ~22 significant bits, so their
+    # absolute error grows with the logits' size).
+    import torch
+
+    rng = np.random.default_rng(seq * 7 + m + nq)
+    hd = 128
+    q = (rng.standard_normal((m, nq * hd)) * mag).astype(np.float32)
+    k = (rng.standard_normal((seq, nkv * hd)) * mag).astype(np.float32)
+    v = (rng.standard_normal((seq, nkv * hd)) * mag).astype(np.float32)
+    scale = float(np.float32(1 / np.sqrt(hd) / (mag * mag)))
+    out = torch.empty(m, nq * hd, device=dev)
+    ctx.mha_attn(to_dev(q, dev), to_dev(k, dev), to_dev(v, dev), out, m, nq, nkv, hd, seq, scale, q_pos0, causal)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for r in range(m):
+        ref = oracle.mha_attn(q[r], k, v, nq, nkv, hd, seq, scale, q_pos0 + r, causal)
+        check_tol(got[r], ref, 1e-5, f"attn row {r}")
+    ctx.device_status()
