@@ -1421,7 +1421,11 @@ int tma_tensor_map(CUtensorMap *tm, const void *w, uint32_t k, uint32_t n) {
 // More warps (20 at <= 96 registers for one token) measured slower.
 __host__ __device__ constexpr int q4t_warps(int) { return 15; }
 constexpr int kTmaCluster = 4;
-constexpr int kTmaMaxStages = 4;
+// Units in flight per consumer warp.  Two measured fastest on B200 (Q4_K 4096->14336
+// at m = 1: 10.2 us with 2, 10.5 with 3, 12.2 with 4, 13.3 with 6 per launch): the
+// 15 warps x 2 units already keep ~69 KB per SM in flight, and deeper rings only
+// lengthen the producer's start-up fill.
+constexpr int kTmaMaxStages = 2;
 
 // Launch geometry of the TMA GEMV: clusters, ring depth, tiles per cluster.
 struct TmaPlan {
