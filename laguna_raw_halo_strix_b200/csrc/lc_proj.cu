@@ -1420,7 +1420,10 @@ int tma_tensor_map(CUtensorMap *tm, const void *w, uint32_t k, uint32_t n) {
 // Consumer warps per CTA (+ 1 producer warp = 512 threads, <= 128 registers).
 // More warps (20 at <= 96 registers for one token) measured slower.
 __host__ __device__ constexpr int q4t_warps(int) { return 15; }
-constexpr int kTmaCluster = 4;
+// Clusters of 2: more of them are co-resident than clusters of 4 (which left 16 of the
+// 148 SMs idle), at a slightly coarser split of the tiles (9.6 against 10.2 us per Q4_K
+// 4096->14336 launch at m = 1).
+constexpr int kTmaCluster = 2;
 // Units in flight per consumer warp.  Two measured fastest on B200 (Q4_K 4096->14336
 // at m = 1: 10.2 us with 2, 10.5 with 3, 12.2 with 4, 13.3 with 6 per launch): the
 // 15 warps x 2 units already keep ~69 KB per SM in flight, and deeper rings only
