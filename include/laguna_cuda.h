@@ -21,7 +21,7 @@
  *    (e.g. kernels/proj_q8_0.comp:17-20); byte counts are size_t.
  *  - Quantized weights are row-major: element (i, j) of an n x k projection is
  *    element i*k + j of the GGUF tensor (kernels/proj_q8_0.comp:54,
- *    kernels/proj_q4k.comp:134).  The quantized kernels require k to be a
+ *    kernels/proj_q4k.comp:67).  The quantized kernels require k to be a
  *    multiple of the block size (32 for Q8_0, 256 for Q4_K) and the weight
  *    pointer to be 16-byte aligned; other shapes return LC_ERR_UNSUPPORTED.
  *  - f16 scales decode by the reference rule by default: subnormal halves map
@@ -97,6 +97,10 @@ int lc_set_sync(lc_ctx *ctx, int sync);
  * copies gave up (the launch's outputs are then invalid), else LC_OK.  Kernels
  * never hang on such a wait; this call is how the host learns of it. */
 int lc_device_status(lc_ctx *ctx);
+/* Device memory (bytes) the context holds in its grow-only scratch slots;
+ * 0 until a call needs scratch.  No counterpart in the reference, whose
+ * buffers are all created up front (ForwardBuffers::new, src/dflash.rs:259-285). */
+int lc_ctx_scratch_bytes(lc_ctx *ctx, size_t *bytes);
 /* LC_HALF_REF (default) or LC_HALF_IEEE for every f16 scale decode. */
 int lc_set_half_mode(lc_ctx *ctx, int mode);
 /* Device the context runs on. */
@@ -134,7 +138,7 @@ int lc_proj_f32(lc_ctx *ctx, const float *x, const float *w, float *c,
 int lc_proj_q8_0(lc_ctx *ctx, const float *x, const void *w, float *c,
                  uint32_t k, uint32_t n);
 /* Q4_K projection, the WeightType::Q4_K arm (src/target.rs:1139-1160) running
- * kernels/proj_q4k.comp:127-159; expert_offset is in elements (multiple of 256). */
+ * kernels/proj_q4k.comp:60-92; expert_offset is in elements (multiple of 256). */
 int lc_proj_q4k(lc_ctx *ctx, const float *x, const void *w, float *c,
                 uint32_t k, uint32_t n, uint32_t expert_offset);
 /* dispatch_proj_quant_expert (src/target.rs:1098-1162): dtype switch over
@@ -147,24 +151,35 @@ int lc_proj_quant(lc_ctx *ctx, int dtype, const float *x, const void *w,
  * the reference would reach by m calls of the single-row dispatch. */
 int lc_proj_m(lc_ctx *ctx, int dtype, const float *x, const void *w, float *c,
               uint32_t m, uint32_t k, uint32_t n, uint32_t expert_offset);
-/* Q4_K projection of m = 1..16 rows of x [m, k] (same results as lc_proj_m
- * with LC_Q4_K) that allocates no device memory, for callers that cannot
- * allocate on the call path.  m <= 4 needs no scratch; for m = 5..16 the
- * packed activations live in a fixed static device array of 1 MiB (k <= 15360
- * at m = 16).  Shapes beyond that, m > 16, or (m <= 4) m * k beyond shared
- * memory return LC_ERR_UNSUPPORTED.  The first call on a device resolves the
- * array's address; make it before any stream capture.  Calls that overlap on
- * one GPU share the array and race: serialise them.  No counterpart in the
- * reference. */
+/* Q4_K projection of m = 1..16 rows of x [m, k] that allocates no device
+ * memory, for callers that cannot allocate on the call path: a serving loop
+ * whose memory plan has given all of HBM to weights and K/V, or a decode loop
+ * that must not pay cudaMalloc's device-wide synchronisation.  Results equal
+ * lc_proj_m with LC_Q4_K within the projection tolerance (some m run different
+ * kernels).  m <= 4 needs no scratch; for m = 5..16 the packed activations
+ * live in a fixed static device array of 1 MiB (k <= 15360 at m = 16),
+ * resolved per context at lc_init.  Shapes beyond that, m > 16, or (m = 3, 4)
+ * m * k beyond shared memory return LC_ERR_UNSUPPORTED.  Calls that overlap
+ * on one GPU share the array and race: serialise them.  A context must not be
+ * used across a cudaDeviceReset.  No counterpart in the reference. */
 int lc_proj_q4k_static(lc_ctx *ctx, const float *x, const void *w, float *c,
                        uint32_t m, uint32_t k, uint32_t n, uint32_t expert_offset);
+
+/* The FFN block of a DFlash decoder layer (src/dflash.rs:965-968:
+ * dispatch_proj gate and up, dispatch_activation, dispatch_proj down) in one
+ * call: y [m, n_embd] = down(SiLU(x W_gate^T) * (x W_up^T)) for x [m, n_embd]
+ * (device), Q8_0 or Q4_K weights (gate / up: n_ff x n_embd, down: n_embd x
+ * n_ff).  The intermediate [2, m, n_ff] lives in the context's scratch.  The
+ * residual add stays with the caller. */
+int lc_ffn(lc_ctx *ctx, int dtype, const float *x, const void *w_gate, const void *w_up, const void *w_down,
+           float *y, uint32_t m, uint32_t n_embd, uint32_t n_ff);
 
 /* ---- dequant ------------------------------------------------------------- */
 
 /* dequant_to_f32 (src/dflash.rs:331-465) on the device.  LC_Q8_0 / LC_F16 /
  * LC_BF16 / LC_F32 / LC_Q4_K_DFLASH_CPU follow the CPU decoder branch for
  * branch (reads bounded by src_bytes, missing elements 0); LC_Q4_K decodes
- * GGUF Q4_K with the GPU shader formula of kernels/proj_q4k.comp:139-154.
+ * GGUF Q4_K with the GPU shader formula of kernels/proj_q4k.comp:72-87.
  * Other dtypes produce zeros like the reference's fallback arm. */
 int lc_dequant(lc_ctx *ctx, int dtype, const void *src, size_t src_bytes,
                size_t n, float *out);

@@ -37,11 +37,6 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t 
                  "l"(src), "r"(src_bytes)
                  : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
 
 // Partials: o[split][row][head][d], ml[split][row][head] = (m, l).
 __global__ void __launch_bounds__(kThreads) attn_partial_kernel(const float *__restrict__ q,

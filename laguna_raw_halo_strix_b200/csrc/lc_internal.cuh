@@ -30,6 +30,9 @@ struct lc_ctx {
     // Device word that kernels set (atomicOr of LC_DEV_*) when a bounded wait
     // gives up; read and cleared by lc_device_status().  Allocated at init.
     unsigned *dev_status = nullptr;
+    // Device address of lc_proj.cu's static scratch array on this device,
+    // resolved at lc_init (lc_static_pack_resolve).
+    void *static_pack = nullptr;
 };
 
 // Bits of lc_ctx::dev_status.
@@ -55,6 +58,7 @@ enum {
     LC_SCRATCH_MODEL = 2,
     LC_SCRATCH_ATTN = 3,
     LC_SCRATCH_FIXUP = 4,
+    LC_SCRATCH_FFN = 5,
     LC_SCRATCH_COUNT = 8
 };
 // Grow-only scratch slot of at least `bytes` (256-byte aligned).  Returns
@@ -63,6 +67,8 @@ enum {
 void *lc_scratch(lc_ctx *ctx, int slot, size_t bytes);
 // Same, and a newly allocated slot is zero-filled (on the context's stream).
 void *lc_scratch_zeroed(lc_ctx *ctx, int slot, size_t bytes);
+// Resolve ctx->static_pack with ctx->device current (lc_proj.cu; called by lc_init).
+int lc_static_pack_resolve(lc_ctx *ctx);
 // Make ctx->device current on this thread.
 int lc_use_device(lc_ctx *ctx);
 // Raise a kernel's dynamic shared memory limit to at least `bytes` on the
@@ -187,6 +193,12 @@ int gemm_dq_group(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *out
 int qk_norm_rope_pair(lc_ctx *ctx, const float *xa, const float *wa, float *ya, uint32_t n_heads_a, const float *xb,
                       const float *wb, float *yb, uint32_t n_heads_b, const float *freq, uint32_t m,
                       uint32_t head_dim, uint32_t rope_dim, float eps, uint32_t pos0);
+// Projections of 1 or 2 tokens with f32 activations (lc_gemv.cu): up to
+// kGroupMax weight matrices of one format and one k sharing the activations
+// (src.x, or SiLU(src.x) * src.x2 for LC_PACK_SWIGLU), rows streamed from HBM
+// once.  LC_ERR_UNSUPPORTED when the shape is not covered (gemv_rows_covers).
+bool gemv_rows_covers(const lc_ctx *ctx, int dtype, uint32_t m, uint32_t k);
+int gemv_rows(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *outs, int ng, uint32_t m, uint32_t k);
 // True when a projection of m rows would run the tcgen05 GEMM (gemm_dq).
 bool routes_to_gemm_dq(const lc_ctx *ctx, uint32_t m);
 // 3..16-token projections on tcgen05 kind::i8 (lc_gemm.cu); LC_ERR_UNSUPPORTED when

@@ -252,7 +252,7 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ src, size_t nbytes, i
             }
             break;
         }
-        case LC_Q4_K: {  // proj_q4k.comp:134-154 (GGUF Q4_K, shader formula)
+        case LC_Q4_K: {  // proj_q4k.comp:67-87 (GGUF Q4_K, shader formula)
             size_t b = i / 256, base = b * 144;
             if (base + 144 <= nbytes) {
                 const uint8_t *p = src + base;

@@ -1,6 +1,6 @@
 // lc_proj.cu -- fused GGUF dequant + projection (GEMV / small-M GEMM).
 //
-// Reference: kernels/proj_q4k.comp:127-159, kernels/proj_q8_0.comp:47-67 and
+// Reference: kernels/proj_q4k.comp:60-92, kernels/proj_q8_0.comp:47-67 and
 // kernels/proj.comp:23-33 compute c[i] = sum_j x[j] * w(i, j) one output per
 // invocation with a serial K loop.  Here each warp owns a 16-row tile of W and
 // streams its raw blocks from HBM exactly once; the dot products run on the
@@ -236,7 +236,7 @@ __device__ __forceinline__ void q4k_unit(const Q4Unit &U, const uint2 *tb, int l
     const float dg = lc_half_to_f32(U.H0.x & 0xFFFFu, half_mode), dmg = lc_half_to_f32(U.H0.x >> 16, half_mode);
     const float dg8 = lc_half_to_f32(U.H1.x & 0xFFFFu, half_mode), dmg8 = lc_half_to_f32(U.H1.x >> 16, half_mode);
 
-    // Scales of this thread's sub-blocks (get_scale_min_k4, proj_q4k.comp:113-125):
+    // Scales of this thread's sub-blocks (get_scale_min_k4, proj_q4k.comp:46-58):
     // lo0 = 2p0, hi0 = 2p0+1 (j < 4); lo1 = 2p0+4, hi1 = 2p0+5 (j >= 4).
     __half2 mul[2][4], add[2][4];  // [row g / g+8][lo0, hi0, lo1, hi1]
     uint32_t mpk[2];
@@ -1571,8 +1571,18 @@ int proj_q4k(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m, 
                expert_offset);
     LC_REQUIRE(((uintptr_t)wv & 15) == 0, LC_ERR_INVALID, "proj_q4k: weight pointer not 16-byte aligned");
     const uint8_t *w = (const uint8_t *)wv + (size_t)(expert_offset / 256) * 144;
-    // 1-2 tokens: the TMA GEMV; 3-8: the int8 tcgen05 GEMV; 9-32: the f16 tcgen05
-    // GEMM; more: the lm_head tiles
+    // 1-2 tokens: the f32-activation row GEMV (lc_gemv.cu); 3-8: the int8 tcgen05
+    // GEMV; 9-32: the f16 tcgen05 GEMM; more: the lm_head tiles
+    if (m <= 2 && gemv_rows_covers(ctx, LC_Q4_K, m, k)) {
+        PackSrc src;
+        src.x = x;
+        ProjOut o;
+        o.w = w;
+        o.y = c;
+        o.n = n;
+        const int s = gemv_rows(ctx, LC_Q4_K, src, &o, 1, m, k);
+        if (s != LC_ERR_UNSUPPORTED) return s;
+    }
     if (ctx->gemm_tc && (int)m >= ctx->gemv_i8_min && (int)m <= ctx->gemv_i8_max) {
         const int s = gemv_i8(ctx, LC_Q4_K, x, w, c, m, k, n);
         if (s != LC_ERR_UNSUPPORTED) return s;
@@ -1630,6 +1640,16 @@ int proj_q8_0(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m,
         return LC_OK;
     }
     const int nblk = k / 32;
+    if (m == 1 && gemv_rows_covers(ctx, LC_Q8_0, m, k)) {  // as proj_q4k
+        PackSrc src;
+        src.x = x;
+        ProjOut o;
+        o.w = w;
+        o.y = c;
+        o.n = n;
+        const int s = gemv_rows(ctx, LC_Q8_0, src, &o, 1, m, k);
+        if (s != LC_ERR_UNSUPPORTED) return s;
+    }
     if (ctx->gemm_tc && (int)m >= ctx->gemv_i8_min && (int)m <= ctx->gemv_i8_max) {  // as proj_q4k
         const int s = gemv_i8(ctx, LC_Q8_0, x, w, c, m, k, n);
         if (s != LC_ERR_UNSUPPORTED) return s;
@@ -1762,42 +1782,32 @@ extern "C" int lc_proj_m(lc_ctx *ctx, int dtype, const float *x, const void *w, 
 // or a latency-bound decode loop that must not pay cudaMalloc's implicit
 // device-wide synchronisation, which stalls every other stream on the GPU.
 // This entry point takes that scratch from a fixed static device array
-// instead; for m <= 4 it runs the cluster GEMV, which needs no scratch.
+// instead; for m <= 2 it runs the f32-activation row GEMV and for m = 3, 4 the
+// cluster GEMV, neither of which needs scratch.
 //
-// Limits: m in 1..16 tokens; for m <= 4 the activation table of m * k must fit
-// in shared memory; for m > 4 the packed activations of m * k must fit in the
-// array (k <= 15360 at m = 16).  Nothing in the array needs to start at zero:
-// each call writes the part it reads.  Calls that overlap on the GPU (two
+// Limits: m in 1..16 tokens; for m = 3, 4 the activation table of m * k must
+// fit in shared memory; for m > 4 the packed activations of m * k must fit in
+// the array (k <= 15360 at m = 16).  Nothing in the array needs to start at
+// zero: each call writes the part it reads.  Calls that overlap on the GPU (two
 // streams, or two contexts on one device) share the array and race; callers
 // serialise them.
+//
+// The array's device address is resolved once per context, at lc_init, with
+// the context's device current (lc_static_pack_resolve); host code never uses
+// the symbol itself, which on the host names a host-side stand-in.
 
 constexpr size_t kStaticPackBytes = (size_t)1 << 20;
 
 static __device__ __align__(256) unsigned char g_static_pack[kStaticPackBytes];
 
-namespace {
-
-std::mutex g_static_mu;
-void *g_static_ptr[64];  // per device ordinal, set up once with that device current
-
-// Set-up on the first call per device: resolve the array's device address.
-// That first call should come before any stream capture on the device.
-int static_pack_ptr(lc_ctx *ctx, void **out) {
-    LC_REQUIRE(ctx->device >= 0 && ctx->device < 64, LC_ERR_INVALID, "static scratch: device %d out of range",
-               ctx->device);
-    std::lock_guard<std::mutex> lk(g_static_mu);
-    if (!g_static_ptr[ctx->device]) {
-        void *p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_pack);
-        LC_REQUIRE(e == cudaSuccess && p, LC_ERR_CUDA, "static scratch: cudaGetSymbolAddress failed: %s",
-                   cudaGetErrorString(e));
-        g_static_ptr[ctx->device] = p;
-    }
-    *out = g_static_ptr[ctx->device];
+int lc_static_pack_resolve(lc_ctx *ctx) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_pack);
+    LC_REQUIRE(e == cudaSuccess && p, LC_ERR_CUDA, "static scratch: cudaGetSymbolAddress failed: %s",
+               cudaGetErrorString(e));
+    ctx->static_pack = p;
     return LC_OK;
 }
-
-}  // namespace
 
 extern "C" int lc_proj_q4k_static(lc_ctx *ctx, const float *x, const void *wv, float *c, uint32_t m, uint32_t k,
                                   uint32_t n, uint32_t expert_offset) {
@@ -1810,10 +1820,21 @@ extern "C" int lc_proj_q4k_static(lc_ctx *ctx, const float *x, const void *wv, f
     LC_REQUIRE(expert_offset % 256 == 0, LC_ERR_UNSUPPORTED,
                "lc_proj_q4k_static: expert_offset=%u not a multiple of 256", expert_offset);
     LC_REQUIRE(((uintptr_t)wv & 15) == 0, LC_ERR_INVALID, "lc_proj_q4k_static: weight pointer not 16-byte aligned");
+    LC_REQUIRE(ctx->static_pack, LC_ERR_INVALID, "lc_proj_q4k_static: context has no static scratch address");
     int s = lc_use_device(ctx);
     if (s) return s;
     const uint8_t *w = (const uint8_t *)wv + (size_t)(expert_offset / 256) * 144;
-    if (m <= 4) {
+    s = LC_ERR_UNSUPPORTED;
+    if (m <= 2 && lc::gemv_rows_covers(ctx, LC_Q4_K, m, k)) {
+        lc::PackSrc src;
+        src.x = x;
+        lc::ProjOut o;
+        o.w = w, o.y = c, o.n = n;
+        s = lc::gemv_rows(ctx, LC_Q4_K, src, &o, 1, m, k);
+    }
+    if (s != LC_ERR_UNSUPPORTED) {
+        // the row GEMV ran (or failed)
+    } else if (m <= 4) {
         const TmaPlan p = q4k_tma_plan(ctx, (int)m, (int)k, (int)n);
         LC_REQUIRE(p.R, LC_ERR_UNSUPPORTED,
                    "lc_proj_q4k_static: m*k=%u*%u activations exceed shared memory (%zu of %zu bytes)", m, k,
@@ -1824,10 +1845,7 @@ extern "C" int lc_proj_q4k_static(lc_ctx *ctx, const float *x, const void *wv, f
         LC_REQUIRE(need <= kStaticPackBytes, LC_ERR_UNSUPPORTED,
                    "lc_proj_q4k_static: packed activations of m*k=%u*%u need %zu bytes, the static scratch has %zu", m,
                    k, need, kStaticPackBytes);
-        void *pack = nullptr;
-        s = static_pack_ptr(ctx, &pack);
-        if (s) return s;
-        s = lc::proj_q4k_tiled(ctx, x, w, c, m, k, n, pack);
+        s = lc::proj_q4k_tiled(ctx, x, w, c, m, k, n, ctx->static_pack);
     }
     if (s) return s;
     return lc_after_launch(ctx, "lc_proj_q4k_static");

@@ -70,7 +70,22 @@ extern "C" int lc_init(int device, lc_ctx **out) {
         delete ctx;
         return lc_fail(LC_ERR_CUDA, "lc_init: status word: %s", cudaGetErrorString(e));
     }
+    const int sp = lc_static_pack_resolve(ctx);
+    if (sp) {
+        cudaFree(ctx->dev_status);
+        cudaStreamDestroy(ctx->own_stream);
+        delete ctx;
+        return sp;
+    }
     *out = ctx;
+    return LC_OK;
+}
+
+extern "C" int lc_ctx_scratch_bytes(lc_ctx *ctx, size_t *bytes) {
+    LC_REQUIRE(ctx && bytes, LC_ERR_INVALID, "lc_ctx_scratch_bytes: null argument");
+    size_t t = 0;
+    for (int i = 0; i < LC_SCRATCH_COUNT; i++) t += ctx->scratch_bytes[i];
+    *bytes = t;
     return LC_OK;
 }
 

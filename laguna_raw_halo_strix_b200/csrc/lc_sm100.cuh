@@ -286,4 +286,41 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared by this thread (cp.async through
+// L2 only); completes in the thread's current group.
+__device__ __forceinline__ void cp_async16_l2(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+// Close the thread's current group of cp.async copies.
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+// Wait until at most N of the thread's groups are still in flight.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// Named barrier `id` (1..15) over `nthreads` threads (a multiple of 32); the
+// id is an immediate in every form issued.
+__device__ __forceinline__ void named_barrier_sync_id(int id, int nthreads) {
+    switch (id) {
+#define LC_NAMED_BAR(N) \
+    case N: asm volatile("bar.sync " #N ", %0;\n" ::"r"(nthreads) : "memory"); break;
+        LC_NAMED_BAR(1) LC_NAMED_BAR(2) LC_NAMED_BAR(3) LC_NAMED_BAR(4) LC_NAMED_BAR(5)
+        LC_NAMED_BAR(6) LC_NAMED_BAR(7) LC_NAMED_BAR(8) LC_NAMED_BAR(9) LC_NAMED_BAR(10)
+        LC_NAMED_BAR(11) LC_NAMED_BAR(12) LC_NAMED_BAR(13) LC_NAMED_BAR(14) LC_NAMED_BAR(15)
+#undef LC_NAMED_BAR
+        default: break;
+    }
+}
+
+// Same, without an L2 hint (for data many CTAs read).
+__device__ __forceinline__ void bulk_load_plain(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
 }  // namespace

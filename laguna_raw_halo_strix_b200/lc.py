@@ -69,6 +69,7 @@ SIGNATURES = {
     "lc_set_sync": (_i, [_vp, _i]),
     "lc_set_half_mode": (_i, [_vp, _i]),
     "lc_ctx_device": (_i, [_vp, C.POINTER(_i)]),
+    "lc_ctx_scratch_bytes": (_i, [_vp, C.POINTER(_sz)]),
     "lc_buf_alloc": (_i, [_vp, _sz, C.POINTER(_vp)]),
     "lc_buf_free": (_i, [_vp]),
     "lc_buf_device_ptr": (_vp, [_vp]),
@@ -84,6 +85,7 @@ SIGNATURES = {
     "lc_device_status": (_i, [_vp]),
     "lc_proj_m": (_i, [_vp, _i, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
     "lc_proj_q4k_static": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
+    "lc_ffn": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32]),
     "lc_dequant": (_i, [_vp, _i, _vp, _sz, _sz, _vp]),
     "lc_rmsnorm": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _f]),
     "lc_qk_norm_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _f, _u32]),
@@ -263,9 +265,18 @@ class Context:
     def proj_m(self, dtype, x, w, c, m, k, n, expert_offset=0):
         check(self.L.lc_proj_m(self.h, dtype, ptr(x), ptr(w), ptr(c), m, k, n, expert_offset), "lc_proj_m")
 
+    def scratch_bytes(self) -> int:
+        v = _sz(0)
+        check(self.L.lc_ctx_scratch_bytes(self.h, C.byref(v)), "lc_ctx_scratch_bytes")
+        return int(v.value)
+
     def proj_q4k_static(self, x, w, c, m, k, n, expert_offset=0):
         check(self.L.lc_proj_q4k_static(self.h, ptr(x), ptr(w), ptr(c), m, k, n, expert_offset),
               "lc_proj_q4k_static")
+
+    def ffn(self, dtype, x, w_gate, w_up, w_down, y, m, n_embd, n_ff):
+        check(self.L.lc_ffn(self.h, dtype, ptr(x), ptr(w_gate), ptr(w_up), ptr(w_down), ptr(y), m, n_embd, n_ff),
+              "lc_ffn")
 
     def dequant(self, dtype, src, src_bytes, n, out):
         check(self.L.lc_dequant(self.h, dtype, ptr(src), src_bytes, n, ptr(out)), "lc_dequant")

@@ -5,7 +5,7 @@ Q8_0 block (34 B, 32 elements; src/gguf.rs:97,134): f16 d = |N(0,1)|*0.02/127,
 int8 q uniform in [-127, 127].
 Q4_K super-block (144 B, 256 elements; src/gguf.rs:101,136): f16 d, dmin =
 |N(0,1)|*1e-3; eight 6-bit (scale, min) pairs uniform in 0..63 packed into 12
-bytes the way kernels/proj_q4k.comp:113-125 (get_scale_min_k4) unpacks them;
+bytes the way kernels/proj_q4k.comp:46-58 (get_scale_min_k4) unpacks them;
 128 bytes of nibbles uniform in 0..15.
 """
 from __future__ import annotations

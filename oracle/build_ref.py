@@ -21,7 +21,8 @@ uint32_t invocations)` entry that binds the buffers and push block, then runs
 invocations 0..invocations-1 (OpenMP over invocations, as on the GPU every
 invocation is independent).
 
-Usage: python oracle/build_ref.py [--reference DIR]   (default /root/reference)
+Usage: python oracle/build_ref.py [--reference DIR]   (default: $LAGUNA_REFERENCE, else
+       a directory named `reference` beside the repository root)
 """
 from __future__ import annotations
 
@@ -104,7 +105,12 @@ def translate(name: str, src: str) -> str:
     return "\n".join(lines) + "\n"
 
 
-def build(reference: str = "/root/reference", cxx: str = "g++", verbose: bool = False) -> str:
+def _default_tree() -> str:
+    here = os.path.dirname(os.path.abspath(__file__))
+    return os.environ.get("LAGUNA_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(here)), "reference")
+
+
+def build(reference: str, cxx: str = "g++", verbose: bool = False) -> str:
     kdir = os.path.join(reference, "kernels")
     if not os.path.isdir(kdir):
         raise FileNotFoundError(f"reference shaders not found under {kdir}")
@@ -133,11 +139,11 @@ def build(reference: str = "/root/reference", cxx: str = "g++", verbose: bool = 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("LAGUNA_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=None)
     ap.add_argument("--cxx", default="g++")
     a = ap.parse_args()
     try:
-        build(a.reference, a.cxx, verbose=True)
+        build(a.reference or _default_tree(), a.cxx, verbose=True)
     except Exception as e:  # noqa: BLE001
         print(f"build_ref: {e}", file=sys.stderr)
         sys.exit(1)

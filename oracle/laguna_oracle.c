@@ -159,7 +159,7 @@ float lco_q8_0_weight(const uint8_t *w, uint32_t lin) {
     return (float)q * d;
 }
 
-/* proj_q4k.comp:113-125 get_scale_min_k4. */
+/* proj_q4k.comp:46-58 get_scale_min_k4. */
 static inline void scale_min_k4(uint32_t j, const uint8_t *q, uint32_t *d, uint32_t *m) {
     uint32_t b0 = q[j];
     uint32_t b4 = q[4u + (j & 3u)];
@@ -174,7 +174,7 @@ static inline void scale_min_k4(uint32_t j, const uint8_t *q, uint32_t *d, uint3
     }
 }
 
-/* proj_q4k.comp:134-154: 144-B super-block, d/dmin f16 at 0/2, scales at 4,
+/* proj_q4k.comp:67-87: 144-B super-block, d/dmin f16 at 0/2, scales at 4,
  * nibbles at 16 + (e/64)*32 + e%32 (low nibble when e%64 < 32). */
 float lco_q4k_weight(const uint8_t *w, uint32_t lin) {
     uint32_t blk = lin / 256u, elm = lin % 256u;

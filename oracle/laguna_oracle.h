@@ -56,7 +56,7 @@ void lco_dequant_to_f32(const uint8_t *data, size_t nbytes, int dtype,
                         size_t n_elements, float *out);
 
 /* Per-element weight decode of the GPU shaders: element `lin` of a Q8_0 tensor
- * (proj_q8_0.comp:54-63) and of a GGUF Q4_K tensor (proj_q4k.comp:134-154). */
+ * (proj_q8_0.comp:54-63) and of a GGUF Q4_K tensor (proj_q4k.comp:67-87). */
 float lco_q8_0_weight(const uint8_t *w, uint32_t lin);
 float lco_q4k_weight(const uint8_t *w, uint32_t lin);
 /* Dequantize n elements starting at element 0 with the shader formulas. */
@@ -70,7 +70,7 @@ void lco_proj_f32(const float *x, const float *w, float *c, uint32_t k,
 /* kernels/proj_q8_0.comp:47-67. */
 void lco_proj_q8_0(const float *x, const uint8_t *w, float *c, uint32_t k,
                    uint32_t n);
-/* kernels/proj_q4k.comp:127-159 (lin = expert_offset + i*k + j). */
+/* kernels/proj_q4k.comp:60-92 (lin = expert_offset + i*k + j). */
 void lco_proj_q4k(const float *x, const uint8_t *w, float *c, uint32_t k,
                   uint32_t n, uint32_t expert_offset);
 /* M-row forms: the single-row shader applied to each of m rows of x

@@ -45,8 +45,15 @@ def build_oracle() -> str:
     return ORACLE_LIB
 
 
-def build_ref(reference: str = "/root/reference") -> str | None:
+def reference_tree() -> str:
+    """Where the reference source tree is read from: $LAGUNA_REFERENCE, else a
+    directory named `reference` beside this repository's root."""
+    return os.environ.get("LAGUNA_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+
+
+def build_ref(reference: str | None = None) -> str | None:
     """Build oracle/_ref when the reference tree exists; return its path or None."""
+    reference = reference or reference_tree()
     if os.path.exists(REF_LIB):
         return REF_LIB
     if not os.path.isdir(os.path.join(reference, "kernels")):

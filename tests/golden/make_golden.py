@@ -40,7 +40,7 @@ def f32b(v):
 
 
 def main():
-    ref = orc.RefShaders(build(os.environ.get("LAGUNA_REFERENCE", "/root/reference")))
+    ref = orc.RefShaders(build(orc.reference_tree()))
     G = orc.RefShaders.groups
 
     # ---- projections --------------------------------------------------------
