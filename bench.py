@@ -2,18 +2,24 @@
 """Benchmark of the quantized projection hot path (BASELINE metric:
 "Q4_K/Q8_0 GEMV HBM GB/s (% of peak); DFlash 16-token draft-block fwd/s").
 
-Default workload (the M = 1 Q4_K GEMV): one step is the
-DFlash decoder FFN of one token -- gate 4096->14336, up 4096->14336 (Q4_K),
-SiLU-gate, down 14336->4096 (Q4_K) -- through the C ABI (liblaguna_cuda.so).
-Weights are raw Q4_K super-blocks rotated through a pool larger than 3x the
-126 MB L2, so every step streams its 99 MB of weights from HBM.
+With no --workload the run covers every BASELINE config and prints one JSON
+line per config, the headline (config 1) last:
+  gemv_q8_0     config 0: Q8_0 4096x4096 GEMV, one token
+  ffn_q4k_m16   config 2: the DFlash FFN (gate/up 4096->14336, down 14336->4096) for 16 tokens
+  dflash_block  config 3: the 6-layer DFlash decoder, one 16-token block over 2048 context rows
+  lm_head_q8_0  config 4: lm_head Q8_0 4096->128256 for 1024 rows with the argmax
+                (vocab-sharded over the ranks, MAX all-reduce of the keys)
+  ffn_q4k_m1    config 1: the DFlash FFN for one token (the headline)
+Each step goes through the C ABI (liblaguna_cuda.so); weights are raw GGUF
+blocks rotated through a pool larger than 3x the 126 MB L2, so every step
+streams its weights from HBM.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
   python bench.py --impl reference ...   # the reference's own shader code on host cores
 
-Multi-GPU (torchrun, one rank per GPU): each rank runs an independent token
-stream on its own weights (replicas, no collective on the data path);
-value = all ranks' bytes / max-over-ranks time ("scaling": "weak").
+Multi-GPU (torchrun, one rank per GPU): configs 0-3 run independent token
+streams on every rank (replicas, no collective on the data path;
+"scaling": "weak"); config 4 shards the vocab rows ("scaling": "strong").
 """
 from __future__ import annotations
 
@@ -37,14 +43,38 @@ L2_BYTES = 126 * 1024 * 1024
 METRIC = "Q4_K/Q8_0 GEMV HBM GB/s (% of peak); DFlash 16-token draft-block fwd/s"
 
 
-def _traffic(workload):
+def _traffic(workload, kernel):
     """DRAM bytes (read + write) of one launch of the workload's dominant kernel,
-    from the ncu capture summarised in profiles/ (None if not recorded)."""
+    from the ncu capture summarised in profiles/ -- only when that capture was
+    of the same kernel (None otherwise)."""
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            return json.load(f).get(workload)
+            rec = json.load(f).get(workload)
     except Exception:
         return None
+    if isinstance(rec, dict) and rec.get("kernel") == kernel:
+        return rec.get("traffic")
+    return None
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def set_host_threads(n):
+    """OpenMP threads of the CPU baselines: torchrun sets OMP_NUM_THREADS=1, so
+    the count is set explicitly (env for libraries not loaded yet, and the
+    runtime call for an OpenMP runtime already loaded)."""
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    try:
+        import ctypes
+
+        ctypes.CDLL("libgomp.so.1").omp_set_num_threads(int(n))
+    except Exception:
+        pass
 
 
 def peaks():
@@ -65,7 +95,7 @@ WORKLOADS = {
                                                   ("down", 14336, 4096)], ffn=True, config=1),
     # config 0: Q8_0 4096x4096 GEMV
     "gemv_q8_0": dict(dtype="q8_0", m=1, shapes=[("w", 4096, 4096)], ffn=False, config=0),
-    # config 2: M=16 draft block through the same FFN projections
+    # config 2: M=16 draft block through the same FFN projections (one lc_ffn call per step)
     "ffn_q4k_m16": dict(dtype="q4k", m=16, shapes=[("gate", 4096, 14336), ("up", 4096, 14336),
                                                     ("down", 14336, 4096)], ffn=True, config=2),
 }
@@ -210,7 +240,7 @@ class CpuReference:
         self.orc, self.wl = orc, wl
         self.dtype = orc.Q4_K if wl["dtype"] == "q4k" else orc.Q8_0
         self.ref = orc.RefShaders() if os.path.exists(orc.REF_LIB) else None
-        self.port = orc.Oracle()
+        self.port = orc.Oracle(threads=host_threads())
         self.cores = self.port.lib.lco_get_threads()
         self.kind = "reference" if self.ref is not None else "port"
         self.w = {nm: synth.weight_blocks(self.dtype, n, k, rng) for nm, k, n in wl["shapes"]}
@@ -293,7 +323,8 @@ def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    wl = WORKLOADS[args.workload]
+    set_host_threads(host_threads())
+    wl = WORKLOADS[args.workload if args.workload in WORKLOADS else "ffn_q4k_m1"]
     cr = CpuReference(wl, np.random.default_rng(0))
     # each step: the workload's step, sampled to the rows that keep the whole
     # run near 2 minutes of CPU time
@@ -317,7 +348,8 @@ def run_reference_arm(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
-        "config": dict(workload_config(args.workload, wl), parallelism="host cores (rank 0 only)"),
+        "config": dict(workload_config(args.workload if args.workload in WORKLOADS else "ffn_q4k_m1", wl),
+                       parallelism="host cores (rank 0 only)"),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -326,7 +358,10 @@ def run_reference_arm(args):
 
 
 # ---------------------------------------------------------------------------
-# Shared plumbing of the special workloads.
+# Shared plumbing.
+_PG = {"init": False}
+
+
 def _dist_init():
     import torch
     import torch.distributed as dist
@@ -334,11 +369,12 @@ def _dist_init():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
+    if world > 1 and not _PG["init"]:
         from datetime import timedelta
 
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+        _PG["init"] = True
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     return world, rank, local_rank, dev
@@ -352,6 +388,13 @@ def _max_over_ranks(v, dev, world):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
 
 
 def _graph_kernel_nodes(g):
@@ -394,7 +437,229 @@ def _emit(line):
     print(json.dumps(line), flush=True)
 
 
+def _timed_graph(g, stream, dev, world, rank):
+    """Replay g once between barriers and synchronisation with CUDA events on
+    its stream and the clocks sampled; returns (max-over-ranks ms, clocks)."""
+    import torch
+
+    _barrier(world)
+    sampler = ClockSampler(dev) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    torch.cuda.synchronize(dev)
+    _barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.mark_begin()
+    e0.record(stream)
+    g.replay()
+    e1.record(stream)
+    stream.synchronize()
+    if sampler:
+        sampler.mark_end()
+    torch.cuda.synchronize(dev)
+    _barrier(world)
+    ms = _max_over_ranks(e0.elapsed_time(e1), dev, world)
+    return ms, (sampler.stop() if sampler else None)
+
+
 # ---------------------------------------------------------------------------
+def _kernel_name(wl):
+    m, q4 = wl["m"], wl["dtype"] == "q4k"
+    if m <= 2:
+        return "gemv_rows_kernel<Q4Lane<%d>>" % m if q4 else "gemv_rows_kernel<Q8Lane>"
+    if m <= 32:
+        return "x16_pack_kernel + dq_gemm_kernel"
+    return "lmh_pack_kernel + lmh_kernel"
+
+
+def _dtype_label(wl):
+    m, w = wl["m"], ("q4k" if wl["dtype"] == "q4k" else "q8_0")
+    if m <= 2:
+        return w + "*f32 (f32 activations, f32 FMA accumulate)"
+    if m <= 32:
+        return w + "*f16x2 (activations as f16 hi+lo, ~22 bits; tcgen05 f32 accumulate)"
+    return w + "*f16 (activations as one f16 after a power-of-two scale; tcgen05 f32 accumulate)"
+
+
+def run_projection(args, name):
+    """BASELINE configs 0, 1 and 2: projections of m tokens; the FFN workloads
+    run the decoder FFN block (gate, up, SiLU-gate, down) as one lc_ffn call."""
+    import torch
+
+    from laguna_raw_halo_strix_b200 import lc, synth
+
+    world, rank, local_rank, dev = _dist_init()
+    stream = torch.cuda.Stream(dev)
+    ctx = lc.Context(local_rank)
+    ctx.set_stream(stream)
+
+    wl = WORKLOADS[name]
+    dtype = lc.Q4_K if wl["dtype"] == "q4k" else lc.Q8_0
+    m = wl["m"]
+    rng = np.random.default_rng(1000 + rank)
+
+    # weight sets rotated through a pool > 3x L2
+    set_bytes = sum(weight_bytes(wl["dtype"], k, n) for _, k, n in wl["shapes"])
+    pool = max(2, -(-3 * L2_BYTES // set_bytes))
+    base = {nm: torch.from_numpy(synth.weight_blocks(dtype, n, k, rng)).to(dev) for nm, k, n in wl["shapes"]}
+    weights = []
+    for p in range(pool):
+        # distinct bytes per pool entry (flip nibbles / ints deterministically; scales stay finite)
+        weights.append({nm: (t if p == 0 else t ^ torch.tensor(p * 37 % 255, dtype=torch.uint8, device=dev))
+                        for nm, t in base.items()})
+    k0 = wl["shapes"][0][1]
+    x = torch.from_numpy(synth.activations(m, k0, rng)).to(dev)
+    bufs = {nm: torch.empty(m, n, device=dev) for nm, k, n in wl["shapes"]}
+    out_name = wl["shapes"][-1][0]
+
+    def step(i):
+        ws = weights[i % pool]
+        if wl["ffn"]:
+            (_, kg, ng), _, (_, kd, nd) = wl["shapes"]
+            ctx.ffn(dtype, x, ws["gate"], ws["up"], ws["down"], bufs["down"], m, kg, ng)
+        else:
+            for nm, k, n in wl["shapes"]:
+                ctx.proj_m(dtype, x, ws[nm], bufs[nm], m, k, n)
+
+    # the dominant kernel alone: the first projection shape, its weights rotated
+    # through their own pool > 3x L2
+    dname, dk, dn = wl["shapes"][0]
+    dbytes = weight_bytes(wl["dtype"], dk, dn)
+    dpool = max(2, -(-3 * L2_BYTES // dbytes))
+    dweights = [weights[p % pool][dname] if p < pool else
+                weights[0][dname] ^ torch.tensor((p * 53 + 11) % 255, dtype=torch.uint8, device=dev)
+                for p in range(dpool)]
+    dx = torch.from_numpy(synth.activations(m, dk, rng)).to(dev)
+    dy = torch.empty(m, dn, device=dev)
+
+    def dominant(i):
+        ctx.proj_m(dtype, dx, dweights[i % dpool], dy, m, dk, dn)
+
+    n_dom = max(args.steps, 3 * dpool)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):  # eager warm-up: sizes scratch, sets kernel attributes
+            step(i)
+            dominant(i)
+        stream.synchronize()
+        g_steps = torch.cuda.CUDAGraph(keep_graph=True)
+        with torch.cuda.graph(g_steps, stream=stream):
+            for i in range(args.steps):
+                step(args.warmup + i)
+        g_dom = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_dom, stream=stream):
+            for i in range(n_dom):
+                dominant(i)
+        g_steps.replay()
+        g_dom.replay()
+        stream.synchronize()
+        launches = _graph_kernel_nodes(g_steps)
+        ms, clocks = _timed_graph(g_steps, stream, dev, world, rank)
+        d0 = torch.cuda.Event(enable_timing=True)
+        d1 = torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        g_dom.replay()
+        d1.record(stream)
+        stream.synchronize()
+        per_launch_ms = d0.elapsed_time(d1) / n_dom
+        del g_steps, g_dom
+
+        # e2e: the input copied from pinned host memory and the result read back
+        # every step, eager calls through the C ABI, one host sync per step
+        x_host = torch.from_numpy(synth.activations(m, k0, rng)).pin_memory()
+        y_host = torch.empty(bufs[out_name].shape, dtype=torch.float32).pin_memory()
+        e2e_steps = max(10, args.steps // 2)
+        for i in range(3):
+            x.copy_(x_host, non_blocking=True)
+            step(i)
+            y_host.copy_(bufs[out_name], non_blocking=True)
+            stream.synchronize()
+        _barrier(world)
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            x.copy_(x_host, non_blocking=True)
+            step(i)
+            y_host.copy_(bufs[out_name], non_blocking=True)
+            stream.synchronize()
+        e2e_s = _max_over_ranks(time.perf_counter() - t0, dev, world)
+
+    sb = step_bytes(wl)
+    value = world * sb * args.steps / (ms / 1e3) / 1e9
+    e2e_value = world * sb * e2e_steps / e2e_s / 1e9
+    hbm, tflops, peak_src = peaks()
+    lb = dbytes + 4 * m * (dk + dn)
+    achieved = lb / (per_launch_ms / 1e3) / 1e9
+    kernel = _kernel_name(wl)
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            v, kind, cores, sample = cpu_baseline(wl, 10.0, np.random.default_rng(7))
+            cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample}
+        _emit({
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": _dtype_label(wl),
+            "data": "synthetic (seeded; BASELINE block/activation distributions)",
+            "config": dict(workload_config(name, wl),
+                           step=("lc_ffn: gate+up grouped, SiLU-gate fused into down" if wl["ffn"] else
+                                 "lc_proj_m per projection"),
+                           l2=f"weights rotated through {pool} sets of {set_bytes / 1e6:.1f} MB (> 3x the 126 MB L2)",
+                           parallelism=f"replicas x{world} (independent token streams, no collective)"),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "peak_source": peak_src, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": _traffic(name, kernel), "kernel": kernel,
+                         "dominant": f"{dname} {dk}->{dn}, weights rotated through {dpool} copies "
+                                     f"({dpool * dbytes / 1e6:.0f} MB, > 3x L2)",
+                         "per_launch_us": per_launch_ms * 1e3, "bytes_per_launch": lb},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": int(x_host.numel() * 4),
+                    "d2h_bytes_per_step": int(y_host.numel() * 4), "steps": e2e_steps},
+            "clocks": clocks, "gpu_launches": None if launches is None else launches,
+        })
+    ctx.close()
+    return 0
+
+
+# ---------------------------------------------------------------------------
+def lm_head_cpu_baseline(m, k, vocab, seconds, rng):
+    """The reference's lm_head (target.rs:580-605: the Q8_0 projection shader
+    per hidden row) and argmax on the host cores, on a sample of token rows and
+    vocab rows, extrapolated to the full step; GB/s of the step's bytes."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    from laguna_raw_halo_strix_b200 import synth
+
+    o = orc.Oracle(threads=host_threads())
+    ref = orc.RefShaders() if os.path.exists(orc.REF_LIB) else None
+    rows, toks = min(vocab, 16384), 4
+    w = synth.q8_0_blocks(rows, k, rng)
+    wp = orc.pad4(w) if ref is not None else None
+    x = synth.activations(toks, k, rng)
+    t0 = time.perf_counter()
+    passes = 0
+    while True:
+        for r in range(toks):
+            c = np.zeros(rows, np.float32)
+            if ref is not None:
+                ref.run("proj_q8_0", [np.ascontiguousarray(x[r]), wp, c],
+                        np.array([k, rows], np.uint32).tobytes(), orc.RefShaders.groups(rows))
+            else:
+                c = o.proj(orc.Q8_0, x[r:r + 1], w, k, rows)[0]
+            o.argmax(c)
+        passes += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    t = (time.perf_counter() - t0) / passes
+    step_s = t * (m / toks) * (vocab / rows)
+    step_b = vocab * (k // 32) * 34 + 4 * m * k
+    kind = "reference" if ref is not None else "port"
+    sample = (f"{toks} token rows x {rows} vocab rows per pass ({passes} passes, {t * 1e3:.0f} ms each), "
+              f"extrapolated to {m} rows x {vocab} vocab rows; "
+              + ("reference GLSL proj_q8_0 compiled for the CPU (oracle/_ref)" if ref is not None else
+                 "C restatement (oracle/)") + " + argmax")
+    return step_b / step_s / 1e9, kind, o.lib.lco_get_threads(), sample
+
+
 def run_lm_head(args):
     """lm_head Q8_0 4096 -> 128256 for 1024 rows (16-token
     blocks x 64 sequences) fused with argmax.  The vocab rows are split into
@@ -402,7 +667,6 @@ def run_lm_head(args):
     int64 MAX all-reduce (NCCL) gives every rank the global draft tokens.
     Total work is fixed as ranks are added ("scaling": "strong")."""
     import torch
-    import torch.distributed as dist
 
     from laguna_raw_halo_strix_b200 import lc, synth
     from laguna_raw_halo_strix_b200.lm_head import ShardedLmHead
@@ -439,14 +703,12 @@ def run_lm_head(args):
         for i in range(args.warmup):
             step(i)
         stream.synchronize()
-        if world > 1:
-            dist.barrier()
+        _barrier(world)
         sampler = ClockSampler(dev) if rank == 0 else None
         if sampler:
             sampler.start()
         torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
+        _barrier(world)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         if sampler:
@@ -458,8 +720,7 @@ def run_lm_head(args):
         stream.synchronize()
         if sampler:
             sampler.mark_end()
-        if world > 1:
-            dist.barrier()
+        _barrier(world)
         ms = _max_over_ranks(e0.elapsed_time(e1), dev, world)
         clocks = sampler.stop() if sampler else None
         # local (kernel-only) time of one shard, for the roofline figure
@@ -482,8 +743,7 @@ def run_lm_head(args):
         x_host = torch.from_numpy(synth.activations(m, k, rng)).pin_memory()
         k_host = torch.empty(m, dtype=torch.int64).pin_memory()
         e2e_steps = max(3, min(args.steps, 20))
-        if world > 1:
-            dist.barrier()
+        _barrier(world)
         t0 = time.perf_counter()
         for i in range(e2e_steps):
             x.copy_(x_host, non_blocking=True)
@@ -499,11 +759,17 @@ def run_lm_head(args):
     local_b = shard_bytes + 4 * m * k
     local_f = 2.0 * m * k * head.n_local
     if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            v, kind, cores, sample = lm_head_cpu_baseline(m, k, vocab, 10.0, np.random.default_rng(8))
+            cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample}
+        kernel = "lmh_pack_kernel + lmh_kernel"
         _emit({
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "q8_0*f32", "data": "synthetic (seeded; BASELINE block/activation "
-                                                               "distributions)",
+            "vs_baseline": None,
+            "dtype": "q8_0*f16 (activations as one f16 after a per-row power of two; tcgen05 f32 accumulate)",
+            "data": "synthetic (seeded; BASELINE block/activation distributions)",
             "config": {"workload": "lm_head_q8_0", "baseline_config": LM_HEAD["config"], "m": m, "k": k,
                        "vocab": vocab, "rows_per_rank": head.n_local, "bytes_per_step": step_b,
                        "tokens_per_s": m * args.steps / (ms / 1e3),
@@ -512,22 +778,54 @@ def run_lm_head(args):
             # tensor-bound: 2 m k n_local useful flops per launch (the tcgen05 tiles)
             "roofline": {"bound": "tensor", "achieved": local_f / (local_ms / 1e3) / 1e12, "peak": tflops,
                          "peak_source": peak_src + " (dense bf16 burst)", "unit": "TFLOP/s",
-                         "frac": local_f / (local_ms / 1e3) / 1e12 / tflops, "traffic": _traffic("lm_head_q8_0"),
-                         "kernel": "lc_lm_head_argmax (one shard: packing + lmh_kernel)",
+                         "frac": local_f / (local_ms / 1e3) / 1e12 / tflops,
+                         "traffic": _traffic("lm_head_q8_0", kernel),
+                         "kernel": kernel + " (one shard)",
                          "per_launch_us": local_ms * 1e3, "flops_per_launch": local_f,
                          "hbm_gbs_per_launch": local_b / (local_ms / 1e3) / 1e9},
-            "cpu_baseline": None,
+            "cpu_baseline": cpu,
             "e2e": {"value": step_b * e2e_steps / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * m * k,
                     "d2h_bytes_per_step": 8 * m, "steps": e2e_steps},
             "clocks": clocks, "gpu_launches": None if per_step is None else per_step * args.steps,
         })
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    ctx.close()
     return 0
 
 
 # ---------------------------------------------------------------------------
+def dflash_cpu_baseline(seconds, rng):
+    """The reference's decoder op sequence (dflash.rs:877-976, restated over
+    the C kernels in oracle/dflash_oracle.py) on the host cores: one layer of
+    the config-3 decoder for a sample of the block's tokens over the full
+    context, extrapolated to the 6-layer 16-token block; forwards per second."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import dflash_oracle as dfo
+    import oracle as orc
+
+    hp = dict(DFLASH_HP, n_layers=1)
+    o = orc.Oracle(threads=host_threads())
+    t = dfo.make_model(hp, orc.Q4_K, rng)
+    model = dfo.DFlashOracle(hp, t, o)
+    E, KVD = hp["n_embd"], hp["n_kv_heads"] * hp["head_dim"]
+    kv = [(rng.standard_normal((DFLASH_CTX, KVD)).astype(np.float32),
+           rng.standard_normal((DFLASH_CTX, KVD)).astype(np.float32))]
+    toks = 2
+    x = rng.standard_normal((toks, E)).astype(np.float32)
+    t0 = time.perf_counter()
+    passes = 0
+    while True:
+        model.decode_block(x, kv)
+        passes += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    per = (time.perf_counter() - t0) / passes
+    fwd_s = per * DFLASH_HP["n_layers"] * (DFLASH_BLOCK / toks)
+    sample = (f"one decoder layer for {toks} block tokens over {DFLASH_CTX} context rows per pass ({passes} passes, "
+              f"{per:.2f} s each), extrapolated to {DFLASH_HP['n_layers']} layers x {DFLASH_BLOCK} tokens; "
+              "C restatement of the reference kernels (oracle/) in the dflash.rs op order")
+    return 1.0 / fwd_s, "port", o.lib.lco_get_threads(), sample
+
+
 def run_dflash(args):
     """the DFlash decoder (6 layers, hidden 4096, 32 Q / 8 KV
     heads of 128, FFN 14336, Q4_K projections) for one 16-token draft block over
@@ -535,7 +833,6 @@ def run_dflash(args):
     encoder prefill (fc 5x4096 -> 4096 over 2048 rows, context K/V) runs once
     and is timed apart.  Independent sequences on each rank ("scaling": "weak")."""
     import torch
-    import torch.distributed as dist
 
     from laguna_raw_halo_strix_b200 import lc, synth
     from laguna_raw_halo_strix_b200.model import DFlash, hparams
@@ -549,9 +846,9 @@ def run_dflash(args):
     model = DFlash(ctx, hparams(**hp), max_ctx=DFLASH_CTX, max_block=DFLASH_BLOCK)
     tensors = synth.dflash_tensors(hp, lc.Q4_K, rng, share=True)
     wbytes = 0
-    for name, (dt, a) in tensors.items():
-        model.set_tensor(name, dt, a)
-        if name.startswith("blk."):
+    for nm, (dt, a) in tensors.items():
+        model.set_tensor(nm, dt, a)
+        if nm.startswith("blk."):
             wbytes += a.nbytes
     E, A, M = hp["n_embd"], hp["n_aux"], DFLASH_BLOCK
     kvd = hp["n_kv_heads"] * hp["head_dim"]
@@ -579,33 +876,13 @@ def run_dflash(args):
         g.replay()
         stream.synchronize()
         launches = _graph_kernel_nodes(g)
-        if world > 1:
-            dist.barrier()
-        sampler = ClockSampler(dev) if rank == 0 else None
-        if sampler:
-            sampler.start()
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        if sampler:
-            sampler.mark_begin()
-        e0.record(stream)
-        g.replay()
-        e1.record(stream)
-        stream.synchronize()
-        if sampler:
-            sampler.mark_end()
-        ms = _max_over_ranks(e0.elapsed_time(e1), dev, world)
-        clocks = sampler.stop() if sampler else None
+        ms, clocks = _timed_graph(g, stream, dev, world, rank)
         del g
         # e2e: the block's token inputs from pinned host memory, hidden states back
         x_host = torch.from_numpy(rng.standard_normal((M, E)).astype(np.float32)).pin_memory()
         h_host = torch.empty(M, E).pin_memory()
         e2e_steps = max(5, min(args.steps, 50))
-        if world > 1:
-            dist.barrier()
+        _barrier(world)
         t0 = time.perf_counter()
         for i in range(e2e_steps):
             x.copy_(x_host, non_blocking=True)
@@ -621,10 +898,16 @@ def run_dflash(args):
     hbm, _, peak_src = peaks()
     per_fwd_s = ms / 1e3 / args.steps
     if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            v, kind, cores, sample = dflash_cpu_baseline(10.0, np.random.default_rng(9))
+            cpu = {"value": v, "unit": "fwd/s", "cores": cores, "kind": kind, "sample": sample}
         _emit({
             "metric": METRIC, "value": fwd_s, "unit": "fwd/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q4k*f32",
+            "vs_baseline": None,
+            "dtype": "q4k*f16x2 projections (activations as f16 hi+lo, ~22 bits; tcgen05 f32 accumulate), "
+                     "f32 element-wise ops, attention f16 hi/lo on tcgen05",
             "data": "synthetic (seeded; BASELINE distributions; one set of projection weights per shape, "
                     "uploaded separately for every layer)",
             "config": {"workload": "dflash_block", "baseline_config": 3, "layers": hp["n_layers"], "hidden": E,
@@ -637,24 +920,34 @@ def run_dflash(args):
                          "peak_source": peak_src, "unit": "GB/s", "frac": fwd_bytes / per_fwd_s / 1e9 / hbm,
                          "traffic": None, "kernel": "whole decoder step (all kernels)",
                          "per_launch_us": per_fwd_s * 1e6, "bytes_per_launch": fwd_bytes},
-            "cpu_baseline": None,
+            "cpu_baseline": cpu,
             "e2e": {"value": world * e2e_steps / e2e_s, "unit": "fwd/s", "h2d_bytes_per_step": 4 * M * E,
                     "d2h_bytes_per_step": 4 * M * E, "steps": e2e_steps},
             "clocks": clocks, "gpu_launches": launches,
         })
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    ctx.close()
     return 0
 
 
 # ---------------------------------------------------------------------------
+DEFAULT_SEQUENCE = ("gemv_q8_0", "ffn_q4k_m16", "dflash_block", "lm_head_q8_0", "ffn_q4k_m1")
+
+
+def run_workload(args, name):
+    if name == "lm_head_q8_0":
+        return run_lm_head(args)
+    if name == "dflash_block":
+        return run_dflash(args)
+    return run_projection(args, name)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", default="ffn_q4k_m1", choices=sorted(WORKLOADS) + list(SPECIAL))
+    ap.add_argument("--workload", default="all", choices=["all"] + sorted(WORKLOADS) + list(SPECIAL),
+                    help="one workload, or all of them with the headline (ffn_q4k_m1) last (default)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--vocab", type=int, default=0,
@@ -665,206 +958,12 @@ def main():
 
     if args.impl == "reference":
         return run_reference_arm(args)
-    if args.workload == "lm_head_q8_0":
-        return run_lm_head(args)
-    if args.workload == "dflash_block":
-        return run_dflash(args)
+    names = DEFAULT_SEQUENCE if args.workload == "all" else (args.workload,)
+    for name in names:
+        run_workload(args, name)
+    if _PG["init"]:
+        import torch.distributed as dist
 
-    import torch
-    import torch.distributed as dist
-
-    from laguna_raw_halo_strix_b200 import lc, synth
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        torch.cuda.set_device(local_rank)
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
-    dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
-    stream = torch.cuda.Stream(dev)
-    ctx = lc.Context(local_rank)
-    ctx.set_stream(stream)
-
-    wl = WORKLOADS[args.workload]
-    dtype = lc.Q4_K if wl["dtype"] == "q4k" else lc.Q8_0
-    m = wl["m"]
-    rng = np.random.default_rng(1000 + rank)
-
-    # weight pool > 3x L2
-    set_bytes = sum(weight_bytes(wl["dtype"], k, n) for _, k, n in wl["shapes"])
-    pool = max(2, -(-3 * L2_BYTES // set_bytes))
-    base = {name: synth.weight_blocks(dtype, n, k, rng) for name, k, n in wl["shapes"]}
-    weights = []
-    for p in range(pool):
-        s = {}
-        for name, k, n in wl["shapes"]:
-            t = torch.from_numpy(base[name]).to(dev)
-            if p:
-                # distinct bytes per pool entry (flip nibbles/ints deterministically)
-                t = t ^ torch.tensor(p * 37 % 255, dtype=torch.uint8, device=dev)
-            s[name] = t
-        weights.append(s)
-    k0 = wl["shapes"][0][1]
-    x = torch.from_numpy(synth.activations(m, k0, rng)).to(dev)
-    bufs = {name: torch.empty(m, n, device=dev) for name, k, n in wl["shapes"]}
-    h = torch.empty(m, wl["shapes"][-1][1], device=dev) if wl["ffn"] else None
-    def step(i):
-        ws = weights[i % pool]
-        if wl["ffn"]:
-            (_, kg, ng), (_, ku, nu), (_, kd, nd) = wl["shapes"]
-            ctx.proj_m(dtype, x, ws["gate"], bufs["gate"], m, kg, ng)
-            ctx.proj_m(dtype, x, ws["up"], bufs["up"], m, ku, nu)
-            ctx.activation(bufs["gate"], bufs["up"], h, m * ng)
-            ctx.proj_m(dtype, h, ws["down"], bufs["down"], m, kd, nd)
-        else:
-            for name, k, n in wl["shapes"]:
-                ctx.proj_m(dtype, x, ws[name], bufs[name], m, k, n)
-
-    def dominant(i):
-        # the dominant kernel alone: the first projection shape, rotating weights
-        name, k, n = wl["shapes"][0]
-        ctx.proj_m(dtype, x, weights[i % pool][name], bufs[name], m, k, n)
-
-    # m <= 4: one persistent stream-K kernel per projection; m > 4: pack + tiled kernel
-    per_proj = 1 if m <= 4 else 2
-    launches_per_step = per_proj * len(wl["shapes"]) + (1 if wl["ffn"] else 0)
-    n_dom = max(args.steps, 3 * pool)
-
-    with torch.cuda.stream(stream):
-        # eager warm-up: sizes scratch, sets kernel attributes
-        for i in range(args.warmup):
-            step(i)
-        stream.synchronize()
-        # The decode loop runs as CUDA graphs: exactly K steps, and n_dom launches
-        # of the dominant projection (for its per-launch roofline figure).
-        g_steps = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_steps, stream=stream):
-            for i in range(args.steps):
-                step(args.warmup + i)
-        g_dom = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_dom, stream=stream):
-            for i in range(n_dom):
-                dominant(i)
-        g_steps.replay()
-        g_dom.replay()
-        stream.synchronize()
-        if world > 1:
-            dist.barrier()
-        sampler = ClockSampler(dev) if rank == 0 else None
-        if sampler:
-            sampler.start()
-        start = torch.cuda.Event(enable_timing=True)
-        end = torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        if sampler:
-            sampler.mark_begin()
-        start.record(stream)
-        g_steps.replay()
-        end.record(stream)
-        stream.synchronize()
-        if sampler:
-            sampler.mark_end()
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        ms = start.elapsed_time(end)
-        d0 = torch.cuda.Event(enable_timing=True)
-        d1 = torch.cuda.Event(enable_timing=True)
-        d0.record(stream)
-        g_dom.replay()
-        d1.record(stream)
-        stream.synchronize()
-        clocks = sampler.stop() if sampler else None
-        per_launch_ms = d0.elapsed_time(d1) / n_dom
-
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
-        del g_steps, g_dom
-
-        # ---- e2e: host buffers, H2D of the step's input + D2H of its result,
-        # eager calls through the C ABI (ctypes), one host sync per step ----
-        x_host = torch.from_numpy(synth.activations(m, k0, rng)).pin_memory()
-        out_name = wl["shapes"][-1][0]
-        y_host = torch.empty(bufs[out_name].shape, dtype=torch.float32).pin_memory()
-        e2e_steps = max(10, args.steps // 2)
-        for i in range(3):
-            x.copy_(x_host, non_blocking=True)
-            step(i)
-            y_host.copy_(bufs[out_name], non_blocking=True)
-            stream.synchronize()
-        if world > 1:
-            dist.barrier()
-        t0 = time.perf_counter()
-        for i in range(e2e_steps):
-            x.copy_(x_host, non_blocking=True)
-            step(i)
-            y_host.copy_(bufs[out_name], non_blocking=True)
-            stream.synchronize()
-        e2e_s = time.perf_counter() - t0
-        te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e_s = float(te.item())
-
-    sb = step_bytes(wl)
-    value = world * sb * args.steps / (ms_max / 1e3) / 1e9
-    e2e_value = world * sb * e2e_steps / e2e_s / 1e9
-    hbm, tflops, peak_src = peaks()
-    achieved = launch_bytes(wl) / (per_launch_ms / 1e3) / 1e9
-
-    if rank == 0:
-        cpu = None
-        if not args.no_cpu_baseline and world == 1:
-            v, kind, cores, sample = cpu_baseline(wl, 10.0, np.random.default_rng(7))
-            cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample}
-        traffic = _traffic(args.workload)
-        line = {
-            "metric": METRIC,
-            "value": value,
-            "unit": "GB/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": ms_max / args.steps,
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": "q4k*f32" if wl["dtype"] == "q4k" else "q8_0*f32",
-            "data": "synthetic (seeded; BASELINE block/activation distributions)",
-            "config": dict(workload_config(args.workload, wl),
-                           l2=f"weights rotated through {pool} sets of {set_bytes / 1e6:.1f} MB (> 3x the 126 MB L2)",
-                           parallelism=f"replicas x{world} (independent token streams, no collective)"),
-            "roofline": {
-                "bound": "hbm",
-                "achieved": achieved,
-                "peak": hbm,
-                "peak_source": peak_src,
-                "unit": "GB/s",
-                "frac": achieved / hbm,
-                "traffic": traffic,
-                "kernel": ((f"tma_gemv_kernel<FmtQ4K,{m}>" if wl["dtype"] == "q4k" else f"tma_gemv_kernel<FmtQ8_0,{m}>")
-                           if m <= 4 else ("dq_gemm_kernel + x16_pack_kernel" if m <= 32 else
-                                           "q4k_mma_kernel / q8_mma_kernel + x_pack")),
-                "per_launch_us": per_launch_ms * 1e3,
-                "bytes_per_launch": launch_bytes(wl),
-            },
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": int(x_host.numel() * 4),
-                    "d2h_bytes_per_step": int(y_host.numel() * 4), "steps": e2e_steps},
-            "clocks": clocks,
-            "gpu_launches": launches_per_step * args.steps,
-        }
-        print(json.dumps(line), flush=True)
-    ctx.close()
-    if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0

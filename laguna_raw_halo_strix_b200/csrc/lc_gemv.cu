@@ -499,12 +499,16 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, 1) gemv_rows_kernel(const __
     const int nmy = r1 - r0 > rgi ? (r1 - r0 - rgi + a.rg - 1) / a.rg : 0;  // rows r0 + rgi + i * rg
     // this warp's bytes of a row: the slice (the last one may be shorter)
     const int sbytes = min(L::SLICE, a.row_bytes - slice * L::SLICE);
+    // source of the warp's slice of its i-th row (one matrix: a fixed stride)
+    const size_t rstride = (size_t)a.rg * a.row_bytes;
+    const uint8_t *src0 = a.w[0] + (size_t)(r0 + rgi) * a.row_bytes + (size_t)slice * L::SLICE;
     auto slice_ptr = [&](int i) {
+        if (a.ng == 1) return src0 + (size_t)i * rstride;
         int g, ri;
         gv_row(a, r0 + rgi + i * a.rg, g, ri);
         return a.w[g] + (size_t)ri * a.row_bytes + (size_t)slice * L::SLICE;
     };
-    // the first kGvDepth rows, one cp.async group each (empty past the end)
+    // rows 0 .. kGvDepth-1 in flight, one cp.async group per row: group r holds row r
 #pragma unroll
     for (int d = 0; d < kGvDepth; d++) {
         if (d < nmy) gv_copy_slice(slice_ptr(d), ring + d * L::SLICE, sbytes, lane);
@@ -524,21 +528,22 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, 1) gemv_rows_kernel(const __
 #pragma unroll
         for (int q = 0; q < kGvQuad; q++) {
             const int i = i0 + q;
-            // row i's group is complete once at most kGvDepth - 1 newer ones are
-            // pending; the warp barrier makes every lane's copies visible
-            cp_async_wait<kGvDepth - 1>();
+            // Row i has landed for this lane once at most kGvDepth - 2 newer
+            // groups are pending (groups 0..i+kGvDepth-2 were committed before
+            // this point); the warp barrier makes every lane's copies visible
+            // and also means every lane is done with row i - 1.
+            cp_async_wait<kGvDepth - 2>();
             __syncwarp();
+            // refill row i - 1's buffer with row i - 1 + kGvDepth
+            if (i > 0 && i - 1 + kGvDepth < nmy)
+                gv_copy_slice(slice_ptr(i - 1 + kGvDepth), ring + ((i - 1) % kGvDepth) * L::SLICE, sbytes, lane);
+            if (i > 0) cp_async_commit();
             typename L::Bytes bt;
-            uint8_t *slot = ring + (i % kGvDepth) * L::SLICE;
-            ln.fetch(slot, bt);
+            ln.fetch(ring + (i % kGvDepth) * L::SLICE, bt);
             float o[M];
             ln.row(bt, ref_mask, o);
 #pragma unroll
             for (int j = 0; j < M; j++) p[q][j] = i < nmy ? o[j] : 0.f;
-            // every lane has consumed the slot (o depends on it): refill it
-            __syncwarp();
-            if (i + kGvDepth < nmy) gv_copy_slice(slice_ptr(i + kGvDepth), slot, sbytes, lane);
-            cp_async_commit();
         }
         reduce4<M>(p, lane);
         float *pb = part + (size_t)(buf * a.rg + rgi) * kGvQuad * a.ks * M;
@@ -658,8 +663,9 @@ int gemv_rows(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *outs, i
 // C ABI: the FFN block of the DFlash decoder layer (src/dflash.rs:965-968):
 // y = down(SiLU(gate(x)) * up(x)) for m rows of x [m, n_embd].  One or two
 // tokens run as two launches: gate and up in one grouped GEMV over x, then
-// down with SiLU(gate) * up formed while its activations load.  Other m run
-// the projections and the activation kernel one by one.
+// down with SiLU(gate) * up formed while its activations load; 5..32 tokens
+// the same on the grouped tcgen05 GEMM; other m the projections and the
+// activation kernel one by one.
 
 extern "C" int lc_ffn(lc_ctx *ctx, int dtype, const float *x, const void *w_gate, const void *w_up,
                       const void *w_down, float *y, uint32_t m, uint32_t n_embd, uint32_t n_ff) {
@@ -696,6 +702,25 @@ extern "C" int lc_ffn(lc_ctx *ctx, int dtype, const float *x, const void *w_gate
             // activation kernel forms SiLU(gate) * up first
             if ((s = lc_activation(ctx, g, u, g, m * n_ff)) || (s = proj(g, w_down, y, n_ff, n_embd))) return s;
             return lc_after_launch(ctx, "lc_ffn");
+        }
+        if (s != LC_ERR_UNSUPPORTED) return s;
+    }
+    if (lc::routes_to_gemm_dq(ctx, m)) {
+        // 5..32 tokens: gate and up in one grouped tcgen05 GEMM, SiLU-gate formed
+        // while the down projection packs its activations (as the decoder does)
+        lc::PackSrc src;
+        src.x = x;
+        lc::ProjOut o[2];
+        o[0].w = w_gate, o[0].y = g, o[0].n = n_ff;
+        o[1].w = w_up, o[1].y = u, o[1].n = n_ff;
+        s = lc::gemm_dq_group(ctx, dtype, src, o, 2, m, n_embd);
+        if (s == LC_OK) {
+            lc::PackSrc hs;
+            hs.x = g, hs.x2 = u, hs.op = lc::LC_PACK_SWIGLU;
+            lc::ProjOut d;
+            d.w = w_down, d.y = y, d.n = n_embd;
+            s = lc::gemm_dq_group(ctx, dtype, hs, &d, 1, m, n_ff);
+            if (s == LC_OK) return lc_after_launch(ctx, "lc_ffn");
         }
         if (s != LC_ERR_UNSUPPORTED) return s;
     }
