@@ -24,14 +24,42 @@ LAYER_TENSORS = ["attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "attn
                  "attn_gate", "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"]
 
 
+def proj_blas(o: orc.Oracle, dtype: int, x: np.ndarray, w: np.ndarray, k: int, n: int,
+              chunk_rows: int = 16384) -> np.ndarray:
+    """x [m, k] . W^T for a weight of n rows: W dequantised bit-exactly by the
+    shader formula (oracle.dequant_shader, kernels/proj_q4k.comp:87 and
+    proj_q8_0.comp:53-64), products summed by BLAS in f32 (blocked sums), in
+    row chunks.  It differs from the reference's serial f32 sum by ~1e-6
+    relative -- far below the parity tolerances -- and runs the full-size
+    configurations in seconds on the host cores."""
+    x = np.ascontiguousarray(np.atleast_2d(np.asarray(x, np.float32)))
+    out = np.empty((x.shape[0], n), np.float32)
+    if dtype == orc.F32:
+        wf = np.asarray(w, np.float32).reshape(n, k)
+        return (x @ wf.T).astype(np.float32)
+    bb = 144 if dtype == orc.Q4_K else 34
+    be = 256 if dtype == orc.Q4_K else 32
+    raw = np.ascontiguousarray(w).view(np.uint8).ravel()
+    rb = k // be * bb
+    chunk_rows = max(1, min(chunk_rows, (1 << 26) // k))  # <= 256 MB of f32 weights at a time
+    for r0 in range(0, n, chunk_rows):
+        r1 = min(n, r0 + chunk_rows)
+        wf = o.dequant_shader(raw[r0 * rb:r1 * rb], dtype, (r1 - r0) * k).reshape(r1 - r0, k)
+        out[:, r0:r1] = x @ wf.T
+    return out
+
+
 class DFlashOracle:
-    def __init__(self, hp: dict, tensors: dict, o: orc.Oracle | None = None):
+    def __init__(self, hp: dict, tensors: dict, o: orc.Oracle | None = None, fast_proj: bool = False):
         """hp: n_layers, n_embd, n_heads, n_kv_heads, head_dim, rope_dim, n_ff,
         n_aux, rope_base, norm_eps, qk_eps.  tensors: name -> (dtype, array);
-        f32 tensors as float32 arrays, quantized ones as raw uint8 blocks."""
+        f32 tensors as float32 arrays, quantized ones as raw uint8 blocks.
+        fast_proj: projections through proj_blas (full-size configurations)
+        instead of the shader restatement."""
         self.hp = hp
         self.t = tensors
         self.o = o or orc.Oracle()
+        self.fast_proj = fast_proj
         self.freq = self.o.rope_freq(hp["rope_dim"], hp["rope_base"])
 
     def _f32(self, name):
@@ -41,6 +69,8 @@ class DFlashOracle:
 
     def _proj(self, name, x, k, n):
         dt, w = self.t[name]
+        if self.fast_proj:
+            return proj_blas(self.o, dt, x, w, k, n)
         return self.o.proj(dt, np.atleast_2d(x), w, k, n).reshape(-1, n)
 
     def encode(self, feats):
