@@ -669,14 +669,16 @@ def run_lm_head(args):
     import torch
 
     from laguna_raw_halo_strix_b200 import lc, synth
-    from laguna_raw_halo_strix_b200.lm_head import ShardedLmHead
+    from laguna_raw_halo_strix_b200.lm_head import ShardedLmHead, make_comm
 
     world, rank, local_rank, dev = _dist_init()
     stream = torch.cuda.Stream(dev)
     ctx = lc.Context(local_rank)
     ctx.set_stream(stream)
     m, k, vocab = LM_HEAD["m"], LM_HEAD["k"], args.vocab or LM_HEAD["vocab"]
-    head = ShardedLmHead(ctx, lc.Q8_0, k, vocab, rank, world)
+    # the reduction through the library's own NCCL communicator (one C-ABI call per step)
+    comm = make_comm(ctx, rank, world, timeout_ms=60000)
+    head = ShardedLmHead(ctx, lc.Q8_0, k, vocab, rank, world, comm=comm)
     rng = np.random.default_rng(2000 + rank)
     shard = synth.q8_0_blocks(head.n_local, k, rng)
     shard_bytes = shard.nbytes
@@ -684,7 +686,7 @@ def run_lm_head(args):
     heads = []
     base = torch.from_numpy(shard.reshape(-1)).to(dev)
     for p in range(pool):
-        h = ShardedLmHead(ctx, lc.Q8_0, k, vocab, rank, world)
+        h = ShardedLmHead(ctx, lc.Q8_0, k, vocab, rank, world, comm=comm)
         # distinct bytes per copy: flip only the int8 q bytes (the f16 scales stay valid)
         if p:
             w = base.view(-1, 34).clone()
@@ -748,9 +750,11 @@ def run_lm_head(args):
         for i in range(e2e_steps):
             x.copy_(x_host, non_blocking=True)
             step(i)
+            comm.wait()  # the bounded wait of the reduction (host deadline)
             k_host.copy_(keys, non_blocking=True)
             stream.synchronize()
         e2e_s = _max_over_ranks(time.perf_counter() - t0, dev, world)
+    comm.close()
 
     w_total = vocab * (k // 32) * 34
     step_b = w_total + world * 4 * m * k  # every weight byte once; x read by every rank
@@ -774,7 +778,8 @@ def run_lm_head(args):
                        "vocab": vocab, "rows_per_rank": head.n_local, "bytes_per_step": step_b,
                        "tokens_per_s": m * args.steps / (ms / 1e3),
                        "l2": f"weights rotated through {pool} copies of {shard_bytes / 1e6:.1f} MB per rank",
-                       "parallelism": f"vocab-sharded x{world}, int64 MAX all-reduce of {m} keys per step"},
+                       "parallelism": f"vocab-sharded x{world}, int64 MAX all-reduce of {m} keys per step "
+                                      "(lc_lm_head_argmax_sharded: the library's NCCL communicator)"},
             # tensor-bound: 2 m k n_local useful flops per launch (the tcgen05 tiles)
             "roofline": {"bound": "tensor", "achieved": local_f / (local_ms / 1e3) / 1e12, "peak": tflops,
                          "peak_source": peak_src + " (dense bf16 burst)", "unit": "TFLOP/s",

@@ -247,6 +247,51 @@ int lc_lm_head_argmax(lc_ctx *ctx, int dtype, const float *x, const void *w,
                       uint32_t m, uint32_t k, uint32_t n_local,
                       uint32_t row_offset, uint64_t *keys, float *logits);
 
+/* ---- vocab-sharded lm_head over several GPUs (NCCL owned by the library) -- */
+
+/* The reference projects each hidden row onto the whole vocabulary on one
+ * device (project_normalized_hidden, src/target.rs:580-605, then argmax,
+ * src/lib.rs:456-464).  Sharded, each rank holds a contiguous range of vocab
+ * rows; its shard's keys (lc_lm_head_argmax) are combined by one int64 MAX
+ * all-reduce, which yields the reference's argmax over the whole vocabulary.
+ * NCCL is loaded at run time (libnccl.so.2); without it these calls return
+ * LC_ERR_UNSUPPORTED.  Every wait is bounded by the communicator's timeout:
+ * when it expires (a rank never arrived) the communicator is aborted -- its
+ * kernels end, the context stays usable -- and LC_ERR_TIMEOUT is returned. */
+typedef struct lc_comm lc_comm;
+/* A 128-byte id for lc_comm_init, made by one rank and handed to the others
+ * out of band (ncclGetUniqueId). */
+int lc_comm_unique_id(void *id128);
+/* The communicator of rank `rank` of n_ranks on the context's device
+ * (ncclCommInitRankConfig, non-blocking, waited on for at most timeout_ms). */
+int lc_comm_init(lc_ctx *ctx, const void *id128, int n_ranks, int rank, int timeout_ms, lc_comm **out);
+/* Finalise (bounded) and free; an aborted communicator is just freed. */
+int lc_comm_destroy(lc_comm *comm);
+int lc_comm_rank(const lc_comm *comm, int *rank, int *n_ranks);
+/* keys[n] (device, packed by lc_pack_key) <- their maximum over the ranks,
+ * enqueued on the context's stream. */
+int lc_comm_allreduce_max_keys(lc_ctx *ctx, lc_comm *comm, uint64_t *keys, uint32_t n);
+/* Wait for the context's stream, polling the communicator for errors, for at
+ * most its timeout: LC_OK, or LC_ERR_TIMEOUT / LC_ERR_CUDA with the
+ * communicator aborted. */
+int lc_comm_wait(lc_ctx *ctx, lc_comm *comm);
+/* This rank's shard of the lm_head (rows row_offset .. row_offset + n_local
+ * of the vocabulary) for m hidden rows x [m, k], then the MAX all-reduce:
+ * keys[m] (device) end with the global (logit, token) of every row.  Enqueued
+ * on the context's stream (lc_comm_wait bounds the wait; a context in sync
+ * mode waits here). */
+int lc_lm_head_argmax_sharded(lc_ctx *ctx, lc_comm *comm, int dtype, const float *x, const void *w_shard,
+                              uint32_t m, uint32_t k, uint32_t n_local, uint32_t row_offset, uint64_t *keys);
+
+/* ---- failure detection ----------------------------------------------------- */
+
+/* Self-check of the device-side bounded waits: one CTA waits on a barrier
+ * nobody arrives on, gives up after `spins` polls and records it in the
+ * status word, so that lc_device_status(ctx) returns LC_ERR_TIMEOUT and the
+ * context stays usable.  No counterpart in the reference, whose waits are
+ * unbounded fences (src/vulkan.rs:326-334). */
+int lc_check_bounded_wait(lc_ctx *ctx, uint32_t spins);
+
 /* ---- GGUF v3 reader: replaces GGUFReader (src/gguf.rs) ------------------- */
 
 typedef struct lc_gguf lc_gguf;
@@ -270,6 +315,11 @@ int lc_gguf_tensor_info(const lc_gguf *g, uint64_t i, const char **name, int *dt
 int lc_gguf_find(const lc_gguf *g, const char *name, uint64_t *index);
 /* GGUFReader::read_tensor_data (src/gguf.rs:415-421): raw bytes into host memory. */
 int lc_gguf_read(lc_gguf *g, uint64_t index, void *dst, uint64_t bytes);
+/* The same bytes without a copy: *data points into the reader's read-only
+ * mapping of the file (valid until lc_gguf_close), *bytes = n_bytes.  A tensor
+ * that lies past the end of the file is LC_ERR_IO, as read_exact's short read
+ * is in the reference. */
+int lc_gguf_tensor_data(const lc_gguf *g, uint64_t index, const void **data, uint64_t *bytes);
 /* Numeric / string metadata by key (any integer or float type). */
 int lc_gguf_meta_u64(const lc_gguf *g, const char *key, uint64_t *out);
 int lc_gguf_meta_f32(const lc_gguf *g, const char *key, float *out);
@@ -307,7 +357,21 @@ int lc_dflash_create(lc_ctx *ctx, const lc_dflash_hparams *hp, uint32_t max_ctx,
 int lc_dflash_set_tensor(lc_dflash *m, const char *name, int dtype, const void *host_data, size_t bytes);
 /* DFlashModel::load (src/dflash.rs:34-119) from a GGUF file, raw-block upload. */
 int lc_dflash_load_gguf(lc_ctx *ctx, const char *path, uint32_t max_ctx, uint32_t max_block, lc_dflash **out);
+/* lc_dflash_load_gguf with load flags.  The file is mapped, every tensor the
+ * draft path uses goes into one device allocation through pinned staging
+ * buffers (host copies of one chunk overlap the DMA of the previous one), with
+ * one synchronisation at the end.  LC_LOAD_BF16_NATIVE decodes BF16 tensors
+ * as bfloat16 (f32 = bits << 16); without it they follow the reference, which
+ * reads BF16 bits with the f16 layout (src/dflash.rs:351-378). */
+enum { LC_LOAD_BF16_NATIVE = 1 };
+int lc_dflash_load_gguf_ex(lc_ctx *ctx, const char *path, uint32_t max_ctx, uint32_t max_block, uint32_t flags,
+                           lc_dflash **out);
 int lc_dflash_destroy(lc_dflash *m);
+/* The device copy of a loaded tensor (the slots DFlashModel::load fills,
+ * src/dflash.rs:60-107): its address, dtype as stored (F16 / BF16 tensors are
+ * held as LC_F32) and byte size.  LC_ERR_INVALID for a name the model does
+ * not hold. */
+int lc_dflash_weight(const lc_dflash *m, const char *name, const void **data, int *dtype, uint64_t *bytes);
 int lc_dflash_get_hparams(const lc_dflash *m, lc_dflash_hparams *out);
 /* DFlashModel::encode (src/dflash.rs:157-234) for n_ctx rows of target
  * features [n_ctx, n_aux*n_embd] (device) -> enc_out [n_ctx, n_embd] (device). */

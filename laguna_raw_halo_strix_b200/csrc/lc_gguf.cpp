@@ -1,9 +1,13 @@
 // lc_gguf.cpp -- GGUF v3 reader, the C++ counterpart of the reference's
 // GGUFReader (src/gguf.rs:321-421) and of Model::from_reader's
 // hyper-parameter lookup (src/model.rs:29-129, src/gguf.rs:516-653).
+#include <fcntl.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <map>
 #include <string>
@@ -46,8 +50,13 @@ struct Tensor {
 
 }  // namespace
 
+// The whole file is mapped read-only; tensor data is read (or handed out) from
+// the mapping, so a tensor costs no read() copy and the page cache feeds the
+// upload directly.
 struct lc_gguf {
-    FILE *f = nullptr;
+    int fd = -1;
+    const uint8_t *map = nullptr;
+    uint64_t size = 0;
     uint32_t version = 0;
     std::vector<std::pair<std::string, Value>> meta;
     std::map<std::string, size_t> meta_index;
@@ -57,14 +66,26 @@ struct lc_gguf {
 
 namespace {
 
-bool rd(FILE *f, void *p, size_t n) { return fread(p, 1, n, f) == n; }
+// Bounds-checked cursor over the mapping: every header read fails instead of
+// running past the end of a truncated file.
+struct Src {
+    const uint8_t *p;
+    uint64_t n, pos;
+};
+
+bool rd(Src &f, void *p, size_t n) {
+    if (n > f.n - f.pos) return false;
+    memcpy(p, f.p + f.pos, n);
+    f.pos += n;
+    return true;
+}
 
 template <typename T>
-bool rdv(FILE *f, T *v) {
+bool rdv(Src &f, T *v) {
     return rd(f, v, sizeof(T));
 }
 
-bool read_string(FILE *f, std::string *s) {
+bool read_string(Src &f, std::string *s) {
     uint64_t n;
     if (!rdv(f, &n) || n > (1ull << 32)) return false;
     s->resize(n);
@@ -72,7 +93,7 @@ bool read_string(FILE *f, std::string *s) {
 }
 
 // read_value (src/gguf.rs:441-514): GGUF value type ids 0..12.
-bool read_value(FILE *f, uint32_t type, Value *v, int depth = 0) {
+bool read_value(Src &f, uint32_t type, Value *v, int depth = 0) {
     if (depth > 4) return false;
     switch (type) {
     case 0: { uint8_t x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_U; v->u = x; return true; }
@@ -152,10 +173,26 @@ extern "C" uint64_t lc_tensor_bytes(int dtype, uint64_t n) {
 extern "C" int lc_gguf_open(const char *path, lc_gguf **out) {
     if (!path || !out) return lc_fail(LC_ERR_INVALID, "lc_gguf_open: null argument");
     *out = nullptr;
-    FILE *f = fopen(path, "rb");
-    if (!f) return lc_fail(LC_ERR_IO, "lc_gguf_open: cannot open %s", path);
+    const int fd = open(path, O_RDONLY | O_CLOEXEC);
+    if (fd < 0) return lc_fail(LC_ERR_IO, "lc_gguf_open: cannot open %s", path);
     lc_gguf *g = new lc_gguf();
-    g->f = f;
+    g->fd = fd;
+    struct stat st;
+    if (fstat(fd, &st) != 0) {
+        lc_gguf_close(g);
+        return lc_fail(LC_ERR_IO, "lc_gguf_open: cannot stat %s", path);
+    }
+    g->size = (uint64_t)st.st_size;
+    if (g->size) {
+        void *p = mmap(nullptr, g->size, PROT_READ, MAP_PRIVATE, fd, 0);
+        if (p == MAP_FAILED) {
+            lc_gguf_close(g);
+            return lc_fail(LC_ERR_IO, "lc_gguf_open: cannot map %s", path);
+        }
+        g->map = (const uint8_t *)p;
+        madvise(p, g->size, MADV_SEQUENTIAL);  // tensors are read front to back
+    }
+    Src f{g->map, g->size, 0};
     auto bad = [&](const char *what) {
         lc_gguf_close(g);
         return lc_fail(LC_ERR_IO, "lc_gguf_open(%s): %s", path, what);
@@ -186,7 +223,7 @@ extern "C" int lc_gguf_open(const char *path, lc_gguf **out) {
         t.dtype = (int)dt;
         g->tensors.push_back(std::move(t));
     }
-    long pos = ftell(f);
+    const uint64_t pos = f.pos;
     uint64_t align = 32;
     if (const Value *a = find_meta(g, "general.alignment")) {
         uint64_t v;
@@ -199,7 +236,8 @@ extern "C" int lc_gguf_open(const char *path, lc_gguf **out) {
 
 extern "C" int lc_gguf_close(lc_gguf *g) {
     if (!g) return LC_OK;
-    if (g->f) fclose(g->f);
+    if (g->map) munmap((void *)g->map, g->size);
+    if (g->fd >= 0) close(g->fd);
     delete g;
     return LC_OK;
 }
@@ -235,8 +273,23 @@ extern "C" int lc_gguf_read(lc_gguf *g, uint64_t index, void *dst, uint64_t byte
     lc_gguf_tensor_info(g, index, nullptr, nullptr, nullptr, nullptr, nullptr, &need);
     if (bytes < need) return lc_fail(LC_ERR_INVALID, "lc_gguf_read: buffer of %llu < %llu bytes",
                                      (unsigned long long)bytes, (unsigned long long)need);
-    if (fseeko(g->f, (off_t)(g->data_offset + g->tensors[index].offset), SEEK_SET) != 0 || !rd(g->f, dst, need))
-        return lc_fail(LC_ERR_IO, "lc_gguf_read: short read of %s", g->tensors[index].name.c_str());
+    const void *src;
+    if (int s = lc_gguf_tensor_data(g, index, &src, nullptr)) return s;
+    memcpy(dst, src, need);
+    return LC_OK;
+}
+
+extern "C" int lc_gguf_tensor_data(const lc_gguf *g, uint64_t index, const void **data, uint64_t *bytes) {
+    if (!g || !data || index >= g->tensors.size()) return lc_fail(LC_ERR_INVALID, "lc_gguf_tensor_data: bad argument");
+    uint64_t need;
+    lc_gguf_tensor_info(g, index, nullptr, nullptr, nullptr, nullptr, nullptr, &need);
+    const uint64_t at = g->data_offset + g->tensors[index].offset;
+    if (at < g->data_offset || at > g->size || need > g->size - at)
+        return lc_fail(LC_ERR_IO, "lc_gguf: %s lies past the end of the file (%llu + %llu > %llu bytes)",
+                       g->tensors[index].name.c_str(), (unsigned long long)at, (unsigned long long)need,
+                       (unsigned long long)g->size);
+    *data = g->map + at;
+    if (bytes) *bytes = need;
     return LC_OK;
 }
 

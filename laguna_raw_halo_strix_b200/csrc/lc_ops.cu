@@ -219,6 +219,10 @@ __global__ void enc_aux_norm_kernel(const float *x, const float *__restrict__ w,
 
 __device__ __forceinline__ uint32_t rd16(const uint8_t *p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
 
+// dequant_kernel's dtype code for BF16 decoded as bfloat16 (the loader's
+// LC_LOAD_BF16_NATIVE); not a GGUF type id.
+constexpr int kDeqBf16Native = 0x10000 | LC_BF16;
+
 // One thread per output element; reads bounded by nbytes like the Rust code.
 __global__ void dequant_kernel(const uint8_t *__restrict__ src, size_t nbytes, int dtype, size_t n,
                                float *__restrict__ out, int half_mode) {
@@ -234,6 +238,9 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ src, size_t nbytes, i
             break;
         case LC_BF16:  // src/dflash.rs:351-378 decodes these bits with the f16 layout
             if (i * 2 + 2 <= nbytes) v = lc_half_to_f32(rd16(src + 2 * i), LC_HALF_REF);
+            break;
+        case kDeqBf16Native:  // bfloat16 proper: the top half of an f32
+            if (i * 2 + 2 <= nbytes) v = __uint_as_float(rd16(src + 2 * i) << 16);
             break;
         case LC_F16:  // src/dflash.rs:437-462 (IEEE; NaN -> 0x7FC00000)
             if (i * 2 + 2 <= nbytes) {
@@ -455,6 +462,17 @@ extern "C" int lc_dequant(lc_ctx *ctx, int dtype, const void *src, size_t src_by
     LC_REQUIRE(out && (src || src_bytes == 0), LC_ERR_INVALID, "lc_dequant: null pointer");
     dequant_kernel<<<grid_for(ctx, n), 256, 0, ctx->stream>>>((const uint8_t *)src, src ? src_bytes : 0, dtype, n,
                                                               out, ctx->half_mode);
+    return lc_after_launch(ctx, "lc_dequant");
+}
+
+int lc::dequant_f32(lc_ctx *ctx, int dtype, const void *src, size_t src_bytes, size_t n, float *out,
+                    bool bf16_native) {
+    if (!(bf16_native && dtype == LC_BF16)) return lc_dequant(ctx, dtype, src, src_bytes, n, out);
+    LC_BEGIN(ctx, "lc_dequant");
+    if (n == 0) return LC_OK;
+    LC_REQUIRE(out && src, LC_ERR_INVALID, "lc_dequant: null pointer");
+    dequant_kernel<<<grid_for(ctx, n), 256, 0, ctx->stream>>>((const uint8_t *)src, src_bytes, kDeqBf16Native, n, out,
+                                                              ctx->half_mode);
     return lc_after_launch(ctx, "lc_dequant");
 }
 

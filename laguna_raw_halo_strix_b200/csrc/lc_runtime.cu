@@ -9,6 +9,7 @@
 #include <stdlib.h>
 
 #include "lc_internal.cuh"
+#include "lc_sm100.cuh"
 
 static thread_local char g_err[1024] = "";
 
@@ -308,4 +309,28 @@ extern "C" int lc_rope_freq(float *freq, uint32_t rope_dim, float base) {
     for (uint32_t i = 0; i < rope_dim / 2; i++)
         freq[i] = 1.0f / powf(base, (2.0f * (float)i) / (float)rope_dim);
     return LC_OK;
+}
+
+// One CTA waits on a barrier that nobody arrives on, with a bound of `spins`
+// polls, and records the expiry like every bounded wait of the library.
+__global__ void bounded_wait_check_kernel(unsigned *status, uint32_t spins) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    bool ok = false;
+    for (uint32_t i = 0; i < spins && !ok; ++i) ok = mbar_test(&bar, 0u);
+    if (!ok && threadIdx.x == 0) atomicOr(status, LC_DEV_WAIT_TIMEOUT);
+}
+
+extern "C" int lc_check_bounded_wait(lc_ctx *ctx, uint32_t spins) {
+    LC_REQUIRE(ctx, LC_ERR_INVALID, "lc_check_bounded_wait: null ctx");
+    LC_REQUIRE(spins > 0 && spins <= (1u << 20), LC_ERR_INVALID, "lc_check_bounded_wait: spins %u not in 1..2^20",
+               spins);
+    int s = lc_use_device(ctx);
+    if (s) return s;
+    bounded_wait_check_kernel<<<1, 32, 0, ctx->stream>>>(ctx->dev_status, spins);
+    return lc_after_launch(ctx, "lc_check_bounded_wait");
 }

@@ -37,6 +37,8 @@ Q4_K_DFLASH_CPU = 1012
 HALF_REF = 0
 HALF_IEEE = 1
 
+LOAD_BF16_NATIVE = 1  # lc_dflash_load_gguf_ex flag
+
 _STATUS = {0: "LC_OK", 1: "LC_ERR_INVALID", 2: "LC_ERR_UNSUPPORTED", 3: "LC_ERR_CUDA", 4: "LC_ERR_OOM",
            5: "LC_ERR_TIMEOUT", 6: "LC_ERR_IO"}
 
@@ -86,6 +88,14 @@ SIGNATURES = {
     "lc_proj_m": (_i, [_vp, _i, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
     "lc_proj_q4k_static": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
     "lc_ffn": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32]),
+    "lc_comm_unique_id": (_i, [_vp]),
+    "lc_comm_init": (_i, [_vp, _vp, _i, _i, _i, C.POINTER(_vp)]),
+    "lc_comm_destroy": (_i, [_vp]),
+    "lc_comm_rank": (_i, [_vp, C.POINTER(_i), C.POINTER(_i)]),
+    "lc_comm_allreduce_max_keys": (_i, [_vp, _vp, _vp, _u32]),
+    "lc_comm_wait": (_i, [_vp, _vp]),
+    "lc_lm_head_argmax_sharded": (_i, [_vp, _vp, _i, _vp, _vp, _u32, _u32, _u32, _u32, _vp]),
+    "lc_check_bounded_wait": (_i, [_vp, _u32]),
     "lc_dequant": (_i, [_vp, _i, _vp, _sz, _sz, _vp]),
     "lc_rmsnorm": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _f]),
     "lc_qk_norm_rope": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _f, _u32]),
@@ -112,6 +122,7 @@ SIGNATURES = {
                                  C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "lc_gguf_find": (_i, [_vp, C.c_char_p, C.POINTER(C.c_uint64)]),
     "lc_gguf_read": (_i, [_vp, C.c_uint64, _vp, C.c_uint64]),
+    "lc_gguf_tensor_data": (_i, [_vp, C.c_uint64, C.POINTER(_vp), C.POINTER(C.c_uint64)]),
     "lc_gguf_meta_u64": (_i, [_vp, C.c_char_p, C.POINTER(C.c_uint64)]),
     "lc_gguf_meta_f32": (_i, [_vp, C.c_char_p, C.POINTER(_f)]),
     "lc_gguf_meta_str": (_i, [_vp, C.c_char_p, C.POINTER(C.c_char_p)]),
@@ -120,6 +131,8 @@ SIGNATURES = {
     "lc_dflash_create": (_i, [_vp, _vp, _u32, _u32, C.POINTER(_vp)]),
     "lc_dflash_set_tensor": (_i, [_vp, C.c_char_p, _i, _vp, _sz]),
     "lc_dflash_load_gguf": (_i, [_vp, C.c_char_p, _u32, _u32, C.POINTER(_vp)]),
+    "lc_dflash_load_gguf_ex": (_i, [_vp, C.c_char_p, _u32, _u32, _u32, C.POINTER(_vp)]),
+    "lc_dflash_weight": (_i, [_vp, C.c_char_p, C.POINTER(_vp), C.POINTER(_i), C.POINTER(C.c_uint64)]),
     "lc_dflash_destroy": (_i, [_vp]),
     "lc_dflash_get_hparams": (_i, [_vp, _vp]),
     "lc_dflash_encode": (_i, [_vp, _vp, _u32, _vp]),
@@ -312,9 +325,48 @@ class Context:
     def argmax_rows(self, logits, m, n, row_offset, keys):
         check(self.L.lc_argmax_rows(self.h, ptr(logits), m, n, row_offset, ptr(keys)), "lc_argmax_rows")
 
+    def check_bounded_wait(self, spins: int = 1024) -> None:
+        check(self.L.lc_check_bounded_wait(self.h, spins), "lc_check_bounded_wait")
+
     def lm_head_argmax(self, dtype, x, w, m, k, n_local, row_offset, keys, logits=None):
         check(self.L.lc_lm_head_argmax(self.h, dtype, ptr(x), ptr(w), m, k, n_local, row_offset, ptr(keys),
                                        ptr(logits)), "lc_lm_head_argmax")
+
+
+def comm_unique_id() -> bytes:
+    """128-byte id for Comm, made by one rank and passed to the others."""
+    buf = C.create_string_buffer(128)
+    check(lib().lc_comm_unique_id(buf), "lc_comm_unique_id")
+    return buf.raw
+
+
+class Comm:
+    """An lc_comm: the library's NCCL communicator over the ranks' contexts."""
+
+    def __init__(self, ctx: Context, unique_id: bytes, n_ranks: int, rank: int, timeout_ms: int = 30000):
+        self.ctx, self.L = ctx, lib()
+        assert len(unique_id) == 128
+        h = C.c_void_p()
+        check(self.L.lc_comm_init(ctx.h, C.create_string_buffer(unique_id, 128), n_ranks, rank, timeout_ms,
+                                  C.byref(h)), "lc_comm_init")
+        self.h = h
+        self.rank, self.n_ranks = rank, n_ranks
+
+    def allreduce_max_keys(self, keys, n):
+        check(self.L.lc_comm_allreduce_max_keys(self.ctx.h, self.h, ptr(keys), n), "lc_comm_allreduce_max_keys")
+
+    def wait(self):
+        check(self.L.lc_comm_wait(self.ctx.h, self.h), "lc_comm_wait")
+
+    def lm_head_argmax(self, dtype, x, w, m, k, n_local, row_offset, keys):
+        check(self.L.lc_lm_head_argmax_sharded(self.ctx.h, self.h, dtype, ptr(x), ptr(w), m, k, n_local, row_offset,
+                                               ptr(keys)), "lc_lm_head_argmax_sharded")
+
+    def close(self):
+        if getattr(self, "h", None):
+            status = self.L.lc_comm_destroy(self.h)
+            self.h = None
+            check(status, "lc_comm_destroy")
 
 
 def rope_freq(rope_dim: int, base: float = 500000.0):

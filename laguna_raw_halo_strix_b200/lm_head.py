@@ -9,7 +9,11 @@ global index), and one int64 MAX all-reduce combines them.  The keys are
 order-preserving signed integers with ties broken toward the larger index, so
 the reduced key is exactly the reference's max_by result over the whole vocab.
 
-The reduction is the only exchange of the path: 8 bytes per row.
+The reduction is the only exchange of the path: 8 bytes per row.  With a
+library communicator (lc.Comm, NCCL owned by liblaguna_cuda.so, bounded
+waits) the whole step is one C-ABI call, lc_lm_head_argmax_sharded -- what a
+host binding the C ABI alone uses; without one, the keys are reduced through
+the torch.distributed group (NCCL on GPU tensors, gloo on CPU tensors).
 """
 from __future__ import annotations
 
@@ -45,9 +49,9 @@ class ShardedLmHead:
     this rank's shard on the context's device."""
 
     def __init__(self, ctx: lc.Context, dtype: int, k: int, n_vocab: int, rank: int = 0, world: int = 1,
-                 group=None):
+                 group=None, comm: "lc.Comm | None" = None):
         self.ctx, self.dtype, self.k, self.n_vocab = ctx, dtype, k, n_vocab
-        self.rank, self.world, self.group = rank, world, group
+        self.rank, self.world, self.group, self.comm = rank, world, group, comm
         self.lo, self.hi = shard_range(n_vocab, rank, world)
         self.row_bytes = synth.row_bytes(dtype, k)
         self.w = None
@@ -78,5 +82,19 @@ class ShardedLmHead:
 
     def __call__(self, x, m: int, keys):
         """Global argmax keys of x [m, k] (device): local keys, then the MAX all-reduce."""
+        if self.comm is not None:
+            self.comm.lm_head_argmax(self.dtype, x, self.w, m, self.k, self.n_local, self.lo, keys)
+            return keys
         self.local_keys(x, m, keys)
         return reduce_keys(keys, self.group)
+
+
+def make_comm(ctx: lc.Context, rank: int, world: int, timeout_ms: int = 30000, group=None) -> "lc.Comm":
+    """The library communicator over an initialised torch.distributed group:
+    rank 0 makes the NCCL id, the group carries it to the others."""
+    import torch.distributed as dist
+
+    obj = [lc.comm_unique_id() if rank == 0 else None]
+    if world > 1:
+        dist.broadcast_object_list(obj, src=0, group=group)
+    return lc.Comm(ctx, obj[0], world, rank, timeout_ms)

@@ -55,6 +55,21 @@ class Gguf:
         lc.check(self.L.lc_gguf_read(self.h, idx.value, buf.ctypes.data, buf.size), "lc_gguf_read")
         return buf
 
+    def view(self, name: str) -> np.ndarray:
+        """The tensor's bytes in place, a read-only view of the file mapping
+        (lc_gguf_tensor_data); valid while the reader is open."""
+        idx = C.c_uint64()
+        lc.check(self.L.lc_gguf_find(self.h, name.encode(), C.byref(idx)), "lc_gguf_find")
+        p = C.c_void_p()
+        n = C.c_uint64()
+        lc.check(self.L.lc_gguf_tensor_data(self.h, idx.value, C.byref(p), C.byref(n)), "lc_gguf_tensor_data")
+        if n.value == 0:
+            a = np.empty(0, np.uint8)
+        else:
+            a = np.frombuffer((C.c_uint8 * n.value).from_address(p.value), np.uint8)
+        a.flags.writeable = False
+        return a
+
     def meta_u64(self, key: str):
         v = C.c_uint64()
         return v.value if self.L.lc_gguf_meta_u64(self.h, key.encode(), C.byref(v)) == lc.LC_OK else None
@@ -86,13 +101,13 @@ class DFlash:
     or torch CUDA tensors."""
 
     def __init__(self, ctx: lc.Context, hp: lc.HParams | None = None, max_ctx: int = 2048, max_block: int = 16,
-                 gguf_path: str | None = None):
+                 gguf_path: str | None = None, flags: int = 0):
         self.L = lc.lib()
         self.ctx = ctx
         h = C.c_void_p()
         if gguf_path is not None:
-            lc.check(self.L.lc_dflash_load_gguf(ctx.h, gguf_path.encode(), max_ctx, max_block, C.byref(h)),
-                     "lc_dflash_load_gguf")
+            lc.check(self.L.lc_dflash_load_gguf_ex(ctx.h, gguf_path.encode(), max_ctx, max_block, flags,
+                                                   C.byref(h)), "lc_dflash_load_gguf_ex")
         else:
             lc.check(self.L.lc_dflash_create(ctx.h, C.byref(hp), max_ctx, max_block, C.byref(h)), "lc_dflash_create")
         self.h = h
@@ -109,6 +124,15 @@ class DFlash:
             self.close()
         except Exception:
             pass
+
+    def weight(self, name: str):
+        """(device address, dtype as stored, bytes) of a loaded tensor."""
+        p = C.c_void_p()
+        dt = C.c_int()
+        n = C.c_uint64()
+        lc.check(self.L.lc_dflash_weight(self.h, name.encode(), C.byref(p), C.byref(dt), C.byref(n)),
+                 "lc_dflash_weight")
+        return p.value, dt.value, n.value
 
     def set_tensor(self, name: str, dtype: int, data: np.ndarray):
         a = np.ascontiguousarray(data)

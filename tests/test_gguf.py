@@ -90,3 +90,42 @@ def test_rejects_bad_files(tmp_path):
     with pytest.raises(lc.LagunaError):
         Gguf(str(trunc))
     os.remove(str(trunc))
+
+
+def test_mapped_view_matches_read(tmp_path):
+    """lc_gguf_tensor_data hands out the tensor bytes from the file mapping:
+    the same bytes lc_gguf_read copies, at 32-byte aligned file offsets."""
+    rng = np.random.default_rng(4)
+    w4 = synth.q4k_blocks(16, 1024, rng)
+    b16 = rng.integers(0, 1 << 16, size=333, dtype=np.uint16)
+    path = str(tmp_path / "v.gguf")
+    write_gguf(path, {"block_count": 1}, [("q.weight", lc.Q4_K, (1024, 16), w4), ("h.weight", lc.BF16, (333,), b16),
+                                          ("e.weight", lc.F32, (0,), np.zeros(0, np.float32))])
+    g = Gguf(path)
+    for name in ("q.weight", "h.weight", "e.weight"):
+        v = g.view(name)
+        assert not v.flags.writeable
+        assert np.array_equal(v, g.read(name)), name
+    assert np.array_equal(g.view("h.weight").view(np.uint16), b16)
+    g.close()
+
+
+def test_tensor_past_end_of_file(tmp_path):
+    """A file cut inside its data section opens (the header is whole), and
+    reading a tensor that lies past the end is LC_ERR_IO -- read_exact's short
+    read in GGUFReader::read_tensor_data (src/gguf.rs:415-421)."""
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal(64).astype(np.float32)
+    b = rng.standard_normal(4096).astype(np.float32)
+    good = str(tmp_path / "g.gguf")
+    write_gguf(good, {"block_count": 1}, [("a.weight", lc.F32, (64,), a), ("b.weight", lc.F32, (4096,), b)])
+    raw = open(good, "rb").read()
+    cut = tmp_path / "cut.gguf"
+    cut.write_bytes(raw[:-100])
+    g = Gguf(str(cut))
+    assert np.array_equal(g.read("a.weight").view(np.float32), a)
+    for fn in (g.read, g.view):
+        with pytest.raises(lc.LagunaError) as e:
+            fn("b.weight")
+        assert e.value.status == lc.LC_ERR_IO
+    g.close()

@@ -127,3 +127,69 @@ def test_shards_on_one_gpu_combine(ctx, dev, oracle, dtype, m):
         if t != o:
             s = np.sort(logits[r])
             assert s[-1] - s[-2] <= 2e-3 * np.abs(logits[r]).max()
+
+
+# ---- failure detection on the host: a rank that is late or leaves -------------------
+
+def _late_rank_main(rank, world, port, mode, out_dir):
+    """Two gloo ranks reduce keys twice.  In step 2 rank 1 is late past the
+    group's timeout ("late") or has left after step 1 ("leaves"); rank 0's
+    reduction must end with an error within the timeout, not hang."""
+    import time
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=2))
+    outcome = "ok"
+    try:
+        keys = torch.full((4,), rank, dtype=torch.int64)
+        reduce_keys(keys)  # step 1: both ranks
+        assert keys.tolist() == [world - 1] * 4
+        if rank == 1:
+            if mode == "leaves":
+                return  # leaves between steps, nothing in flight
+            time.sleep(6)  # late past the timeout
+        t0 = time.perf_counter()
+        try:
+            reduce_keys(torch.full((4,), rank, dtype=torch.int64))  # step 2
+        except Exception as e:  # noqa: BLE001 -- the error is the outcome under test
+            outcome = f"error after {time.perf_counter() - t0:.1f}s: {type(e).__name__}"
+    finally:
+        with open(os.path.join(out_dir, f"rank{rank}.txt"), "w") as f:
+            f.write(outcome)
+        if outcome == "ok":
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["late", "leaves"])
+def test_key_reduction_with_a_missing_rank(tmp_path, mode):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    ps = [ctx.Process(target=_late_rank_main, args=(r, 2, _free_port_shared(tmp_path), mode, str(tmp_path)))
+          for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=60)
+    for p in ps:
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank hung")
+    out0 = open(tmp_path / "rank0.txt").read()
+    assert out0.startswith("error after"), out0
+    assert float(out0.split()[2].rstrip("s:")) < 10.0, out0
+
+
+_PORTS = {}
+
+
+def _free_port_shared(tmp_path):
+    # one port per test invocation, shared by both ranks
+    key = str(tmp_path)
+    if key not in _PORTS:
+        _PORTS[key] = _free_port()
+    return _PORTS[key]
