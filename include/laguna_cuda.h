@@ -401,6 +401,98 @@ int lc_dflash_forward_from_input(lc_dflash *m, const float *input, float *hidden
  * src/dflash.rs:482-485), then forward_from_input's layer loop. */
 int lc_dflash_forward_token(lc_dflash *m, uint32_t token_id, float *hidden, float *logits, uint32_t *n_vocab);
 
+/* ---- Target (Laguna) model: TargetModel (src/target.rs:105-748) ---------- */
+
+/* Model::from_reader (src/model.rs:29-129) for the target: dense keys as the
+ * DFlash reader, plus the SWA rope and expert sizes (metadata first, then the
+ * shapes of ffn_gate_exps / ffn_gate_shexp). */
+typedef struct {
+    uint32_t n_layers;            /* block_count */
+    uint32_t n_embd;              /* embedding_length */
+    uint32_t n_ff;                /* feed_forward_length (dense FFN) */
+    uint32_t n_heads;             /* attention.head_count (first array element) */
+    uint32_t n_kv_heads;          /* attention.head_count_kv (second array element) */
+    uint32_t head_dim;            /* attention.key_length (no fallback) */
+    uint32_t rope_dim;            /* rope.dimension_count */
+    uint32_t rope_dim_swa;        /* rope.dimension_count_swa */
+    uint32_t swa;                 /* rope_dim_swa > 0 or attention.sliding_window > 0 (src/target.rs:328) */
+    uint32_t n_expert;            /* expert.count, else the last dim of ffn_gate_exps */
+    uint32_t n_expert_used;       /* expert.used_count, else 10 when experts exist */
+    uint32_t n_ff_exp;            /* expert.feed_forward_length, else from the shapes */
+    uint32_t n_ff_shexp;          /* expert.shared_feed_forward_length, else from the shapes */
+    uint32_t has_moe;             /* a tensor named *ffn_gate_exps*: layers >= 1 are MoE */
+    uint32_t has_shexp;           /* a tensor named *ffn_gate_shexp* */
+    uint32_t expert_weights_norm; /* expert_weights_norm (default 0) */
+    uint32_t n_vocab;             /* token_embd elements / n_embd (src/target.rs:287-291) */
+    float rope_base;              /* rope.freq_base, default 500000 */
+    float rope_base_swa;          /* rope.freq_base_swa, default 10000 */
+    float expert_weights_scale;   /* expert_weights_scale, default 1 */
+    float norm_eps;               /* 1e-5 (src/target.rs:970) */
+    float qk_eps;                 /* 1e-6 (src/target.rs:897) */
+} lc_target_hparams;
+
+typedef struct lc_target lc_target;
+
+int lc_gguf_target_hparams(const lc_gguf *g, lc_target_hparams *out);
+
+/* TargetModel::load (src/target.rs:130-266) on the loader of
+ * lc_dflash_load_gguf_ex (mapped file, pinned staging, one allocation; raw
+ * F32 / Q8_0 / Q4_K blocks, F16 / BF16 decoded to f32).  Dense layers take
+ * ffn_gate/up/down, MoE layers (layer >= 1 of a model with experts) the
+ * router, expert and shared-expert tensors.  The K/V cache holds max_ctx
+ * positions per layer; a forward takes at most max_block tokens.  Flags:
+ * LC_LOAD_BF16_NATIVE, and LC_TARGET_REF_EXPERT_OFFSET, which reproduces the
+ * reference's dispatch_proj_quant_expert (src/target.rs:1098-1162), where the
+ * expert offset reaches only the Q4_K kernel so every Q8_0 / F32 expert
+ * projection reads expert 0; by default every format reads its own expert. */
+enum { LC_TARGET_REF_EXPERT_OFFSET = 2 };
+int lc_target_load_gguf(lc_ctx *ctx, const char *path, uint32_t max_ctx, uint32_t max_block, uint32_t flags,
+                        lc_target **out);
+int lc_target_destroy(lc_target *t);
+int lc_target_get_hparams(const lc_target *t, lc_target_hparams *out);
+/* Layer `layer`: MoE or dense, and its query heads (attn_q rows / head_dim,
+ * src/target.rs:225-235). */
+int lc_target_layer_info(const lc_target *t, uint32_t layer, uint32_t *is_moe, uint32_t *n_q_heads);
+/* The device copy of a loaded tensor, as lc_dflash_weight. */
+int lc_target_weight(const lc_target *t, const char *name, const void **data, int *dtype, uint64_t *bytes);
+/* x [m, n_embd] (device) <- the token embeddings of tokens[m] (host): row
+ * token of token_embd decoded with dequant_to_f32 (target_token_embedding,
+ * src/lib.rs:431-454). */
+int lc_target_embed(lc_target *t, const uint32_t *tokens, uint32_t m, float *x);
+/* forward_token_impl (src/target.rs:314-578) for m token inputs x [m, n_embd]
+ * (device).  Without LC_TARGET_CACHED each row is forward_token: position 0,
+ * attending to itself only, nothing cached.  With it the rows are the next m
+ * positions of one sequence (cache_len .. cache_len + m - 1): their K/V are
+ * appended to the cache and each row attends causally over the cache -- one
+ * launch sequence for a block of draft tokens, equal to m calls of
+ * forward_token_cached.  Outputs (device, each optional):
+ *   captured [m, n_capture, n_embd]: the input of each listed layer (index
+ *     n_layers = the last layer's output), in increasing layer order;
+ *   hidden [m, n_embd]: the output_norm'ed state;
+ *   logits [m, n_vocab]: output.weight . hidden (hidden itself without an
+ *     output weight, src/target.rs:564-575);
+ *   keys [m]: lc_pack_key(max logit, token), the last maximum winning. */
+enum { LC_TARGET_CACHED = 1 };
+int lc_target_forward(lc_target *t, const float *x, uint32_t m, uint32_t flags, const uint32_t *capture_layers,
+                      uint32_t n_capture, float *captured, float *hidden, float *logits, uint64_t *keys);
+/* Positions held in the K/V cache (TargetKvCache::len). */
+int lc_target_cache_len(const lc_target *t, uint32_t *len);
+/* Drop cached positions from len on (rejected draft tokens); len = 0 is
+ * TargetKvCache::clear. */
+int lc_target_cache_truncate(lc_target *t, uint32_t len);
+
+/* dispatch_moe_ffn (src/target.rs:607-748) on the device for m rows of the
+ * normalised input x [m, n_embd]: router logits, sigmoid + bias top-k
+ * selection (ties to the lower expert), optional normalisation and scale,
+ * the selected experts' SwiGLU FFNs with the reference's per-expert L2
+ * rescaling of the hidden vector, their weighted sum and the shared expert.
+ * y [m, n_embd] = the FFN output (the residual add stays with the caller).
+ * Expert tensors hold n_expert matrices back to back (gate / up: n_ff_exp x
+ * n_embd each, down: n_embd x n_ff_exp).  ids / scores [m, n_expert_used]
+ * (device, optional) receive the selection.  Uses the target's workspaces. */
+int lc_target_moe_ffn(lc_target *t, uint32_t layer, const float *x, uint32_t m, float *y, int32_t *ids,
+                      float *scores);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,6 +9,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <map>
 #include <string>
 #include <vector>
@@ -21,22 +22,33 @@ namespace {
 
 struct Value {
     enum Kind { NUM_U, NUM_I, NUM_F, BOOL, STR, ARR } kind = NUM_U;
+    uint32_t type = 0;  // GGUF value type id (0..12)
     uint64_t u = 0;
     int64_t i = 0;
     double f = 0;
     std::string s;
     std::vector<Value> arr;
+    // GGUF ids of the 32- and 64-bit numbers, the only ones the accessors take
+    static bool wide_int(uint32_t t) { return t == 4 || t == 5 || t == 10 || t == 11; }
+    static bool wide_float(uint32_t t) { return t == 6 || t == 12; }
     bool as_u64(uint64_t *out) const {
-        // GGUFValue::as_u64 (src/gguf.rs:229-237): U32/U64/I32/I64 only
-        if (kind == NUM_U) return *out = u, true;
-        if (kind == NUM_I) return *out = (uint64_t)i, true;
-        return false;
+        // GGUFValue::as_u64 (src/gguf.rs:228-237): U32/U64/I32/I64 only
+        if (!wide_int(type)) return false;
+        *out = kind == NUM_U ? u : (uint64_t)i;
+        return true;
     }
     bool as_f32(float *out) const {
-        // GGUFValue::as_f32 (src/gguf.rs:239-249)
-        if (kind == NUM_F) return *out = (float)f, true;
-        if (kind == NUM_U) return *out = (float)u, true;
-        if (kind == NUM_I) return *out = (float)i, true;
+        // GGUFValue::as_f32 (src/gguf.rs:239-249): F32/F64 and the wide integers
+        if (wide_float(type)) return *out = (float)f, true;
+        if (!wide_int(type)) return false;
+        *out = kind == NUM_U ? (float)u : (float)i;
+        return true;
+    }
+    bool as_bool(bool *out) const {
+        // GGUFValue::as_bool (src/gguf.rs:251-262): Bool, wide integers, floats
+        if (type == 7) return *out = u != 0, true;
+        if (wide_int(type)) return *out = (kind == NUM_U ? u : (uint64_t)i) != 0, true;
+        if (wide_float(type)) return *out = f != 0.0, true;
         return false;
     }
 };
@@ -95,6 +107,7 @@ bool read_string(Src &f, std::string *s) {
 // read_value (src/gguf.rs:441-514): GGUF value type ids 0..12.
 bool read_value(Src &f, uint32_t type, Value *v, int depth = 0) {
     if (depth > 4) return false;
+    v->type = type;
     switch (type) {
     case 0: { uint8_t x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_U; v->u = x; return true; }
     case 1: { int8_t x; if (!rdv(f, &x)) return false; v->kind = Value::NUM_I; v->i = x; return true; }
@@ -355,5 +368,77 @@ extern "C" int lc_gguf_dflash_hparams(const lc_gguf *g, lc_dflash_hparams *hp) {
         if (v->kind == Value::ARR) hp->n_aux = (uint32_t)v->arr.size();
     hp->norm_eps = 1e-5f;
     hp->qk_eps = 1e-6f;
+    return LC_OK;
+}
+
+extern "C" int lc_gguf_target_hparams(const lc_gguf *g, lc_target_hparams *hp) {
+    if (!g || !hp) return lc_fail(LC_ERR_INVALID, "lc_gguf_target_hparams: null argument");
+    memset(hp, 0, sizeof(*hp));
+    // Model::from_reader (src/model.rs:29-129) over populate_metadata's aliases
+    // (src/gguf.rs:516-653); the DFlash reader shares the dense keys.
+    lc_dflash_hparams d;
+    lc_gguf_dflash_hparams(g, &d);
+    auto u64 = [&](std::initializer_list<const char *> keys) -> uint64_t {
+        const Value *v = find_any(g, keys);
+        uint64_t r = 0;
+        if (v) v->as_u64(&r);
+        return r;
+    };
+    hp->n_layers = d.n_layers;
+    hp->n_embd = d.n_embd;
+    hp->n_ff = d.n_ff;
+    hp->n_heads = d.n_heads;
+    hp->n_kv_heads = d.n_kv_heads;
+    hp->head_dim = (uint32_t)u64({"laguna.attention.key_length", "dflash.attention.key_length"});  // no fallback
+    hp->rope_dim = d.rope_dim;
+    hp->rope_dim_swa = (uint32_t)u64({"rope.dimension_count_swa", "laguna.rope.dimension_count_swa",
+                                      "dflash.rope.dimension_count_swa"});
+    const uint64_t window = u64({"laguna.attention.sliding_window", "dflash.attention.sliding_window"});
+    hp->swa = hp->rope_dim_swa > 0 || window > 0;  // src/target.rs:328
+    hp->rope_base = d.rope_base;
+    hp->rope_base_swa = 10000.0f;  // src/target.rs:362-367
+    if (const Value *v = find_any(g, {"rope.freq_base_swa", "laguna.rope.freq_base_swa", "dflash.rope.freq_base_swa"})) {
+        float f;
+        if (v->as_f32(&f)) hp->rope_base_swa = f;
+    }
+    hp->expert_weights_scale = 1.0f;  // src/target.rs:672
+    if (const Value *v = find_any(g, {"expert_weights_scale", "laguna.expert_weights_scale",
+                                      "dflash.expert_weights_scale"})) {
+        float f;
+        if (v->as_f32(&f)) hp->expert_weights_scale = f;
+    }
+    if (const Value *v = find_any(g, {"expert_weights_norm", "laguna.expert_weights_norm",
+                                      "dflash.expert_weights_norm"})) {
+        bool b;
+        if (v->as_bool(&b)) hp->expert_weights_norm = b;
+    }
+    // expert sizes: metadata first, else the tensors' shapes (src/model.rs:43-107)
+    uint64_t ffn_from_shape = 0, exp_from_shape = 0;
+    bool has_moe = false, has_shexp = false;
+    for (const Tensor &t : g->tensors) {
+        const bool gate_exps = t.name.find("ffn_gate_exps") != std::string::npos;
+        const bool gate_shexp = t.name.find("ffn_gate_shexp") != std::string::npos;
+        if ((gate_exps || gate_shexp) && t.shape.size() >= 2) ffn_from_shape = std::max<uint64_t>(ffn_from_shape, t.shape[1]);
+        if (gate_exps && t.shape.size() == 3) exp_from_shape = std::max<uint64_t>(exp_from_shape, t.shape[2]);
+        has_moe |= gate_exps;
+        has_shexp |= gate_shexp;
+        if (t.name == "token_embd.weight" && hp->n_embd) {
+            uint64_t n = 1;
+            for (uint64_t dim : t.shape) n *= dim;
+            hp->n_vocab = (uint32_t)(n / hp->n_embd);  // TargetModel::vocab_size (src/target.rs:287-291)
+        }
+    }
+    const uint64_t exp_count = u64({"expert.count", "expert_count"});
+    const uint64_t exp_used = u64({"expert.used_count", "expert_used_count"});
+    const uint64_t ffn_exp = u64({"expert.feed_forward_length", "expert_feed_forward_length"});
+    const uint64_t ffn_sh = u64({"expert.shared_feed_forward_length", "expert_shared_feed_forward_length"});
+    hp->n_ff_exp = (uint32_t)(ffn_exp ? ffn_exp : ffn_from_shape);
+    hp->n_ff_shexp = (uint32_t)(ffn_sh ? ffn_sh : ffn_from_shape);
+    hp->n_expert = (uint32_t)(exp_count ? exp_count : exp_from_shape);
+    hp->n_expert_used = (uint32_t)(exp_used ? exp_used : (exp_from_shape ? 10 : 0));
+    hp->has_moe = has_moe;
+    hp->has_shexp = has_shexp;
+    hp->norm_eps = 1e-5f;  // dispatch_rmsnorm (src/target.rs:970)
+    hp->qk_eps = 1e-6f;    // dispatch_qk_norm_rope (src/target.rs:897)
     return LC_OK;
 }

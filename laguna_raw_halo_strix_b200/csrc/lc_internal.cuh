@@ -6,6 +6,9 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <functional>
+#include <vector>
+
 #include "laguna_cuda.h"
 
 // Context: one device, one stream, one grow-only scratch arena.
@@ -189,10 +192,11 @@ struct ProjOut {
     bool accumulate = false;
 };
 int gemm_dq_group(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *outs, int ng, uint32_t m, uint32_t k);
-// lc_qk_norm_rope of the block's Q and K in one launch where possible (lc_ops.cu).
+// lc_qk_norm_rope of the block's Q and K in one launch where possible; row r
+// is rotated at position pos0 + r * pos_step (lc_ops.cu).
 int qk_norm_rope_pair(lc_ctx *ctx, const float *xa, const float *wa, float *ya, uint32_t n_heads_a, const float *xb,
                       const float *wb, float *yb, uint32_t n_heads_b, const float *freq, uint32_t m,
-                      uint32_t head_dim, uint32_t rope_dim, float eps, uint32_t pos0);
+                      uint32_t head_dim, uint32_t rope_dim, float eps, uint32_t pos0, uint32_t pos_step = 1);
 // Projections of 1 or 2 tokens with f32 activations (lc_gemv.cu): up to
 // kGroupMax weight matrices of one format and one k sharing the activations
 // (src.x, or SiLU(src.x) * src.x2 for LC_PACK_SWIGLU), rows streamed from HBM
@@ -202,6 +206,31 @@ int gemv_rows(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *outs, i
 // lc_dequant, or with bf16_native a BF16 tensor decoded as bfloat16 (f32 =
 // bits << 16) instead of the reference's f16 reading (lc_ops.cu).
 int dequant_f32(lc_ctx *ctx, int dtype, const void *src, size_t src_bytes, size_t n, float *out, bool bf16_native);
+// A tensor held on the device by a model: raw GGUF blocks (F32 / Q8_0 / Q4_K)
+// or f32 decoded from F16 / BF16; shape is GGUF's (ne0 first).
+struct DevTensor {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+    int dtype = -1;
+    uint64_t n_el = 0;
+    uint64_t shape[4] = {1, 1, 1, 1};
+    uint32_t n_dims = 0;
+};
+// Upload every tensor of g for which slot(name) returns a DevTensor into one
+// device allocation (appended to *allocs), through pinned staging; F16 / BF16
+// are decoded to f32 (bfloat16 proper with LC_LOAD_BF16_NATIVE).  Waits for
+// the copies before returning (lc_load.cu).
+int load_tensors(lc_ctx *ctx, lc_gguf *g, const std::function<DevTensor *(const char *)> &slot, uint32_t flags,
+                 std::vector<void *> *allocs);
+// A projection by the tensor's own dtype with its size checked (lc_model.cu).
+int proj_w(lc_ctx *c, const DevTensor &w, const char *what, const float *x, float *y, uint32_t rows, uint32_t k,
+           uint32_t n);
+// Projections of one activation block: grouped into one tcgen05 launch where
+// the shapes allow, else one projection per weight with the input op
+// materialised in `materialized` and accumulated outputs summed through `tmp`
+// (lc_model.cu).
+int proj_w_block(lc_ctx *c, float *tmp, const PackSrc &src, float *materialized, ProjOut *outs,
+                 const DevTensor *const *ws, const char *const *names, int ng, uint32_t rows, uint32_t k);
 // True when a projection of m rows would run the tcgen05 GEMM (gemm_dq).
 bool routes_to_gemm_dq(const lc_ctx *ctx, uint32_t m);
 // 3..16-token projections on tcgen05 kind::i8 (lc_gemm.cu); LC_ERR_UNSUPPORTED when

@@ -12,19 +12,13 @@
 
 #include <algorithm>
 #include <string>
-#include <thread>
 #include <vector>
 
 #include "lc_internal.cuh"
 
 namespace {
 
-struct Weight {
-    void *ptr = nullptr;
-    size_t bytes = 0;
-    int dtype = -1;
-    uint64_t n_el = 0;
-};
+using Weight = lc::DevTensor;
 
 struct LayerW {
     Weight attn_norm, q, k, v, o, q_norm, k_norm, gate_attn, ffn_norm, gate, up, down;
@@ -115,28 +109,27 @@ static int grow(float **buf, size_t *cap, size_t count) {
 }
 
 // A projection by the weight's own dtype, with the shape checked against it.
-static int proj(lc_dflash *m, const Weight &w, const char *what, const float *x, float *y, uint32_t rows, uint32_t k,
-                uint32_t n) {
-    if (!w.ptr) return lc_fail(LC_ERR_INVALID, "lc_dflash: missing tensor %s", what);
+int lc::proj_w(lc_ctx *c, const DevTensor &w, const char *what, const float *x, float *y, uint32_t rows, uint32_t k,
+               uint32_t n) {
+    if (!w.ptr) return lc_fail(LC_ERR_INVALID, "missing tensor %s", what);
     if (w.n_el < (uint64_t)k * n)
-        return lc_fail(LC_ERR_INVALID, "lc_dflash: %s has %llu elements, need %u x %u", what,
-                       (unsigned long long)w.n_el, n, k);
-    return lc_proj_m(m->ctx, w.dtype, x, w.ptr, y, rows, k, n, 0);
+        return lc_fail(LC_ERR_INVALID, "%s has %llu elements, need %u x %u", what, (unsigned long long)w.n_el, n, k);
+    return lc_proj_m(c, w.dtype, x, w.ptr, y, rows, k, n, 0);
 }
 
 // Projections of one activation block (lc::gemm_dq_group): one packing and one
 // tcgen05 GEMM launch when every weight has the same quantized dtype and the
 // block size runs that GEMM.  Otherwise one projection per weight, with the
 // element-wise input op and the residual adds as their own launches, in the
-// reference's order; `materialized` (rows x k) receives the op's result there.
-static int proj_block(lc_dflash *m, const lc::PackSrc &src, float *materialized, lc::ProjOut *outs,
-                      const Weight *const *ws, const char *const *names, int ng, uint32_t rows, uint32_t k) {
-    lc_ctx *c = m->ctx;
+// reference's order; `materialized` (rows x k) receives the op's result there
+// and `tmp` (rows x the widest accumulated output) the summands.
+int lc::proj_w_block(lc_ctx *c, float *tmp, const PackSrc &src, float *materialized, ProjOut *outs,
+                     const DevTensor *const *ws, const char *const *names, int ng, uint32_t rows, uint32_t k) {
     bool grouped = lc::routes_to_gemm_dq(c, rows);
     for (int i = 0; i < ng; i++) {
-        if (!ws[i]->ptr) return lc_fail(LC_ERR_INVALID, "lc_dflash: missing tensor %s", names[i]);
+        if (!ws[i]->ptr) return lc_fail(LC_ERR_INVALID, "missing tensor %s", names[i]);
         if (ws[i]->n_el < (uint64_t)k * outs[i].n)
-            return lc_fail(LC_ERR_INVALID, "lc_dflash: %s has %llu elements, need %u x %u", names[i],
+            return lc_fail(LC_ERR_INVALID, "%s has %llu elements, need %u x %u", names[i],
                            (unsigned long long)ws[i]->n_el, outs[i].n, k);
         outs[i].w = ws[i]->ptr;
         if (ws[i]->dtype != ws[0]->dtype) grouped = false;
@@ -159,13 +152,23 @@ static int proj_block(lc_dflash *m, const lc::PackSrc &src, float *materialized,
     }
     for (int i = 0; i < ng; i++) {
         if (!outs[i].accumulate) {
-            LC_TRY(proj(m, *ws[i], names[i], x, outs[i].y, rows, k, outs[i].n));
+            LC_TRY(proj_w(c, *ws[i], names[i], x, outs[i].y, rows, k, outs[i].n));
         } else {
-            LC_TRY(proj(m, *ws[i], names[i], x, m->tmp, rows, k, outs[i].n));
-            LC_TRY(lc_add(c, outs[i].y, m->tmp, outs[i].y, rows * outs[i].n));
+            LC_TRY(proj_w(c, *ws[i], names[i], x, tmp, rows, k, outs[i].n));
+            LC_TRY(lc_add(c, outs[i].y, tmp, outs[i].y, rows * outs[i].n));
         }
     }
     return LC_OK;
+}
+
+static int proj(lc_dflash *m, const Weight &w, const char *what, const float *x, float *y, uint32_t rows, uint32_t k,
+                uint32_t n) {
+    return lc::proj_w(m->ctx, w, what, x, y, rows, k, n);
+}
+
+static int proj_block(lc_dflash *m, const lc::PackSrc &src, float *materialized, lc::ProjOut *outs,
+                      const Weight *const *ws, const char *const *names, int ng, uint32_t rows, uint32_t k) {
+    return lc::proj_w_block(m->ctx, m->tmp, src, materialized, outs, ws, names, ng, rows, k);
 }
 
 static const float *need(const Weight &w, const char *what, int *status) {
@@ -288,149 +291,6 @@ extern "C" int lc_dflash_set_tensor(lc_dflash *m, const char *name, int dtype, c
     return LC_OK;
 }
 
-namespace {
-
-// Host copy of n bytes split over up to `threads` threads (the source is the
-// file mapping, so the page faults of a cold file are taken in parallel too).
-void par_copy(uint8_t *dst, const uint8_t *src, size_t n, unsigned threads) {
-    constexpr size_t kMinSlice = 4u << 20;
-    unsigned t = (unsigned)std::min<size_t>(threads, std::max<size_t>(1, n / kMinSlice));
-    if (t <= 1) {
-        memcpy(dst, src, n);
-        return;
-    }
-    const size_t slice = (n / t + 4095) & ~(size_t)4095;
-    std::vector<std::thread> pool;
-    for (unsigned i = 1; i < t; i++) {
-        const size_t a = std::min(n, i * slice), b = std::min(n, (i + 1) * slice);
-        if (a < b) pool.emplace_back([=] { memcpy(dst + a, src + a, b - a); });
-    }
-    memcpy(dst, src, std::min(n, slice));
-    for (auto &th : pool) th.join();
-}
-
-// One tensor of the device image: bytes [src, src + bytes) of the file mapping
-// go to image offset `at`; F16 / BF16 tensors are then decoded to f32 at `f32_at`.
-struct Piece {
-    Weight *slot;
-    int dtype;
-    const uint8_t *src;
-    uint64_t bytes, n_el, at, f32_at;
-};
-
-// Pinned staging of the device image: kBufs buffers of kChunk bytes.  The host
-// fills chunk c (every piece overlapping it) while the copy engine drains the
-// chunks before it; a buffer is refilled only after its event has fired.
-class Stager {
-  public:
-    static constexpr size_t kChunk = 64ull << 20;
-    static constexpr int kBufs = 3;
-
-    ~Stager() {
-        for (int i = 0; i < kBufs; i++) {
-            if (done_[i]) {
-                cudaEventSynchronize(done_[i]);
-                cudaEventDestroy(done_[i]);
-            }
-            if (buf_[i]) cudaFreeHost(buf_[i]);
-        }
-    }
-    int init(cudaStream_t st, size_t image_bytes) {
-        st_ = st;
-        const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
-        threads_ = std::min(8u, std::max(1u, hw / 2));
-        const int n = (int)std::min<size_t>(kBufs, (image_bytes + kChunk - 1) / kChunk);
-        for (int i = 0; i < n; i++) {
-            LC_CUDA(cudaHostAlloc((void **)&buf_[i], kChunk, cudaHostAllocDefault));
-            LC_CUDA(cudaEventCreateWithFlags(&done_[i], cudaEventDisableTiming));
-        }
-        nbuf_ = std::max(n, 1);
-        return LC_OK;
-    }
-    // Copy the image [0, image_bytes) described by `pieces` (sorted by `at`,
-    // non-overlapping) to dev.  Alignment gaps are left as they are.
-    int upload(uint8_t *dev, const std::vector<Piece> &pieces, size_t image_bytes) {
-        size_t first = 0;
-        for (size_t c0 = 0, chunk = 0; c0 < image_bytes; c0 += kChunk, chunk++) {
-            const size_t c1 = std::min(image_bytes, c0 + kChunk);
-            const int b = (int)(chunk % (size_t)nbuf_);
-            LC_CUDA(cudaEventSynchronize(done_[b]));
-            while (first < pieces.size() && pieces[first].at + pieces[first].bytes <= c0) first++;
-            for (size_t i = first; i < pieces.size() && pieces[i].at < c1; i++) {
-                const Piece &p = pieces[i];
-                const size_t a = std::max<size_t>(c0, p.at), e = std::min<size_t>(c1, p.at + p.bytes);
-                if (a < e) par_copy(buf_[b] + (a - c0), p.src + (a - p.at), e - a, threads_);
-            }
-            LC_CUDA(cudaMemcpyAsync(dev + c0, buf_[b], c1 - c0, cudaMemcpyHostToDevice, st_));
-            LC_CUDA(cudaEventRecord(done_[b], st_));
-        }
-        return LC_OK;
-    }
-
-  private:
-    cudaStream_t st_ = nullptr;
-    uint8_t *buf_[kBufs] = {};
-    cudaEvent_t done_[kBufs] = {};
-    int nbuf_ = 1;
-    unsigned threads_ = 1;
-};
-
-// The upload half of lc_dflash_load_gguf_ex: lay every used tensor out in one
-// device image (256-byte aligned, file order), stream it through the stager,
-// decode F16 / BF16 tensors to f32 behind it on the same stream, then wait once.
-int load_weights(lc_dflash *m, lc_gguf *g, uint32_t flags) {
-    std::vector<Piece> pieces;
-    uint64_t image = 0;
-    auto align = [](uint64_t v) { return (v + 255) & ~(uint64_t)255; };
-    for (uint64_t i = 0; i < lc_gguf_tensor_count(g); i++) {
-        const char *name;
-        int dtype;
-        uint64_t nbytes;
-        LC_TRY(lc_gguf_tensor_info(g, i, &name, &dtype, nullptr, nullptr, nullptr, &nbytes));
-        Weight *w = slot_for(m, name);
-        if (!w) continue;  // tensors the draft path does not use, like DFlashModel::load
-        const uint64_t be = lc_type_block_elements(dtype), bb = lc_type_block_bytes(dtype);
-        LC_REQUIRE(be && bb, LC_ERR_UNSUPPORTED, "lc_dflash_load_gguf: %s has unsupported type %d", name, dtype);
-        const void *src;
-        LC_TRY(lc_gguf_tensor_data(g, i, &src, nullptr));
-        image = align(image);
-        pieces.push_back(Piece{w, dtype, (const uint8_t *)src, nbytes, nbytes / bb * be, image, 0});
-        image += nbytes;
-    }
-    uint64_t total = align(image);
-    for (Piece &p : pieces)
-        if (p.dtype == LC_F16 || p.dtype == LC_BF16) {
-            p.f32_at = total;
-            total = align(total + p.n_el * 4);
-        }
-    if (pieces.empty()) return LC_OK;
-    void *arena = nullptr;
-    LC_TRY(dalloc(m, total, &arena));
-    uint8_t *dev = (uint8_t *)arena;
-    {
-        Stager stager;
-        LC_TRY(stager.init(m->ctx->stream, image));
-        LC_TRY(stager.upload(dev, pieces, image));
-        for (const Piece &p : pieces) {
-            Weight *w = p.slot;
-            if (p.dtype == LC_F16 || p.dtype == LC_BF16) {
-                // dequant_to_f32 rules (src/dflash.rs:351-378, :437-462), or bfloat16 on request
-                const bool native = p.dtype == LC_BF16 && (flags & LC_LOAD_BF16_NATIVE);
-                LC_TRY(lc::dequant_f32(m->ctx, p.dtype, dev + p.at, p.bytes, p.n_el, (float *)(dev + p.f32_at),
-                                       native));
-                *w = Weight{dev + p.f32_at, (size_t)p.n_el * 4, LC_F32, p.n_el};
-            } else {
-                *w = Weight{dev + p.at, (size_t)p.bytes, p.dtype, p.n_el};
-            }
-        }
-        // The stager's destructor waits for its buffers before freeing them.
-    }
-    LC_CUDA(cudaStreamSynchronize(m->ctx->stream));
-    return LC_OK;
-}
-
-}  // namespace
-
 extern "C" int lc_dflash_load_gguf_ex(lc_ctx *ctx, const char *path, uint32_t max_ctx, uint32_t max_block,
                                       uint32_t flags, lc_dflash **out) {
     LC_REQUIRE(ctx && path && out, LC_ERR_INVALID, "lc_dflash_load_gguf: null argument");
@@ -443,7 +303,8 @@ extern "C" int lc_dflash_load_gguf_ex(lc_ctx *ctx, const char *path, uint32_t ma
     int s = lc_gguf_dflash_hparams(g, &hp);
     lc_dflash *m = nullptr;
     if (!s) s = lc_dflash_create(ctx, &hp, max_ctx, max_block, &m);
-    if (!s) s = load_weights(m, g, flags);
+    if (!s)
+        s = lc::load_tensors(ctx, g, [m](const char *name) { return slot_for(m, name); }, flags, &m->allocs);
     lc_gguf_close(g);
     if (s) {
         lc_dflash_destroy(m);

@@ -91,7 +91,7 @@ struct QkPair {
 };
 
 __global__ void qk_norm_rope128_kernel(const QkPair p, const float *__restrict__ freq, int rope, float eps,
-                                       uint32_t pos0) {
+                                       uint32_t pos0, uint32_t pos_step) {
     __shared__ float2 cs[64];
     const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const bool second = (int)blockIdx.y >= p.nb0;
@@ -100,7 +100,7 @@ __global__ void qk_norm_rope128_kernel(const QkPair p, const float *__restrict__
     float *y = second ? p.y[1] : p.y[0];
     const int n_heads = second ? p.n_heads[1] : p.n_heads[0];
     const int h = ((int)blockIdx.y - (second ? p.nb0 : 0)) * 4 + warp;
-    const uint32_t pos = pos0 + row;
+    const uint32_t pos = pos0 + row * pos_step;
     if (rope && threadIdx.x < 64) {
         float sf, cf;
         sincosf(freq[threadIdx.x] * (float)pos, &sf, &cf);
@@ -129,15 +129,17 @@ __global__ void qk_norm_rope128_kernel(const QkPair p, const float *__restrict__
 }
 
 // qk_norm_rope.comp:29-67 for one row (n_heads*head_dim) per CTA at position
-// pos0 + row.  The row is staged in shared memory first so out may alias x.
+// pos0 + row * pos_step.  The row is staged in shared memory first so out may
+// alias x.
 __global__ void qk_norm_rope_kernel(const float *x, const float *__restrict__ w, const float *__restrict__ freq,
-                                    float *y, int n_heads, int head_dim, int rope_dim, float eps, uint32_t pos0) {
+                                    float *y, int n_heads, int head_dim, int rope_dim, float eps, uint32_t pos0,
+                                    uint32_t pos_step) {
     extern __shared__ float srow[];  // total + n_heads
     const int total = n_heads * head_dim;
     float *rms = srow + total;
     const float *xr = x + (size_t)blockIdx.x * total;
     float *yr = y + (size_t)blockIdx.x * total;
-    const uint32_t pos = pos0 + blockIdx.x;
+    const uint32_t pos = pos0 + blockIdx.x * pos_step;
     for (int i = threadIdx.x; i < total; i += blockDim.x) srow[i] = xr[i];
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -357,9 +359,9 @@ extern "C" int lc_rmsnorm(lc_ctx *ctx, const float *w, const float *x, float *ou
     return lc_after_launch(ctx, "lc_rmsnorm");
 }
 
-extern "C" int lc_qk_norm_rope(lc_ctx *ctx, const float *x, const float *w, const float *freq, float *out,
-                               uint32_t m, uint32_t n_heads, uint32_t head_dim, uint32_t rope_dim, float eps,
-                               uint32_t pos0) {
+static int qk_norm_rope_steps(lc_ctx *ctx, const float *x, const float *w, const float *freq, float *out,
+                              uint32_t m, uint32_t n_heads, uint32_t head_dim, uint32_t rope_dim, float eps,
+                              uint32_t pos0, uint32_t pos_step) {
     LC_BEGIN(ctx, "lc_qk_norm_rope");
     if (m == 0 || n_heads == 0) return LC_OK;
     LC_REQUIRE(x && w && out && (freq || rope_dim == 0), LC_ERR_INVALID, "lc_qk_norm_rope: null pointer");
@@ -373,7 +375,7 @@ extern "C" int lc_qk_norm_rope(lc_ctx *ctx, const float *x, const float *w, cons
                "lc_qk_norm_rope: rope_dim %u must be 0 or head_dim %u", rope_dim, head_dim);
     if (head_dim == 128 && (((uintptr_t)x | (uintptr_t)w | (uintptr_t)out) & 15) == 0) {
         QkPair p = {{x, x}, {w, w}, {out, out}, {(int)n_heads, 0}, (int)(n_heads + 3) / 4};
-        qk_norm_rope128_kernel<<<dim3(m, p.nb0), 128, 0, ctx->stream>>>(p, freq, rope_dim ? 1 : 0, eps, pos0);
+        qk_norm_rope128_kernel<<<dim3(m, p.nb0), 128, 0, ctx->stream>>>(p, freq, rope_dim ? 1 : 0, eps, pos0, pos_step);
         return lc_after_launch(ctx, "lc_qk_norm_rope");
     }
     const size_t smem = ((size_t)n_heads * head_dim + n_heads) * 4;
@@ -382,8 +384,14 @@ extern "C" int lc_qk_norm_rope(lc_ctx *ctx, const float *x, const float *w, cons
     if (smem > 48 * 1024)
         if (int s = lc_set_smem_attr((const void *)qk_norm_rope_kernel, smem)) return s;
     qk_norm_rope_kernel<<<m, 256, smem, ctx->stream>>>(x, w, freq, out, (int)n_heads, (int)head_dim, (int)rope_dim,
-                                                        eps, pos0);
+                                                        eps, pos0, pos_step);
     return lc_after_launch(ctx, "lc_qk_norm_rope");
+}
+
+extern "C" int lc_qk_norm_rope(lc_ctx *ctx, const float *x, const float *w, const float *freq, float *out,
+                               uint32_t m, uint32_t n_heads, uint32_t head_dim, uint32_t rope_dim, float eps,
+                               uint32_t pos0) {
+    return qk_norm_rope_steps(ctx, x, w, freq, out, m, n_heads, head_dim, rope_dim, eps, pos0, 1);
 }
 
 namespace lc {
@@ -392,21 +400,22 @@ namespace lc {
 // head_dim 128 kernel.
 int qk_norm_rope_pair(lc_ctx *ctx, const float *xa, const float *wa, float *ya, uint32_t n_heads_a, const float *xb,
                       const float *wb, float *yb, uint32_t n_heads_b, const float *freq, uint32_t m,
-                      uint32_t head_dim, uint32_t rope_dim, float eps, uint32_t pos0) {
+                      uint32_t head_dim, uint32_t rope_dim, float eps, uint32_t pos0, uint32_t pos_step) {
     const bool fused = m > 0 && n_heads_a > 0 && n_heads_b > 0 && head_dim == 128 &&
                        (rope_dim == 0 || rope_dim == head_dim) && xa && wa && ya && xb && wb && yb &&
                        (freq || rope_dim == 0) &&
                        (((uintptr_t)xa | (uintptr_t)wa | (uintptr_t)ya | (uintptr_t)xb | (uintptr_t)wb |
                          (uintptr_t)yb) & 15) == 0;
     if (!fused) {
-        const int s = lc_qk_norm_rope(ctx, xa, wa, freq, ya, m, n_heads_a, head_dim, rope_dim, eps, pos0);
+        const int s = qk_norm_rope_steps(ctx, xa, wa, freq, ya, m, n_heads_a, head_dim, rope_dim, eps, pos0, pos_step);
         if (s) return s;
-        return lc_qk_norm_rope(ctx, xb, wb, freq, yb, m, n_heads_b, head_dim, rope_dim, eps, pos0);
+        return qk_norm_rope_steps(ctx, xb, wb, freq, yb, m, n_heads_b, head_dim, rope_dim, eps, pos0, pos_step);
     }
     LC_BEGIN(ctx, "lc_qk_norm_rope");
     const int nb0 = (int)(n_heads_a + 3) / 4, nb1 = (int)(n_heads_b + 3) / 4;
     QkPair p = {{xa, xb}, {wa, wb}, {ya, yb}, {(int)n_heads_a, (int)n_heads_b}, nb0};
-    qk_norm_rope128_kernel<<<dim3(m, nb0 + nb1), 128, 0, ctx->stream>>>(p, freq, rope_dim ? 1 : 0, eps, pos0);
+    qk_norm_rope128_kernel<<<dim3(m, nb0 + nb1), 128, 0, ctx->stream>>>(p, freq, rope_dim ? 1 : 0, eps, pos0,
+                                                                         pos_step);
     return lc_after_launch(ctx, "lc_qk_norm_rope");
 }
 }  // namespace lc

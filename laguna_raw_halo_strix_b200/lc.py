@@ -133,6 +133,18 @@ SIGNATURES = {
     "lc_dflash_load_gguf": (_i, [_vp, C.c_char_p, _u32, _u32, C.POINTER(_vp)]),
     "lc_dflash_load_gguf_ex": (_i, [_vp, C.c_char_p, _u32, _u32, _u32, C.POINTER(_vp)]),
     "lc_dflash_weight": (_i, [_vp, C.c_char_p, C.POINTER(_vp), C.POINTER(_i), C.POINTER(C.c_uint64)]),
+    # target model
+    "lc_gguf_target_hparams": (_i, [_vp, _vp]),
+    "lc_target_load_gguf": (_i, [_vp, C.c_char_p, _u32, _u32, _u32, C.POINTER(_vp)]),
+    "lc_target_destroy": (_i, [_vp]),
+    "lc_target_get_hparams": (_i, [_vp, _vp]),
+    "lc_target_layer_info": (_i, [_vp, _u32, C.POINTER(_u32), C.POINTER(_u32)]),
+    "lc_target_weight": (_i, [_vp, C.c_char_p, C.POINTER(_vp), C.POINTER(_i), C.POINTER(C.c_uint64)]),
+    "lc_target_embed": (_i, [_vp, C.POINTER(_u32), _u32, _vp]),
+    "lc_target_forward": (_i, [_vp, _vp, _u32, _u32, C.POINTER(_u32), _u32, _vp, _vp, _vp, _vp]),
+    "lc_target_cache_len": (_i, [_vp, C.POINTER(_u32)]),
+    "lc_target_cache_truncate": (_i, [_vp, _u32]),
+    "lc_target_moe_ffn": (_i, [_vp, _u32, _vp, _u32, _vp, _vp, _vp]),
     "lc_dflash_destroy": (_i, [_vp]),
     "lc_dflash_get_hparams": (_i, [_vp, _vp]),
     "lc_dflash_encode": (_i, [_vp, _vp, _u32, _vp]),
@@ -150,6 +162,24 @@ class HParams(C.Structure):
     _fields_ = [("n_layers", _u32), ("n_embd", _u32), ("n_heads", _u32), ("n_kv_heads", _u32),
                 ("head_dim", _u32), ("rope_dim", _u32), ("n_ff", _u32), ("n_aux", _u32),
                 ("rope_base", _f), ("norm_eps", _f), ("qk_eps", _f)]
+
+
+class TargetHParams(C.Structure):
+    """lc_target_hparams (include/laguna_cuda.h)."""
+
+    _fields_ = [("n_layers", _u32), ("n_embd", _u32), ("n_ff", _u32), ("n_heads", _u32), ("n_kv_heads", _u32),
+                ("head_dim", _u32), ("rope_dim", _u32), ("rope_dim_swa", _u32), ("swa", _u32),
+                ("n_expert", _u32), ("n_expert_used", _u32), ("n_ff_exp", _u32), ("n_ff_shexp", _u32),
+                ("has_moe", _u32), ("has_shexp", _u32), ("expert_weights_norm", _u32), ("n_vocab", _u32),
+                ("rope_base", _f), ("rope_base_swa", _f), ("expert_weights_scale", _f), ("norm_eps", _f),
+                ("qk_eps", _f)]
+
+    def as_dict(self) -> dict:
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+TARGET_CACHED = 1  # lc_target_forward flag
+TARGET_REF_EXPERT_OFFSET = 2  # lc_target_load_gguf flag
 
 
 def _sources_newer(lib: str) -> bool:

@@ -403,5 +403,53 @@ size_t lco_argmax(const float *logits, size_t n) {
     return best;
 }
 
+void lco_gate_attn(const float *attn, const float *gate, float *out, uint32_t n_heads, uint32_t head_dim) {
+    for (uint32_t i = 0; i < n_heads * head_dim; i++) {
+        float g = logf(1.0f + expf(gate[i / head_dim]));
+        out[i] = attn[i] * g;
+    }
+}
+
+uint32_t lco_moe_select(const float *logits, const float *bias, uint32_t n_exp, uint32_t n_used, int norm,
+                        float scale, int32_t *ids, float *scores) {
+    /* sort_by(|a, b| b.0.partial_cmp(&a.0)) is stable: among equal selection
+     * values the lower expert comes first.  Picking the best remaining expert
+     * n_used times gives the same order. */
+    uint32_t n_sel = n_used < n_exp ? n_used : n_exp;
+    for (uint32_t s = 0; s < n_sel; s++) {
+        int32_t best = -1;
+        float best_v = 0.0f;
+        for (uint32_t e = 0; e < n_exp; e++) {
+            int taken = 0;
+            for (uint32_t t = 0; t < s; t++) taken |= ids[t] == (int32_t)e;
+            if (taken) continue;
+            float p = 1.0f / (1.0f + expf(-logits[e]));
+            float v = p + bias[e];
+            if (best < 0 || v > best_v) best = (int32_t)e, best_v = v;
+        }
+        ids[s] = best;
+        scores[s] = 1.0f / (1.0f + expf(-logits[best]));
+    }
+    if (norm) {
+        float sum = 0.0f;
+        for (uint32_t s = 0; s < n_sel; s++) sum += scores[s];
+        float denom = sum > 6.103515625e-5f ? sum : 6.103515625e-5f;
+        for (uint32_t s = 0; s < n_sel; s++) scores[s] /= denom;
+    }
+    if (scale != 0.0f && scale != 1.0f)
+        for (uint32_t s = 0; s < n_sel; s++) scores[s] *= scale;
+    return n_sel;
+}
+
+float lco_moe_l2_scale(const float *h, uint32_t n, float *out) {
+    float sum = 0.0f;
+    for (uint32_t i = 0; i < n; i++) sum += h[i] * h[i];
+    float col = sqrtf(sum);
+    if (col < 1e-8f) col = 1e-8f;
+    if (col > 1e30f) col = 1e30f;
+    for (uint32_t i = 0; i < n; i++) out[i] = h[i] * 32768.0f / col;
+    return col;
+}
+
 /* keep f32_bits referenced for debug builds */
 uint32_t lco__f32_bits(float f) { return f32_bits(f); }

@@ -116,6 +116,20 @@ void lco_rope_freq(float *freq, uint32_t rope_dim, float base);
  * maximal index wins and a NaN compares Equal. */
 size_t lco_argmax(const float *logits, size_t n);
 
+/* ---- target model (src/target.rs) ---- */
+/* gate_attn.comp:22-31: out[i] = attn[i] * log(1 + exp(gate[i / head_dim])). */
+void lco_gate_attn(const float *attn, const float *gate, float *out, uint32_t n_heads, uint32_t head_dim);
+/* Router selection of dispatch_moe_ffn (src/target.rs:653-677): probs =
+ * 1 / (1 + exp(-logit)); the min(n_used, n_exp) largest probs + bias by a
+ * stable descending sort (equal values keep expert order); scores = their
+ * probs, divided by max(sum, 6.103515625e-5) when norm, times scale when scale
+ * is neither 0 nor 1.  Returns the number selected. */
+uint32_t lco_moe_select(const float *logits, const float *bias, uint32_t n_exp, uint32_t n_used, int norm,
+                        float scale, int32_t *ids, float *scores);
+/* src/target.rs:700-712: col_l2 = clamp(sqrt(sum h^2), 1e-8, 1e30), the sum
+ * taken in order in f32; out[i] = h[i] * 32768 / col_l2.  Returns col_l2. */
+float lco_moe_l2_scale(const float *h, uint32_t n, float *out);
+
 /* Number of OpenMP threads the oracle runs with (0 = library default). */
 void lco_set_threads(int n);
 int lco_get_threads(void);

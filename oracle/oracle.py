@@ -91,6 +91,12 @@ class Oracle:
         L.lco_rope_freq.argtypes = [_fp, C.c_uint32, C.c_float]
         L.lco_argmax.restype = C.c_size_t
         L.lco_argmax.argtypes = [_fp, C.c_size_t]
+        L.lco_gate_attn.argtypes = [_fp, _fp, _fp, C.c_uint32, C.c_uint32]
+        L.lco_moe_select.restype = C.c_uint32
+        L.lco_moe_select.argtypes = [_fp, _fp, C.c_uint32, C.c_uint32, C.c_int, C.c_float,
+                                     C.POINTER(C.c_int32), _fp]
+        L.lco_moe_l2_scale.restype = C.c_float
+        L.lco_moe_l2_scale.argtypes = [_fp, C.c_uint32, _fp]
         L.lco_set_threads.argtypes = [C.c_int]
         L.lco_get_threads.restype = C.c_int
         if threads:
@@ -201,6 +207,27 @@ class Oracle:
         f = np.empty(rope_dim // 2, np.float32)
         self.lib.lco_rope_freq(_p(f), rope_dim, base)
         return f
+
+    # -- target model --------------------------------------------------------
+    def gate_attn(self, attn, gate, n_heads, head_dim):
+        a = np.ascontiguousarray(attn, np.float32)
+        out = np.empty_like(a)
+        self.lib.lco_gate_attn(_p(a), _p(np.ascontiguousarray(gate, np.float32)), _p(out), n_heads, head_dim)
+        return out
+
+    def moe_select(self, logits, bias, n_used, norm=False, scale=1.0):
+        lg = np.ascontiguousarray(logits, np.float32)
+        ids = np.zeros(n_used, np.int32)
+        sc = np.zeros(n_used, np.float32)
+        n = self.lib.lco_moe_select(_p(lg), _p(np.ascontiguousarray(bias, np.float32)), lg.size, n_used,
+                                    int(bool(norm)), scale, ids.ctypes.data_as(C.POINTER(C.c_int32)), _p(sc))
+        return ids[:n], sc[:n]
+
+    def moe_l2_scale(self, h):
+        h = np.ascontiguousarray(h, np.float32)
+        out = np.empty_like(h)
+        col = self.lib.lco_moe_l2_scale(_p(h), h.size, _p(out))
+        return out, np.float32(col)
 
     def argmax(self, logits) -> int:
         l = np.ascontiguousarray(logits, np.float32)
