@@ -57,7 +57,12 @@ def _traffic(workload, kernel):
     return None
 
 
+_CPU_THREADS = [0]  # --cpu-threads; 0 = every host thread this process may use
+
+
 def host_threads():
+    if _CPU_THREADS[0] > 0:
+        return _CPU_THREADS[0]
     try:
         return len(os.sched_getaffinity(0))
     except Exception:
@@ -958,8 +963,11 @@ def main():
     ap.add_argument("--vocab", type=int, default=0,
                     help="lm_head_q8_0 only: vocab rows (default: BASELINE config 4's 128256); a smaller vocab "
                          "keeps an ncu capture short")
+    ap.add_argument("--cpu-threads", type=int, default=0,
+                    help="threads of the CPU baselines and the reference arm (default: all usable host threads)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    _CPU_THREADS[0] = max(0, args.cpu_threads)
 
     if args.impl == "reference":
         return run_reference_arm(args)
