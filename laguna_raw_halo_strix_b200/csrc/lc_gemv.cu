@@ -51,7 +51,6 @@ namespace {
 
 constexpr int kGvMaxWarps = 16;  // warps per CTA
 constexpr int kGvQuad = 4;       // rows reduced together
-constexpr int kGvDepth = 4;      // rows in flight per lane
 
 // Launch arguments (a __grid_constant__ parameter block).  Up to lc::kGroupMax
 // matrices of one format and one k share the activations: their rows form one
@@ -65,22 +64,24 @@ struct GvArgs {
     const float *x2;  // when set, the activation is silu(x) * x2 (kernels/activation.comp)
     int k, row_bytes;
     int ks, rg;  // k-slices (warps per row group), row groups
+    int part_rows;  // rows of a CTA's range the partial-sum array holds (>= every range)
     int half_mode;
     unsigned *status;
 };
 
-// Shared memory: the ring [warps][kGvDepth][slice bytes], the activation table
-// [ks][tab bytes per slice], partial sums part [2][rg][kGvQuad][ks][M] floats.
+// Shared memory: the ring [warps][depth][slice bytes], the activation table
+// [ks][tab bytes per slice], partial sums part [part_rows][ks][M] floats (one
+// per row of the CTA's range and k-slice, summed once at the end).
 struct GvLayout {
     size_t ring, tab, part, total;
 };
-__host__ __device__ __forceinline__ GvLayout gv_layout(int warps, int slice_bytes, int tab_bytes, int rg, int ks,
-                                                       int m) {
+__host__ __device__ __forceinline__ GvLayout gv_layout(int warps, int depth, int slice_bytes, int tab_bytes,
+                                                       int part_rows, int ks, int m) {
     GvLayout L;
     L.ring = 0;
-    L.tab = (size_t)warps * kGvDepth * slice_bytes;
+    L.tab = (size_t)warps * depth * slice_bytes;
     L.part = L.tab + (size_t)ks * tab_bytes;
-    L.total = L.part + (size_t)2 * rg * kGvQuad * ks * m * 4 + 128;  // + slack to 128-align the base
+    L.total = L.part + (size_t)part_rows * ks * m * 4 + 128;  // + slack to 128-align the base
     return L;
 }
 
@@ -168,6 +169,7 @@ struct Q4Lane {
     static constexpr int NP = M == 1 ? 4 : 2;  // word pairs per lane
     static constexpr int SPW = M == 1 ? 8 : 4;  // super-blocks per warp slice
     static constexpr int SLICE = SPW * 144;           // bytes of a row per warp slice
+    static constexpr int DEPTH = 8;                   // rows in flight per warp (a power of two)
     static constexpr int TAB = M * (NP * 8 * 32 * 8 + 32 * 16);  // table bytes per slice
     uint64_t xp[M][NP][8];                      // pre-scaled activation pairs
     float sx[M][2];                             // S(x) over the lane's low / high elements
@@ -349,6 +351,7 @@ struct Q4Lane {
 // shifted down by 16), and read as subnormals.
 struct Q8Lane {
     static constexpr int SLICE = 64 * 34;                  // 64 blocks per warp slice
+    static constexpr int DEPTH = 4;                        // rows in flight per warp (a power of two)
     static constexpr int TAB = 64 * 32 * 4 + 32 * 16;      // table bytes per slice
     float xp[64];  // pre-scaled activations: block A elements 0..31, block B 32..63
     float sx[2];   // S(x) over block A, block B
@@ -470,10 +473,16 @@ __device__ __forceinline__ void reduce4(float (&p)[kGvQuad][M], int lane) {
     }
 }
 
-// Warp-cooperative copy of the warp's slice of row `row` (nb bytes, a multiple
-// of 16) into `slot`: lane l copies 16-byte chunks l, l + 32, ...
+// Warp-cooperative copy of the warp's slice of a row (nb <= NB bytes, a
+// multiple of 16) into `slot`: lane l copies 16-byte chunks l, l + 32, ...
+// (a fixed number of predicated copies: no loop).
+template <int NB>
 __device__ __forceinline__ void gv_copy_slice(const uint8_t *src, uint8_t *slot, int nb, int lane) {
-    for (int c = lane * 16; c < nb; c += 512) cp_async16_l2(slot + c, src + c);
+#pragma unroll
+    for (int c = 0; c < (NB + 511) / 512; c++) {
+        const int off = lane * 16 + c * 512;
+        if (off < nb) cp_async16_l2(slot + off, src + off);
+    }
 }
 
 template <class L, int M>
@@ -489,8 +498,9 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, 1) gemv_rows_kernel(const __
     typename L::Raw raw;
     if (rgi == 0) ln.load(a, raw);
 
-    const GvLayout Lo = gv_layout(nwarps, L::SLICE, L::TAB, a.rg, a.ks, M);
-    unsigned char *ring = smem + Lo.ring + (size_t)warp * kGvDepth * L::SLICE;
+    constexpr int D = L::DEPTH;
+    const GvLayout Lo = gv_layout(nwarps, D, L::SLICE, L::TAB, a.part_rows, a.ks, M);
+    unsigned char *ring = smem + Lo.ring + (size_t)warp * D * L::SLICE;
     unsigned char *tab = smem + Lo.tab + (size_t)slice * L::TAB;
     float *part = reinterpret_cast<float *>(smem + Lo.part);
     const int total = a.rows_end[a.ng - 1];
@@ -508,10 +518,10 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, 1) gemv_rows_kernel(const __
         gv_row(a, r0 + rgi + i * a.rg, g, ri);
         return a.w[g] + (size_t)ri * a.row_bytes + (size_t)slice * L::SLICE;
     };
-    // rows 0 .. kGvDepth-1 in flight, one cp.async group per row: group r holds row r
+    // rows 0 .. D-1 in flight, one cp.async group per row: group r holds row r
 #pragma unroll
-    for (int d = 0; d < kGvDepth; d++) {
-        if (d < nmy) gv_copy_slice(slice_ptr(d), ring + d * L::SLICE, sbytes, lane);
+    for (int d = 0; d < D; d++) {
+        if (d < nmy) gv_copy_slice<L::SLICE>(slice_ptr(d), ring + d * L::SLICE, sbytes, lane);
         cp_async_commit();
     }
     if (rgi == 0) {
@@ -522,61 +532,59 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, 1) gemv_rows_kernel(const __
     if (rgi != 0) ln.load_table(tab, lane);
 
     const uint32_t ref_mask = a.half_mode == LC_HALF_REF ? 0x04000400u : 0u;
-    int buf = 0;
     for (int i0 = 0; i0 < nmy; i0 += kGvQuad) {
         float p[kGvQuad][M];
 #pragma unroll
         for (int q = 0; q < kGvQuad; q++) {
             const int i = i0 + q;
-            // Row i has landed for this lane once at most kGvDepth - 2 newer
-            // groups are pending (groups 0..i+kGvDepth-2 were committed before
-            // this point); the warp barrier makes every lane's copies visible
-            // and also means every lane is done with row i - 1.
-            cp_async_wait<kGvDepth - 2>();
+            // Row i has landed for this lane once at most D - 2 newer groups
+            // are pending (groups 0..i+D-2 were committed before this point);
+            // the warp barrier makes every lane's copies visible and also
+            // means every lane is done with row i - 1.
+            cp_async_wait<D - 2>();
             __syncwarp();
-            // refill row i - 1's buffer with row i - 1 + kGvDepth
-            if (i > 0 && i - 1 + kGvDepth < nmy)
-                gv_copy_slice(slice_ptr(i - 1 + kGvDepth), ring + ((i - 1) % kGvDepth) * L::SLICE, sbytes, lane);
+            // refill row i - 1's buffer with row i - 1 + D
+            if (i > 0 && i - 1 + D < nmy)
+                gv_copy_slice<L::SLICE>(slice_ptr(i - 1 + D), ring + ((unsigned)(i - 1) & (D - 1)) * L::SLICE, sbytes,
+                                        lane);
             if (i > 0) cp_async_commit();
             typename L::Bytes bt;
-            ln.fetch(ring + (i % kGvDepth) * L::SLICE, bt);
+            ln.fetch(ring + ((unsigned)i & (D - 1)) * L::SLICE, bt);
             float o[M];
             ln.row(bt, ref_mask, o);
 #pragma unroll
             for (int j = 0; j < M; j++) p[q][j] = i < nmy ? o[j] : 0.f;
         }
         reduce4<M>(p, lane);
-        float *pb = part + (size_t)(buf * a.rg + rgi) * kGvQuad * a.ks * M;
-        {
-            const int q = lane >> 3;
-            if ((lane & 7) == 0) {
+        // this k-slice's sums of the quad's rows, by row of the CTA's range;
+        // no barrier: the k-slices meet once, after the last row
+        const int q = lane >> 3, i = i0 + q;
+        if ((lane & 7) == 0 && i < nmy) {
+            const int lr = rgi + i * a.rg;
 #pragma unroll
-                for (int j = 0; j < M; j++) pb[((size_t)q * a.ks + slice) * M + j] = p[0][j];
-            }
+            for (int j = 0; j < M; j++) part[((size_t)lr * a.ks + slice) * M + j] = p[0][j];
         }
-        // the row group's k-slices meet; its first warp adds them in order
-        named_barrier_sync_id(1 + rgi, a.ks * 32);
-        if (slice == 0 && lane < kGvQuad * M) {
-            const int q = lane / M, j = lane - q * M, i = i0 + q;
-            if (i < nmy) {
-                float v = 0.f;
-                for (int t = 0; t < a.ks; t++) v += pb[((size_t)q * a.ks + t) * M + j];
-                int g, ri;
-                gv_row(a, r0 + rgi + i * a.rg, g, ri);
-                const int nrow = a.rows_end[g] - (g ? a.rows_end[g - 1] : 0);
-                a.y[g][(size_t)j * nrow + ri] = v;
-            }
-        }
-        buf ^= 1;
     }
     cp_async_wait_all();
+    __syncthreads();
+    // every row of the range: its k-slices added in slice order
+    const int nrows = r1 - r0;
+    for (int t = threadIdx.x; t < nrows * M; t += blockDim.x) {
+        const int lr = t / M, j = t - lr * M;
+        float v = 0.f;
+        for (int sl = 0; sl < a.ks; sl++) v += part[((size_t)lr * a.ks + sl) * M + j];
+        int g, ri;
+        gv_row(a, r0 + lr, g, ri);
+        const int nrow = a.rows_end[g] - (g ? a.rows_end[g - 1] : 0);
+        a.y[g][(size_t)j * nrow + ri] = v;
+    }
 }
 
 // ---------------------------------------------------------------------------
 // Host side.
 
 struct GvPlan {
-    int ks = 0, rg = 0, grid = 0, threads = 0;
+    int ks = 0, rg = 0, grid = 0, threads = 0, part_rows = 0;
     size_t smem = 0;
 };
 
@@ -587,15 +595,22 @@ GvPlan gv_plan(const lc_ctx *ctx, int dtype, int m, int k, int rows) {
     const int se = m == 1 ? 2048 : 1024;  // elements per warp slice
     const int ks = (k + se - 1) / se;
     if (ks < 1 || ks > kGvMaxWarps) return p;
-    // row groups: as many as fit in 16 warps, at most 15 (named barriers 1..15)
-    const int rg = std::min(15, std::max(1, kGvMaxWarps / ks));
+    // row groups: as many as fit in 16 warps
+    const int rg = std::max(1, kGvMaxWarps / ks);
     const int threads = ks * rg * 32;
     const int slice_bytes = dtype == LC_Q8_0 ? Q8Lane::SLICE : (m == 1 ? Q4Lane<1>::SLICE : Q4Lane<2>::SLICE);
+    const int depth = dtype == LC_Q8_0 ? Q8Lane::DEPTH : (m == 1 ? Q4Lane<1>::DEPTH : Q4Lane<2>::DEPTH);
     const int tab_bytes = dtype == LC_Q8_0 ? Q8Lane::TAB : (m == 1 ? Q4Lane<1>::TAB : Q4Lane<2>::TAB);
-    const size_t need = gv_layout(ks * rg, slice_bytes, tab_bytes, rg, ks, m).total;
+    // one CTA per SM; more (in waves) only when a CTA's row range would need
+    // more than 32 KB of partial sums
+    int grid = std::max(1, std::min(ctx->num_sms, rows));
+    const long long max_rows = std::max(1, (32 << 10) / (ks * m * 4));
+    if ((rows + grid - 1) / grid > max_rows) grid = (int)((rows + max_rows - 1) / max_rows);
+    const int part_rows = (rows + grid - 1) / grid + 1;
+    const size_t need = gv_layout(ks * rg, depth, slice_bytes, tab_bytes, part_rows, ks, m).total;
     if (need > ctx->smem_optin) return p;
-    p.ks = ks, p.rg = rg, p.threads = threads, p.smem = need;
-    p.grid = std::max(1, std::min(ctx->num_sms, rows));
+    p.ks = ks, p.rg = rg, p.threads = threads, p.smem = need, p.part_rows = part_rows;
+    p.grid = grid;
     return p;
 }
 
@@ -606,7 +621,8 @@ int gv_launch(lc_ctx *ctx, const GvPlan &p, GvArgs &a) {
         const int s = lc_set_smem_attr((const void *)kern, p.smem);
         if (s) return s;
     }
-    a.ks = p.ks, a.rg = p.rg;
+    a.ks = p.ks, a.rg = p.rg, a.part_rows = p.part_rows;
+
     kern<<<p.grid, p.threads, p.smem, ctx->stream>>>(a);
     return LC_OK;
 }
