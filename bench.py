@@ -108,7 +108,7 @@ WORKLOADS = {
 
 # Workloads with their own drivers (below): BASELINE config 4 (lm_head, vocab
 # sharded over the ranks) and config 3 (the DFlash decoder, 16-token block).
-SPECIAL = ("lm_head_q8_0", "dflash_block")
+SPECIAL = ("lm_head_q8_0", "dflash_block", "target_verify")
 LM_HEAD = dict(m=1024, k=4096, vocab=128256, config=4)
 DFLASH_HP = dict(n_layers=6, n_embd=4096, n_heads=32, n_kv_heads=8, head_dim=128, rope_dim=128, n_ff=14336, n_aux=5,
                  rope_base=500000.0, norm_eps=1e-5, qk_eps=1e-6)
@@ -940,10 +940,128 @@ def run_dflash(args):
 
 
 # ---------------------------------------------------------------------------
+# The target model's verify step (no BASELINE configuration names one): a
+# Laguna-shaped model -- hidden 4096, 32 Q / 8 KV heads of 128, layer 0 dense
+# (FFN 14336), layers 1-3 MoE (64 experts of 1024, 8 used, a shared expert of
+# 1024), Q4_K projections, a 32000-row Q8_0 lm_head -- verifying a block of 16
+# draft tokens through its K/V cache of 2048 positions, then rolled back.
+TARGET_HP = dict(n_layers=4, n_embd=4096, n_heads=32, n_kv_heads=8, head_dim=128, rope_dim=128, rope_dim_swa=128,
+                 n_ff=14336, n_expert=64, n_expert_used=8, n_ff_exp=1024, n_ff_shexp=1024, n_vocab=32000)
+TARGET_CTX, TARGET_BLOCK = 2048, 16
+
+
+def run_target_verify(args):
+    """Verify throughput (draft tokens checked per second) of lc_target_forward
+    with LC_TARGET_CACHED: one step = a 16-token block at positions 2048..2063
+    (K/V appended, causal attention over the cache, MoE routed on the device,
+    lm_head keys), the cache then truncated back to 2048."""
+    import tempfile
+
+    import torch
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from gguf_writer import write_gguf
+
+    from laguna_raw_halo_strix_b200 import lc, synth
+    from laguna_raw_halo_strix_b200.target import Target
+
+    world, rank, local_rank, dev = _dist_init()
+    stream = torch.cuda.Stream(dev)
+    ctx = lc.Context(local_rank)
+    ctx.set_stream(stream)
+    hp, C, M = TARGET_HP, TARGET_CTX, TARGET_BLOCK
+    E = hp["n_embd"]
+    rng = np.random.default_rng(4000 + rank)
+    tens = synth.target_tensors(hp, rng, share=True)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "target.gguf")
+        write_gguf(path, synth.target_meta(hp),
+                   [(n, dt, shape, np.ascontiguousarray(a).view(np.uint8).reshape(-1))
+                    for n, (dt, a, shape) in tens.items()])
+        file_bytes = os.path.getsize(path)
+        t0 = time.perf_counter()
+        tm = Target(ctx, path, max_ctx=C + M, max_block=M)
+        load_s = time.perf_counter() - t0
+    with torch.cuda.stream(stream):
+        x = torch.from_numpy((0.5 * rng.standard_normal((M, E))).astype(np.float32)).to(dev)
+        keys = torch.empty(M, dtype=torch.int64, device=dev)
+        for _ in range(C // M):  # the cache: 2048 positions
+            tm.forward(x, M, cached=True)
+        for _ in range(args.warmup):
+            tm.forward(x, M, cached=True, keys=keys)
+            tm.truncate(C)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph(keep_graph=True)
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(args.steps):
+                tm.forward(x, M, cached=True, keys=keys)
+                tm.truncate(C)
+        g.replay()
+        stream.synchronize()
+        launches = _graph_kernel_nodes(g)
+        ms, clocks = _timed_graph(g, stream, dev, world, rank)
+        del g
+        x_host = torch.from_numpy((0.5 * rng.standard_normal((M, E))).astype(np.float32)).pin_memory()
+        k_host = torch.empty(M, dtype=torch.int64).pin_memory()
+        e2e_steps = max(5, min(args.steps, 50))
+        _barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            x.copy_(x_host, non_blocking=True)
+            tm.forward(x, M, cached=True, keys=keys)
+            tm.truncate(C)
+            k_host.copy_(keys, non_blocking=True)
+            stream.synchronize()
+        e2e_s = _max_over_ranks(time.perf_counter() - t0, dev, world)
+    tm.close()
+    # bytes one verify step must read: every dense projection, the router and
+    # shared expert, the experts the block selects (expected distinct count of
+    # 16 tokens x 8 of 64: 64 (1 - (1 - 8/64)^16) = 56.4), the K/V cache and the
+    # lm_head
+    q4 = 144 / 256
+    H, KVD, F = hp["n_heads"], hp["n_kv_heads"] * hp["head_dim"], hp["n_ff"]
+    QD = H * hp["head_dim"]
+    NE, U, Fe, S, V = hp["n_expert"], hp["n_expert_used"], hp["n_ff_exp"], hp["n_ff_shexp"], hp["n_vocab"]
+    attn_b = ((QD + 2 * KVD + H) * E + E * QD) * q4
+    distinct = NE * (1 - (1 - U / NE) ** M)
+    moe_b = E * NE * 4 + 3 * S * E * q4 + distinct * 3 * Fe * E * q4
+    step_b = (hp["n_layers"] * attn_b + 3 * F * E * q4 + (hp["n_layers"] - 1) * moe_b
+              + hp["n_layers"] * (C + M) * KVD * 2 * 4 + V * E * 34 / 32)
+    hbm, _, peak_src = peaks()
+    per_step_s = ms / 1e3 / args.steps
+    if rank == 0:
+        _emit({
+            "metric": METRIC, "value": world * M * args.steps / (ms / 1e3), "unit": "verified tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "q4k*f16x2 projections (tcgen05 f32 accumulate), f32 expert GEMV, f32 element-wise ops",
+            "data": "synthetic (seeded; one array per distinct shape, its own device copy per layer and expert)",
+            "config": {"workload": "target_verify", "baseline_config": None, "layers": hp["n_layers"],
+                       "hidden": E, "heads": H, "kv_heads": hp["n_kv_heads"], "ffn_dense": F, "experts": NE,
+                       "experts_used": U, "ffn_expert": Fe, "ffn_shared": S, "vocab": V, "cache": C, "block": M,
+                       "bytes_per_step": step_b, "expected_distinct_experts": distinct, "gguf_bytes": file_bytes,
+                       "load_s": load_s, "load_gbs": file_bytes / load_s / 1e9,
+                       "l2": f"{step_b / 1e6:.0f} MB read per step (> 3x the 126 MB L2)",
+                       "parallelism": f"replicas x{world} (independent sequences, no collective)"},
+            "roofline": {"bound": "hbm", "achieved": step_b / per_step_s / 1e9, "peak": hbm,
+                         "peak_source": peak_src, "unit": "GB/s", "frac": step_b / per_step_s / 1e9 / hbm,
+                         "traffic": None, "kernel": "whole verify step (all kernels)",
+                         "per_launch_us": per_step_s * 1e6, "bytes_per_launch": step_b},
+            "cpu_baseline": None,
+            "e2e": {"value": world * M * e2e_steps / e2e_s, "unit": "verified tokens/s",
+                    "h2d_bytes_per_step": 4 * M * E, "d2h_bytes_per_step": 8 * M, "steps": e2e_steps},
+            "clocks": clocks, "gpu_launches": launches,
+        })
+    ctx.close()
+    return 0
+
+
 DEFAULT_SEQUENCE = ("gemv_q8_0", "ffn_q4k_m16", "dflash_block", "lm_head_q8_0", "ffn_q4k_m1")
 
 
 def run_workload(args, name):
+    if name == "target_verify":
+        return run_target_verify(args)
     if name == "lm_head_q8_0":
         return run_lm_head(args)
     if name == "dflash_block":
