@@ -167,62 +167,80 @@ __global__ void moe_items_kernel(const int32_t *__restrict__ ids, int n_pairs, i
     }
 }
 
-// Eight consecutive weights w[k0 + 8*lane .. +8] of one row, with the
-// shaders' per-element formulas (proj_q4k.comp:72-87, proj_q8_0.comp:53-64).
+// The bytes a lane needs for eight consecutive weights w[k0 + 8*lane .. +8]
+// of one row, loaded before any is decoded so a warp keeps the loads of several
+// rows in flight: Q4_K the block's 16-byte header (d, dmin, the packed
+// scales) and the lane's 8 nibble bytes; Q8_0 the scale and 8 bytes; F32 the
+// 8 floats.
 template <int DT>
-__device__ __forceinline__ bool expert_weights8(const uint8_t *__restrict__ wr, int k0, int k, int lane, int half_mode,
-                                                float (&w)[8]) {
+struct ExpRaw {
+    uint4 a;  // Q4_K header; Q8_0 .x = the f16 scale; F32 floats 0..3
+    uint4 b;  // Q4_K nibbles in .x/.y; Q8_0 bytes in .x/.y; F32 floats 4..7
+};
+
+template <int DT>
+__device__ __forceinline__ void expert_load8(const uint8_t *__restrict__ wr, int k0, int lane, ExpRaw<DT> &r) {
     const int kk = k0 + 8 * lane;
-    if (kk >= k) return false;
     if constexpr (DT == LC_Q4_K) {
         const uint8_t *blk = wr + (size_t)(k0 / 256) * 144;
-        const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
-        const float d = lc_half_to_f32(dd & 0xFFFFu, half_mode), dmin = lc_half_to_f32(dd >> 16, half_mode);
-        uint8_t s[12];
-#pragma unroll
-        for (int i = 0; i < 3; i++) {
-            const uint32_t v = *reinterpret_cast<const uint32_t *>(blk + 4 + 4 * i);
-            s[4 * i] = v & 0xFF, s[4 * i + 1] = (v >> 8) & 0xFF, s[4 * i + 2] = (v >> 16) & 0xFF, s[4 * i + 3] = v >> 24;
-        }
+        r.a = __ldg(reinterpret_cast<const uint4 *>(blk));
+        const uint2 q = __ldg(reinterpret_cast<const uint2 *>(blk + 16 + (lane >> 3) * 32 + (lane & 3) * 8));
+        r.b = make_uint4(q.x, q.y, 0u, 0u);
+    } else if constexpr (DT == LC_Q8_0) {
+        const uint8_t *blk = wr + (size_t)(kk / 32) * 34;
+        const uint16_t *qs = reinterpret_cast<const uint16_t *>(blk + 2 + (kk & 31));
+        r.a = make_uint4(__ldg(reinterpret_cast<const uint16_t *>(blk)), 0u, 0u, 0u);
+        const uint32_t q0 = __ldg(qs), q1 = __ldg(qs + 1), q2 = __ldg(qs + 2), q3 = __ldg(qs + 3);
+        r.b = make_uint4(q0 | (q1 << 16), q2 | (q3 << 16), 0u, 0u);
+    } else {
+        r.a = __ldg(reinterpret_cast<const uint4 *>(wr + (size_t)kk * 4));
+        r.b = __ldg(reinterpret_cast<const uint4 *>(wr + (size_t)kk * 4 + 16));
+    }
+}
+
+// The eight weights, with the shaders' per-element formulas
+// (proj_q4k.comp:72-87, proj_q8_0.comp:53-64).
+template <int DT>
+__device__ __forceinline__ void expert_decode8(const ExpRaw<DT> &r, int lane, int half_mode, float (&w)[8]) {
+    if constexpr (DT == LC_Q4_K) {
+        const float d = lc_half_to_f32(r.a.x & 0xFFFFu, half_mode), dmin = lc_half_to_f32(r.a.x >> 16, half_mode);
+        const uint32_t sw[3] = {r.a.y, r.a.z, r.a.w};  // scale bytes 0..11
+        auto sb = [&](int i) { return (sw[i >> 2] >> (8 * (i & 3))) & 0xFFu; };
         const int j = lane >> 2;  // sub-block of 32
         uint32_t sc, mn;
         if (j < 4) {
-            sc = s[j] & 63u;
-            mn = s[j + 4] & 63u;
+            sc = sb(j) & 63u;
+            mn = sb(j + 4) & 63u;
         } else {
-            sc = (s[j + 4] & 15u) | ((s[j - 4] >> 6) << 4);
-            mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+            sc = (sb(j + 4) & 15u) | ((sb(j - 4) >> 6) << 4);
+            mn = (sb(j + 4) >> 4) | ((sb(j) >> 6) << 4);
         }
-        const uint2 q = *reinterpret_cast<const uint2 *>(blk + 16 + (lane >> 3) * 32 + (lane & 3) * 8);
         const int shift = (lane & 4) ? 4 : 0;
         const float dsc = __fmul_rn(d, (float)sc), dmn = __fmul_rn(dmin, (float)mn);
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            const uint32_t byte = ((i < 4 ? q.x : q.y) >> (8 * (i & 3))) & 0xFFu;
+            const uint32_t byte = ((i < 4 ? r.b.x : r.b.y) >> (8 * (i & 3))) & 0xFFu;
             w[i] = __fsub_rn(__fmul_rn(dsc, (float)((byte >> shift) & 15u)), dmn);
         }
     } else if constexpr (DT == LC_Q8_0) {
-        const uint8_t *blk = wr + (size_t)(kk / 32) * 34;
-        const float d = lc_half_to_f32(*reinterpret_cast<const uint16_t *>(blk), half_mode);
-        const uint16_t *qs = reinterpret_cast<const uint16_t *>(blk + 2 + (kk & 31));
+        const float d = lc_half_to_f32(r.a.x, half_mode);
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint16_t v = qs[i];
-            w[2 * i] = __fmul_rn((float)(int8_t)(v & 0xFF), d);
-            w[2 * i + 1] = __fmul_rn((float)(int8_t)(v >> 8), d);
-        }
+        for (int i = 0; i < 8; i++)
+            w[i] = __fmul_rn((float)(int8_t)(((i < 4 ? r.b.x : r.b.y) >> (8 * (i & 3))) & 0xFFu), d);
     } else {
-        const float4 a = *reinterpret_cast<const float4 *>(wr + (size_t)kk * 4);
-        const float4 b = *reinterpret_cast<const float4 *>(wr + (size_t)kk * 4 + 16);
-        w[0] = a.x, w[1] = a.y, w[2] = a.z, w[3] = a.w, w[4] = b.x, w[5] = b.y, w[6] = b.z, w[7] = b.w;
+        w[0] = __uint_as_float(r.a.x), w[1] = __uint_as_float(r.a.y), w[2] = __uint_as_float(r.a.z);
+        w[3] = __uint_as_float(r.a.w), w[4] = __uint_as_float(r.b.x), w[5] = __uint_as_float(r.b.y);
+        w[6] = __uint_as_float(r.b.z), w[7] = __uint_as_float(r.b.w);
     }
-    return true;
 }
 
 // Y[pair][row] = X[pair / act_div] . W_e[row] for the pairs of each work item:
-// expert e's matrix is read once for all of its pairs.  blockIdx.z picks one of
-// two weight stacks sharing the items (gate and up).  expert_fixed >= 0 makes
-// every item read that expert (the reference's Q8_0 / F32 expert quirk).
+// expert e's matrix is read once for all of its pairs.  A warp takes kExpRows
+// rows at a time (their loads in flight together, each activation load
+// shared by them).  blockIdx.z picks one of two weight stacks sharing the
+// items (gate and up).  expert_fixed >= 0 makes every item read that expert
+// (the reference's Q8_0 / F32 expert quirk).
+constexpr int kExpRows = 4;
 template <int DT>
 __global__ void __launch_bounds__(256) expert_gemv_kernel(const uint8_t *__restrict__ w0, const uint8_t *__restrict__ w1,
                                                           size_t expert_bytes, size_t row_bytes, int expert_fixed,
@@ -239,33 +257,56 @@ __global__ void __launch_bounds__(256) expert_gemv_kernel(const uint8_t *__restr
     const float *xr[kTok];
 #pragma unroll
     for (int t = 0; t < kTok; t++) xr[t] = X + (size_t)(it.pair[t] / act_div) * k;
-    const int row_end = min(n, ((int)blockIdx.x + 1) * kRowsCta);
-    for (int row = (int)blockIdx.x * kRowsCta + warp; row < row_end; row += 8) {
-        const uint8_t *wr = W + (size_t)row * row_bytes;
-        float acc[kTok];
+    const int row0 = (int)blockIdx.x * kRowsCta, row_end = min(n, row0 + kRowsCta);
+    // warp w: rows row0 + w + 8 * (r + kExpRows * g), r < kExpRows
+    for (int g = 0; g < kRowsCta / (8 * kExpRows); g++) {
+        int rows[kExpRows];
+        bool live[kExpRows];
+        const uint8_t *wr[kExpRows];
 #pragma unroll
-        for (int t = 0; t < kTok; t++) acc[t] = 0.f;
+        for (int r = 0; r < kExpRows; r++) {
+            rows[r] = row0 + warp + 8 * (r + kExpRows * g);
+            live[r] = rows[r] < row_end;
+            wr[r] = W + (size_t)(live[r] ? rows[r] : row0) * row_bytes;
+        }
+        if (!live[0]) break;
+        float acc[kExpRows][kTok];
+#pragma unroll
+        for (int r = 0; r < kExpRows; r++)
+#pragma unroll
+            for (int t = 0; t < kTok; t++) acc[r][t] = 0.f;
         for (int k0 = 0; k0 < k; k0 += 256) {
-            float w[8];
-            if (!expert_weights8<DT>(wr, k0, k, lane, half_mode, w)) continue;
             const int kk = k0 + 8 * lane;
+            if (kk >= k) break;  // Q8_0 / F32 with k not a multiple of 256: the tail lanes
+            ExpRaw<DT> raw[kExpRows];
+#pragma unroll
+            for (int r = 0; r < kExpRows; r++) expert_load8<DT>(wr[r], k0, lane, raw[r]);
+            float w[kExpRows][8];
+#pragma unroll
+            for (int r = 0; r < kExpRows; r++) expert_decode8<DT>(raw[r], lane, half_mode, w[r]);
 #pragma unroll
             for (int t = 0; t < kTok; t++) {
                 if (t >= it.count) break;
                 const float4 a = __ldg(reinterpret_cast<const float4 *>(xr[t] + kk));
                 const float4 b = __ldg(reinterpret_cast<const float4 *>(xr[t] + kk + 4));
-                float s = acc[t];
-                s = fmaf(w[0], a.x, s), s = fmaf(w[1], a.y, s), s = fmaf(w[2], a.z, s), s = fmaf(w[3], a.w, s);
-                s = fmaf(w[4], b.x, s), s = fmaf(w[5], b.y, s), s = fmaf(w[6], b.z, s), s = fmaf(w[7], b.w, s);
-                acc[t] = s;
+#pragma unroll
+                for (int r = 0; r < kExpRows; r++) {
+                    float s = acc[r][t];
+                    s = fmaf(w[r][0], a.x, s), s = fmaf(w[r][1], a.y, s), s = fmaf(w[r][2], a.z, s);
+                    s = fmaf(w[r][3], a.w, s), s = fmaf(w[r][4], b.x, s), s = fmaf(w[r][5], b.y, s);
+                    s = fmaf(w[r][6], b.z, s), s = fmaf(w[r][7], b.w, s);
+                    acc[r][t] = s;
+                }
             }
         }
 #pragma unroll
-        for (int t = 0; t < kTok; t++) {
-            if (t >= it.count) break;
-            const float v = warp_sum(acc[t]);
-            if (lane == 0) Y[(size_t)it.pair[t] * n + row] = v;
-        }
+        for (int r = 0; r < kExpRows; r++)
+#pragma unroll
+            for (int t = 0; t < kTok; t++) {
+                if (t >= it.count) break;
+                const float v = warp_sum(acc[r][t]);
+                if (lane == 0 && live[r]) Y[(size_t)it.pair[t] * n + rows[r]] = v;
+            }
     }
 }
 
@@ -473,9 +514,9 @@ int expert_layout(const DevTensor &w, const char *what, uint32_t n_exp, uint32_t
                        w.dtype, k, need);
     *row_bytes = (size_t)k / be * bb;
     *expert_bytes = *row_bytes * rows;
-    // the widest load of each format: the Q4_K header words and nibble pairs
-    // (8 B), the Q8_0 scale and quant pairs (2 B), the F32 float4 (16 B)
-    const size_t align = w.dtype == LC_Q4_K ? 8 : w.dtype == LC_Q8_0 ? 2 : 16;
+    // the widest load of each format: the Q4_K block header (16 B), the Q8_0
+    // scale and quant pairs (2 B), the F32 float4 (16 B)
+    const size_t align = w.dtype == LC_Q8_0 ? 2 : 16;
     if ((((uintptr_t)w.ptr) | *expert_bytes | *row_bytes) & (align - 1))
         return lc_fail(LC_ERR_UNSUPPORTED, "lc_target: %s: expert rows must be %zu-byte aligned", what, align);
     return LC_OK;
