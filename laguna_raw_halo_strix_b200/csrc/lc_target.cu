@@ -198,10 +198,15 @@ __device__ __forceinline__ void expert_load8(const uint8_t *__restrict__ wr, int
     }
 }
 
-// The eight weights, with the shaders' per-element formulas
-// (proj_q4k.comp:72-87, proj_q8_0.comp:53-64).
+// The lane's eight quantised values as exact floats, and the scale terms of
+// its sub-block / block:  w_i = mul * q_i - sub  (Q4_K: mul = d*sc, sub =
+// dmin*m, proj_q4k.comp:72-87; Q8_0: mul = d, sub = 0, proj_q8_0.comp:53-64;
+// F32: q_i = w_i, mul = 1).  An integer 0..255 becomes a float exactly through
+// the bit pattern of 2^23 + q minus 2^23 (no conversion instruction).
 template <int DT>
-__device__ __forceinline__ void expert_decode8(const ExpRaw<DT> &r, int lane, int half_mode, float (&w)[8]) {
+__device__ __forceinline__ void expert_decode8(const ExpRaw<DT> &r, int lane, int half_mode, float (&q)[8], float &mul,
+                                               float &sub) {
+    constexpr uint32_t kMagic = 0x4B000000u;  // 2^23
     if constexpr (DT == LC_Q4_K) {
         const float d = lc_half_to_f32(r.a.x & 0xFFFFu, half_mode), dmin = lc_half_to_f32(r.a.x >> 16, half_mode);
         const uint32_t sw[3] = {r.a.y, r.a.z, r.a.w};  // scale bytes 0..11
@@ -215,22 +220,29 @@ __device__ __forceinline__ void expert_decode8(const ExpRaw<DT> &r, int lane, in
             sc = (sb(j + 4) & 15u) | ((sb(j - 4) >> 6) << 4);
             mn = (sb(j + 4) >> 4) | ((sb(j) >> 6) << 4);
         }
+        mul = __fmul_rn(d, (float)sc);
+        sub = __fmul_rn(dmin, (float)mn);
         const int shift = (lane & 4) ? 4 : 0;
-        const float dsc = __fmul_rn(d, (float)sc), dmn = __fmul_rn(dmin, (float)mn);
+        const uint32_t lo = r.b.x >> shift, hi = r.b.y >> shift;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t nib = ((i < 4 ? lo : hi) >> (8 * (i & 3))) & 15u;
+            q[i] = __uint_as_float(kMagic | nib) - 8388608.0f;
+        }
+    } else if constexpr (DT == LC_Q8_0) {
+        mul = lc_half_to_f32(r.a.x, half_mode);
+        sub = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const uint32_t byte = ((i < 4 ? r.b.x : r.b.y) >> (8 * (i & 3))) & 0xFFu;
-            w[i] = __fsub_rn(__fmul_rn(dsc, (float)((byte >> shift) & 15u)), dmn);
+            q[i] = __uint_as_float(kMagic | (byte ^ 0x80u)) - 8388736.0f;  // (q + 128) - 128
         }
-    } else if constexpr (DT == LC_Q8_0) {
-        const float d = lc_half_to_f32(r.a.x, half_mode);
-#pragma unroll
-        for (int i = 0; i < 8; i++)
-            w[i] = __fmul_rn((float)(int8_t)(((i < 4 ? r.b.x : r.b.y) >> (8 * (i & 3))) & 0xFFu), d);
     } else {
-        w[0] = __uint_as_float(r.a.x), w[1] = __uint_as_float(r.a.y), w[2] = __uint_as_float(r.a.z);
-        w[3] = __uint_as_float(r.a.w), w[4] = __uint_as_float(r.b.x), w[5] = __uint_as_float(r.b.y);
-        w[6] = __uint_as_float(r.b.z), w[7] = __uint_as_float(r.b.w);
+        mul = 1.f;
+        sub = 0.f;
+        q[0] = __uint_as_float(r.a.x), q[1] = __uint_as_float(r.a.y), q[2] = __uint_as_float(r.a.z);
+        q[3] = __uint_as_float(r.a.w), q[4] = __uint_as_float(r.b.x), q[5] = __uint_as_float(r.b.y);
+        q[6] = __uint_as_float(r.b.z), q[7] = __uint_as_float(r.b.w);
     }
 }
 
@@ -281,21 +293,24 @@ __global__ void __launch_bounds__(256) expert_gemv_kernel(const uint8_t *__restr
             ExpRaw<DT> raw[kExpRows];
 #pragma unroll
             for (int r = 0; r < kExpRows; r++) expert_load8<DT>(wr[r], k0, lane, raw[r]);
-            float w[kExpRows][8];
+            float q[kExpRows][8], mul[kExpRows], sub[kExpRows];
 #pragma unroll
-            for (int r = 0; r < kExpRows; r++) expert_decode8<DT>(raw[r], lane, half_mode, w[r]);
+            for (int r = 0; r < kExpRows; r++) expert_decode8<DT>(raw[r], lane, half_mode, q[r], mul[r], sub[r]);
 #pragma unroll
             for (int t = 0; t < kTok; t++) {
                 if (t >= it.count) break;
                 const float4 a = __ldg(reinterpret_cast<const float4 *>(xr[t] + kk));
                 const float4 b = __ldg(reinterpret_cast<const float4 *>(xr[t] + kk + 4));
+                // S(x) of the lane's eight elements, shared by the rows
+                const float sx = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
 #pragma unroll
                 for (int r = 0; r < kExpRows; r++) {
-                    float s = acc[r][t];
-                    s = fmaf(w[r][0], a.x, s), s = fmaf(w[r][1], a.y, s), s = fmaf(w[r][2], a.z, s);
-                    s = fmaf(w[r][3], a.w, s), s = fmaf(w[r][4], b.x, s), s = fmaf(w[r][5], b.y, s);
-                    s = fmaf(w[r][6], b.z, s), s = fmaf(w[r][7], b.w, s);
-                    acc[r][t] = s;
+                    float s = q[r][0] * a.x;
+                    s = fmaf(q[r][1], a.y, s), s = fmaf(q[r][2], a.z, s), s = fmaf(q[r][3], a.w, s);
+                    s = fmaf(q[r][4], b.x, s), s = fmaf(q[r][5], b.y, s), s = fmaf(q[r][6], b.z, s);
+                    s = fmaf(q[r][7], b.w, s);
+                    // y += mul * S(q x) - sub * S(x)
+                    acc[r][t] = fmaf(mul[r], s, fmaf(-sub[r], sx, acc[r][t]));
                 }
             }
         }
