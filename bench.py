@@ -1013,19 +1013,22 @@ def run_target_verify(args):
             k_host.copy_(keys, non_blocking=True)
             stream.synchronize()
         e2e_s = _max_over_ranks(time.perf_counter() - t0, dev, world)
+        # the experts the last verify step selected, per MoE layer (lc_target_routing)
+        distinct_per_layer = []
+        for layer in range(1, hp["n_layers"]):
+            ids, _ = tm.routing(layer)
+            distinct_per_layer.append(int(torch.unique(ids[ids >= 0]).numel()))
     tm.close()
     # bytes one verify step must read: every dense projection, the router and
-    # shared expert, the experts the block selects (expected distinct count of
-    # 16 tokens x 8 of 64: 64 (1 - (1 - 8/64)^16) = 56.4), the K/V cache and the
-    # lm_head
+    # shared expert, the experts the block selected, the K/V cache and the lm_head
     q4 = 144 / 256
     H, KVD, F = hp["n_heads"], hp["n_kv_heads"] * hp["head_dim"], hp["n_ff"]
     QD = H * hp["head_dim"]
     NE, U, Fe, S, V = hp["n_expert"], hp["n_expert_used"], hp["n_ff_exp"], hp["n_ff_shexp"], hp["n_vocab"]
     attn_b = ((QD + 2 * KVD + H) * E + E * QD) * q4
-    distinct = NE * (1 - (1 - U / NE) ** M)
-    moe_b = E * NE * 4 + 3 * S * E * q4 + distinct * 3 * Fe * E * q4
-    step_b = (hp["n_layers"] * attn_b + 3 * F * E * q4 + (hp["n_layers"] - 1) * moe_b
+    distinct = sum(distinct_per_layer)
+    moe_b = (hp["n_layers"] - 1) * (E * NE * 4 + 3 * S * E * q4) + distinct * 3 * Fe * E * q4
+    step_b = (hp["n_layers"] * attn_b + 3 * F * E * q4 + moe_b
               + hp["n_layers"] * (C + M) * KVD * 2 * 4 + V * E * 34 / 32)
     hbm, _, peak_src = peaks()
     per_step_s = ms / 1e3 / args.steps
@@ -1039,7 +1042,8 @@ def run_target_verify(args):
             "config": {"workload": "target_verify", "baseline_config": None, "layers": hp["n_layers"],
                        "hidden": E, "heads": H, "kv_heads": hp["n_kv_heads"], "ffn_dense": F, "experts": NE,
                        "experts_used": U, "ffn_expert": Fe, "ffn_shared": S, "vocab": V, "cache": C, "block": M,
-                       "bytes_per_step": step_b, "expected_distinct_experts": distinct, "gguf_bytes": file_bytes,
+                       "bytes_per_step": step_b, "distinct_experts_per_moe_layer": distinct_per_layer,
+                       "gguf_bytes": file_bytes,
                        "load_s": load_s, "load_gbs": file_bytes / load_s / 1e9,
                        "l2": f"{step_b / 1e6:.0f} MB read per step (> 3x the 126 MB L2)",
                        "parallelism": f"replicas x{world} (independent sequences, no collective)"},

@@ -475,6 +475,10 @@ int lc_target_embed(lc_target *t, const uint32_t *tokens, uint32_t m, float *x);
 enum { LC_TARGET_CACHED = 1 };
 int lc_target_forward(lc_target *t, const float *x, uint32_t m, uint32_t flags, const uint32_t *capture_layers,
                       uint32_t n_capture, float *captured, float *hidden, float *logits, uint64_t *keys);
+/* The expert selection of MoE layer `layer` in the most recent forward (or
+ * lc_target_moe_ffn) that ran it: ids[m][n_expert_used] (device, enqueued on
+ * the context's stream) and m, the rows of that call. */
+int lc_target_routing(const lc_target *t, uint32_t layer, int32_t *ids, uint32_t *m);
 /* Positions held in the K/V cache (TargetKvCache::len). */
 int lc_target_cache_len(const lc_target *t, uint32_t *len);
 /* Drop cached positions from len on (rejected draft tokens); len = 0 is

@@ -391,6 +391,8 @@ struct lc_target {
     float *router = nullptr, *scores = nullptr, *gu = nullptr, *hs = nullptr, *col = nullptr, *dout = nullptr;
     float *sh_g = nullptr, *sh_u = nullptr, *sh_h = nullptr, *sh_out = nullptr, *moe_y = nullptr;
     int32_t *ids = nullptr;
+    int32_t *route_log = nullptr;  // [layer][max_block][n_sel]: the last selection of each layer
+    uint32_t route_rows[64] = {};  // rows of that selection per layer (layers < 64)
     int *n_items = nullptr;
     MoeItem *items = nullptr;
     std::vector<void *> allocs;
@@ -489,6 +491,7 @@ int workspace(lc_target *t) {
         const size_t NE = h.n_expert, P = B * t->n_sel, Fe = h.n_ff_exp, S = h.n_ff_shexp;
         LC_TRY(talloc_t(t, B * NE, &t->router));
         LC_TRY(talloc_t(t, std::max<size_t>(P, 1), &t->ids));
+        LC_TRY(talloc_t(t, std::max<size_t>((size_t)h.n_layers * P, 1), &t->route_log));
         LC_TRY(talloc_t(t, std::max<size_t>(P, 1), &t->scores));
         LC_TRY(talloc_t(t, std::max<size_t>(P, 1), &t->items));
         LC_TRY(talloc_t(t, 1, &t->n_items));
@@ -575,6 +578,9 @@ int moe_ffn(lc_target *t, uint32_t l, const float *x, uint32_t m, float *y) {
                                                                        h.expert_weights_norm ? 1 : 0,
                                                                        h.expert_weights_scale, t->ids, t->scores);
     moe_items_kernel<<<1, 1024, 0, c->stream>>>(t->ids, (int)P, (int)NE, t->items, t->n_items);
+    LC_CUDA(cudaMemcpyAsync(t->route_log + (size_t)l * t->max_block * NS, t->ids, (size_t)P * 4,
+                            cudaMemcpyDeviceToDevice, c->stream));
+    if (l < 64) t->route_rows[l] = m;
     LC_TRY(lc_after_launch(c, "lc_target: routing"));
     // the selected experts, grouped (src/target.rs:681-713)
     float *g = t->gu, *u = t->gu + (size_t)P * Fe;
@@ -710,6 +716,18 @@ extern "C" int lc_target_embed(lc_target *t, const uint32_t *tokens, uint32_t m,
         const size_t off = (size_t)tokens[r] * E / be * bb;
         LC_TRY(lc_dequant(t->ctx, dt, (const uint8_t *)w.ptr + off, (size_t)E / be * bb, E, x + (size_t)r * E));
     }
+    return LC_OK;
+}
+
+extern "C" int lc_target_routing(const lc_target *t, uint32_t layer, int32_t *ids, uint32_t *m) {
+    LC_REQUIRE(t && ids && m, LC_ERR_INVALID, "lc_target_routing: null argument");
+    LC_REQUIRE(layer < t->layers.size() && layer < 64 && t->layers[layer].is_moe, LC_ERR_INVALID,
+               "lc_target_routing: layer %u is not a MoE layer", layer);
+    *m = t->route_rows[layer];
+    if (*m == 0) return LC_OK;
+    const lc_ctx *c = t->ctx;
+    LC_CUDA(cudaMemcpyAsync(ids, t->route_log + (size_t)layer * t->max_block * t->n_sel, (size_t)*m * t->n_sel * 4,
+                            cudaMemcpyDeviceToDevice, c->stream));
     return LC_OK;
 }
 

@@ -142,6 +142,7 @@ SIGNATURES = {
     "lc_target_weight": (_i, [_vp, C.c_char_p, C.POINTER(_vp), C.POINTER(_i), C.POINTER(C.c_uint64)]),
     "lc_target_embed": (_i, [_vp, C.POINTER(_u32), _u32, _vp]),
     "lc_target_forward": (_i, [_vp, _vp, _u32, _u32, C.POINTER(_u32), _u32, _vp, _vp, _vp, _vp]),
+    "lc_target_routing": (_i, [_vp, _u32, _vp, C.POINTER(_u32)]),
     "lc_target_cache_len": (_i, [_vp, C.POINTER(_u32)]),
     "lc_target_cache_truncate": (_i, [_vp, _u32]),
     "lc_target_moe_ffn": (_i, [_vp, _u32, _vp, _u32, _vp, _vp, _vp]),

@@ -17,6 +17,7 @@ class Target:
     def __init__(self, ctx: lc.Context, gguf_path: str, max_ctx: int = 256, max_block: int = 16, flags: int = 0):
         self.L = lc.lib()
         self.ctx = ctx
+        self.max_block = max_block
         h = C.c_void_p()
         lc.check(self.L.lc_target_load_gguf(ctx.h, gguf_path.encode(), max_ctx, max_block, flags, C.byref(h)),
                  "lc_target_load_gguf")
@@ -59,6 +60,16 @@ class Target:
                                           cap.ctypes.data_as(C.POINTER(C.c_uint32)) if cap.size else None, cap.size,
                                           lc.ptr(captured), lc.ptr(hidden), lc.ptr(logits), lc.ptr(keys)),
                  "lc_target_forward")
+
+    def routing(self, layer: int):
+        """(ids [m, n_expert_used] int32 on the device, m) of the last call that ran MoE layer `layer`."""
+        import torch
+
+        n_sel = min(self.hp.n_expert_used, self.hp.n_expert)
+        ids = torch.empty(self.max_block * n_sel, dtype=torch.int32, device="cuda")
+        m = C.c_uint32()
+        lc.check(self.L.lc_target_routing(self.h, layer, lc.ptr(ids), C.byref(m)), "lc_target_routing")
+        return ids[: m.value * n_sel].view(m.value, n_sel), m.value
 
     @property
     def cache_len(self) -> int:

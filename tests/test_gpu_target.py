@@ -142,7 +142,9 @@ def test_moe_routing_and_experts(model, dev):
         ids = torch.empty(m, NU, dtype=torch.int32, device=dev)
         sc = torch.empty(m, NU, device=dev)
         tm.moe_ffn(layer, to_dev(nx, dev), m, y, ids, sc)
+        logged, rows = tm.routing(layer)  # lc_target_routing: the same selection
         torch.cuda.synchronize()
+        assert rows == m and torch.equal(logged, ids)
         for r in range(m):
             ry, rids, rsc = om.moe_ffn(layer, nx[r])
             assert list(ids[r].cpu().numpy()) == list(rids), (layer, r)
