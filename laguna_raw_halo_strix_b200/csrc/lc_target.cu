@@ -325,15 +325,25 @@ __global__ void __launch_bounds__(256) expert_gemv_kernel(const uint8_t *__restr
     }
 }
 
-// Per (token, slot) pair: h = SiLU(gate) * up (activation.comp), col_l2 =
+// Per (token, slot) pair p: h = SiLU(gate) * up (activation.comp), col_l2 =
 // clamp(|h|, 1e-8, 1e30) and hs = h * 32768 / col_l2 (src/target.rs:700-712).
+// gate / up rows: g + p * F (the per-expert projections), or, with `dense`, row
+// p / n_sel of every expert's outputs side by side, at ids[p] * F.
 __global__ void moe_swiglu_l2_kernel(const float *__restrict__ g, const float *__restrict__ u, int F,
+                                     const int32_t *__restrict__ ids, int n_sel, int dense, size_t dense_stride,
                                      float *__restrict__ hs, float *__restrict__ col) {
     __shared__ float red[32];
-    const size_t base = (size_t)blockIdx.x * F;
+    const int p = blockIdx.x;
+    const size_t base = (size_t)p * F;
+    const int e = ids[p];
+    if (e < 0) {  // an unfilled slot (the combine skips it)
+        if (threadIdx.x == 0) col[p] = 1.f;
+        return;
+    }
+    const size_t src = dense ? (size_t)(p / n_sel) * dense_stride + (size_t)e * F : base;
     float sq = 0.f;
     for (int i = threadIdx.x; i < F; i += blockDim.x) {
-        const float h = lc_swiglu(g[base + i], u[base + i]);
+        const float h = lc_swiglu(g[src + i], u[src + i]);
         hs[base + i] = h;
         sq = fmaf(h, h, sq);
     }
@@ -347,7 +357,7 @@ __global__ void moe_swiglu_l2_kernel(const float *__restrict__ g, const float *_
     }
     __syncthreads();
     const float c = red[0];
-    if (threadIdx.x == 0) col[blockIdx.x] = c;
+    if (threadIdx.x == 0) col[p] = c;
     for (int i = threadIdx.x; i < F; i += blockDim.x) hs[base + i] = __fdiv_rn(__fmul_rn(hs[base + i], 32768.f), c);
 }
 
@@ -389,6 +399,7 @@ struct lc_target {
     float *kbuf = nullptr, *vbuf = nullptr, *ffg = nullptr, *ffu = nullptr, *ffh = nullptr;
     // MoE workspace
     float *router = nullptr, *scores = nullptr, *gu = nullptr, *hs = nullptr, *col = nullptr, *dout = nullptr;
+    float *gu_dense = nullptr;  // [2][max_block][n_expert * n_ff_exp]: every expert's gate / up outputs
     float *sh_g = nullptr, *sh_u = nullptr, *sh_h = nullptr, *sh_out = nullptr, *moe_y = nullptr;
     int32_t *ids = nullptr;
     int32_t *route_log = nullptr;  // [layer][max_block][n_sel]: the last selection of each layer
@@ -496,6 +507,7 @@ int workspace(lc_target *t) {
         LC_TRY(talloc_t(t, std::max<size_t>(P, 1), &t->items));
         LC_TRY(talloc_t(t, 1, &t->n_items));
         LC_TRY(talloc_t(t, 2 * P * Fe, &t->gu));
+        LC_TRY(talloc_t(t, 2 * B * NE * Fe, &t->gu_dense));
         LC_TRY(talloc_t(t, P * Fe, &t->hs));
         LC_TRY(talloc_t(t, std::max<size_t>(P, 1), &t->col));
         LC_TRY(talloc_t(t, P * E, &t->dout));
@@ -582,15 +594,39 @@ int moe_ffn(lc_target *t, uint32_t l, const float *x, uint32_t m, float *y) {
                             cudaMemcpyDeviceToDevice, c->stream));
     if (l < 64) t->route_rows[l] = m;
     LC_TRY(lc_after_launch(c, "lc_target: routing"));
-    // the selected experts, grouped (src/target.rs:681-713)
-    float *g = t->gu, *u = t->gu + (size_t)P * Fe;
-    if (L.gate_exps.dtype == L.up_exps.dtype && gb == ub) {
-        LC_TRY(launch_expert_gemv(t, L.gate_exps, &L.up_exps, gb, gr, Fe, E, x, (int)NS, g, u, P));
+    // the selected experts' gate / up (src/target.rs:681-698).  A block whose
+    // selections can cover the expert set (m * n_used >= n_expert) and whose
+    // rows run the tcgen05 GEMM computes every expert at once: the stacks are
+    // one [n_expert * n_ff_exp, n_embd] matrix each, streamed once at tensor-core
+    // speed, and the pairs then take their expert's columns.  Smaller blocks
+    // (decode) read only the selected experts.
+    const bool dense = P >= NE && lc::routes_to_gemm_dq(c, m) && !(t->flags & LC_TARGET_REF_EXPERT_OFFSET) &&
+                       L.gate_exps.dtype == L.up_exps.dtype &&
+                       (L.gate_exps.dtype == LC_Q4_K || L.gate_exps.dtype == LC_Q8_0);
+    float *g, *u;
+    size_t dstride = 0;
+    if (dense) {
+        dstride = (size_t)NE * Fe;
+        g = t->gu_dense;
+        u = t->gu_dense + (size_t)m * dstride;
+        lc::PackSrc src;
+        src.x = x;
+        lc::ProjOut outs[2] = {{nullptr, g, NE * Fe, false}, {nullptr, u, NE * Fe, false}};
+        const DevTensor *ws[2] = {&L.gate_exps, &L.up_exps};
+        const char *names[2] = {"ffn_gate_exps.weight", "ffn_up_exps.weight"};
+        LC_TRY(lc::proj_w_block(c, t->tmp, src, nullptr, outs, ws, names, 2, m, E));
     } else {
-        LC_TRY(launch_expert_gemv(t, L.gate_exps, nullptr, gb, gr, Fe, E, x, (int)NS, g, nullptr, P));
-        LC_TRY(launch_expert_gemv(t, L.up_exps, nullptr, ub, ur, Fe, E, x, (int)NS, u, nullptr, P));
+        g = t->gu;
+        u = t->gu + (size_t)P * Fe;
+        if (L.gate_exps.dtype == L.up_exps.dtype && gb == ub) {
+            LC_TRY(launch_expert_gemv(t, L.gate_exps, &L.up_exps, gb, gr, Fe, E, x, (int)NS, g, u, P));
+        } else {
+            LC_TRY(launch_expert_gemv(t, L.gate_exps, nullptr, gb, gr, Fe, E, x, (int)NS, g, nullptr, P));
+            LC_TRY(launch_expert_gemv(t, L.up_exps, nullptr, ub, ur, Fe, E, x, (int)NS, u, nullptr, P));
+        }
     }
-    moe_swiglu_l2_kernel<<<P, 256, 0, c->stream>>>(g, u, (int)Fe, t->hs, t->col);
+    moe_swiglu_l2_kernel<<<P, 256, 0, c->stream>>>(g, u, (int)Fe, t->ids, (int)NS, dense ? 1 : 0, dstride, t->hs,
+                                                   t->col);
     LC_TRY(launch_expert_gemv(t, L.down_exps, nullptr, db, dr, E, Fe, t->hs, 1, t->dout, nullptr, P));
     // shared expert (src/target.rs:726-745)
     {

@@ -125,16 +125,18 @@ def test_cached_verify_blocks_and_rollback(model, dev):
     tm.truncate(0)
 
 
-def test_moe_routing_and_experts(model, dev):
+@pytest.mark.parametrize("m", [2, 12])
+def test_moe_routing_and_experts(model, dev, m):
     """lc_target_moe_ffn: the selected experts and their order are the
     oracle's, the scores agree to rounding, the FFN output to the projection
-    bound."""
+    bound -- for a 2-row block (only the selected experts are read) and a
+    12-row block (its 48 selections can cover the 16 experts: every expert's
+    gate / up run as one tensor-core GEMM)."""
     import torch
 
     hp, t, tm = model
     E, NU = hp["n_embd"], hp["n_expert_used"]
-    rng = np.random.default_rng(11)
-    m = 12
+    rng = np.random.default_rng(11 + m)
     nx = rng.standard_normal((m, E)).astype(np.float32)
     om = T.TargetOracle(hp, t)
     for layer in (1, 3):
