@@ -44,6 +44,7 @@ struct TLayer {
     DevTensor attn_norm, q_norm, k_norm, q, k, v, o, gate_attn, ffn_norm, gate, up, down;
     DevTensor probs_bias, gate_inp, gate_exps, up_exps, down_exps, gate_shexp, up_shexp, down_shexp;
     bool is_moe = false;
+    bool down_kcat = false;  // ffn_down_exps held k-concatenated ([row][expert][k])
     uint32_t n_q_heads = 0;
 };
 
@@ -255,7 +256,7 @@ __device__ __forceinline__ void expert_decode8(const ExpRaw<DT> &r, int lane, in
 constexpr int kExpRows = 4;
 template <int DT>
 __global__ void __launch_bounds__(256) expert_gemv_kernel(const uint8_t *__restrict__ w0, const uint8_t *__restrict__ w1,
-                                                          size_t expert_bytes, size_t row_bytes, int expert_fixed,
+                                                          size_t expert_stride, size_t row_stride, int expert_fixed,
                                                           int n, int k, const float *__restrict__ X, int act_div,
                                                           const MoeItem *__restrict__ items,
                                                           const int *__restrict__ n_items, float *Y0, float *Y1,
@@ -263,7 +264,7 @@ __global__ void __launch_bounds__(256) expert_gemv_kernel(const uint8_t *__restr
     if ((int)blockIdx.y >= *n_items) return;
     const MoeItem it = items[blockIdx.y];
     const int e = expert_fixed >= 0 ? expert_fixed : it.expert;
-    const uint8_t *W = (blockIdx.z ? w1 : w0) + (size_t)e * expert_bytes;
+    const uint8_t *W = (blockIdx.z ? w1 : w0) + (size_t)e * expert_stride;
     float *Y = blockIdx.z ? Y1 : Y0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float *xr[kTok];
@@ -279,7 +280,7 @@ __global__ void __launch_bounds__(256) expert_gemv_kernel(const uint8_t *__restr
         for (int r = 0; r < kExpRows; r++) {
             rows[r] = row0 + warp + 8 * (r + kExpRows * g);
             live[r] = rows[r] < row_end;
-            wr[r] = W + (size_t)(live[r] ? rows[r] : row0) * row_bytes;
+            wr[r] = W + (size_t)(live[r] ? rows[r] : row0) * row_stride;
         }
         if (!live[0]) break;
         float acc[kExpRows][kTok];
@@ -359,6 +360,37 @@ __global__ void moe_swiglu_l2_kernel(const float *__restrict__ g, const float *_
     const float c = red[0];
     if (threadIdx.x == 0) col[p] = c;
     for (int i = threadIdx.x; i < F; i += blockDim.x) hs[base + i] = __fdiv_rn(__fmul_rn(hs[base + i], 32768.f), c);
+}
+
+// The down-projection stack from expert-major [expert][row][k] to
+// k-concatenated [row][expert][k] (row r holds every expert's row r side by
+// side), one warp per (expert, row); row_bytes a multiple of 16.
+__global__ void kcat_rows_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int n_exp, int rows,
+                                 int row_bytes) {
+    const int lane = threadIdx.x & 31;
+    const long long unit = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (unit >= (long long)n_exp * rows) return;
+    const int e = (int)(unit / rows), r = (int)(unit % rows);
+    const uint8_t *sp = src + ((size_t)e * rows + r) * row_bytes;
+    uint8_t *dp = dst + ((size_t)r * n_exp + e) * row_bytes;
+    for (int c = lane * 16; c < row_bytes; c += 512)
+        *reinterpret_cast<uint4 *>(dp + c) = *reinterpret_cast<const uint4 *>(sp + c);
+}
+
+// The down projection's input for every token and expert at once: H[t][e*F +
+// i] = hs[p][i] * s_p for the token's selected experts (zero elsewhere, set
+// before), s_p = (col_p / 32768) * score_p when score_p > 0, else 1 -- the
+// per-expert output scale of src/target.rs:714-722 moved before the (linear)
+// projection.
+__global__ void moe_scatter_kernel(const float *__restrict__ hs, const float *__restrict__ col,
+                                   const float *__restrict__ scores, const int32_t *__restrict__ ids, int n_sel, int ne,
+                                   int F, float *__restrict__ H) {
+    const int p = blockIdx.x, e = ids[p];
+    if (e < 0) return;
+    const float sc = scores[p];
+    const float s = sc > 0.f ? __fmul_rn(__fdiv_rn(col[p], 32768.f), sc) : 1.f;
+    float *dst = H + (size_t)(p / n_sel) * ne * F + (size_t)e * F;
+    for (int i = threadIdx.x; i < F; i += blockDim.x) dst[i] = __fmul_rn(hs[(size_t)p * F + i], s);
 }
 
 // y[t] = ((0 + o_0) + o_1) + ... + shared, o_j = down_j * ((col_j / 32768) *
@@ -552,14 +584,17 @@ int expert_layout(const DevTensor &w, const char *what, uint32_t n_exp, uint32_t
     return LC_OK;
 }
 
-int launch_expert_gemv(lc_target *t, const DevTensor &wa, const DevTensor *wb, size_t expert_bytes, size_t row_bytes,
+// expert_stride / row_stride: bytes between experts / between the rows of one
+// expert (expert-major stacks: one matrix and one row; the k-concatenated down
+// stack: one row and n_expert rows).
+int launch_expert_gemv(lc_target *t, const DevTensor &wa, const DevTensor *wb, size_t expert_stride, size_t row_stride,
                        uint32_t n, uint32_t k, const float *X, int act_div, float *Ya, float *Yb, uint32_t max_items) {
     lc_ctx *c = t->ctx;
     const bool ref = (t->flags & LC_TARGET_REF_EXPERT_OFFSET) && wa.dtype != LC_Q4_K;
     const dim3 grid((n + kRowsCta - 1) / kRowsCta, max_items, wb ? 2 : 1);
     const uint8_t *pa = (const uint8_t *)wa.ptr, *pb = wb ? (const uint8_t *)wb->ptr : pa;
 #define LC_EXPERT_LAUNCH(DT)                                                                                      \
-    expert_gemv_kernel<DT><<<grid, 256, 0, c->stream>>>(pa, pb, expert_bytes, row_bytes, ref ? 0 : -1, (int)n,      \
+    expert_gemv_kernel<DT><<<grid, 256, 0, c->stream>>>(pa, pb, expert_stride, row_stride, ref ? 0 : -1, (int)n,    \
                                                          (int)k, X, act_div, t->items, t->n_items, Ya, Yb ? Yb : Ya, \
                                                          c->half_mode)
     switch (wa.dtype) {
@@ -627,7 +662,10 @@ int moe_ffn(lc_target *t, uint32_t l, const float *x, uint32_t m, float *y) {
     }
     moe_swiglu_l2_kernel<<<P, 256, 0, c->stream>>>(g, u, (int)Fe, t->ids, (int)NS, dense ? 1 : 0, dstride, t->hs,
                                                    t->col);
-    LC_TRY(launch_expert_gemv(t, L.down_exps, nullptr, db, dr, E, Fe, t->hs, 1, t->dout, nullptr, P));
+    if (!(dense && L.down_kcat)) {
+        const size_t es = L.down_kcat ? dr : db, rs = L.down_kcat ? (size_t)NE * dr : dr;
+        LC_TRY(launch_expert_gemv(t, L.down_exps, nullptr, es, rs, E, Fe, t->hs, 1, t->dout, nullptr, P));
+    }
     // shared expert (src/target.rs:726-745)
     {
         lc::PackSrc src;
@@ -647,10 +685,66 @@ int moe_ffn(lc_target *t, uint32_t l, const float *x, uint32_t m, float *y) {
         const char *names[1] = {"ffn_down_shexp.weight"};
         LC_TRY(lc::proj_w_block(c, t->tmp, src, t->sh_h, outs, ws, names, 1, m, S));
     }
+    if (dense && L.down_kcat) {
+        // every expert's down projection as one GEMM over k = n_expert * n_ff_exp:
+        // y = [H_e ...] . [W_e ...]^T sums the selected experts (the rest are zero)
+        float *H = t->gu_dense;  // the gate outputs are consumed
+        LC_CUDA(cudaMemsetAsync(H, 0, (size_t)m * NE * Fe * 4, c->stream));
+        moe_scatter_kernel<<<P, 256, 0, c->stream>>>(t->hs, t->col, t->scores, t->ids, (int)NS, (int)NE, (int)Fe, H);
+        LC_TRY(lc::proj_w(c, L.down_exps, "ffn_down_exps.weight", H, t->dout, m, NE * Fe, E));
+        return lc_add(c, t->dout, t->sh_out, y, m * E);
+    }
     const int threads = 256, blocks = (int)std::min<size_t>(((size_t)m * E + threads - 1) / threads, 4 * 148);
     moe_combine_kernel<<<blocks, threads, 0, c->stream>>>(t->dout, t->col, t->scores, t->ids, t->sh_out, (int)NS,
                                                            (int)E, (int)m, y);
     return lc_after_launch(c, "lc_target: expert sum");
+}
+
+}  // namespace
+
+namespace {
+
+// Q4_K / Q8_0 down-projection stacks go k-concatenated at load time, so a
+// block that covers the expert set runs all experts' down projections as one
+// GEMM; the per-expert kernel reads the same layout with other strides.  The
+// reference's expert-offset behaviour needs the original order and keeps it.
+int kcat_down_stacks(lc_target *t) {
+    const lc_target_hparams &h = t->hp;
+    if (!h.has_moe || (t->flags & LC_TARGET_REF_EXPERT_OFFSET) || h.n_ff_exp % 256 != 0) return LC_OK;
+    const uint32_t NE = h.n_expert, E = h.n_embd, Fe = h.n_ff_exp;
+    void *tmp = nullptr;
+    size_t tmp_bytes = 0;
+    int s = LC_OK;
+    for (TLayer &L : t->layers) {
+        DevTensor &w = L.down_exps;
+        if (!L.is_moe || !w.ptr || (w.dtype != LC_Q4_K && w.dtype != LC_Q8_0) || w.n_el < (uint64_t)NE * E * Fe)
+            continue;
+        const size_t row_bytes = (size_t)Fe / lc_type_block_elements(w.dtype) * lc_type_block_bytes(w.dtype);
+        const size_t bytes = row_bytes * E * NE;
+        if (row_bytes % 16 || ((uintptr_t)w.ptr & 15)) continue;
+        if (bytes > tmp_bytes) {
+            if (tmp) cudaFree(tmp);
+            tmp = nullptr;
+            if (cudaMalloc(&tmp, bytes) != cudaSuccess) {
+                cudaGetLastError();
+                s = lc_fail(LC_ERR_OOM, "lc_target: cudaMalloc(%zu) for the down-projection layout", bytes);
+                break;
+            }
+            tmp_bytes = bytes;
+        }
+        const long long units = (long long)NE * E;
+        kcat_rows_kernel<<<(unsigned)((units + 7) / 8), 256, 0, t->ctx->stream>>>(
+            (const uint8_t *)w.ptr, (uint8_t *)tmp, (int)NE, (int)E, (int)row_bytes);
+        cudaError_t e = cudaMemcpyAsync(w.ptr, tmp, bytes, cudaMemcpyDeviceToDevice, t->ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(t->ctx->stream);
+        if (e != cudaSuccess) {
+            s = lc_fail(LC_ERR_CUDA, "lc_target: down-projection layout: %s", cudaGetErrorString(e));
+            break;
+        }
+        L.down_kcat = true;
+    }
+    if (tmp) cudaFree(tmp);
+    return s;
 }
 
 }  // namespace
@@ -694,7 +788,8 @@ extern "C" int lc_target_load_gguf(lc_ctx *ctx, const char *path, uint32_t max_c
             t->heads_max = std::max(t->heads_max, L.n_q_heads);
         }
         t->qd_max = t->heads_max * h.head_dim;
-        s = workspace(t);
+        s = kcat_down_stacks(t);
+        if (!s) s = workspace(t);
     }
     if (s) {
         delete t;
