@@ -1028,6 +1028,11 @@ def run_target_verify(args):
     attn_b = ((QD + 2 * KVD + H) * E + E * QD) * q4
     distinct = sum(distinct_per_layer)
     moe_b = (hp["n_layers"] - 1) * (E * NE * 4 + 3 * S * E * q4) + distinct * 3 * Fe * E * q4
+    # what the step actually streams: a 16-row block covers the expert set
+    # (16 x 8 >= 64), so every expert's gate / up / down run as dense GEMMs
+    read_b = (hp["n_layers"] * attn_b + 3 * F * E * q4
+              + (hp["n_layers"] - 1) * (E * NE * 4 + 3 * S * E * q4 + NE * 3 * Fe * E * q4)
+              + hp["n_layers"] * (C + M) * KVD * 2 * 4 + V * E * 34 / 32)
     step_b = (hp["n_layers"] * attn_b + 3 * F * E * q4 + moe_b
               + hp["n_layers"] * (C + M) * KVD * 2 * 4 + V * E * 34 / 32)
     hbm, _, peak_src = peaks()
@@ -1043,6 +1048,7 @@ def run_target_verify(args):
                        "hidden": E, "heads": H, "kv_heads": hp["n_kv_heads"], "ffn_dense": F, "experts": NE,
                        "experts_used": U, "ffn_expert": Fe, "ffn_shared": S, "vocab": V, "cache": C, "block": M,
                        "bytes_per_step": step_b, "distinct_experts_per_moe_layer": distinct_per_layer,
+                       "bytes_streamed_per_step": read_b,
                        "gguf_bytes": file_bytes,
                        "load_s": load_s, "load_gbs": file_bytes / load_s / 1e9,
                        "l2": f"{step_b / 1e6:.0f} MB read per step (> 3x the 126 MB L2)",
