@@ -69,18 +69,21 @@ struct GvArgs {
     unsigned *status;
 };
 
-// Shared memory: the ring [warps][depth][slice bytes], the activation table
-// [ks][tab bytes per slice], partial sums part [part_rows][ks][M] floats (one
-// per row of the CTA's range and k-slice, summed once at the end).
+// Shared memory: the ring [warps][depth][slice bytes], the activations xs
+// [M][kpad] (f32, SiLU-gated for the SwiGLU form, 4 floats of padding after
+// every 64 so the lanes' 16-byte reads of their runs fall in distinct banks),
+// partial sums part [part_rows][ks][M] floats (one per row of the CTA's range
+// and k-slice, summed once at the end).
+__host__ __device__ __forceinline__ int gv_kpad(int k) { return k + (k >> 4); }
 struct GvLayout {
-    size_t ring, tab, part, total;
+    size_t ring, xs, part, total;
 };
-__host__ __device__ __forceinline__ GvLayout gv_layout(int warps, int depth, int slice_bytes, int tab_bytes,
-                                                       int part_rows, int ks, int m) {
+__host__ __device__ __forceinline__ GvLayout gv_layout(int warps, int depth, int slice_bytes, int k, int part_rows,
+                                                       int ks, int m) {
     GvLayout L;
     L.ring = 0;
-    L.tab = (size_t)warps * depth * slice_bytes;
-    L.part = L.tab + (size_t)ks * tab_bytes;
+    L.xs = (size_t)warps * depth * slice_bytes;
+    L.part = L.xs + (size_t)m * gv_kpad(k) * 4;  // k rounded up to whole k-slices by the caller
     L.total = L.part + (size_t)part_rows * ks * m * 4 + 128;  // + slack to 128-align the base
     return L;
 }
@@ -127,22 +130,15 @@ __device__ __forceinline__ int lane_exp(float mx) {
 }
 __device__ __forceinline__ float lane_f(int E) { return __uint_as_float((uint32_t)(276 - E) << 23); }
 
-// n (multiple of 4) activations from element e0 of token row xr (and x2r for
-// the SwiGLU form), global memory, 16-byte aligned.
+// N activations of a run [e0, e0 + N) inside one 64-element block, from the
+// padded shared copy of a token's row.
 template <int N>
-__device__ __forceinline__ void load_act(const float *xr, const float *x2r, int e0, float (&v)[N]) {
+__device__ __forceinline__ void load_pad(const float *xs, int e0, float (&v)[N]) {
+    const float *p = xs + e0 + ((e0 >> 6) << 2);
 #pragma unroll
     for (int i = 0; i < N; i += 4) {
-        const float4 a = __ldg(reinterpret_cast<const float4 *>(xr + e0 + i));
+        const float4 a = *reinterpret_cast<const float4 *>(p + i);
         v[i] = a.x, v[i + 1] = a.y, v[i + 2] = a.z, v[i + 3] = a.w;
-    }
-    if (x2r) {
-#pragma unroll
-        for (int i = 0; i < N; i += 4) {
-            const float4 b = __ldg(reinterpret_cast<const float4 *>(x2r + e0 + i));
-            v[i] = lc_swiglu(v[i], b.x), v[i + 1] = lc_swiglu(v[i + 1], b.y);
-            v[i + 2] = lc_swiglu(v[i + 2], b.z), v[i + 3] = lc_swiglu(v[i + 3], b.w);
-        }
     }
 }
 
@@ -170,7 +166,6 @@ struct Q4Lane {
     static constexpr int SPW = M == 1 ? 8 : 4;  // super-blocks per warp slice
     static constexpr int SLICE = SPW * 144;           // bytes of a row per warp slice
     static constexpr int DEPTH = 8;                   // rows in flight per warp (a power of two)
-    static constexpr int TAB = M * (NP * 8 * 32 * 8 + 32 * 16);  // table bytes per slice
     uint64_t xp[M][NP][8];                      // pre-scaled activation pairs
     float sx[M][2];                             // S(x) over the lane's low / high elements
     float f[M];                                 // 2^(149 - E)
@@ -206,14 +201,12 @@ struct Q4Lane {
     }
 
     // The lane's activations (the SwiGLU form reads both inputs).
-    __device__ __forceinline__ void load(const GvArgs &a, Raw &v) const {
+    __device__ __forceinline__ void load(const float *xs, int kpad, Raw &v) const {
 #pragma unroll
         for (int j = 0; j < M; j++) {
             if (on) {
-                const float *xr = a.x + (size_t)j * a.k;
-                const float *x2r = a.x2 ? a.x2 + (size_t)j * a.k : nullptr;
-                load_act<NE>(xr, x2r, e0, v[j][0]);
-                load_act<NE>(xr, x2r, e0 + 32, v[j][1]);
+                load_pad<NE>(xs + (size_t)j * kpad, e0, v[j][0]);
+                load_pad<NE>(xs + (size_t)j * kpad, e0 + 32, v[j][1]);
             } else {
 #pragma unroll
                 for (int h = 0; h < 2; h++)
@@ -223,8 +216,12 @@ struct Q4Lane {
         }
     }
 
-    // The pre-scaled pairs, sums and f of the lane to / from the slice's table:
-    // [j][p][pos][lane] pairs, then [j][lane] (sx0, sx1, f).
+    // One token: the first warp of each k-slice publishes its lanes' pre-scaled
+    // pairs, sums and f as a table the slice's other warps load, written over
+    // the slice's own 8704 bytes of xs: [p][pos][lane] pairs, then [lane]
+    // (sx0, sx1, f).
+    static constexpr bool SHARE = M == 1;
+    static constexpr int SLICE_ELEMS = M == 1 ? 2048 : 1024;
     __device__ __forceinline__ void store_table(unsigned char *t, int lane) const {
         uint64_t *tp = reinterpret_cast<uint64_t *>(t);
         float4 *ta = reinterpret_cast<float4 *>(t + M * NP * 8 * 32 * 8);
@@ -352,7 +349,6 @@ struct Q4Lane {
 struct Q8Lane {
     static constexpr int SLICE = 64 * 34;                  // 64 blocks per warp slice
     static constexpr int DEPTH = 4;                        // rows in flight per warp (a power of two)
-    static constexpr int TAB = 64 * 32 * 4 + 32 * 16;      // table bytes per slice
     float xp[64];  // pre-scaled activations: block A elements 0..31, block B 32..63
     float sx[2];   // S(x) over block A, block B
     float f;
@@ -370,15 +366,10 @@ struct Q8Lane {
         e0 = 32 * blk;
     }
 
-    __device__ __forceinline__ void load(const GvArgs &a, Raw &v) const {
-        if (on) {
-            load_act<64>(a.x, a.x2, e0, v);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 64; i++) v[i] = 0.f;
-        }
-    }
-
+    // As the one-token Q4_K lane: the slice's table over its 8704 bytes of xs,
+    // [i][lane] activations, then [lane] (sx0, sx1, f).
+    static constexpr bool SHARE = true;
+    static constexpr int SLICE_ELEMS = 2048;
     __device__ __forceinline__ void store_table(unsigned char *t, int lane) const {
         float *tp = reinterpret_cast<float *>(t);
 #pragma unroll
@@ -392,6 +383,17 @@ struct Q8Lane {
         const float4 v = reinterpret_cast<const float4 *>(t + 64 * 32 * 4)[lane];
         sx[0] = v.x, sx[1] = v.y, f = v.z;
     }
+
+    __device__ __forceinline__ void load(const float *xs, int kpad, Raw &v) const {
+        (void)kpad;
+        if (on) {
+            load_pad<64>(xs, e0, v);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 64; i++) v[i] = 0.f;
+        }
+    }
+
 
     struct Bytes {
         uint32_t w[17];
@@ -493,16 +495,45 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, 1) gemv_rows_kernel(const __
     const int slice = warp % a.ks, rgi = warp / a.ks;
     L ln;
     ln.geom(a, slice, lane);
-    // the first warp of each k-slice loads the activations before any weight
-    // request: requests leave an SM in order
-    typename L::Raw raw;
-    if (rgi == 0) ln.load(a, raw);
-
     constexpr int D = L::DEPTH;
-    const GvLayout Lo = gv_layout(nwarps, D, L::SLICE, L::TAB, a.part_rows, a.ks, M);
+    const int kpad = gv_kpad(a.k);
+    const GvLayout Lo = gv_layout(nwarps, D, L::SLICE, a.ks * L::SLICE_ELEMS, a.part_rows, a.ks, M);
     unsigned char *ring = smem + Lo.ring + (size_t)warp * D * L::SLICE;
-    unsigned char *tab = smem + Lo.tab + (size_t)slice * L::TAB;
+    float *xs = reinterpret_cast<float *>(smem + Lo.xs);
     float *part = reinterpret_cast<float *>(smem + Lo.part);
+    // The activations: every thread loads kXB float4 of x (and of x2) per
+    // phase, the first phase before any weight request (requests leave an SM
+    // in order), and stores them, SiLU-gated for the SwiGLU form, into xs.
+    constexpr int kXB = 8;
+    const int n4 = M * a.k / 4;
+    const float4 *x4 = reinterpret_cast<const float4 *>(a.x), *x24 = reinterpret_cast<const float4 *>(a.x2);
+    float4 xa[kXB], xb[kXB];
+    auto x_load = [&](int start) {
+#pragma unroll
+        for (int b = 0; b < kXB; b++) {
+            const int idx = start + b * (int)blockDim.x;
+            if (idx < n4) {
+                xa[b] = __ldg(x4 + idx);
+                if (x24) xb[b] = __ldg(x24 + idx);
+            }
+        }
+    };
+    auto x_store = [&](int start) {
+#pragma unroll
+        for (int b = 0; b < kXB; b++) {
+            const int idx = start + b * (int)blockDim.x;
+            if (idx < n4) {
+                float4 v = xa[b];
+                if (x24) {
+                    v.x = lc_swiglu(v.x, xb[b].x), v.y = lc_swiglu(v.y, xb[b].y);
+                    v.z = lc_swiglu(v.z, xb[b].z), v.w = lc_swiglu(v.w, xb[b].w);
+                }
+                const int e = idx * 4, j = e / a.k, ee = e - j * a.k;
+                *reinterpret_cast<float4 *>(xs + (size_t)j * kpad + ee + ((ee >> 6) << 2)) = v;
+            }
+        }
+    };
+    x_load((int)threadIdx.x);
     const int total = a.rows_end[a.ng - 1];
     const int r0 = (int)((long long)total * blockIdx.x / gridDim.x);
     const int r1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
@@ -524,12 +555,32 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, 1) gemv_rows_kernel(const __
         if (d < nmy) gv_copy_slice<L::SLICE>(slice_ptr(d), ring + d * L::SLICE, sbytes, lane);
         cp_async_commit();
     }
-    if (rgi == 0) {
-        ln.prep(raw);
-        ln.store_table(tab, lane);
+    x_store((int)threadIdx.x);
+    for (int start = (int)threadIdx.x + kXB * (int)blockDim.x; start < n4; start += kXB * (int)blockDim.x) {
+        x_load(start);
+        x_store(start);
     }
     __syncthreads();
-    if (rgi != 0) ln.load_table(tab, lane);
+    if constexpr (L::SHARE) {
+        // the first warp of each slice forms the pre-scaled activations and
+        // publishes them over the slice's own part of xs (it alone reads that
+        // part: its lanes' runs lie inside the slice); the other warps load them
+        unsigned char *tab = reinterpret_cast<unsigned char *>(xs) + (size_t)slice * gv_kpad(L::SLICE_ELEMS) * 4;
+        if (rgi == 0) {
+            typename L::Raw raw;
+            ln.load(xs, kpad, raw);
+            __syncwarp();
+            ln.prep(raw);
+            ln.store_table(tab, lane);
+        }
+        __syncthreads();
+        if (rgi != 0) ln.load_table(tab, lane);
+    } else {
+        // every warp forms its lanes' pre-scaled activations from xs
+        typename L::Raw raw;
+        ln.load(xs, kpad, raw);
+        ln.prep(raw);
+    }
 
     const uint32_t ref_mask = a.half_mode == LC_HALF_REF ? 0x04000400u : 0u;
     for (int i0 = 0; i0 < nmy; i0 += kGvQuad) {
@@ -600,14 +651,13 @@ GvPlan gv_plan(const lc_ctx *ctx, int dtype, int m, int k, int rows) {
     const int threads = ks * rg * 32;
     const int slice_bytes = dtype == LC_Q8_0 ? Q8Lane::SLICE : (m == 1 ? Q4Lane<1>::SLICE : Q4Lane<2>::SLICE);
     const int depth = dtype == LC_Q8_0 ? Q8Lane::DEPTH : (m == 1 ? Q4Lane<1>::DEPTH : Q4Lane<2>::DEPTH);
-    const int tab_bytes = dtype == LC_Q8_0 ? Q8Lane::TAB : (m == 1 ? Q4Lane<1>::TAB : Q4Lane<2>::TAB);
     // one CTA per SM; more (in waves) only when a CTA's row range would need
     // more than 32 KB of partial sums
     int grid = std::max(1, std::min(ctx->num_sms, rows));
     const long long max_rows = std::max(1, (32 << 10) / (ks * m * 4));
     if ((rows + grid - 1) / grid > max_rows) grid = (int)((rows + max_rows - 1) / max_rows);
     const int part_rows = (rows + grid - 1) / grid + 1;
-    const size_t need = gv_layout(ks * rg, depth, slice_bytes, tab_bytes, part_rows, ks, m).total;
+    const size_t need = gv_layout(ks * rg, depth, slice_bytes, ks * se, part_rows, ks, m).total;
     if (need > ctx->smem_optin) return p;
     p.ks = ks, p.rg = rg, p.threads = threads, p.smem = need, p.part_rows = part_rows;
     p.grid = grid;
