@@ -434,8 +434,8 @@ struct lc_target {
     float *gu_dense = nullptr;  // [2][max_block][n_expert * n_ff_exp]: every expert's gate / up outputs
     float *sh_g = nullptr, *sh_u = nullptr, *sh_h = nullptr, *sh_out = nullptr, *moe_y = nullptr;
     int32_t *ids = nullptr;
-    int32_t *route_log = nullptr;  // [layer][max_block][n_sel]: the last selection of each layer
-    uint32_t route_rows[64] = {};  // rows of that selection per layer (layers < 64)
+    int32_t *route_log = nullptr;       // [layer][max_block][n_sel]: the last selection of each layer
+    std::vector<uint32_t> route_rows;  // rows of that selection per layer
     int *n_items = nullptr;
     MoeItem *items = nullptr;
     std::vector<void *> allocs;
@@ -627,7 +627,7 @@ int moe_ffn(lc_target *t, uint32_t l, const float *x, uint32_t m, float *y) {
     moe_items_kernel<<<1, 1024, 0, c->stream>>>(t->ids, (int)P, (int)NE, t->items, t->n_items);
     LC_CUDA(cudaMemcpyAsync(t->route_log + (size_t)l * t->max_block * NS, t->ids, (size_t)P * 4,
                             cudaMemcpyDeviceToDevice, c->stream));
-    if (l < 64) t->route_rows[l] = m;
+    t->route_rows[l] = m;
     LC_TRY(lc_after_launch(c, "lc_target: routing"));
     // the selected experts' gate / up (src/target.rs:681-698).  A block whose
     // selections can cover the expert set (m * n_used >= n_expert) and whose
@@ -774,6 +774,7 @@ extern "C" int lc_target_load_gguf(lc_ctx *ctx, const char *path, uint32_t max_c
                     h.n_expert_used, kMaxExperts);
     if (!s) {
         t->layers.resize(h.n_layers);
+        t->route_rows.assign(h.n_layers, 0);
         for (uint32_t l = 0; l < h.n_layers; l++) t->layers[l].is_moe = h.has_moe && l > 0;  // src/target.rs:140
         t->n_sel = std::min(h.n_expert_used, h.n_expert);
         s = lc::load_tensors(ctx, g, [t](const char *name) { return target_slot(t, name); }, flags & LC_LOAD_BF16_NATIVE,
@@ -852,7 +853,7 @@ extern "C" int lc_target_embed(lc_target *t, const uint32_t *tokens, uint32_t m,
 
 extern "C" int lc_target_routing(const lc_target *t, uint32_t layer, int32_t *ids, uint32_t *m) {
     LC_REQUIRE(t && ids && m, LC_ERR_INVALID, "lc_target_routing: null argument");
-    LC_REQUIRE(layer < t->layers.size() && layer < 64 && t->layers[layer].is_moe, LC_ERR_INVALID,
+    LC_REQUIRE(layer < t->layers.size() && t->layers[layer].is_moe, LC_ERR_INVALID,
                "lc_target_routing: layer %u is not a MoE layer", layer);
     *m = t->route_rows[layer];
     if (*m == 0) return LC_OK;

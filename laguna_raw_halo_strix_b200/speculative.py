@@ -27,11 +27,13 @@ def verify_steps(target: Target, draft: DFlash, start_token: int, n_steps: int, 
     """Returns (accepted, draft_tokens, target_tokens), one entry per step."""
     import torch
 
-    dev = torch.device("cuda", target.ctx.device if hasattr(target.ctx, "device") else 0)
+    dev = torch.device("cuda", target.ctx.device)
     E = target.hp.n_embd
     layers = sorted(set(int(v) for v in target_layers))
     n_aux = len(layers)
-    assert draft.hp.n_embd == E and draft.hp.n_aux == n_aux, "draft and target do not fit together"
+    if draft.hp.n_embd != E or draft.hp.n_aux != n_aux:
+        raise ValueError(f"draft (n_embd {draft.hp.n_embd}, {draft.hp.n_aux} target layers) does not fit the target "
+                         f"(n_embd {E}, {n_aux} capture layers)")
     w_out, dt_out, _ = target.weight("output.weight")
     V = target.hp.n_vocab
     emb = torch.empty(1, E, device=dev)
@@ -67,7 +69,7 @@ def verify_block(target: Target, tokens, emb=None, keys=None):
     toks = np.asarray(tokens, np.uint32)
     m = toks.size
     E = target.hp.n_embd
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", target.ctx.device)
     if emb is None:
         emb = torch.empty(m, E, device=dev)
     if keys is None:

@@ -66,7 +66,7 @@ class Target:
         import torch
 
         n_sel = min(self.hp.n_expert_used, self.hp.n_expert)
-        ids = torch.empty(self.max_block * n_sel, dtype=torch.int32, device="cuda")
+        ids = torch.empty(self.max_block * n_sel, dtype=torch.int32, device=torch.device("cuda", self.ctx.device))
         m = C.c_uint32()
         lc.check(self.L.lc_target_routing(self.h, layer, lc.ptr(ids), C.byref(m)), "lc_target_routing")
         return ids[: m.value * n_sel].view(m.value, n_sel), m.value
