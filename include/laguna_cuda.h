@@ -434,6 +434,10 @@ typedef struct {
 typedef struct lc_target lc_target;
 
 int lc_gguf_target_hparams(const lc_gguf *g, lc_target_hparams *out);
+/* The target_layers metadata array (a DFlash draft's capture layers,
+ * src/gguf.rs:633-638): its integer elements, the first `cap` into out[];
+ * *n receives the count (0 when the key is absent). */
+int lc_gguf_target_layers(const lc_gguf *g, int64_t *out, uint32_t cap, uint32_t *n);
 
 /* TargetModel::load (src/target.rs:130-266) on the loader of
  * lc_dflash_load_gguf_ex (mapped file, pinned staging, one allocation; raw

@@ -11,11 +11,20 @@
 //   test-rmsnorm           4-element rmsnorm self-test   (run_test_rmsnorm, lib.rs:167)
 //   draft <gguf> [ctx] [m] block draft forward: encode ctx rows of synthetic
 //                          target features, then decode an m-token block
+//   target-info <gguf>     target metadata + layer kinds (run_target_info, lib.rs:257)
+//   target-forward <gguf> [tok]  forward_token, all layers captured (lib.rs:284)
+//   target-generate <gguf> [start] [n]  greedy, K/V cached (lib.rs:335)
+//   target-dflash <t> <d> [tok]  one draft step's logits (lib.rs:384)
+//   target-dflash-verify <t> <d> [tok] [n]  draft / verify loop (lib.rs:466)
+//   project-ref <gguf> <file>    lm_head of an f32 hidden state (lib.rs:530)
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
+#include <cmath>
+#include <string>
 #include <vector>
 
 #include "laguna_cuda.h"
@@ -252,6 +261,331 @@ static int run_draft(const char *path, uint32_t n_ctx, uint32_t mt) {
     return finite ? 0 : 1;
 }
 
+// ---- target model (src/lib.rs:257-560) ---------------------------------------
+
+// Device buffers of the target commands; freed at exit.
+template <typename T>
+static T *dev_alloc(size_t n) {
+    void *p = nullptr;
+    if (cudaMalloc(&p, (n ? n : 1) * sizeof(T)) != cudaSuccess) {
+        fprintf(stderr, "cudaMalloc failed\n");
+        exit(1);
+    }
+    return (T *)p;
+}
+
+template <typename T>
+static std::vector<T> to_host(const T *d, size_t n) {
+    std::vector<T> h(n);
+    if (cudaMemcpy(h.data(), d, n * sizeof(T), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        fprintf(stderr, "cudaMemcpy failed\n");
+        exit(1);
+    }
+    return h;
+}
+
+static lc_target *target_open(lc_ctx *c, const char *path, uint32_t max_ctx, uint32_t max_block) {
+    lc_target *t;
+    CHECK(lc_target_load_gguf(c, path, max_ctx, max_block, 0, &t));
+    return t;
+}
+
+static std::vector<int64_t> gguf_target_layers(const char *path) {
+    lc_gguf *g;
+    CHECK(lc_gguf_open(path, &g));
+    uint32_t n = 0;
+    CHECK(lc_gguf_target_layers(g, nullptr, 0, &n));
+    std::vector<int64_t> v(n);
+    if (n) CHECK(lc_gguf_target_layers(g, v.data(), n, &n));
+    lc_gguf_close(g);
+    return v;
+}
+
+static void print_list(const char *label, const std::vector<int64_t> &v) {
+    printf("%s[", label);
+    for (size_t i = 0; i < v.size(); i++) printf(i ? ", %lld" : "%lld", (long long)v[i]);
+    printf("]\n");
+}
+
+// An f32 as Rust's Display writes it: the fewest significant digits that read
+// back as the same f32, in plain decimal notation (no exponent).
+static std::string rust_f32(float v) {
+    if (std::isnan(v)) return "NaN";
+    if (std::isinf(v)) return v < 0 ? "-inf" : "inf";
+    if (v == 0) return std::signbit(v) ? "-0" : "0";
+    char b[64];
+    for (int p = 0; p < 9; p++) {
+        snprintf(b, sizeof b, "%.*e", p, (double)v);
+        if (strtof(b, nullptr) == v) break;
+    }
+    std::string s(b), digits;
+    const bool neg = s[0] == '-';
+    if (neg) s.erase(0, 1);
+    const size_t e = s.find('e');
+    for (size_t i = 0; i < e; i++)
+        if (s[i] != '.') digits += s[i];
+    const int point = atoi(s.c_str() + e + 1) + 1;  // digits left of the decimal point
+    std::string out;
+    if (point <= 0) out = "0." + std::string(-point, '0') + digits;
+    else if (point >= (int)digits.size()) out = digits + std::string(point - digits.size(), '0');
+    else out = digits.substr(0, point) + "." + digits.substr(point);
+    return neg ? "-" + out : out;
+}
+
+static void print_logit(size_t i, float v) { printf("  logit[%zu] = %s\n", i, rust_f32(v).c_str()); }
+
+// The n largest logits, in the order of a stable descending sort (equal
+// values keep index order), as the reference prints them.
+static void print_top(const std::vector<float> &lg, int n) {
+    std::vector<int> idx(lg.size());
+    for (size_t i = 0; i < idx.size(); i++) idx[i] = (int)i;
+    std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return lg[a] > lg[b]; });
+    for (int i = 0; i < n && i < (int)idx.size(); i++) print_logit(idx[i], lg[idx[i]]);
+}
+
+// The argmax of a row (the last maximum), lib.rs:456-464.
+static uint32_t key_token(const uint64_t *keys_dev) {
+    return lc_key_index(to_host(keys_dev, 1)[0]);
+}
+
+static int run_target_info(const char *path) {
+    lc_ctx *c = ctx_open();
+    lc_target *t = target_open(c, path, 1, 1);
+    lc_target_hparams h;
+    CHECK(lc_target_get_hparams(t, &h));
+    printf("Target Model Info:\n");
+    printf("  layers: %u\n  embedding_length: %u\n  ffn_length: %u\n  head_count: %u\n  head_count_kv: %u\n",
+           h.n_layers, h.n_embd, h.n_ff, h.n_heads, h.n_kv_heads);
+    printf("  head_dim: %u\n  rope_dim: %u\n  rope_dim_swa: %u\n", h.head_dim, h.rope_dim, h.rope_dim_swa);
+    printf("  expert_count: %u\n  expert_used_count: %u\n  expert_ffn_length: %u\n  shared_ffn_length: %u\n",
+           h.n_expert, h.n_expert_used, h.n_ff_exp, h.n_ff_shexp);
+    printf("  has_moe: %s\n  has_shexp: %s\n  vocab_size: %u\n", h.has_moe ? "true" : "false",
+           h.has_shexp ? "true" : "false", h.n_vocab);
+    print_list("  target_layers: ", gguf_target_layers(path));
+    for (uint32_t l = 0; l < h.n_layers; l++) {
+        uint32_t moe;
+        CHECK(lc_target_layer_info(t, l, &moe, nullptr));
+        printf("  layer %u [%s]\n", l, moe ? "MoE" : "Dense");
+    }
+    lc_target_destroy(t);
+    lc_destroy(c);
+    return 0;
+}
+
+// target-forward: forward_token of the token's embedding, every layer's input
+// captured (run_target_forward, lib.rs:284-331).
+static int run_target_forward(const char *path, uint32_t tok) {
+    lc_ctx *c = ctx_open();
+    lc_target *t = target_open(c, path, 1, 1);
+    lc_target_hparams h;
+    CHECK(lc_target_get_hparams(t, &h));
+    const uint32_t E = h.n_embd, V = h.n_vocab ? h.n_vocab : E;
+    const void *emb_w;
+    const bool has_emb = lc_target_weight(t, "token_embd.weight", &emb_w, nullptr, nullptr) == LC_OK;
+    float *x = dev_alloc<float>(E), *cap = dev_alloc<float>((size_t)h.n_layers * E);
+    float *logits = dev_alloc<float>(std::max(V, E));
+    if (has_emb) {
+        if (tok >= h.n_vocab) {
+            fprintf(stderr, "token_id %u >= vocab_size %u\n", tok, h.n_vocab);
+            return 1;
+        }
+        CHECK(lc_target_embed(t, &tok, 1, x));
+        printf("Running target model forward pass with token_id=%u\n", tok);
+    } else {
+        std::vector<float> d(E, 0.1f);
+        cudaMemcpy(x, d.data(), E * 4, cudaMemcpyHostToDevice);
+    }
+    std::vector<uint32_t> layers(h.n_layers);
+    for (uint32_t l = 0; l < h.n_layers; l++) layers[l] = l;
+    CHECK(lc_target_forward(t, x, 1, 0, layers.data(), h.n_layers, cap, nullptr, logits, nullptr));
+    const uint32_t n_logits = lc_target_weight(t, "output.weight", &emb_w, nullptr, nullptr) == LC_OK ? V : E;
+    std::vector<float> lg = to_host(logits, n_logits);
+    printf("Forward pass complete: %u logits, %u captured states\n", n_logits, h.n_layers);
+    if (has_emb) {
+        printf("Top logits:\n");
+        print_top(lg, 10);
+        printf("Specific indices:\n");
+    }
+    for (uint32_t i = 0; i < 10 && i < n_logits; i++) print_logit(i, lg[i]);
+    lc_target_destroy(t);
+    lc_destroy(c);
+    return 0;
+}
+
+// target-generate: greedy tokens through the K/V cache (run_target_generate,
+// lib.rs:335-380).
+static int run_target_generate(const char *path, uint32_t start, uint32_t n) {
+    lc_ctx *c = ctx_open();
+    lc_target *t = target_open(c, path, n + 1, 1);
+    lc_target_hparams h;
+    CHECK(lc_target_get_hparams(t, &h));
+    const void *w;
+    if (lc_target_weight(t, "token_embd.weight", &w, nullptr, nullptr) != LC_OK) {
+        fprintf(stderr, "model has no token embeddings; cannot generate\n");
+        return 1;
+    }
+    float *x = dev_alloc<float>(h.n_embd);
+    uint64_t *keys = dev_alloc<uint64_t>(1);
+    std::vector<int64_t> out;
+    uint32_t cur = start;
+    printf("Generating %u tokens from start_token=%u\n", n, start);
+    for (uint32_t step = 0; step < n; step++) {
+        if (cur >= h.n_vocab) {
+            fprintf(stderr, "token %u out of range\n", cur);
+            break;
+        }
+        CHECK(lc_target_embed(t, &cur, 1, x));
+        CHECK(lc_target_forward(t, x, 1, LC_TARGET_CACHED, nullptr, 0, nullptr, nullptr, nullptr, keys));
+        const uint32_t next = key_token(keys);
+        printf("  step %u: input=%u -> next=%u\n", step, cur, next);
+        out.push_back(next);
+        cur = next;
+    }
+    print_list("Generated tokens: ", out);
+    lc_target_destroy(t);
+    lc_destroy(c);
+    return 0;
+}
+
+// One draft step of the verify loops: the target's forward_token with the
+// draft's target layers captured, the draft's forward_injected_decode_hidden,
+// the target's lm_head on the draft's hidden state (lib.rs:404-426, :486-496).
+struct DraftPair {
+    lc_ctx *c;
+    lc_target *t;
+    lc_dflash *d;
+    lc_target_hparams h;
+    std::vector<int64_t> draft_layers;  // as the draft lists them
+    std::vector<uint32_t> layers;       // captured: sorted, distinct
+    const void *out_w = nullptr;
+    int out_dt = 0;
+    float *x, *cap, *enc, *dh, *logits;
+    uint64_t *keys;
+};
+
+static DraftPair pair_open(const char *tpath, const char *dpath) {
+    DraftPair p;
+    p.c = ctx_open();
+    p.t = target_open(p.c, tpath, 1, 1);
+    CHECK(lc_target_get_hparams(p.t, &p.h));
+    CHECK(lc_dflash_load_gguf(p.c, dpath, 1, 1, &p.d));
+    // forward_token captures the layers in layer order, each once, and the
+    // final state for index n_layers (src/target.rs:398-407, :550-551).
+    p.draft_layers = gguf_target_layers(dpath);
+    for (int64_t v : p.draft_layers)
+        if (v >= 0 && v <= p.h.n_layers) p.layers.push_back((uint32_t)v);
+    std::sort(p.layers.begin(), p.layers.end());
+    p.layers.erase(std::unique(p.layers.begin(), p.layers.end()), p.layers.end());
+    lc_dflash_hparams dh;
+    CHECK(lc_dflash_get_hparams(p.d, &dh));
+    if (dh.n_embd != p.h.n_embd || dh.n_aux != p.layers.size()) {
+        fprintf(stderr, "draft (n_embd %u, %u target layers) does not fit the target (n_embd %u, %zu capture layers)\n",
+                dh.n_embd, dh.n_aux, p.h.n_embd, p.layers.size());
+        exit(1);
+    }
+    CHECK(lc_target_weight(p.t, "output.weight", &p.out_w, &p.out_dt, nullptr));
+    const uint32_t E = p.h.n_embd, n = (uint32_t)p.layers.size();
+    p.x = dev_alloc<float>(E), p.cap = dev_alloc<float>((size_t)(n ? n : 1) * E), p.enc = dev_alloc<float>(E);
+    p.dh = dev_alloc<float>(E), p.logits = dev_alloc<float>(p.h.n_vocab), p.keys = dev_alloc<uint64_t>(2);
+    return p;
+}
+
+// Returns (target token, draft token); the draft's logits stay in p.logits.
+static void pair_step(DraftPair &p, uint32_t tok, uint32_t *target_tok, uint32_t *draft_tok) {
+    const uint32_t E = p.h.n_embd, n = (uint32_t)p.layers.size();
+    CHECK(lc_target_embed(p.t, &tok, 1, p.x));
+    CHECK(lc_target_forward(p.t, p.x, 1, 0, p.layers.data(), n, p.cap, nullptr, nullptr, p.keys));
+    CHECK(lc_dflash_encode(p.d, p.cap, 1, p.enc));
+    CHECK(lc_dflash_set_context(p.d, p.enc, 1));
+    CHECK(lc_dflash_decode_block(p.d, p.x, 1, p.dh));
+    CHECK(lc_lm_head_argmax(p.c, p.out_dt, p.dh, p.out_w, 1, E, p.h.n_vocab, 0, p.keys + 1, p.logits));
+    std::vector<uint64_t> k = to_host(p.keys, 2);
+    *target_tok = lc_key_index(k[0]);
+    *draft_tok = lc_key_index(k[1]);
+}
+
+// target-dflash: one draft step, the draft's logits (run_target_dflash,
+// lib.rs:384-429).
+static int run_target_dflash(const char *tpath, const char *dpath, uint32_t tok) {
+    DraftPair p = pair_open(tpath, dpath);
+    if (tok >= p.h.n_vocab) {
+        fprintf(stderr, "token_id %u >= vocab_size %u\n", tok, p.h.n_vocab);
+        return 1;
+    }
+    print_list("DFlash target layers: ", p.draft_layers);
+    uint32_t tt, dt;
+    pair_step(p, tok, &tt, &dt);
+    printf("Captured %zu states, %zu feature floats\n", p.layers.size(), p.layers.size() * p.h.n_embd);
+    printf("DFlash draft logits: %u\n", p.h.n_vocab);
+    printf("Top draft logits:\n");
+    print_top(to_host(p.logits, p.h.n_vocab), 10);
+    lc_dflash_destroy(p.d);
+    lc_target_destroy(p.t);
+    lc_destroy(p.c);
+    return 0;
+}
+
+// target-dflash-verify: the draft / verify loop (run_target_dflash_verify,
+// lib.rs:466-528).
+static int run_target_dflash_verify(const char *tpath, const char *dpath, uint32_t tok, uint32_t steps) {
+    DraftPair p = pair_open(tpath, dpath);
+    std::vector<int64_t> accepted;
+    print_list("DFlash target layers: ", p.draft_layers);
+    uint32_t exact = 0;
+    for (uint32_t s = 0; s < steps; s++) {
+        if (tok >= p.h.n_vocab) {
+            fprintf(stderr, "token_id %u >= vocab_size %u\n", tok, p.h.n_vocab);
+            return 1;
+        }
+        uint32_t tt, dt;
+        pair_step(p, tok, &tt, &dt);
+        const bool ok = dt == tt;
+        exact += ok;
+        const uint32_t next = ok ? dt : tt;
+        accepted.push_back(next);
+        printf("step %u: input=%u draft=%u target=%u %s -> accepted=%u\n", s, tok, dt, tt, ok ? "ACCEPT" : "REJECT",
+               next);
+        tok = next;
+    }
+    print_list("accepted tokens: ", accepted);
+    printf("exact draft accept rate: %u/%u\n", exact, steps);
+    lc_dflash_destroy(p.d);
+    lc_target_destroy(p.t);
+    lc_destroy(p.c);
+    return 0;
+}
+
+// project-ref: the lm_head on a hidden state read from a file of n_embd f32
+// (run_project_ref, lib.rs:530-556).
+static int run_project_ref(const char *path, const char *hidden_path) {
+    lc_ctx *c = ctx_open();
+    lc_target *t = target_open(c, path, 1, 1);
+    lc_target_hparams h;
+    CHECK(lc_target_get_hparams(t, &h));
+    std::vector<float> hid(h.n_embd);
+    FILE *f = fopen(hidden_path, "rb");
+    if (!f || fread(hid.data(), 4, h.n_embd, f) != h.n_embd || fgetc(f) != EOF) {
+        fprintf(stderr, "%s: expected %u f32 values\n", hidden_path, h.n_embd);
+        return 1;
+    }
+    fclose(f);
+    const void *w;
+    int dt;
+    CHECK(lc_target_weight(t, "output.weight", &w, &dt, nullptr));
+    float *x = dev_alloc<float>(h.n_embd), *logits = dev_alloc<float>(h.n_vocab);
+    uint64_t *keys = dev_alloc<uint64_t>(1);
+    cudaMemcpy(x, hid.data(), h.n_embd * 4, cudaMemcpyHostToDevice);
+    CHECK(lc_lm_head_argmax(c, dt, x, w, 1, h.n_embd, h.n_vocab, 0, keys, logits));
+    std::vector<float> lg = to_host(logits, h.n_vocab);
+    printf("Top logits:\n");
+    print_top(lg, 10);
+    printf("Specific indices:\n");
+    for (uint32_t i = 0; i < 8 && i < h.n_vocab; i++) print_logit(i, lg[i]);
+    lc_target_destroy(t);
+    lc_destroy(c);
+    return 0;
+}
+
 int main(int argc, char **argv) {
     if (argc < 2) {
         fprintf(stderr,
@@ -263,7 +597,13 @@ int main(int argc, char **argv) {
                 "  draft <gguf_path> [ctx] [block] - block draft forward\n"
                 "  test-dequant              - test dequantization\n"
                 "  test-matmul               - test matmul on GPU\n"
-                "  test-rmsnorm              - test rmsnorm on GPU\n",
+                "  test-rmsnorm              - test rmsnorm on GPU\n"
+                "  target-info <gguf>        - show target model metadata\n"
+                "  target-forward <gguf> [tok] - target forward pass\n"
+                "  target-generate <gguf> [start] [n] - greedy cached generation\n"
+                "  target-dflash <target> <dflash> [tok] - one DFlash draft step\n"
+                "  target-dflash-verify <target> <dflash> [tok] [n] - draft/verify loop\n"
+                "  project-ref <gguf> <hidden_f32_file> - lm_head of a hidden state\n",
                 argv[0]);
         return 1;
     }
@@ -284,6 +624,13 @@ int main(int argc, char **argv) {
     if (!strcmp(cmd, "test-dequant")) return run_test_dequant();
     if (!strcmp(cmd, "test-matmul")) return run_test_matmul();
     if (!strcmp(cmd, "test-rmsnorm")) return run_test_rmsnorm();
+    auto num = [&](int i, uint32_t dflt) { return argc > i ? (uint32_t)strtoul(argv[i], nullptr, 10) : dflt; };
+    if (!strcmp(cmd, "target-info")) return run_target_info(arg(2));
+    if (!strcmp(cmd, "target-forward")) return run_target_forward(arg(2), num(3, 0));
+    if (!strcmp(cmd, "target-generate")) return run_target_generate(arg(2), num(3, 0), num(4, 16));
+    if (!strcmp(cmd, "target-dflash")) return run_target_dflash(arg(2), arg(3), num(4, 0));
+    if (!strcmp(cmd, "target-dflash-verify")) return run_target_dflash_verify(arg(2), arg(3), num(4, 0), num(5, 4));
+    if (!strcmp(cmd, "project-ref")) return run_project_ref(arg(2), arg(3));
     fprintf(stderr, "unknown command: %s\n", cmd);
     return 1;
 }

@@ -442,3 +442,18 @@ extern "C" int lc_gguf_target_hparams(const lc_gguf *g, lc_target_hparams *hp) {
     hp->qk_eps = 1e-6f;    // dispatch_qk_norm_rope (src/target.rs:897)
     return LC_OK;
 }
+
+extern "C" int lc_gguf_target_layers(const lc_gguf *g, int64_t *out, uint32_t cap, uint32_t *n) {
+    if (!g || !n || (cap && !out)) return lc_fail(LC_ERR_INVALID, "lc_gguf_target_layers: null argument");
+    // populate_metadata (src/gguf.rs:633-638): the array's integer elements
+    *n = 0;
+    const Value *v = find_any(g, {"target_layers", "laguna.target_layers", "dflash.target_layers"});
+    if (!v || v->kind != Value::ARR) return LC_OK;
+    for (const Value &e : v->arr) {
+        uint64_t u;
+        if (!e.as_u64(&u)) continue;
+        if (*n < cap) out[*n] = (int64_t)u;
+        ++*n;
+    }
+    return LC_OK;
+}

@@ -135,6 +135,7 @@ SIGNATURES = {
     "lc_dflash_weight": (_i, [_vp, C.c_char_p, C.POINTER(_vp), C.POINTER(_i), C.POINTER(C.c_uint64)]),
     # target model
     "lc_gguf_target_hparams": (_i, [_vp, _vp]),
+    "lc_gguf_target_layers": (_i, [_vp, C.POINTER(C.c_int64), _u32, C.POINTER(_u32)]),
     "lc_target_load_gguf": (_i, [_vp, C.c_char_p, _u32, _u32, _u32, C.POINTER(_vp)]),
     "lc_target_destroy": (_i, [_vp]),
     "lc_target_get_hparams": (_i, [_vp, _vp]),
