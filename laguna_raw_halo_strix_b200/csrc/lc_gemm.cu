@@ -23,10 +23,12 @@
 // contiguous range per CTA.
 //
 // With only 2 NT token columns per MMA, an A operand in shared memory would
-// cost 4 KB of shared-memory reads per 16-cycle MMA plus the converters'
-// writes: shared-memory bandwidth, not the tensor cores, would bound the
-// kernel.  Tensor memory takes that traffic instead (columns 0-255: four A
-// half-unit stages of 64 columns; columns 256-511: accumulators).
+// cost 4 KB of shared-memory reads per MMA plus the converters' writes:
+// shared-memory bandwidth, not the tensor cores, would bound the kernel.
+// Tensor memory takes that traffic instead: three A unit slots of 128
+// columns (two when the accumulators need more room), then the accumulator
+// buffers.  The converters of unit j + slots wait only for the MMAs of unit
+// j, so the slots set how far conversion runs ahead of the tensor cores.
 //
 // Q4_K keeps the weights exact on the tensor cores: A holds the integers
 // sc_j * q, so each unit's product P = sum sc_j q x and min term
@@ -300,27 +302,30 @@ __global__ void x16_pack_kernel(const float *__restrict__ x, const float *__rest
 
 struct GemmLayout {
     size_t amin = 0, x = 0, raw = 0, sc = 0, bars = 0, tslot = 0, total = 0;
-    int XS = 0, RS = 0, ND = 0, xstage = 0, bufcols = 0;
+    int XS = 0, RS = 0, ND = 0, xstage = 0, bufcols = 0, AS = 0, acc = 0;
 };
 
 // Shared memory: Q4_K min-term operands (one per TMEM A stage), activation
 // stages (+ the sub-block sums for Q4_K), raw weight stages, per-unit
 // (d, dmin) slots (Q4_K), barriers.  Every stage size is a multiple of 1024
-// bytes.  TMEM: accumulator buffers of `bufcols` columns from column 256.
+// bytes.  TMEM: AS A slots of 128 columns, then ND accumulator buffers of
+// `bufcols` columns from column `acc`.
 template <class F, int NT>
 __host__ __device__ constexpr GemmLayout gemm_layout() {
     GemmLayout L{};
     L.XS = NT >= 32 ? 3 : 4;
     L.RS = F::kQ8 ? (NT >= 32 ? 3 : 4) : (NT >= 32 ? 5 : 6);
     L.bufcols = F::kQ8 ? 2 * NT : 4 * NT;  // hi / lo columns (+ the Q4_K min term)
-    L.ND = (kTmemCols - kAccBase) / L.bufcols < 4 ? (kTmemCols - kAccBase) / L.bufcols : 4;
+    L.AS = (kTmemCols - 3 * kACols) / L.bufcols >= 2 ? 3 : 2;
+    L.acc = L.AS * kACols;
+    L.ND = (kTmemCols - L.acc) / L.bufcols < 4 ? (kTmemCols - L.acc) / L.bufcols : 4;
     L.xstage = 2 * NT * 512 + (F::kQ8 ? 0 : 2 * NT * 32);  // both halves of a unit
     L.amin = 0;
-    L.x = L.amin + (F::kQ8 ? 0 : (size_t)kASlots * kMinBytes);
+    L.x = L.amin + (F::kQ8 ? 0 : (size_t)L.AS * kMinBytes);
     L.raw = L.x + (size_t)L.XS * L.xstage;
     L.sc = L.raw + (size_t)L.RS * kRows * F::kRowBytes;
     L.bars = L.sc + (F::kQ8 ? 0 : (size_t)L.ND * kRows * 8);
-    L.tslot = L.bars + (size_t)(2 * L.RS + 2 * kASlots + 2 * L.XS + 3 * L.ND + 1) * 8;
+    L.tslot = L.bars + (size_t)(2 * L.RS + 2 * L.AS + 2 * L.XS + 3 * L.ND + 1) * 8;
     L.total = L.tslot + 16 + 1024;  // + slack to 1024-align the base
     return L;
 }
@@ -343,8 +348,20 @@ __device__ __forceinline__ int group_of(const DqGroup *G, int tile, int &ltile) 
     return gi;
 }
 
+// Warps of the dq GEMM.  For NT = 16 the converters are two sets of eight that
+// take alternate units, so one set's tensor-memory stores and barrier waits
+// overlap the other's conversion; NT = 32 keeps one set (its epilogue needs
+// the registers).
+template <int NT>
+struct DqWarps {
+    static constexpr int kSets = NT <= 16 ? 2 : 1;
+    static constexpr int kConv = kConvWarps * kSets;
+    static constexpr int kMma = 1 + kConv;  // first of the two MMA warps
+    static constexpr int kAll = kMma + kMmaWarps + 4;
+};
+
 template <class F, int NT>
-__global__ void __launch_bounds__(kGemmWarps * 32, 1)
+__global__ void __launch_bounds__(DqWarps<NT>::kAll * 32, 1)
     dq_gemm_kernel(const __grid_constant__ DqGroup grp, const __grid_constant__ CUtensorMap tmx,
                    const uint8_t *__restrict__ sx16, const float *__restrict__ inv, int m, int k, int half_mode,
                    unsigned *__restrict__ status) {
@@ -356,13 +373,14 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
     constexpr int NB = 2 * NT;  // UMMA N: hi and lo rows of the tokens
     constexpr int kXTiles = NB * 512;  // activations of one unit: two halves of two 64-column boxes
     constexpr int kRawStage = kRows * F::kRowBytes;
-    constexpr int ND = L.ND;
+    constexpr int ND = L.ND, AS = L.AS;
+    using W = DqWarps<NT>;
     uint8_t *amin_ring = smem + L.amin, *x_ring = smem + L.x, *raw_ring = smem + L.raw;
     float2 *dslot = reinterpret_cast<float2 *>(smem + L.sc);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *raw_full = bars, *raw_empty = raw_full + L.RS;
-    uint64_t *a_full = raw_empty + L.RS, *a_empty = a_full + kASlots;
-    uint64_t *x_full = a_empty + kASlots, *x_empty = x_full + L.XS;
+    uint64_t *a_full = raw_empty + L.RS, *a_empty = a_full + AS;
+    uint64_t *x_full = a_empty + AS, *x_empty = x_full + L.XS;
     uint64_t *d_full = x_empty + L.XS, *d_empty = d_full + ND, *s_full = d_empty + ND, *drain = s_full + ND;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(smem + L.tslot);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -372,13 +390,13 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < L.RS; i++) mbar_init(raw_full + i, 1), mbar_init(raw_empty + i, kConvWarps);
-        for (int i = 0; i < kASlots; i++) mbar_init(a_full + i, kConvWarps), mbar_init(a_empty + i, 1);
+        for (int i = 0; i < AS; i++) mbar_init(a_full + i, kConvWarps), mbar_init(a_empty + i, 1);
         for (int i = 0; i < L.XS; i++) mbar_init(x_full + i, 1), mbar_init(x_empty + i, 1);
         for (int i = 0; i < ND; i++) mbar_init(d_full + i, 1), mbar_init(d_empty + i, 4), mbar_init(s_full + i, 4);
         mbar_init(drain, kMmaWarps);
         mbar_init_fence();
     }
-    if (warp == kMmaWarp) {
+    if (warp == W::kMma) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tslot)),
                      "r"(kTmemCols)
                      : "memory");
@@ -419,19 +437,19 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
                 if (Q4) bulk_load(xst + kXTiles, sx16 + (size_t)sb * NB * 32, NB * 32, x_full + xs, xpol);
             }
         }
-    } else if (warp <= kConvWarps) {  // converters: group g converts half g of row r of every unit
-        const int g = (warp - 1) >> 2, quad = warp & 3, r = 32 * quad + lane;
+    } else if (warp <= W::kConv) {  // converters: group g of set `set` converts half g of row r
+        const int set = (warp - 1) >> 3, g = ((warp - 1) >> 2) & 1, quad = warp & 3, r = 32 * quad + lane;
         const uint32_t tlane = tbase + ((uint32_t)(32 * quad) << 16);
         const uint32_t ref_mask = half_mode == LC_HALF_REF ? 0x04000400u : 0u;
-        if (Q4 && g == 0)  // columns 8..15 of the min-term operands stay zero
-            for (int i = 0; i < kASlots; i++)
+        if (Q4 && g == 0 && set == 0)  // columns 8..15 of the min-term operands stay zero
+            for (int i = 0; i < AS; i++)
                 *reinterpret_cast<uint4 *>(amin_ring + i * kMinBytes + core16_off(r, 8)) = make_uint4(0u, 0u, 0u, 0u);
-        for (int u = U0; u < U1 && ok; u++) {
+        for (int u = U0 + set; u < U1 && ok; u += W::kSets) {  // set s takes units s, s + kSets, ...
             const int j = u - U0, rs = j % L.RS;
             if (!mbar_wait(raw_full + rs, (j / L.RS) & 1)) { fail(); break; }
             const uint8_t *raw = raw_ring + (size_t)rs * kRawStage + (size_t)r * F::kRowBytes;
-            const int as = j % kASlots;
-            if (!mbar_wait(a_empty + as, ((j / kASlots) & 1) ^ 1)) { fail(); break; }
+            const int as = j % AS;
+            if (!mbar_wait(a_empty + as, ((j / AS) & 1) ^ 1)) { fail(); break; }
             tc_fence_after();
             const uint32_t ta = tlane + as * kACols + g * 64;
             if constexpr (Q4) {
@@ -473,7 +491,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
                 mbar_arrive(raw_empty + rs);
             }
         }
-    } else if (warp < kMmaWarp + kMmaWarps) {
+    } else if (warp < W::kMma + kMmaWarps) {
         if (lane == 0) {  // MMA issuer
             constexpr uint32_t idesc = umma_idesc_f16(kRows, NB);
             // Descriptors of x stage 0 and of the min-term operand stage 0; the
@@ -486,22 +504,21 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
             // One synchronisation point per unit: the accumulator buffer, the
             // unit's A slot (both converter groups) and its activations, one
             // fence, 16 (+1) MMAs, three commits.
-            for (int u = U0 + (warp - kMmaWarp); u < U1 && ok; u += kMmaWarps) {
-                const int j = u - U0, db = j % ND, as = j % kASlots, xs = j % L.XS;
-                if (!mbar_wait(d_empty + db, ((j / ND) & 1) ^ 1) || !mbar_wait(a_full + as, (j / kASlots) & 1) ||
+            for (int u = U0 + (warp - W::kMma); u < U1 && ok; u += kMmaWarps) {
+                const int j = u - U0, db = j % ND, as = j % AS, xs = j % L.XS;
+                if (!mbar_wait(d_empty + db, ((j / ND) & 1) ^ 1) || !mbar_wait(a_full + as, (j / AS) & 1) ||
                     !mbar_wait(x_full + xs, (j / L.XS) & 1)) {
                     fail();
                     break;
                 }
                 tc_fence_after();
-                const uint32_t dcol = tbase + kAccBase + db * L.bufcols;
+                const uint32_t dcol = tbase + L.acc + db * L.bufcols;
                 const uint64_t xd = xdesc0 + (uint64_t)((xs * L.xstage) >> 4);
                 const uint32_t ta = tbase + as * kACols;
-                umma_f16_ts(dcol, ta, xd, idesc, 0u);
 #pragma unroll
-                for (int kk = 1; kk < 16; kk++)  // half kk / 8 at column 64 (kk / 8) + 8 (kk % 8)
+                for (int kk = 0; kk < 16; kk++)  // half kk / 8 at column 64 (kk / 8) + 8 (kk % 8)
                     umma_f16_ts(dcol, ta + 8 * kk, xd + (uint64_t)(((kk >> 2) * (NB * 128) + (kk & 3) * 32) >> 4), idesc,
-                                1u);
+                                kk ? 1u : 0u);
                 if (Q4)  // min term: sum_j m_j * (sub-block sum of x) / 32
                     umma_f16_ss(dcol + NB, mdesc0 + (uint64_t)((as * kMinBytes) >> 4),
                                 sdesc0 + (uint64_t)((xs * L.xstage) >> 4), idesc, 0u);
@@ -525,36 +542,42 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
             const uint32_t par = (j / ND) & 1;
             if (!mbar_wait(d_full + db, par)) { fail(); break; }
             tc_fence_after();
-            const uint32_t col = tbase + lanes + kAccBase + db * L.bufcols;
+            const uint32_t col = tbase + lanes + L.acc + db * L.bufcols;
             float2 dd = make_float2(1.f, 0.f);
             if constexpr (Q4) {
                 if (!mbar_wait(s_full + db, par)) { fail(); break; }
                 dd = dslot[db * kRows + 32 * q + lane];
             }
+            // Per 16 tokens: the hi and lo columns (and the Q4_K min term's)
+            // summed, scaled into the row's partial sums.
 #pragma unroll
             for (int c = 0; c < NT / 16; c++) {
-                float iv[16], ph[16], pl[16];
+                float iv[16], pr[16], mn[16], h[16], l[16];
 #pragma unroll
                 for (int t = 0; t < 16; t += 4) {
                     const float4 f = __ldg(reinterpret_cast<const float4 *>(inv + sb * NT + 16 * c + t));
                     iv[t] = f.x, iv[t + 1] = f.y, iv[t + 2] = f.z, iv[t + 3] = f.w;
                 }
-                tmem_ld16(col + 16 * c, ph);
-                tmem_ld16(col + NT + 16 * c, pl);
+                tmem_ld16(col + 16 * c, h);
+                tmem_ld16(col + NT + 16 * c, l);
+                tmem_ld_wait();
+                tmem_regs_ready(h), tmem_regs_ready(l);
+#pragma unroll
+                for (int i = 0; i < 16; i++) pr[i] = h[i] + l[i];
                 if constexpr (Q4) {
-                    float mh[16], ml[16];
-                    tmem_ld16(col + NB + 16 * c, mh);
-                    tmem_ld16(col + NB + NT + 16 * c, ml);
+                    tmem_ld16(col + NB + 16 * c, h);
+                    tmem_ld16(col + NB + NT + 16 * c, l);
                     tmem_ld_wait();
-                    tmem_regs_ready(ph), tmem_regs_ready(pl), tmem_regs_ready(mh), tmem_regs_ready(ml);
+                    tmem_regs_ready(h), tmem_regs_ready(l);
 #pragma unroll
-                    for (int i = 0; i < 16; i++)
-                        acc[16 * c + i] += iv[i] * (dd.x * (ph[i] + pl[i]) - dd.y * (mh[i] + ml[i]));
-                } else {
-                    tmem_ld_wait();
-                    tmem_regs_ready(ph), tmem_regs_ready(pl);
+                    for (int i = 0; i < 16; i++) mn[i] = h[i] + l[i];
+                }
 #pragma unroll
-                    for (int i = 0; i < 16; i++) acc[16 * c + i] += iv[i] * (ph[i] + pl[i]);
+                for (int i = 0; i < 16; i++) {
+                    if constexpr (Q4)
+                        acc[16 * c + i] += iv[i] * (dd.x * pr[i] - dd.y * mn[i]);
+                    else
+                        acc[16 * c + i] += iv[i] * pr[i];
                 }
             }
             tc_fence_before();
@@ -575,7 +598,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32, 1)
         }
     }
     __syncthreads();
-    if (warp == kMmaWarp) {
+    if (warp == W::kMma) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tbase), "r"(kTmemCols)
                      : "memory");
@@ -1394,6 +1417,7 @@ int launch_dq_gemm(lc_ctx *ctx, const lc::PackSrc &src, const lc::ProjOut *outs,
         x16_pack_kernel<lc::LC_PACK_PLAIN><<<pgrid, 256, 0, ctx->stream>>>(src.x, nullptr, 0, (int)m, (int)k, q8, NT,
                                                                           x16, sx16, inv, zl);
     s = lc_set_smem_attr((const void *)dq_gemm_kernel<F, NT>, L.total);
+    constexpr int kThreads = DqWarps<NT>::kAll * 32;
     if (s) return s;
     const long long TS = (long long)tiles * S;
     const int grid = (int)std::max<long long>(1, std::min<long long>(ctx->num_sms, TS));
@@ -1401,7 +1425,7 @@ int launch_dq_gemm(lc_ctx *ctx, const lc::PackSrc &src, const lc::ProjOut *outs,
     // activations are packed
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kGemmWarps * 32);
+    cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = ctx->stream;
     cudaLaunchAttribute attr[1];
