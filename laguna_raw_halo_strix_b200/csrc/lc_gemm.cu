@@ -220,21 +220,16 @@ struct ZeroList {
 //                         of x * s / 32 (hi in row t, lo in row NT + t),
 //                         columns 8..15 zero.
 // x is the projection input, or (OP) the SwiGLU product / the softplus head
-// gate of two inputs, formed here with the element-wise kernels' own functions.
-// The CTAs also zero the outputs in `zl`.
+// gate of two inputs, formed here with the element-wise kernels' own functions,
+// or x RMS-normalised with the weight x2 (x16_pack_norm_kernel, one CTA per
+// token slot: the norm costs no launch of its own).  The CTAs also zero the
+// outputs in `zl`.
+// The packing of one (super-block sb, token slot t) by one warp (lane c);
+// rms is the row's norm factor for LC_PACK_RMSNORM.
 template <int OP>
-__global__ void x16_pack_kernel(const float *__restrict__ x, const float *__restrict__ x2, int head_dim, int m, int k,
-                                int q8, int nt, __half *__restrict__ x16, uint8_t *__restrict__ sx16,
-                                float *__restrict__ inv, const __grid_constant__ ZeroList zl) {
-    griddep_launch_dependents();  // the GEMM may start streaming its weights now
-    const long long nthreads = (long long)gridDim.x * gridDim.y * blockDim.x;
-    const long long tid0 = ((long long)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x;
-    const ZeroList *Z = &zl;
-    for (int z = 0; z < Z->cnt; z++) {
-        float *p = Z->p[z];
-        for (long long i = tid0; i < Z->n[z]; i += nthreads) p[i] = 0.f;
-    }
-    const int sb = blockIdx.x, t = blockIdx.y * 8 + (threadIdx.x >> 5), c = threadIdx.x & 31;
+__device__ __forceinline__ void pack_warp(const float *__restrict__ x, const float *__restrict__ x2, int head_dim,
+                                          float rms, int m, int k, int q8, int nt, __half *__restrict__ x16,
+                                          uint8_t *__restrict__ sx16, float *__restrict__ inv, int sb, int t, int c) {
     int e0, e1;
     if (q8) {
         e0 = 32 * (c >> 2) + 8 * (c & 3);
@@ -260,6 +255,12 @@ __global__ void x16_pack_kernel(const float *__restrict__ x, const float *__rest
             const float gb = lc_softplus_f(gr[(sb * 256 + e1) / head_dim]);
             a = make_float4(a.x * ga, a.y * ga, a.z * ga, a.w * ga);
             b = make_float4(b.x * gb, b.y * gb, b.z * gb, b.w * gb);
+        } else if constexpr (OP == lc::LC_PACK_RMSNORM) {
+            // rmsnorm.comp: (x * w) * rms, rms of the whole row from the caller
+            const float *wr = x2 + (size_t)sb * 256;
+            const float4 wa = *reinterpret_cast<const float4 *>(wr + e0), wb = *reinterpret_cast<const float4 *>(wr + e1);
+            a = make_float4(a.x * wa.x * rms, a.y * wa.y * rms, a.z * wa.z * rms, a.w * wa.w * rms);
+            b = make_float4(b.x * wb.x * rms, b.y * wb.y * rms, b.z * wb.z * rms, b.w * wb.w * rms);
         }
     }
     float mx = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
@@ -298,6 +299,58 @@ __global__ void x16_pack_kernel(const float *__restrict__ x, const float *__rest
         *reinterpret_cast<__half *>(blk + core16_off(t, kk)) = h;
         *reinterpret_cast<__half *>(blk + core16_off(t + nt, kk)) = __float2half_rn(sum - __half2float(h));
     }
+}
+
+__device__ __forceinline__ void zero_outputs(const ZeroList *Z, long long tid0, long long nthreads) {
+    for (int z = 0; z < Z->cnt; z++) {
+        float *p = Z->p[z];
+        for (long long i = tid0; i < Z->n[z]; i += nthreads) p[i] = 0.f;
+    }
+}
+
+template <int OP>
+__global__ void x16_pack_kernel(const float *__restrict__ x, const float *__restrict__ x2, int head_dim, int m, int k,
+                                int q8, int nt, __half *__restrict__ x16, uint8_t *__restrict__ sx16,
+                                float *__restrict__ inv, const __grid_constant__ ZeroList zl) {
+    griddep_launch_dependents();  // the GEMM may start streaming its weights now
+    const long long nthreads = (long long)gridDim.x * gridDim.y * blockDim.x;
+    zero_outputs(&zl, ((long long)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x, nthreads);
+    pack_warp<OP>(x, x2, head_dim, 0.f, m, k, q8, nt, x16, sx16, inv, blockIdx.x, blockIdx.y * 8 + (threadIdx.x >> 5),
+                  threadIdx.x & 31);
+}
+
+// LC_PACK_RMSNORM: CTA t forms token slot t's sum of squares over the row
+// once (rmsnorm.comp: rsqrt(sum / k + eps)), then its warps pack the
+// super-blocks with (x * w) * rms.
+__global__ void x16_pack_norm_kernel(const float *__restrict__ x, const float *__restrict__ w, float eps, int m, int k,
+                                     int q8, int nt, __half *__restrict__ x16, uint8_t *__restrict__ sx16,
+                                     float *__restrict__ inv, const __grid_constant__ ZeroList zl) {
+    griddep_launch_dependents();
+    __shared__ float red[33];
+    zero_outputs(&zl, (long long)blockIdx.x * blockDim.x + threadIdx.x, (long long)gridDim.x * blockDim.x);
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    float ss = 0.f;
+    if (t < m) {
+        const float4 *xr4 = reinterpret_cast<const float4 *>(x + (size_t)t * k);
+        for (int i = threadIdx.x; i < (k >> 2); i += blockDim.x) {
+            const float4 v = xr4[i];
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (warp == 0) {
+        float v = lane < nw ? red[lane] : 0.f;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[32] = v;
+    }
+    __syncthreads();
+    const float rms = rsqrtf(red[32] / (float)k + eps);
+    for (int sb = warp; sb < (k >> 8); sb += nw)
+        pack_warp<lc::LC_PACK_RMSNORM>(x, w, 0, rms, m, k, q8, nt, x16, sx16, inv, sb, t, lane);
 }
 
 struct GemmLayout {
@@ -1413,6 +1466,9 @@ int launch_dq_gemm(lc_ctx *ctx, const lc::PackSrc &src, const lc::ProjOut *outs,
     else if (src.op == lc::LC_PACK_HEADGATE)
         x16_pack_kernel<lc::LC_PACK_HEADGATE><<<pgrid, 256, 0, ctx->stream>>>(src.x, src.x2, src.head_dim, (int)m,
                                                                              (int)k, q8, NT, x16, sx16, inv, zl);
+    else if (src.op == lc::LC_PACK_RMSNORM)
+        x16_pack_norm_kernel<<<NT, 32 * std::min(S, 16u), 0, ctx->stream>>>(src.x, src.x2, src.eps, (int)m, (int)k, q8,
+                                                                           NT, x16, sx16, inv, zl);
     else
         x16_pack_kernel<lc::LC_PACK_PLAIN><<<pgrid, 256, 0, ctx->stream>>>(src.x, nullptr, 0, (int)m, (int)k, q8, NT,
                                                                           x16, sx16, inv, zl);
@@ -1542,7 +1598,8 @@ int gemm_dq_group(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *out
     if (m == 0 || m > 32 || ng < 1 || ng > kGroupMax || k % 256 != 0 || ((uintptr_t)src.x & 15) != 0 ||
         (long long)k * 32 >= (1ll << 31))
         return LC_ERR_UNSUPPORTED;
-    if (src.op == LC_PACK_SWIGLU && ((uintptr_t)src.x2 & 15) != 0) return LC_ERR_UNSUPPORTED;
+    if ((src.op == LC_PACK_SWIGLU || src.op == LC_PACK_RMSNORM) && ((uintptr_t)src.x2 & 15) != 0)
+        return LC_ERR_UNSUPPORTED;
     if (src.op == LC_PACK_HEADGATE && (src.head_dim <= 0 || src.head_dim % 4 != 0 || k % src.head_dim != 0))
         return LC_ERR_UNSUPPORTED;
     long long tiles = 0;

@@ -175,15 +175,18 @@ int gemm_dq(lc_ctx *ctx, int dtype, const float *x, const void *w, float *y, uin
 // inputs applied while packing:
 //   LC_PACK_SWIGLU:   x * sigmoid(x) * x2                (activation.comp)
 //   LC_PACK_HEADGATE: x * softplus(x2[row * k / hd + col / hd])  (softplus, gate_mul.comp)
+//   LC_PACK_RMSNORM:  (x * x2) * rsqrt(mean(x_row^2) + eps), x2 the norm weight
+//                     of length k                           (rmsnorm.comp)
 // Each output is y = src . W^T, or y += src . W^T when `accumulate` (the residual
 // add of the decoder).  LC_ERR_UNSUPPORTED when the shape is not covered.
-enum { LC_PACK_PLAIN = 0, LC_PACK_SWIGLU = 1, LC_PACK_HEADGATE = 2 };
+enum { LC_PACK_PLAIN = 0, LC_PACK_SWIGLU = 1, LC_PACK_HEADGATE = 2, LC_PACK_RMSNORM = 3 };
 constexpr int kGroupMax = 4;
 struct PackSrc {
     const float *x = nullptr;
     const float *x2 = nullptr;
     int op = LC_PACK_PLAIN;
     int head_dim = 0;
+    float eps = 0.f;  // LC_PACK_RMSNORM
 };
 struct ProjOut {
     const void *w = nullptr;

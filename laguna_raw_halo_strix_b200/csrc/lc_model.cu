@@ -140,7 +140,10 @@ int lc::proj_w_block(lc_ctx *c, float *tmp, const PackSrc &src, float *materiali
         if (s != LC_ERR_UNSUPPORTED) return s;
     }
     const float *x = src.x;
-    if (src.op == lc::LC_PACK_SWIGLU) {
+    if (src.op == lc::LC_PACK_RMSNORM) {
+        LC_TRY(lc_rmsnorm(c, src.x2, src.x, materialized, rows, k, src.eps));
+        x = materialized;
+    } else if (src.op == lc::LC_PACK_SWIGLU) {
         LC_TRY(lc_activation(c, src.x, src.x2, materialized, rows * k));
         x = materialized;
     } else if (src.op == lc::LC_PACK_HEADGATE) {
@@ -396,15 +399,19 @@ extern "C" int lc_dflash_decode_block(lc_dflash *m, const float *x_in, uint32_t 
         float *kblk = m->kl(l) + (size_t)pos0 * KVD, *vblk = m->vl(l) + (size_t)pos0 * KVD;
         // src/dflash.rs:938-943 (+ the head-gate projection of :955, which reads
         // the same normalised block): one activation block, four projections
-        LC_TRY(lc_rmsnorm(c, an, m->x, m->nx, mt, E, h.norm_eps));
+        // attn_norm is formed while the block is packed (m->nx only on the
+        // per-projection route)
         {
             lc::PackSrc src;
-            src.x = m->nx;
+            src.x = m->x;
+            src.x2 = an;
+            src.op = lc::LC_PACK_RMSNORM;
+            src.eps = h.norm_eps;
             lc::ProjOut outs[4] = {{nullptr, m->q, QD, false}, {nullptr, kblk, KVD, false},
                                    {nullptr, vblk, KVD, false}, {nullptr, m->gate, h.n_heads, false}};
             const Weight *ws[4] = {&L.q, &L.k, &L.v, &L.gate_attn};
             const char *names[4] = {"attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_gate.weight"};
-            LC_TRY(proj_block(m, src, nullptr, outs, ws, names, 4, mt, E));
+            LC_TRY(proj_block(m, src, m->nx, outs, ws, names, 4, mt, E));
         }
         LC_TRY(lc::qk_norm_rope_pair(c, m->q, qn, m->q, h.n_heads, kblk, kn, kblk, h.n_kv_heads, m->freq, mt,
                                      h.head_dim, h.rope_dim, h.qk_eps, pos0));
@@ -423,14 +430,16 @@ extern "C" int lc_dflash_decode_block(lc_dflash *m, const float *x_in, uint32_t 
             const char *names[1] = {"attn_output.weight"};
             LC_TRY(proj_block(m, src, m->attn, outs, ws, names, 1, mt, QD));
         }
-        LC_TRY(lc_rmsnorm(c, fn, m->x, m->nx, mt, E, h.norm_eps));
-        {
+        {  // ffn_norm, likewise
             lc::PackSrc src;
-            src.x = m->nx;
+            src.x = m->x;
+            src.x2 = fn;
+            src.op = lc::LC_PACK_RMSNORM;
+            src.eps = h.norm_eps;
             lc::ProjOut outs[2] = {{nullptr, m->ffg, F, false}, {nullptr, m->ffu, F, false}};
             const Weight *ws[2] = {&L.gate, &L.up};
             const char *names[2] = {"ffn_gate.weight", "ffn_up.weight"};
-            LC_TRY(proj_block(m, src, nullptr, outs, ws, names, 2, mt, E));
+            LC_TRY(proj_block(m, src, m->nx, outs, ws, names, 2, mt, E));
         }
         {
             lc::PackSrc src;

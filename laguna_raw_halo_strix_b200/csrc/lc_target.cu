@@ -934,19 +934,23 @@ extern "C" int lc_target_forward(lc_target *t, const float *x_in, uint32_t m, ui
         const float *fn = need_f32(L.ffn_norm, "ffn_norm.weight", E, &s);
         if (s) return s;
         // src/target.rs:414-438: norm, then q / k / v (and the head gate of
-        // :497-503, which reads the same normalised rows) from one block
-        LC_TRY(lc_rmsnorm(c, an, t->x, t->nx, m, E, h.norm_eps));
+        // :497-503, which reads the same normalised rows) from one block; the
+        // norm is formed while the block is packed (t->nx only on the
+        // per-projection route)
         float *kd = cached ? t->kl(l) + (size_t)pos0 * KVD : t->kbuf;
         float *vd = cached ? t->vl(l) + (size_t)pos0 * KVD : t->vbuf;
         const bool gated = L.gate_attn.ptr != nullptr;
         {
             lc::PackSrc src;
-            src.x = t->nx;
+            src.x = t->x;
+            src.x2 = an;
+            src.op = lc::LC_PACK_RMSNORM;
+            src.eps = h.norm_eps;
             lc::ProjOut outs[4] = {{nullptr, t->q, QD, false}, {nullptr, kd, KVD, false}, {nullptr, vd, KVD, false},
                                    {nullptr, t->gate, H, false}};
             const DevTensor *ws[4] = {&L.q, &L.k, &L.v, &L.gate_attn};
             const char *names[4] = {"attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_gate.weight"};
-            LC_TRY(lc::proj_w_block(c, t->tmp, src, nullptr, outs, ws, names, gated ? 4 : 3, m, E));
+            LC_TRY(lc::proj_w_block(c, t->tmp, src, t->nx, outs, ws, names, gated ? 4 : 3, m, E));
         }
         // :440-463 -- SWA layers rotate with their own dimension and base
         const bool swa = h.swa && (l % 4 != 0);
@@ -975,22 +979,25 @@ extern "C" int lc_target_forward(lc_target *t, const float *x_in, uint32_t m, ui
             const char *names[1] = {"attn_output.weight"};
             LC_TRY(lc::proj_w_block(c, t->tmp, src, t->attn, outs, ws, names, 1, m, QD));
         }
-        LC_TRY(lc_rmsnorm(c, fn, t->x, t->nx, m, E, h.norm_eps));
         if (L.is_moe) {
             // :520-524
+            LC_TRY(lc_rmsnorm(c, fn, t->x, t->nx, m, E, h.norm_eps));
             LC_TRY(moe_ffn(t, l, t->nx, m, t->moe_y));
             LC_TRY(lc_add(c, t->x, t->moe_y, t->x, m * E));
         } else {
             // :526-546
             const uint32_t F = h.n_ff;
             LC_REQUIRE(F > 0, LC_ERR_INVALID, "lc_target_forward: dense layer %u without feed_forward_length", l);
-            {
+            {  // ffn_norm formed while packing
                 lc::PackSrc src;
-                src.x = t->nx;
+                src.x = t->x;
+                src.x2 = fn;
+                src.op = lc::LC_PACK_RMSNORM;
+                src.eps = h.norm_eps;
                 lc::ProjOut outs[2] = {{nullptr, t->ffg, F, false}, {nullptr, t->ffu, F, false}};
                 const DevTensor *ws[2] = {&L.gate, &L.up};
                 const char *names[2] = {"ffn_gate.weight", "ffn_up.weight"};
-                LC_TRY(lc::proj_w_block(c, t->tmp, src, nullptr, outs, ws, names, 2, m, E));
+                LC_TRY(lc::proj_w_block(c, t->tmp, src, t->nx, outs, ws, names, 2, m, E));
             }
             {
                 lc::PackSrc src;
