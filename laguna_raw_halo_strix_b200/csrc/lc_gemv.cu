@@ -50,7 +50,6 @@
 namespace {
 
 constexpr int kGvMaxWarps = 16;  // warps per CTA
-constexpr int kGvQuad = 4;       // rows reduced together
 
 // Launch arguments (a __grid_constant__ parameter block).  Up to lc::kGroupMax
 // matrices of one format and one k share the activations: their rows form one
@@ -453,28 +452,6 @@ struct Q8Lane {
 
 
 // ---------------------------------------------------------------------------
-// Sum the partials p[0..3][j] of the 32 lanes: afterwards lane l holds, for
-// each token j, the total of row (l >> 3) (rows 2 bit4 + bit3) in p[0][j].
-template <int M>
-__device__ __forceinline__ void reduce4(float (&p)[kGvQuad][M], int lane) {
-#pragma unroll
-    for (int j = 0; j < M; j++) {
-        const bool b4 = lane & 16, b3 = lane & 8;
-        // xor 16: keep rows {0,1} (bit4 = 0) or {2,3}
-        float k0 = b4 ? p[2][j] : p[0][j], k1 = b4 ? p[3][j] : p[1][j];
-        float s0 = b4 ? p[0][j] : p[2][j], s1 = b4 ? p[1][j] : p[3][j];
-        k0 += __shfl_xor_sync(0xffffffffu, s0, 16);
-        k1 += __shfl_xor_sync(0xffffffffu, s1, 16);
-        // xor 8: keep row 2 bit4 + bit3
-        float k = b3 ? k1 : k0, s = b3 ? k0 : k1;
-        k += __shfl_xor_sync(0xffffffffu, s, 8);
-        k += __shfl_xor_sync(0xffffffffu, k, 4);
-        k += __shfl_xor_sync(0xffffffffu, k, 2);
-        k += __shfl_xor_sync(0xffffffffu, k, 1);
-        p[0][j] = k;
-    }
-}
-
 // Warp-cooperative copy of the warp's slice of a row (nb <= NB bytes, a
 // multiple of 16) into `slot`: lane l copies 16-byte chunks l, l + 32, ...
 // (a fixed number of predicated copies: no loop).
@@ -583,37 +560,34 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, 1) gemv_rows_kernel(const __
     }
 
     const uint32_t ref_mask = a.half_mode == LC_HALF_REF ? 0x04000400u : 0u;
-    for (int i0 = 0; i0 < nmy; i0 += kGvQuad) {
-        float p[kGvQuad][M];
+    // One row at a time: a loop body of one row keeps the kernel's hot code
+    // small (four rows per iteration with a shared reduction ran slower, most
+    // of all for Q8_0).
+    for (int i = 0; i < nmy; i++) {
+        // Row i has landed for this lane once at most D - 2 newer groups are
+        // pending (groups 0..i+D-2 were committed before this point); the warp
+        // barrier makes every lane's copies visible and also means every lane
+        // is done with row i - 1.
+        cp_async_wait<D - 2>();
+        __syncwarp();
+        // refill row i - 1's buffer with row i - 1 + D
+        if (i > 0 && i - 1 + D < nmy)
+            gv_copy_slice<L::SLICE>(slice_ptr(i - 1 + D), ring + ((unsigned)(i - 1) & (D - 1)) * L::SLICE, sbytes, lane);
+        if (i > 0) cp_async_commit();
+        typename L::Bytes bt;
+        ln.fetch(ring + ((unsigned)i & (D - 1)) * L::SLICE, bt);
+        float o[M];
+        ln.row(bt, ref_mask, o);
 #pragma unroll
-        for (int q = 0; q < kGvQuad; q++) {
-            const int i = i0 + q;
-            // Row i has landed for this lane once at most D - 2 newer groups
-            // are pending (groups 0..i+D-2 were committed before this point);
-            // the warp barrier makes every lane's copies visible and also
-            // means every lane is done with row i - 1.
-            cp_async_wait<D - 2>();
-            __syncwarp();
-            // refill row i - 1's buffer with row i - 1 + D
-            if (i > 0 && i - 1 + D < nmy)
-                gv_copy_slice<L::SLICE>(slice_ptr(i - 1 + D), ring + ((unsigned)(i - 1) & (D - 1)) * L::SLICE, sbytes,
-                                        lane);
-            if (i > 0) cp_async_commit();
-            typename L::Bytes bt;
-            ln.fetch(ring + ((unsigned)i & (D - 1)) * L::SLICE, bt);
-            float o[M];
-            ln.row(bt, ref_mask, o);
+        for (int j = 0; j < M; j++)
 #pragma unroll
-            for (int j = 0; j < M; j++) p[q][j] = i < nmy ? o[j] : 0.f;
-        }
-        reduce4<M>(p, lane);
-        // this k-slice's sums of the quad's rows, by row of the CTA's range;
-        // no barrier: the k-slices meet once, after the last row
-        const int q = lane >> 3, i = i0 + q;
-        if ((lane & 7) == 0 && i < nmy) {
+            for (int off = 16; off; off >>= 1) o[j] += __shfl_xor_sync(0xffffffffu, o[j], off);
+        // this k-slice's sum of the row, by row of the CTA's range; no
+        // barrier: the k-slices meet once, after the last row
+        if (lane == 0) {
             const int lr = rgi + i * a.rg;
 #pragma unroll
-            for (int j = 0; j < M; j++) part[((size_t)lr * a.ks + slice) * M + j] = p[0][j];
+            for (int j = 0; j < M; j++) part[((size_t)lr * a.ks + slice) * M + j] = o[j];
         }
     }
     cp_async_wait_all();
