@@ -198,6 +198,20 @@ class ClockSampler:
     def mark_begin(self):
         self.t_begin = time.perf_counter()
 
+    def sample_now(self):
+        """One sample from the calling thread, taken after the timed work is
+        enqueued and before the host waits for it, so that even a timed region
+        shorter than the polling period holds a sample."""
+        if self.handle is None:
+            return
+        nv = self.nv
+        try:
+            sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+            rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+            self.samples.append((time.perf_counter(), sm, rs))
+        except Exception:
+            pass
+
     def mark_end(self):
         self.t_end = time.perf_counter()
 
@@ -460,6 +474,8 @@ def _timed_graph(g, stream, dev, world, rank):
     e0.record(stream)
     g.replay()
     e1.record(stream)
+    if sampler:
+        sampler.sample_now()
     stream.synchronize()
     if sampler:
         sampler.mark_end()
@@ -724,6 +740,8 @@ def run_lm_head(args):
         for i in range(args.steps):
             step(args.warmup + i)
         e1.record(stream)
+        if sampler:
+            sampler.sample_now()
         stream.synchronize()
         if sampler:
             sampler.mark_end()
