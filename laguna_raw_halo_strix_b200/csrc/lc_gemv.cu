@@ -64,6 +64,8 @@ struct GvArgs {
     int k, row_bytes;
     int ks, rg;  // k-slices (warps per row group), row groups
     int part_rows;  // rows of a CTA's range the partial-sum array holds (>= every range)
+    int pairs;      // two matrices of n rows interleaved (row 2i of matrix 0, 2i + 1 of matrix 1):
+                    // y[0] [M][n] receives SiLU(matrix 0 row) * (matrix 1 row), activation.comp
     int half_mode;
     unsigned *status;
 };
@@ -89,6 +91,11 @@ __host__ __device__ __forceinline__ GvLayout gv_layout(int warps, int depth, int
 
 // Virtual row r of the launch -> matrix g and the row within it.
 __device__ __forceinline__ void gv_row(const GvArgs &a, int r, int &g, int &i) {
+    if (a.pairs) {
+        g = r & 1;
+        i = r >> 1;
+        return;
+    }
     g = 0;
     while (g < a.ng - 1 && r >= a.rows_end[g]) g++;
     i = r - (g ? a.rows_end[g - 1] : 0);
@@ -512,8 +519,10 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, 1) gemv_rows_kernel(const __
     };
     x_load((int)threadIdx.x);
     const int total = a.rows_end[a.ng - 1];
-    const int r0 = (int)((long long)total * blockIdx.x / gridDim.x);
-    const int r1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+    // (interleaved pairs stay in one CTA: even range bounds)
+    const int pmask = a.pairs ? ~1 : ~0;
+    const int r0 = (int)((long long)total * blockIdx.x / gridDim.x) & pmask;
+    const int r1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x) & pmask;
     const int nmy = r1 - r0 > rgi ? (r1 - r0 - rgi + a.rg - 1) / a.rg : 0;  // rows r0 + rgi + i * rg
     // this warp's bytes of a row: the slice (the last one may be shorter)
     const int sbytes = min(L::SLICE, a.row_bytes - slice * L::SLICE);
@@ -594,6 +603,19 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, 1) gemv_rows_kernel(const __
     __syncthreads();
     // every row of the range: its k-slices added in slice order
     const int nrows = r1 - r0;
+    if (a.pairs) {  // SiLU(gate) * up of each pair, one output
+        const int n = a.rows_end[0];
+        for (int t = threadIdx.x; t < (nrows >> 1) * M; t += blockDim.x) {
+            const int lp = t / M, j = t - lp * M, lr = 2 * lp;
+            float vg = 0.f, vu = 0.f;
+            for (int sl = 0; sl < a.ks; sl++) {
+                vg += part[((size_t)lr * a.ks + sl) * M + j];
+                vu += part[((size_t)(lr + 1) * a.ks + sl) * M + j];
+            }
+            a.y[0][(size_t)j * n + ((r0 + lr) >> 1)] = lc_swiglu(vg, vu);
+        }
+        return;
+    }
     for (int t = threadIdx.x; t < nrows * M; t += blockDim.x) {
         const int lr = t / M, j = t - lr * M;
         float v = 0.f;
@@ -663,14 +685,33 @@ bool gemv_rows_covers(const lc_ctx *ctx, int dtype, uint32_t m, uint32_t k) {
     return false;
 }
 
-int gemv_rows(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *outs, int ng, uint32_t m, uint32_t k) {
-    LC_REQUIRE(ng >= 1 && ng <= kGroupMax, LC_ERR_INVALID, "gemv_rows: %d matrices", ng);
+static int gv_run(lc_ctx *ctx, int dtype, const PackSrc &src, uint32_t m, uint32_t k, long long rows, GvArgs &a) {
+    if (rows == 0) return LC_OK;
+    a.x = src.x;
+    a.x2 = src.op == LC_PACK_SWIGLU ? src.x2 : nullptr;
+    a.k = (int)k;
+    a.row_bytes = dtype == LC_Q4_K ? (int)(k / 256) * 144 : (int)(k / 32) * 34;
+    a.half_mode = ctx->half_mode;
+    a.status = ctx->dev_status;
+    const GvPlan p = gv_plan(ctx, dtype, (int)m, (int)k, (int)rows);
+    LC_REQUIRE(p.ks, LC_ERR_UNSUPPORTED, "gemv_rows: rows of %d bytes do not fit shared memory", a.row_bytes);
+    if (dtype == LC_Q8_0) return gv_launch<Q8Lane, 1>(ctx, p, a);
+    if (m == 1) return gv_launch<Q4Lane<1>, 1>(ctx, p, a);
+    return gv_launch<Q4Lane<2>, 2>(ctx, p, a);
+}
+
+static int gv_check(lc_ctx *ctx, int dtype, const PackSrc &src, uint32_t m, uint32_t k) {
     LC_REQUIRE(gemv_rows_covers(ctx, dtype, m, k), LC_ERR_UNSUPPORTED, "gemv_rows: dtype %d m=%u k=%u", dtype, m, k);
     LC_REQUIRE(src.op == LC_PACK_PLAIN || src.op == LC_PACK_SWIGLU, LC_ERR_UNSUPPORTED, "gemv_rows: packing op %d",
                src.op);
     LC_REQUIRE(((uintptr_t)src.x & 15) == 0 && ((uintptr_t)src.x2 & 15) == 0, LC_ERR_UNSUPPORTED,
                "gemv_rows: activations not 16-byte aligned");
-    const int row_bytes = dtype == LC_Q4_K ? (int)(k / 256) * 144 : (int)(k / 32) * 34;
+    return LC_OK;
+}
+
+int gemv_rows(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *outs, int ng, uint32_t m, uint32_t k) {
+    LC_REQUIRE(ng >= 1 && ng <= kGroupMax, LC_ERR_INVALID, "gemv_rows: %d matrices", ng);
+    if (int s = gv_check(ctx, dtype, src, m, k)) return s;
     GvArgs a = {};
     long long rows = 0;
     for (int g = 0; g < ng; g++) {
@@ -682,19 +723,23 @@ int gemv_rows(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *outs, i
         a.y[g] = outs[g].y;
         a.rows_end[g] = (int)rows;
     }
-    if (rows == 0) return LC_OK;
     a.ng = ng;
-    a.x = src.x;
-    a.x2 = src.op == LC_PACK_SWIGLU ? src.x2 : nullptr;
-    a.k = (int)k;
-    a.row_bytes = row_bytes;
-    a.half_mode = ctx->half_mode;
-    a.status = ctx->dev_status;
-    const GvPlan p = gv_plan(ctx, dtype, (int)m, (int)k, (int)rows);
-    LC_REQUIRE(p.ks, LC_ERR_UNSUPPORTED, "gemv_rows: rows of %d bytes do not fit shared memory", row_bytes);
-    if (dtype == LC_Q8_0) return gv_launch<Q8Lane, 1>(ctx, p, a);
-    if (m == 1) return gv_launch<Q4Lane<1>, 1>(ctx, p, a);
-    return gv_launch<Q4Lane<2>, 2>(ctx, p, a);
+    return gv_run(ctx, dtype, src, m, k, rows, a);
+}
+
+int gemv_rows_swiglu(lc_ctx *ctx, int dtype, const PackSrc &src, const void *w_gate, const void *w_up, float *h,
+                     uint32_t m, uint32_t k, uint32_t n) {
+    if (int s = gv_check(ctx, dtype, src, m, k)) return s;
+    LC_REQUIRE((((uintptr_t)w_gate | (uintptr_t)w_up) & 15) == 0, LC_ERR_UNSUPPORTED,
+               "gemv_rows: weights not 16-byte aligned");
+    LC_REQUIRE(2ll * n < (1ll << 30), LC_ERR_INVALID, "gemv_rows: too many rows");
+    GvArgs a = {};
+    a.w[0] = (const uint8_t *)w_gate, a.w[1] = (const uint8_t *)w_up;
+    a.y[0] = a.y[1] = h;
+    a.rows_end[0] = (int)n, a.rows_end[1] = (int)(2 * n);
+    a.ng = 2;
+    a.pairs = 1;
+    return gv_run(ctx, dtype, src, m, k, 2ll * n, a);
 }
 
 }  // namespace lc
@@ -702,10 +747,10 @@ int gemv_rows(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *outs, i
 // ---------------------------------------------------------------------------
 // C ABI: the FFN block of the DFlash decoder layer (src/dflash.rs:965-968):
 // y = down(SiLU(gate(x)) * up(x)) for m rows of x [m, n_embd].  One or two
-// tokens run as two launches: gate and up in one grouped GEMV over x, then
-// down with SiLU(gate) * up formed while its activations load; 5..32 tokens
-// the same on the grouped tcgen05 GEMM; other m the projections and the
-// activation kernel one by one.
+// tokens run as two launches: gate and up rows interleaved in one GEMV over x,
+// each pair's SiLU(gate) * up formed once where its sums meet, then down;
+// 5..32 tokens gate and up on the grouped tcgen05 GEMM, SiLU-gate formed while
+// down packs; other m the projections and the activation kernel one by one.
 
 extern "C" int lc_ffn(lc_ctx *ctx, int dtype, const float *x, const void *w_gate, const void *w_up,
                       const void *w_down, float *y, uint32_t m, uint32_t n_embd, uint32_t n_ff) {
@@ -726,21 +771,20 @@ extern "C" int lc_ffn(lc_ctx *ctx, int dtype, const float *x, const void *w_gate
     if (lc::gemv_rows_covers(ctx, dtype, m, n_embd) && lc::gemv_rows_covers(ctx, dtype, m, n_ff)) {
         lc::PackSrc src;
         src.x = x;
-        lc::ProjOut o[2];
-        o[0].w = w_gate, o[0].y = g, o[0].n = n_ff;
-        o[1].w = w_up, o[1].y = u, o[1].n = n_ff;
-        s = lc::gemv_rows(ctx, dtype, src, o, 2, m, n_embd);
+        // gate and up rows interleaved in one launch; each pair's SiLU(gate) * up
+        // is formed once, at the end of its CTA, into g
+        s = lc::gemv_rows_swiglu(ctx, dtype, src, w_gate, w_up, g, m, n_embd, n_ff);
         if (s == LC_OK) {
             lc::PackSrc hs;
-            hs.x = g, hs.x2 = u, hs.op = lc::LC_PACK_SWIGLU;
+            hs.x = g;
             lc::ProjOut d;
             d.w = w_down, d.y = y, d.n = n_embd;
             s = lc::gemv_rows(ctx, dtype, hs, &d, 1, m, n_ff);
             if (s == LC_OK) return lc_after_launch(ctx, "lc_ffn");
             if (s != LC_ERR_UNSUPPORTED) return s;
-            // both activation inputs do not fit the CTA's shared memory: the
-            // activation kernel forms SiLU(gate) * up first
-            if ((s = lc_activation(ctx, g, u, g, m * n_ff)) || (s = proj(g, w_down, y, n_ff, n_embd))) return s;
+            // the down projection's activations do not fit the CTA's shared
+            // memory: its own projection route
+            if ((s = proj(g, w_down, y, n_ff, n_embd))) return s;
             return lc_after_launch(ctx, "lc_ffn");
         }
         if (s != LC_ERR_UNSUPPORTED) return s;

@@ -206,6 +206,10 @@ int qk_norm_rope_pair(lc_ctx *ctx, const float *xa, const float *wa, float *ya, 
 // once.  LC_ERR_UNSUPPORTED when the shape is not covered (gemv_rows_covers).
 bool gemv_rows_covers(const lc_ctx *ctx, int dtype, uint32_t m, uint32_t k);
 int gemv_rows(lc_ctx *ctx, int dtype, const PackSrc &src, const ProjOut *outs, int ng, uint32_t m, uint32_t k);
+// gate and up (n rows each) of one FFN in one gemv_rows launch, rows
+// interleaved; h [m][n] = SiLU(x . gate^T) * (x . up^T) (activation.comp).
+int gemv_rows_swiglu(lc_ctx *ctx, int dtype, const PackSrc &src, const void *w_gate, const void *w_up, float *h,
+                     uint32_t m, uint32_t k, uint32_t n);
 // lc_dequant, or with bf16_native a BF16 tensor decoded as bfloat16 (f32 =
 // bits << 16) instead of the reference's f16 reading (lc_ops.cu).
 int dequant_f32(lc_ctx *ctx, int dtype, const void *src, size_t src_bytes, size_t n, float *out, bool bf16_native);
