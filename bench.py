@@ -587,22 +587,27 @@ def run_projection(args, name):
         del g_steps, g_dom
 
         # e2e: the input copied from pinned host memory and the result read back
-        # every step, eager calls through the C ABI, one host sync per step
+        # every step by the host-buffer entry points (lc_ffn_host /
+        # lc_proj_m_host: upload, compute, read back and wait in one C-ABI call)
         x_host = torch.from_numpy(synth.activations(m, k0, rng)).pin_memory()
-        y_host = torch.empty(bufs[out_name].shape, dtype=torch.float32).pin_memory()
+        y_host = {nm: torch.empty((m, n), dtype=torch.float32).pin_memory() for nm, k, n in wl["shapes"]}
         e2e_steps = max(10, args.steps // 2)
+
+        def host_step(i):
+            ws = weights[i % pool]
+            if wl["ffn"]:
+                (_, kg, ng), _, (dn_name, kd, nd) = wl["shapes"]
+                ctx.ffn_host(dtype, x_host, ws["gate"], ws["up"], ws["down"], y_host[dn_name], m, kg, ng)
+            else:
+                for nm, k, n in wl["shapes"]:
+                    ctx.proj_m_host(dtype, x_host, ws[nm], y_host[nm], m, k, n)
+
         for i in range(3):
-            x.copy_(x_host, non_blocking=True)
-            step(i)
-            y_host.copy_(bufs[out_name], non_blocking=True)
-            stream.synchronize()
+            host_step(i)
         _barrier(world)
         t0 = time.perf_counter()
         for i in range(e2e_steps):
-            x.copy_(x_host, non_blocking=True)
-            step(i)
-            y_host.copy_(bufs[out_name], non_blocking=True)
-            stream.synchronize()
+            host_step(i)
         e2e_s = _max_over_ranks(time.perf_counter() - t0, dev, world)
 
     sb = step_bytes(wl)
@@ -633,8 +638,11 @@ def run_projection(args, name):
                                      f"({dpool * dbytes / 1e6:.0f} MB, > 3x L2)",
                          "per_launch_us": per_launch_ms * 1e3, "bytes_per_launch": lb},
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": int(x_host.numel() * 4),
-                    "d2h_bytes_per_step": int(y_host.numel() * 4), "steps": e2e_steps},
+            "e2e": {"value": e2e_value, "unit": "GB/s",
+                    "h2d_bytes_per_step": int(x_host.numel() * 4) * (1 if wl["ffn"] else len(wl["shapes"])),
+                    "d2h_bytes_per_step": int(y_host[out_name].numel() * 4) if wl["ffn"] else
+                    int(sum(t.numel() for t in y_host.values()) * 4),
+                    "steps": e2e_steps, "call": "lc_ffn_host" if wl["ffn"] else "lc_proj_m_host"},
             "clocks": clocks, "gpu_launches": None if launches is None else launches,
         })
     ctx.close()

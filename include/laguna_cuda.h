@@ -174,6 +174,18 @@ int lc_proj_q4k_static(lc_ctx *ctx, const float *x, const void *w, float *c,
 int lc_ffn(lc_ctx *ctx, int dtype, const float *x, const void *w_gate, const void *w_up, const void *w_down,
            float *y, uint32_t m, uint32_t n_embd, uint32_t n_ff);
 
+/* Host-buffer forms, the reference's upload -> dispatch -> read_f32 sequence
+ * (GpuBuffer::upload src/vulkan.rs:400-430, dispatch_proj* src/dflash.rs:
+ * 1009-1090, GpuBuffer::read_f32 src/vulkan.rs:432-452) in one call: x_host is
+ * copied into the context's scratch, the computation runs, the result is
+ * copied into y_host / c_host, and the call returns once it is there.  Host
+ * buffers in page-locked memory make both copies asynchronous DMA.  Weights
+ * stay device pointers. */
+int lc_ffn_host(lc_ctx *ctx, int dtype, const float *x_host, const void *w_gate, const void *w_up,
+                const void *w_down, float *y_host, uint32_t m, uint32_t n_embd, uint32_t n_ff);
+int lc_proj_m_host(lc_ctx *ctx, int dtype, const float *x_host, const void *w, float *c_host, uint32_t m, uint32_t k,
+                   uint32_t n, uint32_t expert_offset);
+
 /* ---- dequant ------------------------------------------------------------- */
 
 /* dequant_to_f32 (src/dflash.rs:331-465) on the device.  LC_Q8_0 / LC_F16 /

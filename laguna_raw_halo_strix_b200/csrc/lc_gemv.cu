@@ -813,3 +813,55 @@ extern "C" int lc_ffn(lc_ctx *ctx, int dtype, const float *x, const void *w_gate
     if ((s = proj(g, w_down, y, n_ff, n_embd))) return s;
     return lc_after_launch(ctx, "lc_ffn");
 }
+
+// ---------------------------------------------------------------------------
+// Host-buffer forms: one call per step for a host that holds its inputs and
+// outputs in host memory.
+
+namespace {
+
+// Device staging for x [m, k_in] and the result [m, n_out] in the context's
+// scratch (256-byte aligned halves).
+int host_io(lc_ctx *ctx, size_t x_floats, size_t y_floats, float **xd, float **yd) {
+    const size_t xb = (x_floats * 4 + 255) & ~(size_t)255;
+    char *p = (char *)lc_scratch(ctx, LC_SCRATCH_HOSTIO, xb + y_floats * 4 + 256);
+    if (!p) return LC_ERR_OOM;
+    *xd = (float *)p;
+    *yd = (float *)(p + xb);
+    return LC_OK;
+}
+
+}  // namespace
+
+extern "C" int lc_ffn_host(lc_ctx *ctx, int dtype, const float *x_host, const void *w_gate, const void *w_up,
+                           const void *w_down, float *y_host, uint32_t m, uint32_t n_embd, uint32_t n_ff) {
+    LC_REQUIRE(ctx, LC_ERR_INVALID, "lc_ffn_host: null ctx");
+    if (m == 0 || n_embd == 0) return LC_OK;
+    LC_REQUIRE(x_host && y_host, LC_ERR_INVALID, "lc_ffn_host: null host buffer");
+    int s = lc_use_device(ctx);
+    if (s) return s;
+    float *xd, *yd;
+    if ((s = host_io(ctx, (size_t)m * n_embd, (size_t)m * n_embd, &xd, &yd))) return s;
+    const size_t bytes = (size_t)m * n_embd * 4;
+    LC_CUDA(cudaMemcpyAsync(xd, x_host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    if ((s = lc_ffn(ctx, dtype, xd, w_gate, w_up, w_down, yd, m, n_embd, n_ff))) return s;
+    LC_CUDA(cudaMemcpyAsync(y_host, yd, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    LC_CUDA(cudaStreamSynchronize(ctx->stream));
+    return lc_after_launch(ctx, "lc_ffn_host");
+}
+
+extern "C" int lc_proj_m_host(lc_ctx *ctx, int dtype, const float *x_host, const void *w, float *c_host, uint32_t m,
+                              uint32_t k, uint32_t n, uint32_t expert_offset) {
+    LC_REQUIRE(ctx, LC_ERR_INVALID, "lc_proj_m_host: null ctx");
+    if (m == 0 || n == 0) return LC_OK;
+    LC_REQUIRE(x_host && c_host, LC_ERR_INVALID, "lc_proj_m_host: null host buffer");
+    int s = lc_use_device(ctx);
+    if (s) return s;
+    float *xd, *yd;
+    if ((s = host_io(ctx, (size_t)m * k, (size_t)m * n, &xd, &yd))) return s;
+    LC_CUDA(cudaMemcpyAsync(xd, x_host, (size_t)m * k * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if ((s = lc_proj_m(ctx, dtype, xd, w, yd, m, k, n, expert_offset))) return s;
+    LC_CUDA(cudaMemcpyAsync(c_host, yd, (size_t)m * n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    LC_CUDA(cudaStreamSynchronize(ctx->stream));
+    return lc_after_launch(ctx, "lc_proj_m_host");
+}

@@ -62,6 +62,7 @@ enum {
     LC_SCRATCH_ATTN = 3,
     LC_SCRATCH_FIXUP = 4,
     LC_SCRATCH_FFN = 5,
+    LC_SCRATCH_HOSTIO = 6,
     LC_SCRATCH_COUNT = 8
 };
 // Grow-only scratch slot of at least `bytes` (256-byte aligned).  Returns

@@ -88,6 +88,8 @@ SIGNATURES = {
     "lc_proj_m": (_i, [_vp, _i, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
     "lc_proj_q4k_static": (_i, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
     "lc_ffn": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32]),
+    "lc_ffn_host": (_i, [_vp, _i, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32]),
+    "lc_proj_m_host": (_i, [_vp, _i, _vp, _vp, _vp, _u32, _u32, _u32, _u32]),
     "lc_comm_unique_id": (_i, [_vp]),
     "lc_comm_init": (_i, [_vp, _vp, _i, _i, _i, C.POINTER(_vp)]),
     "lc_comm_destroy": (_i, [_vp]),
@@ -322,6 +324,16 @@ class Context:
     def ffn(self, dtype, x, w_gate, w_up, w_down, y, m, n_embd, n_ff):
         check(self.L.lc_ffn(self.h, dtype, ptr(x), ptr(w_gate), ptr(w_up), ptr(w_down), ptr(y), m, n_embd, n_ff),
               "lc_ffn")
+
+    def ffn_host(self, dtype, x_host, w_gate, w_up, w_down, y_host, m, n_embd, n_ff):
+        """lc_ffn_host: x_host / y_host are host buffers (page-locked for
+        asynchronous copies); returns once y_host holds the result."""
+        check(self.L.lc_ffn_host(self.h, dtype, ptr(x_host), ptr(w_gate), ptr(w_up), ptr(w_down), ptr(y_host), m,
+                                 n_embd, n_ff), "lc_ffn_host")
+
+    def proj_m_host(self, dtype, x_host, w, c_host, m, k, n, expert_offset=0):
+        check(self.L.lc_proj_m_host(self.h, dtype, ptr(x_host), ptr(w), ptr(c_host), m, k, n, expert_offset),
+              "lc_proj_m_host")
 
     def dequant(self, dtype, src, src_bytes, n, out):
         check(self.L.lc_dequant(self.h, dtype, ptr(src), src_bytes, n, ptr(out)), "lc_dequant")

@@ -152,3 +152,36 @@ def test_ffn_block(ctx, dev, oracle, dtype, m):
         check_tol(got[j], ref, 1e-3, f"ffn dtype {dtype} token {j}")
         if m <= 2:
             check_tol(got[j], ref, F32_TOL, f"ffn dtype {dtype} token {j} (f32)")
+
+
+@pytest.mark.parametrize("dtype,m", [(orc.Q4_K, 1), (orc.Q8_0, 1), (orc.Q4_K, 16)])
+def test_host_buffer_calls(ctx, dev, dtype, m):
+    """lc_ffn_host / lc_proj_m_host (upload, compute, read back in one call)
+    return what the device-pointer calls leave on the device: bit for bit at
+    one token (fixed summation order), within f32 rounding at 16 (the tcgen05
+    GEMM adds its split sums with atomics, in no fixed order)."""
+    import torch
+
+    def same(a, b):
+        if m == 1:
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+        else:
+            check_tol(a, b, 1e-5, "host-buffer call")
+
+    rng = np.random.default_rng(40 + m)
+    E, F = 4096, 14336
+    wg, wu, wd = (to_dev(synth.weight_blocks(dtype, r, c, rng), dev) for r, c in ((F, E), (F, E), (E, F)))
+    x = synth.activations(m, E, rng)
+    x_host = torch.from_numpy(x).pin_memory()
+    y_host = torch.full((m, E), float("nan")).pin_memory()
+    ctx.ffn_host(dtype, x_host, wg, wu, wd, y_host, m, E, F)
+    y = torch.full((m, E), float("nan"), device=dev)
+    ctx.ffn(dtype, to_dev(x, dev), wg, wu, wd, y, m, E, F)
+    torch.cuda.synchronize()
+    same(y_host.numpy(), y.cpu().numpy())
+    c_host = torch.full((m, F), float("nan")).pin_memory()
+    ctx.proj_m_host(dtype, x_host, wg, c_host, m, E, F)
+    c = torch.full((m, F), float("nan"), device=dev)
+    ctx.proj_m(dtype, to_dev(x, dev), wg, c, m, E, F)
+    torch.cuda.synchronize()
+    same(c_host.numpy(), c.cpu().numpy())
