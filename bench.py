@@ -591,7 +591,7 @@ def run_projection(args, name):
         # lc_proj_m_host: upload, compute, read back and wait in one C-ABI call)
         x_host = torch.from_numpy(synth.activations(m, k0, rng)).pin_memory()
         y_host = {nm: torch.empty((m, n), dtype=torch.float32).pin_memory() for nm, k, n in wl["shapes"]}
-        e2e_steps = max(10, args.steps // 2)
+        e2e_steps = max(100, args.steps)
 
         def host_step(i):
             ws = weights[i % pool]
