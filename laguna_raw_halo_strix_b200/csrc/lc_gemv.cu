@@ -526,11 +526,17 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32, 1) gemv_rows_kernel(const __
     const int nmy = r1 - r0 > rgi ? (r1 - r0 - rgi + a.rg - 1) / a.rg : 0;  // rows r0 + rgi + i * rg
     // this warp's bytes of a row: the slice (the last one may be shorter)
     const int sbytes = min(L::SLICE, a.row_bytes - slice * L::SLICE);
-    // source of the warp's slice of its i-th row (one matrix: a fixed stride)
-    const size_t rstride = (size_t)a.rg * a.row_bytes;
-    const uint8_t *src0 = a.w[0] + (size_t)(r0 + rgi) * a.row_bytes + (size_t)slice * L::SLICE;
+    // source of the warp's slice of its i-th row: a fixed stride when the
+    // warp's rows lie in one matrix -- one matrix, or interleaved pairs with an
+    // even number of row groups (r0 is even, so the warp keeps one parity)
+    const bool fixed = a.ng == 1 || (a.pairs && (a.rg & 1) == 0);
+    const int rw = r0 + rgi;
+    const size_t rstride = (size_t)(a.ng == 1 ? a.rg : a.rg >> 1) * a.row_bytes;
+    const uint8_t *src0 = (a.ng == 1 ? a.w[0] + (size_t)rw * a.row_bytes
+                                     : a.w[rw & 1] + (size_t)(rw >> 1) * a.row_bytes) +
+                          (size_t)slice * L::SLICE;
     auto slice_ptr = [&](int i) {
-        if (a.ng == 1) return src0 + (size_t)i * rstride;
+        if (fixed) return src0 + (size_t)i * rstride;
         int g, ri;
         gv_row(a, r0 + rgi + i * a.rg, g, ri);
         return a.w[g] + (size_t)ri * a.row_bytes + (size_t)slice * L::SLICE;

@@ -154,6 +154,28 @@ def test_ffn_block(ctx, dev, oracle, dtype, m):
             check_tol(got[j], ref, F32_TOL, f"ffn dtype {dtype} token {j} (f32)")
 
 
+@pytest.mark.parametrize("dtype,m,E,F", [(orc.Q4_K, 1, 512, 768), (orc.Q4_K, 2, 256, 1280), (orc.Q8_0, 1, 256, 256),
+                                         (orc.Q4_K, 1, 256, 256), (orc.Q8_0, 1, 2048, 2304)])
+def test_ffn_block_small(ctx, dev, oracle, dtype, m, E, F):
+    """The interleaved gate/up launch at sizes where CTAs hold a few row pairs
+    (2F rows over 148 CTAs, range bounds rounded to whole pairs, some CTAs
+    with none): every SiLU(gate) * up pair formed once, as the oracle's."""
+    import torch
+
+    rng = np.random.default_rng(7 * F + m)
+    wg = synth.weight_blocks(dtype, F, E, rng)
+    wu = synth.weight_blocks(dtype, F, E, rng)
+    wd = synth.weight_blocks(dtype, E, F, rng)
+    x = synth.activations(m, E, rng)
+    y = torch.full((m, E), float("nan"), device=dev)
+    ctx.ffn(dtype, to_dev(x, dev), to_dev(wg, dev), to_dev(wu, dev), to_dev(wd, dev), y, m, E, F)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    for j in range(m):
+        h = oracle.activation(oracle.proj(dtype, x[j:j + 1], wg, E, F)[0], oracle.proj(dtype, x[j:j + 1], wu, E, F)[0])
+        check_tol(got[j], oracle.proj(dtype, h[None, :], wd, F, E)[0], F32_TOL, f"ffn {dtype} m={m} {E}x{F} row {j}")
+
+
 @pytest.mark.parametrize("dtype,m", [(orc.Q4_K, 1), (orc.Q8_0, 1), (orc.Q4_K, 16)])
 def test_host_buffer_calls(ctx, dev, dtype, m):
     """lc_ffn_host / lc_proj_m_host (upload, compute, read back in one call)
