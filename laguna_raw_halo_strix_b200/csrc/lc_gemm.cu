@@ -301,10 +301,17 @@ __device__ __forceinline__ void pack_warp(const float *__restrict__ x, const flo
     }
 }
 
+// 16-byte stores from the first 16-byte boundary, single floats before and after it.
 __device__ __forceinline__ void zero_outputs(const ZeroList *Z, long long tid0, long long nthreads) {
     for (int z = 0; z < Z->cnt; z++) {
         float *p = Z->p[z];
-        for (long long i = tid0; i < Z->n[z]; i += nthreads) p[i] = 0.f;
+        const long long n = Z->n[z];
+        const long long head = min(n, (long long)(((16u - ((uint32_t)(uintptr_t)p & 15u)) & 15u) >> 2));
+        const long long n4 = (n - head) >> 2;
+        if (tid0 < head) p[tid0] = 0.f;
+        float4 *q = reinterpret_cast<float4 *>(p + head);
+        for (long long i = tid0; i < n4; i += nthreads) q[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (long long i = head + 4 * n4 + tid0; i < n; i += nthreads) p[i] = 0.f;
     }
 }
 
@@ -319,15 +326,17 @@ __global__ void x16_pack_kernel(const float *__restrict__ x, const float *__rest
                   threadIdx.x & 31);
 }
 
-// LC_PACK_RMSNORM: CTA t forms token slot t's sum of squares over the row
-// once (rmsnorm.comp: rsqrt(sum / k + eps)), then its warps pack the
-// super-blocks with (x * w) * rms.
+// LC_PACK_RMSNORM: grid (token slots, super-block groups of 8).  A CTA forms
+// its token slot's sum of squares over the row (rmsnorm.comp: rsqrt(sum / k +
+// eps); the super-block groups of a token repeat it), then its 8 warps pack
+// their super-blocks with (x * w) * rms.
 __global__ void x16_pack_norm_kernel(const float *__restrict__ x, const float *__restrict__ w, float eps, int m, int k,
                                      int q8, int nt, __half *__restrict__ x16, uint8_t *__restrict__ sx16,
                                      float *__restrict__ inv, const __grid_constant__ ZeroList zl) {
     griddep_launch_dependents();
     __shared__ float red[33];
-    zero_outputs(&zl, (long long)blockIdx.x * blockDim.x + threadIdx.x, (long long)gridDim.x * blockDim.x);
+    zero_outputs(&zl, ((long long)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x,
+                 (long long)gridDim.x * gridDim.y * blockDim.x);
     const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     float ss = 0.f;
     if (t < m) {
@@ -349,8 +358,8 @@ __global__ void x16_pack_norm_kernel(const float *__restrict__ x, const float *_
     }
     __syncthreads();
     const float rms = rsqrtf(red[32] / (float)k + eps);
-    for (int sb = warp; sb < (k >> 8); sb += nw)
-        pack_warp<lc::LC_PACK_RMSNORM>(x, w, 0, rms, m, k, q8, nt, x16, sx16, inv, sb, t, lane);
+    const int sb = blockIdx.y * nw + warp;
+    if (sb < (k >> 8)) pack_warp<lc::LC_PACK_RMSNORM>(x, w, 0, rms, m, k, q8, nt, x16, sx16, inv, sb, t, lane);
 }
 
 struct GemmLayout {
@@ -1467,8 +1476,8 @@ int launch_dq_gemm(lc_ctx *ctx, const lc::PackSrc &src, const lc::ProjOut *outs,
         x16_pack_kernel<lc::LC_PACK_HEADGATE><<<pgrid, 256, 0, ctx->stream>>>(src.x, src.x2, src.head_dim, (int)m,
                                                                              (int)k, q8, NT, x16, sx16, inv, zl);
     else if (src.op == lc::LC_PACK_RMSNORM)
-        x16_pack_norm_kernel<<<NT, 32 * std::min(S, 16u), 0, ctx->stream>>>(src.x, src.x2, src.eps, (int)m, (int)k, q8,
-                                                                           NT, x16, sx16, inv, zl);
+        x16_pack_norm_kernel<<<dim3(NT, (S + 7) / 8), 256, 0, ctx->stream>>>(src.x, src.x2, src.eps, (int)m, (int)k,
+                                                                            q8, NT, x16, sx16, inv, zl);
     else
         x16_pack_kernel<lc::LC_PACK_PLAIN><<<pgrid, 256, 0, ctx->stream>>>(src.x, nullptr, 0, (int)m, (int)k, q8, NT,
                                                                           x16, sx16, inv, zl);
