@@ -511,12 +511,40 @@ __global__ void __launch_bounds__(kAtThreads, 1)
 // lane-parallel (split s by lane s % 32) and M and the weights formed with
 // shuffles, so every split's loads are independent of the others.  Launched as
 // a programmatic dependent of the partial kernel.
+constexpr int kCombineFast = 24;  // splits merged from registers (2064 keys: 17 tiles)
+
 __global__ void attn_combine_kernel(const float *__restrict__ o_part, const float2 *__restrict__ ml_part,
                                     float *__restrict__ out, int m, int n_q, int splits) {
     griddep_wait();  // the partial states
     const int rh = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (rh >= m * n_q) return;
     const size_t stride = (size_t)m * n_q;
+    if (splits <= kCombineFast) {
+        // every split's output row requested with the (m, l) states, before
+        // the weights they wait for: one round trip to L2 instead of two
+        float4 ov[kCombineFast];
+#pragma unroll
+        for (int j = 0; j < kCombineFast; j++)
+            if (j < splits) ov[j] = *reinterpret_cast<const float4 *>(o_part + ((size_t)j * stride + rh) * kHD + 4 * lane);
+        const float2 ml = lane < splits ? ml_part[lane * stride + rh] : make_float2(kNegInit, 0.f);
+        float M = ml.y != 0.f ? ml.x : kNegInit;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float w = (lane < splits && ml.y != 0.f) ? expf(ml.x - M) : 0.f;
+        float L = lane < splits ? ml.y * w : 0.f;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < kCombineFast; j++)
+            if (j < splits) {
+                const float b = __shfl_sync(0xffffffffu, w, j);
+                O.x += ov[j].x * b, O.y += ov[j].y * b, O.z += ov[j].z * b, O.w += ov[j].w * b;
+            }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        *reinterpret_cast<float4 *>(out + (size_t)rh * kHD + 4 * lane) =
+            L > 0.f ? make_float4(O.x / L, O.y / L, O.z / L, O.w / L) : make_float4(0.f, 0.f, 0.f, 0.f);
+        return;
+    }
     float M = kNegInit;
     for (int s0 = 0; s0 < splits; s0 += 32)
         if (s0 + lane < splits) {
