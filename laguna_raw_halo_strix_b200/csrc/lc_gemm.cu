@@ -610,41 +610,77 @@ __global__ void __launch_bounds__(DqWarps<NT>::kAll * 32, 1)
                 if (!mbar_wait(s_full + db, par)) { fail(); break; }
                 dd = dslot[db * kRows + 32 * q + lane];
             }
-            // Per 16 tokens: the hi and lo columns (and the Q4_K min term's)
-            // summed, scaled into the row's partial sums.
-#pragma unroll
-            for (int c = 0; c < NT / 16; c++) {
-                float iv[16], pr[16], mn[16], h[16], l[16];
-#pragma unroll
-                for (int t = 0; t < 16; t += 4) {
-                    const float4 f = __ldg(reinterpret_cast<const float4 *>(inv + sb * NT + 16 * c + t));
-                    iv[t] = f.x, iv[t + 1] = f.y, iv[t + 2] = f.z, iv[t + 3] = f.w;
-                }
-                tmem_ld16(col + 16 * c, h);
-                tmem_ld16(col + NT + 16 * c, l);
+            if constexpr (NT == 16) {
+                // the accumulators into registers (hi and lo summed), the
+                // buffer released to the next MMAs, then the arithmetic
+                float pr[16], mn[16], h[16], l[16];
+                tmem_ld16(col, h);
+                tmem_ld16(col + NT, l);
                 tmem_ld_wait();
                 tmem_regs_ready(h), tmem_regs_ready(l);
 #pragma unroll
                 for (int i = 0; i < 16; i++) pr[i] = h[i] + l[i];
                 if constexpr (Q4) {
-                    tmem_ld16(col + NB + 16 * c, h);
-                    tmem_ld16(col + NB + NT + 16 * c, l);
+                    tmem_ld16(col + NB, h);
+                    tmem_ld16(col + NB + NT, l);
                     tmem_ld_wait();
                     tmem_regs_ready(h), tmem_regs_ready(l);
 #pragma unroll
                     for (int i = 0; i < 16; i++) mn[i] = h[i] + l[i];
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(d_empty + db);
+                float iv16[16];
+#pragma unroll
+                for (int t = 0; t < 16; t += 4) {
+                    const float4 f = __ldg(reinterpret_cast<const float4 *>(inv + sb * NT + t));
+                    iv16[t] = f.x, iv16[t + 1] = f.y, iv16[t + 2] = f.z, iv16[t + 3] = f.w;
+                }
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
                     if constexpr (Q4)
-                        acc[16 * c + i] += iv[i] * (dd.x * pr[i] - dd.y * mn[i]);
+                        acc[i] += iv16[i] * (dd.x * pr[i] - dd.y * mn[i]);
                     else
-                        acc[16 * c + i] += iv[i] * pr[i];
+                        acc[i] += iv16[i] * pr[i];
                 }
+            } else {
+                // Per 16 tokens: the hi and lo columns (and the Q4_K min term's)
+                // summed, scaled into the row's partial sums.
+    #pragma unroll
+                for (int c = 0; c < NT / 16; c++) {
+                    float iv[16], pr[16], mn[16], h[16], l[16];
+    #pragma unroll
+                    for (int t = 0; t < 16; t += 4) {
+                        const float4 f = __ldg(reinterpret_cast<const float4 *>(inv + sb * NT + 16 * c + t));
+                        iv[t] = f.x, iv[t + 1] = f.y, iv[t + 2] = f.z, iv[t + 3] = f.w;
+                    }
+                    tmem_ld16(col + 16 * c, h);
+                    tmem_ld16(col + NT + 16 * c, l);
+                    tmem_ld_wait();
+                    tmem_regs_ready(h), tmem_regs_ready(l);
+    #pragma unroll
+                    for (int i = 0; i < 16; i++) pr[i] = h[i] + l[i];
+                    if constexpr (Q4) {
+                        tmem_ld16(col + NB + 16 * c, h);
+                        tmem_ld16(col + NB + NT + 16 * c, l);
+                        tmem_ld_wait();
+                        tmem_regs_ready(h), tmem_regs_ready(l);
+    #pragma unroll
+                        for (int i = 0; i < 16; i++) mn[i] = h[i] + l[i];
+                    }
+    #pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        if constexpr (Q4)
+                            acc[16 * c + i] += iv[i] * (dd.x * pr[i] - dd.y * mn[i]);
+                        else
+                            acc[16 * c + i] += iv[i] * pr[i];
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(d_empty + db);
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(d_empty + db);
             if (u == U1 - 1 || sb == S - 1) {  // end of this CTA's run over the tile
                 int ltile;
                 const int gi = group_of(G, tile, ltile);
